@@ -1,0 +1,20 @@
+// Status codes and the thread-local "last error" message of the C-ABI.
+// Every extern "C" entry point returns DN_OK (0) or a negative DN_ERR_* code
+// and never lets a C++ exception cross the boundary.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "../../include/denoiser_b200.h"
+
+namespace dnb {
+
+// Records `msg` as the calling thread's last error and returns `code`.
+int dn_fail(int code, const char* msg);
+int dn_fail_str(int code, const std::string& msg);
+// Records a CUDA error with context and returns DN_ERR_CUDA.
+int dn_cuda_fail(cudaError_t e, const char* where);
+
+}  // namespace dnb
