@@ -119,8 +119,9 @@ def param_specs(cfg: NAFConfig, temporal: str | None = None, num_frames: int = 3
                   ("bottleneck_mix.0.bias", (ch,))]
         for i in (1, 2):
             specs += _block_specs(f"bottleneck_mix.{i}", ch, *ex)
+    middle = []
     for i in range(cfg.middle_blocks):
-        specs += _block_specs(f"middle.{i}", ch, *ex)
+        middle += _block_specs(f"middle.{i}", ch, *ex)
     ups = []
     dec = []
     for lvl, nb in enumerate(cfg.dec_blocks):
@@ -128,7 +129,12 @@ def param_specs(cfg: NAFConfig, temporal: str | None = None, num_frames: int = 3
         ch //= 2
         for i in range(nb):
             dec += _block_specs(f"decoders.{lvl}.{i}", ch, *ex)
-    specs += ups + dec
+    if temporal is None:
+        # NAFNet registers decoders, ups, then middle (models.py:524-537).
+        specs += dec + ups + middle
+    else:
+        # NAFNetTemporal registers middle, ups, decoders (models.py:700-707).
+        specs += middle + ups + dec
     if temporal is not None:
         specs += [("ending.weight", (3, b, 3, 3)), ("ending.bias", (3,))]
     if temporal == "py":
