@@ -48,6 +48,84 @@ int dn_abi_version(void);
 int dn_umma_probe(const void* A, const void* B, float* D, int N, int K, uint32_t* err_dev,
                   void* stream);
 
+/* ------------------------------------------------------------------------
+ * Weights (host half of WeightStore, include/denoiser/weight_loader.h:61-101
+ * of the reference; format of training/export.py:48-118). Every .bin is
+ * memory-mapped and its size checked against numel * sizeof(dtype).
+ * ------------------------------------------------------------------------ */
+
+typedef struct dn_weights dn_weights;
+
+/* WeightStore::WeightStore (weight_loader.cc:63-76): DN_ERR_IO if the
+ * manifest or a .bin is missing, DN_ERR_FORMAT for bad JSON, an unknown
+ * dtype or a .bin whose size does not match its shape. */
+int dn_weights_open(const char* manifest_path, dn_weights** out);
+void dn_weights_close(dn_weights* weights);
+/* Number of manifest layers (Manifest::layers.size()). */
+int dn_weights_count(const dn_weights* weights);
+/* WeightStore::contains (weight_loader.h:76): 1 or 0. */
+int dn_weights_contains(const dn_weights* weights, const char* name);
+/* Shape (up to 8 dims), dtype (0 float32, 1 float16) and the mapped host
+ * bytes of `name`; DN_ERR_NOT_FOUND like WeightStore::get's out_of_range. */
+int dn_weights_info(const dn_weights* weights, const char* name, int64_t* shape, int* ndim, int* dtype,
+                    const void** host_data);
+/* Name of layer `index` in manifest order. */
+int dn_weights_name(const dn_weights* weights, int index, const char** name);
+/* Manifest::Architecture fields (weight_loader.h:30-39). */
+int dn_weights_arch(const dn_weights* weights, char* type_buf, int type_buf_len, int* base_channels,
+                    int* num_levels, int* in_channels, int* num_frames, int* use_warp);
+
+/* ------------------------------------------------------------------------
+ * Models: NAFNet (spatial) and NAFNetTemporal, architecture discovered from
+ * the manifest keys like the reference engine (src/models/nafnet.cu:78-92,
+ * 281-333; src/models/nafnet_temporal.cu:260-356). One model = one device;
+ * drive each model from one host thread (the reference's contract).
+ * ------------------------------------------------------------------------ */
+
+typedef struct dn_model dn_model;
+
+typedef struct dn_model_info {
+    int kind;            /* 0 NAFNet, 1 NAFNetTemporal (C++ engine design) */
+    int in_channels;     /* NAFNet::in_channels()                           */
+    int num_levels;      /* NAFNet::num_levels()                            */
+    int base_channels;
+    int num_frames;      /* NAFNetTemporal::num_frames() (1 for NAFNet)      */
+    int use_warp;        /* NAFNetTemporal::use_warp()                      */
+    int enc_channels[8]; /* NAFNet::enc_channels(), zero-filled              */
+} dn_model_info;
+
+/* Load manifest.json + .bin weights (replaces WeightStore + NAFNet /
+ * NAFNetTemporal construction, include/denoiser/models/nafnet.h:13,
+ * nafnet_temporal.h:13) and upload them, packed, to `device`.
+ * Errors: DN_ERR_IO (missing file), DN_ERR_FORMAT (bad JSON, size or shape),
+ * DN_ERR_NOT_FOUND (missing key), DN_ERR_INVALID_ARG (bad device). */
+int dn_model_create(const char* manifest_path, int device, dn_model** out);
+int dn_model_destroy(dn_model* model);
+int dn_model_get_info(const dn_model* model, dn_model_info* info);
+
+/* Forward on device buffers, asynchronous on `stream` (cudaStream_t, NULL =
+ * legacy default stream). Replaces NAFNet::forward (nafnet.h:20) for
+ * x = (N, C, H, W) fp16 NCHW and NAFNetTemporal::forward (nafnet_temporal.h:20)
+ * for x = (N, T, C, H, W); y = (N, 3, H, W) fp16 NCHW (caller-allocated).
+ * y = beauty + residual, no clamping (training/models.py:575-577). */
+int dn_model_forward(dn_model* model, const void* x, const int64_t* shape, int ndim, void* y,
+                     void* stream);
+
+/* Same with host buffers (pinned for full speed): H2D copy, forward, D2H
+ * copy, then synchronises `stream` and checks the device error word. This is
+ * the CLI's per-frame call (cli/main.cc:300-315 of the reference). */
+int dn_model_forward_host(dn_model* model, const void* x_host, const int64_t* shape, int ndim,
+                          void* y_host, void* stream);
+
+/* Synchronise `stream`; DN_ERR_DEVICE if a kernel reported a device-side
+ * error (e.g. a bounded wait that expired) since the last check. */
+int dn_model_sync(dn_model* model, void* stream);
+
+/* Device bytes of the packed weights and the activation arena of the last
+ * planned shape, and the number of kernels the last forward launched. */
+int dn_model_stats(const dn_model* model, size_t* weight_bytes, size_t* activation_bytes,
+                   int* kernels_per_forward);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -50,11 +50,39 @@ _I64 = _c.c_int64
 _F = _c.c_float
 _U32P = _c.POINTER(_c.c_uint32)
 
+class ModelInfo(ctypes.Structure):
+    """dn_model_info of include/denoiser_b200.h."""
+
+    _fields_ = [("kind", ctypes.c_int), ("in_channels", ctypes.c_int), ("num_levels", ctypes.c_int),
+                ("base_channels", ctypes.c_int), ("num_frames", ctypes.c_int), ("use_warp", ctypes.c_int),
+                ("enc_channels", ctypes.c_int * 8)]
+
+
+_PP = _c.POINTER(_c.c_void_p)
+_I64P = _c.POINTER(_c.c_int64)
+_IP = _c.POINTER(_c.c_int)
+_SZP = _c.POINTER(_c.c_size_t)
+_CPP = _c.POINTER(_c.c_char_p)
+
 # name -> (restype, argtypes); every symbol of include/denoiser_b200.h.
 SIGNATURES = {
     "dn_last_error": (_c.c_char_p, []),
     "dn_abi_version": (_I, []),
     "dn_umma_probe": (_I, [_P, _P, _P, _I, _I, _P, _P]),
+    "dn_weights_open": (_I, [_c.c_char_p, _PP]),
+    "dn_weights_close": (None, [_P]),
+    "dn_weights_count": (_I, [_P]),
+    "dn_weights_contains": (_I, [_P, _c.c_char_p]),
+    "dn_weights_info": (_I, [_P, _c.c_char_p, _I64P, _IP, _IP, _PP]),
+    "dn_weights_name": (_I, [_P, _I, _CPP]),
+    "dn_weights_arch": (_I, [_P, _c.c_char_p, _I, _IP, _IP, _IP, _IP, _IP]),
+    "dn_model_create": (_I, [_c.c_char_p, _I, _PP]),
+    "dn_model_destroy": (_I, [_P]),
+    "dn_model_get_info": (_I, [_P, _c.POINTER(ModelInfo)]),
+    "dn_model_forward": (_I, [_P, _P, _I64P, _I, _P, _P]),
+    "dn_model_forward_host": (_I, [_P, _P, _I64P, _I, _P, _P]),
+    "dn_model_sync": (_I, [_P, _P]),
+    "dn_model_stats": (_I, [_P, _SZP, _SZP, _IP]),
 }
 
 
@@ -109,3 +137,132 @@ def umma_probe(a, b):
     if int(err.item()) != 0:
         raise DenoiserError(DN_ERR_DEVICE, f"device error word {int(err.item()):#x}")
     return d
+
+
+class Weights:
+    """Host half of the reference WeightStore: parsed + validated manifest."""
+
+    def __init__(self, manifest_path: str):
+        h = ctypes.c_void_p()
+        check(lib().dn_weights_open(os.fsencode(manifest_path), ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.dn_weights_close(self._h)
+        self._h = None
+
+    __del__ = close
+
+    def __len__(self) -> int:
+        return lib().dn_weights_count(self._h)
+
+    def __contains__(self, name: str) -> bool:
+        return bool(lib().dn_weights_contains(self._h, name.encode()))
+
+    def names(self) -> list:
+        out = []
+        for i in range(len(self)):
+            p = ctypes.c_char_p()
+            check(lib().dn_weights_name(self._h, i, ctypes.byref(p)))
+            out.append(p.value.decode())
+        return out
+
+    def info(self, name: str):
+        """(shape tuple, dtype str) of `name`; NotFoundError if absent."""
+        shape = (ctypes.c_int64 * 8)()
+        nd = ctypes.c_int()
+        dt = ctypes.c_int()
+        check(lib().dn_weights_info(self._h, name.encode(), shape, ctypes.byref(nd), ctypes.byref(dt), None))
+        return tuple(shape[i] for i in range(nd.value)), ("float16" if dt.value == 1 else "float32")
+
+    def arch(self) -> dict:
+        buf = ctypes.create_string_buffer(64)
+        v = [ctypes.c_int() for _ in range(5)]
+        check(lib().dn_weights_arch(self._h, buf, 64, *[ctypes.byref(x) for x in v]))
+        return {"type": buf.value.decode(), "base_channels": v[0].value, "num_levels": v[1].value,
+                "in_channels": v[2].value, "num_frames": v[3].value, "use_warp": bool(v[4].value)}
+
+
+class Model:
+    """NAFNet / NAFNetTemporal engine instance on one CUDA device.
+
+    ``forward`` takes an fp16 CUDA tensor (N, C, H, W) (spatial) or
+    (N, T, C, H, W) (temporal) and returns the (N, 3, H, W) fp16 output,
+    launched on the current torch stream.
+    """
+
+    def __init__(self, manifest_path: str, device: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().dn_model_create(os.fsencode(manifest_path), device, ctypes.byref(h)))
+        self._h = h
+        self.device = device
+        info = ModelInfo()
+        check(lib().dn_model_get_info(self._h, ctypes.byref(info)))
+        self.kind = info.kind
+        self.in_channels = info.in_channels
+        self.num_levels = info.num_levels
+        self.base_channels = info.base_channels
+        self.num_frames = info.num_frames
+        self.use_warp = bool(info.use_warp)
+        self.enc_channels = [info.enc_channels[i] for i in range(info.num_levels)]
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.dn_model_destroy(self._h)
+        self._h = None
+
+    __del__ = close
+
+    def _shape(self, x):
+        shape = (ctypes.c_int64 * x.dim())(*x.shape)
+        return shape, x.dim()
+
+    def forward(self, x, out=None, stream=None):
+        import torch
+
+        if x.dtype != torch.float16:
+            raise DenoiserError(DN_ERR_DTYPE, "NAFNet::forward: expected FP16 input")
+        if not x.is_cuda:
+            raise InvalidArgumentError(DN_ERR_INVALID_ARG, "forward: input must be a CUDA tensor")
+        x = x.contiguous()
+        n = x.shape[0]
+        h, w = x.shape[-2:]
+        if out is None:
+            out = torch.empty(n, 3, h, w, dtype=torch.float16, device=x.device)
+        shape, nd = self._shape(x)
+        check(lib().dn_model_forward(self._h, x.data_ptr(), shape, nd, out.data_ptr(), stream_handle(stream)))
+        return out
+
+    __call__ = forward
+
+    def forward_host(self, x, out=None, stream=None):
+        """Host (numpy fp16, ideally pinned) in and out, synchronous."""
+        import numpy as np
+
+        x = np.ascontiguousarray(x, dtype=np.float16)
+        n = x.shape[0]
+        h, w = x.shape[-2:]
+        if out is None:
+            out = np.empty((n, 3, h, w), dtype=np.float16)
+        shape = (ctypes.c_int64 * x.ndim)(*x.shape)
+        check(lib().dn_model_forward_host(self._h, x.ctypes.data, shape, x.ndim, out.ctypes.data,
+                                          ctypes.c_void_p(stream or 0)))
+        return out
+
+    def forward_host_ptr(self, x_ptr: int, shape, y_ptr: int, stream_ptr: int = 0) -> None:
+        """Host-buffer forward on raw pointers (e.g. pinned torch tensors)."""
+        sh = (ctypes.c_int64 * len(shape))(*shape)
+        check(lib().dn_model_forward_host(self._h, ctypes.c_void_p(x_ptr), sh, len(shape),
+                                          ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream_ptr)))
+
+    def sync(self, stream=None) -> None:
+        """Synchronise the stream and raise if a kernel flagged a device error."""
+        check(lib().dn_model_sync(self._h, stream_handle(stream)))
+
+    def stats(self) -> dict:
+        wb = ctypes.c_size_t()
+        ab = ctypes.c_size_t()
+        kl = ctypes.c_int()
+        check(lib().dn_model_stats(self._h, ctypes.byref(wb), ctypes.byref(ab), ctypes.byref(kl)))
+        return {"weight_bytes": wb.value, "activation_bytes": ab.value, "kernels_per_forward": kl.value}

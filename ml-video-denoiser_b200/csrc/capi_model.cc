@@ -1,0 +1,175 @@
+// C-ABI of the model engine: the drop-in boundary behind NAFNet::forward /
+// NAFNetTemporal::forward (include/denoiser/models/nafnet.h:11-28,
+// nafnet_temporal.h:11-29 of the reference) and the CLI's per-frame loop.
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <new>
+#include <string>
+
+#include "engine.h"
+#include "status.h"
+
+using namespace dnb;
+
+struct dn_model {
+    std::unique_ptr<Engine> eng;
+    // Device staging for the host-buffer entry point.
+    void* dx = nullptr;
+    void* dy = nullptr;
+    size_t dx_bytes = 0, dy_bytes = 0;
+};
+
+namespace {
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        return f();
+    } catch (const NotFoundError& e) {
+        return dn_fail(DN_ERR_NOT_FOUND, e.what());
+    } catch (const IoError& e) {
+        return dn_fail(DN_ERR_IO, e.what());
+    } catch (const FormatError& e) {
+        return dn_fail(DN_ERR_FORMAT, e.what());
+    } catch (const std::bad_alloc&) {
+        return dn_fail(DN_ERR_CUDA, "host out of memory");
+    } catch (const std::exception& e) {
+        return dn_fail(DN_ERR_CUDA, e.what());
+    } catch (...) {
+        return dn_fail(DN_ERR_CUDA, "unknown error");
+    }
+}
+
+// Parses (N,C,H,W) or (N,T,C,H,W) for the model kind.
+int parse_shape(const Engine& e, const int64_t* shape, int ndim, int& N, int& T, int& C, int& H, int& W) {
+    if (!shape) return dn_fail(DN_ERR_INVALID_ARG, "forward: null shape");
+    const bool temporal = e.info().kind != 0;
+    if (temporal && ndim != 5) return dn_fail(DN_ERR_INVALID_ARG, "NAFNetTemporal::forward: expected 5-D (N,T,C,H,W) clip");
+    if (!temporal && ndim != 4) return dn_fail(DN_ERR_INVALID_ARG, "NAFNet::forward: expected 4-D NCHW input");
+    for (int i = 0; i < ndim; ++i)
+        if (shape[i] <= 0 || shape[i] > (1 << 20)) return dn_fail(DN_ERR_INVALID_ARG, "forward: bad dimension");
+    N = static_cast<int>(shape[0]);
+    T = temporal ? static_cast<int>(shape[1]) : 1;
+    C = static_cast<int>(shape[temporal ? 2 : 1]);
+    H = static_cast<int>(shape[temporal ? 3 : 2]);
+    W = static_cast<int>(shape[temporal ? 4 : 3]);
+    return DN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dn_model_create(const char* manifest_path, int device, dn_model** out) {
+    if (!manifest_path || !out) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_create: null argument");
+    *out = nullptr;
+    return guarded([&] {
+        int count = 0;
+        cudaError_t e = cudaGetDeviceCount(&count);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "cudaGetDeviceCount");
+        if (device < 0 || device >= count)
+            return dn_fail_str(DN_ERR_INVALID_ARG, "CUDA device " + std::to_string(device) + " not available (" +
+                                                       std::to_string(count) + " devices found)");
+        auto m = std::make_unique<dn_model>();
+        m->eng = std::make_unique<Engine>(manifest_path, device);
+        *out = m.release();
+        return DN_OK;
+    });
+}
+
+int dn_model_destroy(dn_model* m) {
+    if (!m) return DN_OK;
+    return guarded([&] {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(m->eng->device());
+        if (m->dx) cudaFree(m->dx);
+        if (m->dy) cudaFree(m->dy);
+        cudaSetDevice(prev);
+        delete m;
+        return DN_OK;
+    });
+}
+
+int dn_model_get_info(const dn_model* m, dn_model_info* info) {
+    if (!m || !info) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_get_info: null argument");
+    const ModelInfo& i = m->eng->info();
+    info->kind = i.kind;
+    info->in_channels = i.in_channels;
+    info->num_levels = i.num_levels;
+    info->base_channels = i.base_channels;
+    info->num_frames = i.num_frames;
+    info->use_warp = i.use_warp;
+    for (int l = 0; l < 8; ++l)
+        info->enc_channels[l] = l < static_cast<int>(i.enc_channels.size()) ? i.enc_channels[l] : 0;
+    return DN_OK;
+}
+
+int dn_model_forward(dn_model* m, const void* x, const int64_t* shape, int ndim, void* y, void* stream) {
+    if (!m || !x || !y) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_forward: null argument");
+    return guarded([&] {
+        int N, T, C, H, W;
+        const int rc = parse_shape(*m->eng, shape, ndim, N, T, C, H, W);
+        if (rc != DN_OK) return rc;
+        return m->eng->forward(static_cast<const __half*>(x), N, T, C, H, W, static_cast<__half*>(y),
+                               static_cast<cudaStream_t>(stream));
+    });
+}
+
+int dn_model_forward_host(dn_model* m, const void* x_host, const int64_t* shape, int ndim, void* y_host,
+                          void* stream) {
+    if (!m || !x_host || !y_host) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_forward_host: null argument");
+    return guarded([&] {
+        int N, T, C, H, W;
+        int rc = parse_shape(*m->eng, shape, ndim, N, T, C, H, W);
+        if (rc != DN_OK) return rc;
+        const size_t xb = static_cast<size_t>(N) * T * C * H * W * 2;
+        const size_t yb = static_cast<size_t>(N) * 3 * H * W * 2;
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(m->eng->device());
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        cudaError_t e = cudaSuccess;
+        if (m->dx_bytes < xb) {
+            if (m->dx) cudaFree(m->dx);
+            m->dx = nullptr;
+            e = cudaMalloc(&m->dx, xb);
+            m->dx_bytes = e == cudaSuccess ? xb : 0;
+        }
+        if (e == cudaSuccess && m->dy_bytes < yb) {
+            if (m->dy) cudaFree(m->dy);
+            m->dy = nullptr;
+            e = cudaMalloc(&m->dy, yb);
+            m->dy_bytes = e == cudaSuccess ? yb : 0;
+        }
+        if (e == cudaSuccess) e = cudaMemcpyAsync(m->dx, x_host, xb, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) {
+            cudaSetDevice(prev);
+            return dn_cuda_fail(e, "dn_model_forward_host: staging");
+        }
+        rc = m->eng->forward(static_cast<const __half*>(m->dx), N, T, C, H, W, static_cast<__half*>(m->dy), s);
+        if (rc == DN_OK) {
+            e = cudaMemcpyAsync(y_host, m->dy, yb, cudaMemcpyDeviceToHost, s);
+            if (e != cudaSuccess) rc = dn_cuda_fail(e, "dn_model_forward_host: copy back");
+        }
+        if (rc == DN_OK) rc = m->eng->check_device(s);
+        cudaSetDevice(prev);
+        return rc;
+    });
+}
+
+int dn_model_sync(dn_model* m, void* stream) {
+    if (!m) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_sync: null model");
+    return guarded([&] { return m->eng->check_device(static_cast<cudaStream_t>(stream)); });
+}
+
+int dn_model_stats(const dn_model* m, size_t* weight_bytes, size_t* activation_bytes, int* kernels_per_forward) {
+    if (!m) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_stats: null model");
+    if (weight_bytes) *weight_bytes = m->eng->weight_bytes();
+    if (activation_bytes) *activation_bytes = m->eng->activation_bytes();
+    if (kernels_per_forward) *kernels_per_forward = m->eng->kernels_per_forward();
+    return DN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,89 @@
+// C-ABI of the host half of WeightStore (include/denoiser/weight_loader.h
+// :61-101 of the reference): parse manifest.json, map and validate every .bin,
+// look tensors up by name. No device is needed, so format errors surface on
+// any host.
+#include <cstring>
+#include <memory>
+#include <new>
+
+#include "manifest.h"
+#include "status.h"
+
+using namespace dnb;
+
+struct dn_weights {
+    std::unique_ptr<HostWeights> hw;
+};
+
+extern "C" {
+
+int dn_weights_open(const char* manifest_path, dn_weights** out) {
+    if (!manifest_path || !out) return dn_fail(DN_ERR_INVALID_ARG, "dn_weights_open: null argument");
+    *out = nullptr;
+    try {
+        auto w = std::make_unique<dn_weights>();
+        w->hw = std::make_unique<HostWeights>(manifest_path);
+        *out = w.release();
+        return DN_OK;
+    } catch (const NotFoundError& e) {
+        return dn_fail(DN_ERR_NOT_FOUND, e.what());
+    } catch (const IoError& e) {
+        return dn_fail(DN_ERR_IO, e.what());
+    } catch (const FormatError& e) {
+        return dn_fail(DN_ERR_FORMAT, e.what());
+    } catch (const std::exception& e) {
+        return dn_fail(DN_ERR_FORMAT, e.what());
+    }
+}
+
+void dn_weights_close(dn_weights* w) { delete w; }
+
+int dn_weights_count(const dn_weights* w) {
+    if (!w) return dn_fail(DN_ERR_INVALID_ARG, "dn_weights_count: null handle");
+    return static_cast<int>(w->hw->entries().size());
+}
+
+int dn_weights_contains(const dn_weights* w, const char* name) {
+    if (!w || !name) return 0;
+    return w->hw->contains(name) ? 1 : 0;
+}
+
+int dn_weights_info(const dn_weights* w, const char* name, int64_t* shape, int* ndim, int* dtype,
+                    const void** host_data) {
+    if (!w || !name) return dn_fail(DN_ERR_INVALID_ARG, "dn_weights_info: null argument");
+    if (!w->hw->contains(name))
+        return dn_fail_str(DN_ERR_NOT_FOUND, std::string("WeightStore: layer not found: ") + name);
+    const WEntry& e = w->hw->entry(name);
+    if (ndim) *ndim = static_cast<int>(e.shape.size());
+    if (shape)
+        for (size_t i = 0; i < e.shape.size() && i < 8; ++i) shape[i] = e.shape[i];
+    if (dtype) *dtype = static_cast<int>(e.dtype);
+    if (host_data) *host_data = e.data;
+    return DN_OK;
+}
+
+int dn_weights_name(const dn_weights* w, int index, const char** name) {
+    if (!w || !name) return dn_fail(DN_ERR_INVALID_ARG, "dn_weights_name: null argument");
+    if (index < 0 || index >= static_cast<int>(w->hw->entries().size()))
+        return dn_fail(DN_ERR_INVALID_ARG, "dn_weights_name: index out of range");
+    *name = w->hw->entries()[index].name.c_str();
+    return DN_OK;
+}
+
+int dn_weights_arch(const dn_weights* w, char* type_buf, int type_buf_len, int* base_channels,
+                    int* num_levels, int* in_channels, int* num_frames, int* use_warp) {
+    if (!w) return dn_fail(DN_ERR_INVALID_ARG, "dn_weights_arch: null handle");
+    const ManifestArch& a = w->hw->arch();
+    if (type_buf && type_buf_len > 0) {
+        std::strncpy(type_buf, a.type.c_str(), type_buf_len - 1);
+        type_buf[type_buf_len - 1] = '\0';
+    }
+    if (base_channels) *base_channels = a.base_channels;
+    if (num_levels) *num_levels = a.num_levels;
+    if (in_channels) *in_channels = a.in_channels;
+    if (num_frames) *num_frames = a.num_frames;
+    if (use_warp) *use_warp = a.use_warp ? 1 : 0;
+    return DN_OK;
+}
+
+}  // extern "C"

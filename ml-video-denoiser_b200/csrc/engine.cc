@@ -1,0 +1,681 @@
+#include "engine.h"
+
+#include <algorithm>
+#include <cstring>
+#include <stdexcept>
+
+#include "status.h"
+
+namespace dnb {
+
+int launch_warp_pixel(const __half* feat, const __half* off, int off_stride, __half* out, int nimg,
+                      int H, int W, int C, cudaStream_t s);
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int d) {
+        cudaGetDevice(&prev);
+        if (prev != d) cudaSetDevice(d);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+uint32_t kmajor_offset_host(uint32_t row, uint32_t kchunk, uint32_t sbo) {
+    return (row >> 3) * sbo + kchunk * 128u + (row & 7u) * 16u;
+}
+
+int next_pow2(int v) {
+    int p = 1;
+    while (p < v) p <<= 1;
+    return p;
+}
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+struct Packer {
+    std::vector<uint8_t> host;
+    size_t add(const void* p, size_t bytes) {
+        const size_t off = align256(host.size());
+        host.resize(off + bytes);
+        if (bytes) std::memcpy(host.data() + off, p, bytes);
+        return off;
+    }
+    size_t add_f32(const std::vector<float>& v) { return add(v.data(), v.size() * sizeof(float)); }
+};
+
+int store_nt(int n) { return std::min(128, next_pow2(std::max(16, n))); }
+
+// Pack logical W[N][K] (row-major fp32) into the tile image the GEMM kernel
+// bulk-copies: tiles [n_tile][k_chunk], each NT x KC fp16 in the no-swizzle
+// K-major core-matrix layout (8 rows x 16 B per core matrix, lbo 128 B).
+GemmW pack_gemm(Packer& pk, const std::vector<float>& W, int N, int K, int NT,
+                const std::vector<float>* bias, int n_out) {
+    GemmW g;
+    g.NT = NT;
+    g.K = K;
+    g.n_out = n_out;
+    const int Kp = K <= 64 ? round_up(K, 16) : round_up(K, 64);
+    g.KC = std::min(64, Kp);
+    g.k_chunks = Kp / g.KC;
+    g.n_tiles = (N + NT - 1) / NT;
+    const uint32_t sbo = static_cast<uint32_t>(g.KC / 8) * 128u;
+    const size_t tile_bytes = static_cast<size_t>(NT) * g.KC * 2;
+    std::vector<uint8_t> buf(tile_bytes * g.n_tiles * g.k_chunks, 0);
+    for (int t = 0; t < g.n_tiles; ++t)
+        for (int j = 0; j < g.k_chunks; ++j) {
+            uint8_t* tile = buf.data() + (static_cast<size_t>(t) * g.k_chunks + j) * tile_bytes;
+            for (int r = 0; r < NT; ++r) {
+                const int n = t * NT + r;
+                if (n >= N) break;
+                for (int k = 0; k < g.KC; ++k) {
+                    const int kk = j * g.KC + k;
+                    if (kk >= K) break;
+                    const __half h = __float2half(W[static_cast<size_t>(n) * K + kk]);
+                    std::memcpy(tile + kmajor_offset_host(r, k / 8, sbo) + (k % 8) * 2, &h, 2);
+                }
+            }
+        }
+    g.bpack = pk.add(buf.data(), buf.size());
+    if (bias) {
+        std::vector<float> b(static_cast<size_t>(g.n_tiles) * NT, 0.f);
+        for (int n = 0; n < N && n < static_cast<int>(bias->size()); ++n) b[n] = (*bias)[n];
+        g.bias = pk.add_f32(b);
+        g.has_bias = true;
+    }
+    return g;
+}
+
+// conv4 of a NAFBlock: the two SimpleGate halves are interleaved per tile so
+// that output channel c and its gate c + half land in the same tile.
+GemmW pack_gate(Packer& pk, const std::vector<float>& W, const std::vector<float>& bias, int half,
+                int K) {
+    const int hnt = std::min(64, next_pow2(std::max(16, half)));
+    const int NT = 2 * hnt;
+    const int n_tiles = (half + hnt - 1) / hnt;
+    const int N = n_tiles * NT;
+    std::vector<float> Wl(static_cast<size_t>(N) * K, 0.f), bl(N, 0.f);
+    for (int t = 0; t < n_tiles; ++t)
+        for (int r = 0; r < hnt; ++r) {
+            const int o = t * hnt + r;
+            if (o >= half) break;
+            std::memcpy(&Wl[static_cast<size_t>(t * NT + r) * K], &W[static_cast<size_t>(o) * K],
+                        K * sizeof(float));
+            std::memcpy(&Wl[static_cast<size_t>(t * NT + hnt + r) * K],
+                        &W[static_cast<size_t>(half + o) * K], K * sizeof(float));
+            bl[t * NT + r] = bias[o];
+            bl[t * NT + hnt + r] = bias[half + o];
+        }
+    return pack_gemm(pk, Wl, N, K, NT, &bl, half);
+}
+
+std::vector<int64_t> shape_of(const HostWeights& hw, const std::string& n) { return hw.entry(n).shape; }
+
+void expect_shape(const HostWeights& hw, const std::string& n, std::vector<int64_t> want) {
+    const auto& s = hw.entry(n).shape;
+    if (s != want) {
+        std::string a, b;
+        for (auto v : s) a += std::to_string(v) + ",";
+        for (auto v : want) b += std::to_string(v) + ",";
+        throw FormatError("unexpected shape for " + n + ": (" + a + ") expected (" + b + ")");
+    }
+}
+
+int count_levels(const HostWeights& hw, const std::string& root) {
+    int n = 0;
+    while (hw.contains(root + "." + std::to_string(n) + ".0.conv1.weight")) ++n;
+    return n;
+}
+
+int count_blocks(const HostWeights& hw, const std::string& root) {
+    int n = 0;
+    while (hw.contains(root + "." + std::to_string(n) + ".conv1.weight")) ++n;
+    return n;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Construction: discover the architecture from the weight keys (the way the
+// reference does, src/models/nafnet.cu:78-92, 281-333) and pack everything.
+// ---------------------------------------------------------------------------
+
+Engine::Engine(const std::string& manifest_path, int device) : device_(device) {
+    HostWeights hw(manifest_path);
+    DeviceGuard g(device_);
+    build(hw);
+}
+
+Engine::~Engine() {
+    DeviceGuard g(device_);
+    if (warena_) cudaFree(warena_);
+    if (aarena_) cudaFree(aarena_);
+}
+
+void Engine::build(const HostWeights& hw) {
+    Packer pk;
+    const int levels = count_levels(hw, "encoders");
+    if (levels <= 0) throw FormatError("NAFNet: no encoder levels found in exported weights");
+    pad_multiple_ = 1 << levels;
+    info_.num_levels = levels;
+
+    const auto intro_s = shape_of(hw, "intro.weight");
+    if (intro_s.size() != 4 || intro_s[2] != 3 || intro_s[3] != 3)
+        throw FormatError("intro.weight must be (C0, Cin, 3, 3)");
+    const int C0 = static_cast<int>(intro_s[0]);
+    info_.in_channels = static_cast<int>(intro_s[1]);
+    info_.base_channels = C0;
+    if (C0 % 8 != 0) throw FormatError("base channel count must be a multiple of 8");
+    expect_shape(hw, "intro.bias", {C0});
+    expect_shape(hw, "ending.weight", {3, C0, 3, 3});
+    expect_shape(hw, "ending.bias", {3});
+    intro_w_ = pk.add_f32(hw.to_f32("intro.weight"));
+    intro_b_ = pk.add_f32(hw.to_f32("intro.bias"));
+    {
+        const auto w = hw.to_f32("ending.weight");
+        std::vector<float> wl(27 * C0);
+        for (int o = 0; o < 3; ++o)
+            for (int c = 0; c < C0; ++c)
+                for (int t = 0; t < 9; ++t) wl[(o * 9 + t) * C0 + c] = w[(o * C0 + c) * 9 + t];
+        ending_w_ = pk.add_f32(wl);
+        ending_b_ = pk.add_f32(hw.to_f32("ending.bias"));
+    }
+
+    auto block = [&](const std::string& pre, int C) {
+        BlockW b;
+        b.C = C;
+        const auto s1 = shape_of(hw, pre + ".conv1.weight");
+        const auto s4 = shape_of(hw, pre + ".conv4.weight");
+        if (s1.size() != 4 || s1[1] != C || s1[0] % 2 != 0)
+            throw FormatError(pre + ".conv1.weight has an unexpected shape");
+        if (s4.size() != 4 || s4[1] != C || s4[0] % 2 != 0)
+            throw FormatError(pre + ".conv4.weight has an unexpected shape");
+        b.dw = static_cast<int>(s1[0] / 2);
+        b.ffn = static_cast<int>(s4[0] / 2);
+        if (b.dw % 8 != 0 || b.ffn % 8 != 0) throw FormatError(pre + ": channel counts must be multiples of 8");
+        expect_shape(hw, pre + ".norm1.weight", {C});
+        expect_shape(hw, pre + ".norm1.bias", {C});
+        expect_shape(hw, pre + ".norm2.weight", {C});
+        expect_shape(hw, pre + ".norm2.bias", {C});
+        expect_shape(hw, pre + ".beta", {1, C, 1, 1});
+        expect_shape(hw, pre + ".gamma", {1, C, 1, 1});
+        expect_shape(hw, pre + ".conv1.bias", {2 * b.dw});
+        expect_shape(hw, pre + ".conv2.weight", {2 * b.dw, 1, 3, 3});
+        expect_shape(hw, pre + ".conv2.bias", {2 * b.dw});
+        expect_shape(hw, pre + ".sca.1.weight", {b.dw, b.dw, 1, 1});
+        expect_shape(hw, pre + ".sca.1.bias", {b.dw});
+        expect_shape(hw, pre + ".conv3.weight", {C, b.dw, 1, 1});
+        expect_shape(hw, pre + ".conv3.bias", {C});
+        expect_shape(hw, pre + ".conv4.bias", {2 * b.ffn});
+        expect_shape(hw, pre + ".conv5.weight", {C, b.ffn, 1, 1});
+        expect_shape(hw, pre + ".conv5.bias", {C});
+        b.ln1w = pk.add_f32(hw.to_f32(pre + ".norm1.weight"));
+        b.ln1b = pk.add_f32(hw.to_f32(pre + ".norm1.bias"));
+        b.ln2w = pk.add_f32(hw.to_f32(pre + ".norm2.weight"));
+        b.ln2b = pk.add_f32(hw.to_f32(pre + ".norm2.bias"));
+        b.beta = pk.add_f32(hw.to_f32(pre + ".beta"));
+        b.gamma = pk.add_f32(hw.to_f32(pre + ".gamma"));
+        const auto b1 = hw.to_f32(pre + ".conv1.bias");
+        b.conv1 = pack_gemm(pk, hw.to_f32(pre + ".conv1.weight"), 2 * b.dw, C, store_nt(2 * b.dw), &b1,
+                            2 * b.dw);
+        {
+            const auto w2 = hw.to_f32(pre + ".conv2.weight");
+            std::vector<float> wt(9 * 2 * b.dw);
+            for (int c = 0; c < 2 * b.dw; ++c)
+                for (int t = 0; t < 9; ++t) wt[t * 2 * b.dw + c] = w2[c * 9 + t];
+            b.dw_w = pk.add_f32(wt);
+            b.dw_b = pk.add_f32(hw.to_f32(pre + ".conv2.bias"));
+        }
+        b.sca_w = pk.add_f32(hw.to_f32(pre + ".sca.1.weight"));
+        b.sca_b = pk.add_f32(hw.to_f32(pre + ".sca.1.bias"));
+        const auto b3 = hw.to_f32(pre + ".conv3.bias");
+        b.conv3 = pack_gemm(pk, hw.to_f32(pre + ".conv3.weight"), C, b.dw, store_nt(C), &b3, C);
+        b.conv4 = pack_gate(pk, hw.to_f32(pre + ".conv4.weight"), hw.to_f32(pre + ".conv4.bias"), b.ffn, C);
+        const auto b5 = hw.to_f32(pre + ".conv5.bias");
+        b.conv5 = pack_gemm(pk, hw.to_f32(pre + ".conv5.weight"), C, b.ffn, store_nt(C), &b5, C);
+        return b;
+    };
+
+    levels_.resize(levels);
+    int C = C0;
+    for (int l = 0; l < levels; ++l) {
+        Level& L = levels_[l];
+        L.C = C;
+        info_.enc_channels.push_back(C);
+        const std::string er = "encoders." + std::to_string(l);
+        for (int i = 0, n = count_blocks(hw, er); i < n; ++i) L.enc.push_back(block(er + "." + std::to_string(i), C));
+        // 2x2 stride-2 down: K index = tap * C + c, tap = ky*2 + kx.
+        const std::string dn = "downs." + std::to_string(l) + ".body";
+        expect_shape(hw, dn + ".weight", {2 * C, C, 2, 2});
+        expect_shape(hw, dn + ".bias", {2 * C});
+        const auto wd = hw.to_f32(dn + ".weight");
+        std::vector<float> wl(static_cast<size_t>(2 * C) * 4 * C);
+        for (int n = 0; n < 2 * C; ++n)
+            for (int c = 0; c < C; ++c)
+                for (int t = 0; t < 4; ++t) wl[static_cast<size_t>(n) * 4 * C + t * C + c] = wd[(n * C + c) * 4 + t];
+        const auto bd = hw.to_f32(dn + ".bias");
+        L.down = pack_gemm(pk, wl, 2 * C, 4 * C, store_nt(2 * C), &bd, 2 * C);
+        C *= 2;
+    }
+    for (int i = 0, n = count_blocks(hw, "middle"); i < n; ++i) middle_.push_back(block("middle." + std::to_string(i), C));
+    for (int d = 0; d < levels; ++d) {
+        // ups.d feeds resolution level lev = levels-1-d: 1x1 C -> 2C (no bias), PixelShuffle(2).
+        const int lev = levels - 1 - d;
+        const int Cin = C, Cout = C / 2;
+        const std::string un = "ups." + std::to_string(d) + ".body.0.weight";
+        expect_shape(hw, un, {2 * Cin, Cin, 1, 1});
+        const auto wu = hw.to_f32(un);
+        // packed column n' = ij * Cout + c  <-  PixelShuffle source channel 4c + ij
+        std::vector<float> wl(static_cast<size_t>(4 * Cout) * Cin);
+        for (int ij = 0; ij < 4; ++ij)
+            for (int c = 0; c < Cout; ++c)
+                std::memcpy(&wl[static_cast<size_t>(ij * Cout + c) * Cin], &wu[static_cast<size_t>(4 * c + ij) * Cin],
+                            Cin * sizeof(float));
+        levels_[lev].up = pack_gemm(pk, wl, 4 * Cout, Cin, store_nt(4 * Cout), nullptr, 4 * Cout);
+        C = Cout;
+        const std::string dr = "decoders." + std::to_string(d);
+        for (int i = 0, n = count_blocks(hw, dr); i < n; ++i)
+            levels_[lev].dec.push_back(block(dr + "." + std::to_string(i), C));
+    }
+
+    // Temporal models.
+    const bool legacy = hw.contains("temporal_mix.0.weight");
+    const bool pyt = hw.contains("temporal_mix.0.0.weight");
+    if (pyt) throw FormatError("NAFNetTemporal (bottleneck_mix / temporal_mix.N.0 export) is not supported by this build");
+    if (legacy) {
+        info_.kind = 1;
+        const int T = hw.arch().num_frames > 0 ? hw.arch().num_frames : 3;
+        if (T < 2) throw FormatError("temporal model needs num_frames >= 2");
+        if (T > kMaxSeg) throw FormatError("temporal model: num_frames > 8 is not supported");
+        info_.num_frames = T;
+        info_.use_warp = hw.contains("offset_heads.0.weight") ? 1 : 0;
+        for (int l = 0; l < levels; ++l) {
+            const int Cl = levels_[l].C;
+            const std::string tn = "temporal_mix." + std::to_string(l);
+            expect_shape(hw, tn + ".weight", {Cl, 2 * Cl, 1, 1});
+            expect_shape(hw, tn + ".bias", {Cl});
+            const auto w = hw.to_f32(tn + ".weight");
+            // concat(ref, mean_t nbr_t) @ W^T == [ref, nbr_1..nbr_{T-1}] @ [W_ref, W_mean/(T-1), ...]^T
+            std::vector<float> wl(static_cast<size_t>(Cl) * T * Cl);
+            const float inv = 1.0f / static_cast<float>(T - 1);
+            for (int o = 0; o < Cl; ++o)
+                for (int c = 0; c < Cl; ++c) {
+                    wl[static_cast<size_t>(o) * T * Cl + c] = w[static_cast<size_t>(o) * 2 * Cl + c];
+                    for (int s = 1; s < T; ++s)
+                        wl[static_cast<size_t>(o) * T * Cl + s * Cl + c] = w[static_cast<size_t>(o) * 2 * Cl + Cl + c] * inv;
+                }
+            const auto tb = hw.to_f32(tn + ".bias");
+            tmix_.push_back(pack_gemm(pk, wl, Cl, T * Cl, store_nt(Cl), &tb, Cl));
+            if (info_.use_warp) {
+                const std::string on = "offset_heads." + std::to_string(l);
+                expect_shape(hw, on + ".weight", {2, 2 * Cl, 1, 1});
+                expect_shape(hw, on + ".bias", {2});
+                const auto ob = hw.to_f32(on + ".bias");
+                // 2 outputs padded to an 8-channel row (dx, dy, 0 x 6).
+                offset_heads_.push_back(pack_gemm(pk, hw.to_f32(on + ".weight"), 2, 2 * Cl, 16, &ob, 8));
+            }
+        }
+    } else if (hw.arch().type == "nafnet_temporal") {
+        throw FormatError("manifest says nafnet_temporal but has no temporal_mix weights");
+    }
+
+    warena_bytes_ = align256(pk.host.size());
+    cudaError_t e = cudaMalloc(&warena_, warena_bytes_);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("weight arena: ") + cudaGetErrorString(e));
+    e = cudaMemcpy(warena_, pk.host.data(), pk.host.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("weight upload: ") + cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+// Activation planning
+// ---------------------------------------------------------------------------
+
+void Engine::plan(const Shape& s) {
+    if (aarena_ && shape_ == s) return;
+    if (aarena_) {
+        cudaFree(aarena_);
+        aarena_ = nullptr;
+    }
+    shape_ = s;
+    const int L = info_.num_levels;
+    const bool temporal = info_.kind != 0;
+    const size_t n_enc = temporal ? s.T : s.N;  // images through the encoder
+    const size_t n_dec = temporal ? 1 : s.N;
+    std::vector<std::pair<size_t, void**>> req;
+    enc_x_.assign(L, nullptr);
+    dec_x_.assign(L, nullptr);
+    fused_skip_.assign(L, nullptr);
+    size_t u = 0, g = 0, y = 0, t = 0, dmax = 8;
+    dw_blocks_max_ = 1;
+    auto account = [&](const std::vector<BlockW>& bl, size_t nimg, int h, int w) {
+        const size_t hw = static_cast<size_t>(h) * w;
+        for (const auto& b : bl) {
+            u = std::max(u, nimg * hw * 2 * b.dw);
+            g = std::max(g, nimg * hw * b.dw);
+            y = std::max(y, nimg * hw * b.C);
+            t = std::max(t, nimg * hw * b.ffn);
+            dmax = std::max(dmax, static_cast<size_t>(b.dw));
+            dw_blocks_max_ = std::max(dw_blocks_max_, dw_blocks_per_img(h, w, b.dw));
+        }
+    };
+    for (int l = 0; l < L; ++l) {
+        const int h = s.Hp >> l, w = s.Wp >> l, C = levels_[l].C;
+        const size_t hw = static_cast<size_t>(h) * w;
+        req.push_back({n_enc * hw * C * 2, reinterpret_cast<void**>(&enc_x_[l])});
+        req.push_back({n_dec * hw * C * 2, reinterpret_cast<void**>(&dec_x_[l])});
+        if (temporal) req.push_back({hw * C * 2, reinterpret_cast<void**>(&fused_skip_[l])});
+        account(levels_[l].enc, n_enc, h, w);
+        account(levels_[l].dec, n_dec, h, w);
+    }
+    const int hm = s.Hp >> L, wm = s.Wp >> L;
+    const size_t hwm = static_cast<size_t>(hm) * wm;
+    const int Cm = levels_[L - 1].C * 2;
+    req.push_back({n_enc * hwm * Cm * 2, reinterpret_cast<void**>(&mid_x_)});
+    account(middle_, 1 * (temporal ? 1 : n_enc), hm, wm);
+    req.push_back({u * 2, reinterpret_cast<void**>(&buf_u_)});
+    req.push_back({g * 2, reinterpret_cast<void**>(&buf_g_)});
+    req.push_back({y * 2, reinterpret_cast<void**>(&buf_y_)});
+    req.push_back({t * 2, reinterpret_cast<void**>(&buf_t_)});
+    if (temporal) {
+        const size_t hw0 = static_cast<size_t>(s.Hp) * s.Wp;
+        req.push_back({static_cast<size_t>(s.T) * hw0 * levels_[0].C * 2, reinterpret_cast<void**>(&warp_buf_)});
+        req.push_back({hw0 * 8 * 2, reinterpret_cast<void**>(&offset_buf_)});
+    }
+    req.push_back({n_enc * dw_blocks_max_ * dmax * 4, reinterpret_cast<void**>(&partials_)});
+    req.push_back({n_enc * 4, reinterpret_cast<void**>(&counters_)});
+    req.push_back({n_enc * dmax * 4, reinterpret_cast<void**>(&sca_s_)});
+    req.push_back({256, reinterpret_cast<void**>(&err_)});
+    size_t total = 0;
+    for (auto& r : req) total = align256(total) + align256(r.first);
+    cudaError_t e = cudaMalloc(&aarena_, total);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("activation arena: ") + cudaGetErrorString(e));
+    aarena_bytes_ = total;
+    size_t off = 0;
+    for (auto& r : req) {
+        off = align256(off);
+        *r.second = aarena_ + off;
+        off += align256(r.first);
+    }
+    e = cudaMemset(counters_, 0, n_enc * 4);
+    if (e == cudaSuccess) e = cudaMemset(err_, 0, 256);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("arena init: ") + cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+
+int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cudaStream_t s) {
+    p.bpack = wptr<uint8_t>(g.bpack);
+    p.n_tiles = g.n_tiles;
+    p.k_chunks = g.k_chunks;
+    p.KC = g.KC;
+    p.K = g.K;
+    p.bias = g.has_bias ? wptr<float>(g.bias) : nullptr;
+    p.n_out = g.n_out;
+    p.err = err_;
+    ++launches_;
+    return launch_gemm(p, pro, epi, amode, g.NT, s);
+}
+
+static GemmParams rows_params(int nimg, int h, int w) {
+    GemmParams p{};
+    p.M = nimg * h * w;
+    p.hw = h * w;
+    p.Ho = h;
+    p.Wo = w;
+    p.nseg = 1;
+    return p;
+}
+
+#define DN_TRY(x)                 \
+    do {                          \
+        const int _rc = (x);      \
+        if (_rc != DN_OK) return _rc; \
+    } while (0)
+
+// NAFBlock (training/models.py:166-185, src/models/nafnet.cu:146-215), in place on x.
+int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaStream_t s) {
+    const long long hw = static_cast<long long>(h) * w;
+    // u = conv1(LN1(x)) + b1
+    GemmParams p = rows_params(nimg, h, w);
+    p.seg_c = b.C;
+    p.a_img_stride = hw * b.C;
+    p.a[0] = x;
+    p.pro_w = wptr<float>(b.ln1w);
+    p.pro_b = wptr<float>(b.ln1b);
+    p.out = buf_u_;
+    p.out_c = 2 * b.dw;
+    DN_TRY(gemm(b.conv1, kProLayerNorm, kEpiStore, kARows, p, s));
+    // g = SG(dw3x3(u) + b2); s = W_sca * mean(g) + b_sca
+    DwParams d{};
+    d.u = buf_u_;
+    d.g = buf_g_;
+    d.w = wptr<float>(b.dw_w);
+    d.b = wptr<float>(b.dw_b);
+    d.N = nimg;
+    d.H = h;
+    d.W = w;
+    d.D = b.dw;
+    d.partials = partials_;
+    d.counter = counters_;
+    d.sca_w = wptr<float>(b.sca_w);
+    d.sca_b = wptr<float>(b.sca_b);
+    d.s_out = sca_s_;
+    ++launches_;
+    DN_TRY(launch_dw_gate_sca(d, dw_blocks_per_img(h, w, b.dw), s));
+    // y = x + beta * (conv3(g * s) + b3)
+    p = rows_params(nimg, h, w);
+    p.seg_c = b.dw;
+    p.a_img_stride = hw * b.dw;
+    p.a[0] = buf_g_;
+    p.pro_scale = sca_s_;
+    p.out = buf_y_;
+    p.out_c = b.C;
+    p.res = x;
+    p.res_scale = wptr<float>(b.beta);
+    DN_TRY(gemm(b.conv3, kProScale, kEpiResidual, kARows, p, s));
+    // t = SG(conv4(LN2(y)) + b4)
+    p = rows_params(nimg, h, w);
+    p.seg_c = b.C;
+    p.a_img_stride = hw * b.C;
+    p.a[0] = buf_y_;
+    p.pro_w = wptr<float>(b.ln2w);
+    p.pro_b = wptr<float>(b.ln2b);
+    p.out = buf_t_;
+    p.out_c = b.ffn;
+    DN_TRY(gemm(b.conv4, kProLayerNorm, kEpiGate, kARows, p, s));
+    // x = y + gamma * (conv5(t) + b5)
+    p = rows_params(nimg, h, w);
+    p.seg_c = b.ffn;
+    p.a_img_stride = hw * b.ffn;
+    p.a[0] = buf_t_;
+    p.out = x;
+    p.out_c = b.C;
+    p.res = buf_y_;
+    p.res_scale = wptr<float>(b.gamma);
+    DN_TRY(gemm(b.conv5, kProNone, kEpiResidual, kARows, p, s));
+    return DN_OK;
+}
+
+int Engine::run_stage(const std::vector<BlockW>& blocks, __half* x, int nimg, int h, int w, cudaStream_t s) {
+    for (const auto& b : blocks) DN_TRY(run_block(b, x, nimg, h, w, s));
+    return DN_OK;
+}
+
+int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* y, cudaStream_t s) {
+    if (!x || !y) return dn_fail(DN_ERR_INVALID_ARG, "forward: null pointer");
+    if (N <= 0 || H <= 0 || W <= 0) return dn_fail(DN_ERR_INVALID_ARG, "forward: empty input");
+    if (C < info_.in_channels)
+        return dn_fail(DN_ERR_INVALID_ARG, "forward: input has fewer channels than model expects");
+    if (C < 3) return dn_fail(DN_ERR_INVALID_ARG, "forward: expected at least 3 input channels");
+    const bool temporal = info_.kind != 0;
+    if (temporal && T != info_.num_frames) return dn_fail(DN_ERR_INVALID_ARG, "forward: frame count mismatch");
+    if (!temporal && T != 1) return dn_fail(DN_ERR_INVALID_ARG, "forward: spatial model takes 4-D input");
+    const int m = pad_multiple_;
+    Shape sh;
+    sh.N = N;
+    sh.T = T;
+    sh.H = H;
+    sh.W = W;
+    sh.Hp = (H + m - 1) / m * m;
+    sh.Wp = (W + m - 1) / m * m;
+    if (sh.Hp - H >= H || sh.Wp - W >= W)
+        return dn_fail(DN_ERR_INVALID_ARG, "forward: frame smaller than the reflect padding it needs");
+    if (static_cast<long long>(N) * T * sh.Hp * sh.Wp > (1LL << 30))
+        return dn_fail(DN_ERR_UNSUPPORTED, "forward: input too large");
+    DeviceGuard dg(device_);
+    try {
+        plan(sh);
+    } catch (const std::exception& e) {
+        return dn_fail(DN_ERR_CUDA, e.what());
+    }
+    launches_ = 0;
+    const int L = info_.num_levels;
+    const int C0 = info_.base_channels;
+    const int in_c = info_.in_channels;
+
+    // Encoder over n_enc images (the frames of one clip for temporal models).
+    auto encode = [&](const __half* src, int nimg) -> int {
+        IntroParams ip{};
+        ip.x = src;
+        ip.N = nimg;
+        ip.Cin = in_c;
+        ip.H = H;
+        ip.W = W;
+        ip.Hp = sh.Hp;
+        ip.Wp = sh.Wp;
+        ip.C0 = C0;
+        ip.in_batch_stride = C * H * W;
+        ip.w = wptr<float>(intro_w_);
+        ip.b = wptr<float>(intro_b_);
+        ip.y = enc_x_[0];
+        ++launches_;
+        DN_TRY(launch_intro(ip, s));
+        for (int l = 0; l < L; ++l) {
+            const int h = sh.Hp >> l, w = sh.Wp >> l;
+            DN_TRY(run_stage(levels_[l].enc, enc_x_[l], nimg, h, w, s));
+            GemmParams p = rows_params(nimg, h / 2, w / 2);
+            p.seg_c = levels_[l].C;
+            p.a_img_stride = static_cast<long long>(h) * w * levels_[l].C;
+            p.a[0] = enc_x_[l];
+            p.out = (l + 1 < L) ? enc_x_[l + 1] : mid_x_;
+            p.out_c = 2 * levels_[l].C;
+            DN_TRY(gemm(levels_[l].down, kProNone, kEpiStore, kAS2x2, p, s));
+        }
+        return DN_OK;
+    };
+    // Middle + decoder on n images with the given per-level skips.
+    auto decode = [&](__half* xm, int nimg, const std::vector<__half*>& skips, const __half* beauty,
+                      int beauty_stride, __half* out) -> int {
+        const int hm = sh.Hp >> L, wm = sh.Wp >> L;
+        DN_TRY(run_stage(middle_, xm, nimg, hm, wm, s));
+        const __half* cur = xm;
+        for (int d = 0; d < L; ++d) {
+            const int lev = L - 1 - d;
+            const int h = sh.Hp >> (lev + 1), w = sh.Wp >> (lev + 1);
+            const int Cin = levels_[lev].C * 2;
+            GemmParams p = rows_params(nimg, h, w);
+            p.seg_c = Cin;
+            p.a_img_stride = static_cast<long long>(h) * w * Cin;
+            p.a[0] = cur;
+            p.out = dec_x_[lev];
+            p.out_c = levels_[lev].C;
+            p.skip = skips[lev];
+            DN_TRY(gemm(levels_[lev].up, kProNone, kEpiShuffleAdd, kARows, p, s));
+            DN_TRY(run_stage(levels_[lev].dec, dec_x_[lev], nimg, 2 * h, 2 * w, s));
+            cur = dec_x_[lev];
+        }
+        EndingParams ep{};
+        ep.x = dec_x_[0];
+        ep.N = nimg;
+        ep.Hp = sh.Hp;
+        ep.Wp = sh.Wp;
+        ep.C0 = C0;
+        ep.H = H;
+        ep.W = W;
+        ep.w = wptr<float>(ending_w_);
+        ep.b = wptr<float>(ending_b_);
+        ep.beauty = beauty;
+        ep.beauty_batch_stride = beauty_stride;
+        ep.y = out;
+        ++launches_;
+        return launch_ending(ep, s);
+    };
+
+    if (!temporal) {
+        DN_TRY(encode(x, N));
+        return decode(mid_x_, N, enc_x_, x, C * H * W, y);
+    }
+
+    // Temporal model of the C++ engine (nafnet_temporal.cu:363-503): every
+    // frame of the clip through the shared encoder (as a batch of T images),
+    // middle on the reference frame, per-level fused skip
+    // temporal_mix(concat(ref, mean_t warp?(nbr_t))), then the decoder.
+    const int ref = T / 2;
+    for (int n = 0; n < N; ++n) {
+        const __half* clip = x + static_cast<size_t>(n) * T * C * H * W;
+        DN_TRY(encode(clip, T));
+        for (int l = 0; l < L; ++l) {
+            const int h = sh.Hp >> l, w = sh.Wp >> l, Cl = levels_[l].C;
+            const size_t plane = static_cast<size_t>(h) * w * Cl;
+            const __half* rf = enc_x_[l] + ref * plane;
+            GemmParams p = rows_params(1, h, w);
+            p.seg_c = Cl;
+            p.a_img_stride = 0;
+            p.nseg = T;
+            p.a[0] = rf;
+            int si = 1;
+            for (int t = 0; t < T; ++t) {
+                if (t == ref) continue;
+                const __half* nb = enc_x_[l] + t * plane;
+                if (info_.use_warp) {
+                    GemmParams q = rows_params(1, h, w);
+                    q.seg_c = Cl;
+                    q.a_img_stride = 0;
+                    q.nseg = 2;
+                    q.a[0] = rf;
+                    q.a[1] = nb;
+                    q.out = offset_buf_;
+                    q.out_c = 8;
+                    DN_TRY(gemm(offset_heads_[l], kProNone, kEpiStore, kARows, q, s));
+                    __half* wb = warp_buf_ + (si - 1) * plane;
+                    ++launches_;
+                    DN_TRY(launch_warp_pixel(nb, offset_buf_, 8, wb, 1, h, w, Cl, s));
+                    nb = wb;
+                }
+                p.a[si++] = nb;
+            }
+            p.out = fused_skip_[l];
+            p.out_c = Cl;
+            DN_TRY(gemm(tmix_[l], kProNone, kEpiStore, kARows, p, s));
+        }
+        const size_t mplane = static_cast<size_t>(sh.Hp >> L) * (sh.Wp >> L) * levels_[L - 1].C * 2;
+        const __half* beauty = clip + static_cast<size_t>(ref) * C * H * W;
+        DN_TRY(decode(mid_x_ + ref * mplane, 1, fused_skip_, beauty, C * H * W,
+                      y + static_cast<size_t>(n) * 3 * H * W));
+    }
+    return DN_OK;
+}
+
+int Engine::check_device(cudaStream_t s) {
+    DeviceGuard dg(device_);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return dn_cuda_fail(e, "stream synchronize");
+    if (!err_) return DN_OK;
+    uint32_t word = 0;
+    e = cudaMemcpy(&word, err_, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return dn_cuda_fail(e, "read device error word");
+    if (word != 0) {
+        cudaMemset(err_, 0, 4);
+        return dn_fail_str(DN_ERR_DEVICE, "kernel reported device error word " + std::to_string(word));
+    }
+    return DN_OK;
+}
+
+}  // namespace dnb

@@ -1,0 +1,130 @@
+// The NAFNet inference engine: weights packed once into one device arena in
+// the layouts the kernels consume, an activation arena planned per input
+// shape, and the launch sequence of the spatial NAFNet
+// (src/models/nafnet.cu:341-389) and of the C++ engine's temporal model
+// (src/models/nafnet_temporal.cu:363-503).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "manifest.h"
+
+namespace dnb {
+
+// Packed 1x1 / 2x2 conv for launch_gemm.
+struct GemmW {
+    size_t bpack = 0;      // arena offset of the packed B tiles
+    size_t bias = 0;       // arena offset of the fp32 bias (packed order), or npos
+    bool has_bias = false;
+    int NT = 0, KC = 0, n_tiles = 0, k_chunks = 0;
+    int K = 0;             // logical K
+    int n_out = 0;         // output channels the epilogue writes
+};
+
+struct BlockW {
+    int C = 0, dw = 0, ffn = 0;
+    size_t ln1w = 0, ln1b = 0, ln2w = 0, ln2b = 0, beta = 0, gamma = 0;  // fp32 [C]
+    GemmW conv1, conv3, conv4, conv5;
+    size_t dw_w = 0, dw_b = 0;     // fp32 [9][2dw], [2dw]
+    size_t sca_w = 0, sca_b = 0;   // fp32 [dw][dw], [dw]
+};
+
+struct ModelInfo {
+    int kind = 0;          // 0 spatial, 1 temporal (C++ engine design), 2 temporal (PyTorch design)
+    int in_channels = 3;
+    int num_levels = 0;
+    int base_channels = 0;
+    int num_frames = 1;
+    int use_warp = 0;
+    std::vector<int> enc_channels;
+};
+
+class Engine {
+public:
+    Engine(const std::string& manifest_path, int device);
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    const ModelInfo& info() const { return info_; }
+    int device() const { return device_; }
+
+    // Spatial: x (N, C, H, W) fp16 NCHW device -> y (N, 3, H, W).
+    // Temporal: x (N, T, C, H, W) clip -> y (N, 3, H, W) (denoised centre frame).
+    // Returns DN_OK or a DN_ERR_* code (message via dn_last_error).
+    int forward(const __half* x, int N, int T, int C, int H, int W, __half* y, cudaStream_t s);
+
+    // Waits for `s` and returns DN_ERR_DEVICE if a kernel flagged an error
+    // since the last check (the word is cleared).
+    int check_device(cudaStream_t s);
+
+    size_t weight_bytes() const { return warena_bytes_; }
+    size_t activation_bytes() const { return aarena_bytes_; }
+    int kernels_per_forward() const { return launches_; }
+
+private:
+    struct Level {
+        int C = 0;
+        std::vector<BlockW> enc, dec;
+        GemmW down;  // C -> 2C, 2x2 s2
+        GemmW up;    // ups feeding this level: 2C -> 4*C, shuffle to C
+    };
+    struct Shape {
+        int N = 0, T = 0, H = 0, W = 0, Hp = 0, Wp = 0;
+        bool operator==(const Shape& o) const {
+            return N == o.N && T == o.T && H == o.H && W == o.W;
+        }
+    };
+
+    void build(const HostWeights& hw);
+    void plan(const Shape& s);
+    int run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaStream_t s);
+    int run_stage(const std::vector<BlockW>& blocks, __half* x, int nimg, int h, int w, cudaStream_t s);
+    int gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cudaStream_t s);
+
+    template <class T>
+    const T* wptr(size_t off) const {
+        return reinterpret_cast<const T*>(warena_ + off);
+    }
+
+    int device_ = 0;
+    ModelInfo info_;
+    int pad_multiple_ = 1;
+
+    // weights
+    uint8_t* warena_ = nullptr;
+    size_t warena_bytes_ = 0;
+    std::vector<Level> levels_;
+    std::vector<BlockW> middle_;
+    size_t intro_w_ = 0, intro_b_ = 0, ending_w_ = 0, ending_b_ = 0;
+    // temporal (C++ engine design): per level temporal_mix over
+    // concat(ref, nbr_1..nbr_{T-1}) with the neighbour mean folded into B,
+    // and optional offset heads (1x1, 2C -> 2).
+    std::vector<GemmW> tmix_;
+    std::vector<GemmW> offset_heads_;
+
+    // activations
+    Shape shape_{};
+    uint8_t* aarena_ = nullptr;
+    size_t aarena_bytes_ = 0;
+    std::vector<__half*> enc_x_, dec_x_;  // per level (encoder state/skip, decoder state)
+    __half* mid_x_ = nullptr;
+    __half *buf_u_ = nullptr, *buf_g_ = nullptr, *buf_y_ = nullptr, *buf_t_ = nullptr;
+    std::vector<__half*> fused_skip_;     // temporal: fused skip per level
+    __half* warp_buf_ = nullptr;          // temporal: warped neighbours [T-1][...]
+    __half* offset_buf_ = nullptr;        // temporal: offsets [HW][16]
+    float* partials_ = nullptr;
+    unsigned* counters_ = nullptr;
+    float* sca_s_ = nullptr;
+    uint32_t* err_ = nullptr;
+    int dw_blocks_max_ = 0;
+    int launches_ = 0;
+};
+
+}  // namespace dnb

@@ -1,0 +1,115 @@
+// Internal kernel interface of the engine: parameter blocks shared by the
+// host planner (engine.cc) and the CUDA kernels, plus their launchers.
+// Activations are NHWC fp16 ("rows" = pixels, channels contiguous).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace dnb {
+
+// ---------------------------------------------------------------------------
+// tcgen05 row-panel GEMM: out[M, N] = epi( pro(A)[M, K] * B[N, K]^T )
+// ---------------------------------------------------------------------------
+
+enum GemmPro : int {
+    kProNone = 0,
+    kProLayerNorm = 1,  // per-row LayerNorm over K (eps 1e-6) then affine pro_w/pro_b
+    kProScale = 2,      // A[m, k] * pro_scale[img(m) * K + k]  (SCA apply)
+};
+
+enum GemmEpi : int {
+    kEpiStore = 0,       // out = acc + bias
+    kEpiGate = 1,        // SimpleGate: out[c] = (acc+b)[c] * (acc+b)[c + half] (in-tile pairs)
+    kEpiResidual = 2,    // out = res + res_scale[n] * (acc + bias)
+    kEpiShuffleAdd = 3,  // PixelShuffle(2) scatter + skip add
+};
+
+enum GemmAMode : int {
+    kARows = 0,   // row m = pixel m of each segment (1x1 conv; K = nseg * seg_c)
+    kAS2x2 = 1,   // 2x2 stride-2 gather: K = 4 * seg_c, tap = k / seg_c
+};
+
+constexpr int kMaxSeg = 8;
+
+struct GemmParams {
+    int M;                     // rows = N_img * Ho * Wo
+    int K;                     // logical K
+    int hw;                    // pixels per image of the output grid (Ho * Wo)
+    int Ho, Wo;                // output grid (S2 gather and pixel shuffle)
+    int nseg, seg_c;           // A = concat of nseg segments of seg_c channels
+    long long a_img_stride;    // elements between images of every segment source
+    const __half* a[kMaxSeg];
+    const float* pro_w;        // LN gamma [K]
+    const float* pro_b;        // LN beta [K]
+    const float* pro_scale;    // [N_img][K]
+    const uint8_t* bpack;      // packed B tiles [n_tiles][k_chunks][NT x KC canonical]
+    int n_tiles, k_chunks, KC;
+    const float* bias;         // [n_tiles * NT] packed order, may be null
+    __half* out;
+    int out_c;                 // channels of an output pixel
+    int n_out;                 // valid output channels (after gating: half)
+    const __half* res;         // residual source (same layout as out)
+    const float* res_scale;    // [n_out]
+    const __half* skip;        // shuffle-add skip (layout of out)
+    uint32_t* err;
+};
+
+// NT in {16, 32, 64, 128, 256}
+int launch_gemm(const GemmParams& p, int pro, int epi, int amode, int nt, cudaStream_t s);
+
+// Bytes of one packed B tile.
+inline size_t gemm_btile_bytes(int nt, int kc) { return static_cast<size_t>(nt) * kc * 2; }
+
+// ---------------------------------------------------------------------------
+// Depthwise 3x3 (zero pad) + bias + SimpleGate + global average pool + SCA
+// ---------------------------------------------------------------------------
+
+struct DwParams {
+    const __half* u;       // [N, H, W, 2D]
+    __half* g;             // [N, H, W, D]
+    const float* w;        // [9][2D] taps (ky*3+kx) x channel
+    const float* b;        // [2D]
+    int N, H, W, D;
+    float* partials;       // [N][blocks][D]
+    unsigned* counter;     // [N], zero on entry, reset by the last block
+    const float* sca_w;    // [D][D] (out, in)
+    const float* sca_b;    // [D]
+    float* s_out;          // [N][D] channel attention scale
+};
+
+int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s);
+int dw_blocks_per_img(int H, int W, int D);
+
+// ---------------------------------------------------------------------------
+// Dense 3x3 convs at the network boundary (CUDA cores)
+// ---------------------------------------------------------------------------
+
+// intro: NCHW fp16 input (N, Cin, H, W) -> nan_to_num -> reflect pad to
+// (Hp, Wp) -> 3x3 conv (zero pad 1) + bias -> NHWC fp16 (N, Hp, Wp, C0).
+struct IntroParams {
+    const __half* x;
+    int N, Cin, H, W, Hp, Wp, C0;
+    int in_batch_stride;   // elements between images of x (Cin*H*W, or T*Cin*H*W for clips)
+    const float* w;        // [C0][Cin][3][3]
+    const float* b;        // [C0]
+    __half* y;
+};
+int launch_intro(const IntroParams& p, cudaStream_t s);
+
+// ending: NHWC (N, Hp, Wp, C0) -> 3x3 conv C0 -> 3 + bias, crop to (H, W),
+// + beauty (nan_to_num of the first 3 channels of the NCHW input) -> NCHW fp16.
+struct EndingParams {
+    const __half* x;       // NHWC
+    int N, Hp, Wp, C0, H, W;
+    const float* w;        // [3][3][3][C0] (out, ky, kx, c)
+    const float* b;        // [3]
+    const __half* beauty;  // NCHW input
+    int beauty_batch_stride;
+    __half* y;             // NCHW (N, 3, H, W)
+};
+int launch_ending(const EndingParams& p, cudaStream_t s);
+
+}  // namespace dnb

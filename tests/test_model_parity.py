@@ -1,0 +1,107 @@
+"""Engine forward vs the reference's outputs (golden vectors) and vs the oracle.
+
+Bar: max |engine - fp32| <= 5e-3 and PSNR >= 50 dB (FP16 engine vs fp32).
+"""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+from parity_util import MAX_ABS, MIN_PSNR, compare, golden_model_dir, load_golden, synth_mod  # noqa: E402
+
+import nafnet_oracle as O  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+SPATIAL = ["spatial_w16l4_64x64", "spatial_w16l4_37x53", "spatial_w32dw1_48x40", "spatial_w8_9ch_dw2_30x44"]
+LEGACY = ["temporal_legacy_w8l2_t3_warp", "temporal_legacy_w8l2_t5"]
+
+
+def run_engine(pkg, path, x):
+    m = pkg.Model(path)
+    xt = torch.from_numpy(x).half().cuda()
+    y = m(xt)
+    m.sync()
+    return y.float().cpu().numpy(), m
+
+
+@pytest.mark.parametrize("name", SPATIAL + LEGACY)
+def test_engine_matches_reference_golden(pkg, tmp_path, name):
+    g = load_golden(name)
+    path, _ = golden_model_dir(pkg, tmp_path, g["meta"])
+    y, _ = run_engine(pkg, path, g["x"])
+    err, psnr = compare(y, g["expected"])
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (name, err, psnr)
+
+
+def _oracle_case(pkg, tmp_path, cfg, seed, x):
+    synth = synth_mod(pkg)
+    path, params = synth.make_model_dir(str(tmp_path), cfg, seed)
+    torch.set_num_threads(min(16, os.cpu_count() or 1))
+    ref = O.nafnet_forward(O.as_torch(params), torch.from_numpy(x)).numpy()
+    y, m = run_engine(pkg, path, x)
+    return compare(y, ref), m
+
+
+def test_tiny_w16_256(pkg, tmp_path):
+    """Tiny w16, 4 levels at 1x3x256x256 (the CPU-runnable configuration)."""
+    synth = synth_mod(pkg)
+    x = synth.gradient_sinusoid_input(256, 256, seed=0).astype(np.float16).astype(np.float32)
+    (err, psnr), _ = _oracle_case(pkg, tmp_path, synth.CONFIG_TINY_W16, 0, x)
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+
+
+def test_w32_batch2_ragged(pkg, tmp_path):
+    """NAFNet-w32 architecture, batch 2, size not divisible by 16 (reflect pad + crop)."""
+    synth = synth_mod(pkg)
+    x = np.concatenate([synth.w32_frame(100, 150, seed=5), synth.w32_frame(100, 150, seed=6)])
+    x = x.astype(np.float16).astype(np.float32)
+    (err, psnr), _ = _oracle_case(pkg, tmp_path, synth.CONFIG_W32, 1, x)
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+
+
+def test_w32_1080p(pkg, tmp_path):
+    """NAFNet-w32 on one 1080p Poisson-Gaussian frame (the benchmark workload)."""
+    synth = synth_mod(pkg)
+    x = synth.w32_frame(1080, 1920, seed=1).astype(np.float16).astype(np.float32)
+    (err, psnr), m = _oracle_case(pkg, tmp_path, synth.CONFIG_W32, 1, x)
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+
+
+def test_repeat_forward_is_deterministic(pkg, tmp_path):
+    synth = synth_mod(pkg)
+    path, _ = synth.make_model_dir(str(tmp_path), synth.CONFIG_TINY_W16, 0)
+    m = pkg.Model(path)
+    x = torch.from_numpy(synth.gradient_sinusoid_input(96, 80, seed=2)).half().cuda()
+    a = m(x).clone()
+    b = m(x)
+    m.sync()
+    assert torch.equal(a, b)
+
+
+def test_forward_host_matches_device(pkg, tmp_path):
+    synth = synth_mod(pkg)
+    path, _ = synth.make_model_dir(str(tmp_path), synth.CONFIG_TINY_W16, 0)
+    m = pkg.Model(path)
+    x = synth.gradient_sinusoid_input(64, 96, seed=3).astype(np.float16)
+    yh = m.forward_host(x)
+    yd = m(torch.from_numpy(x).cuda())
+    m.sync()
+    assert np.array_equal(yh, yd.cpu().numpy())
+
+
+def test_rejects_fp32_input(pkg, tmp_path):
+    synth = synth_mod(pkg)
+    path, _ = synth.make_model_dir(str(tmp_path), synth.CONFIG_TINY_W16, 0)
+    m = pkg.Model(path)
+    with pytest.raises(pkg.DenoiserError):
+        m(torch.zeros(1, 3, 32, 32, device="cuda"))
+
+
+def test_rejects_too_few_channels(pkg, tmp_path):
+    synth = synth_mod(pkg)
+    path, _ = synth.make_model_dir(str(tmp_path), synth.CONFIG_TINY_W16, 0)
+    m = pkg.Model(path)
+    with pytest.raises(pkg.InvalidArgumentError):
+        m(torch.zeros(1, 2, 32, 32, device="cuda", dtype=torch.float16))
