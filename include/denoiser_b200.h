@@ -126,6 +126,14 @@ int dn_model_sync(dn_model* model, void* stream);
 int dn_model_stats(const dn_model* model, size_t* weight_bytes, size_t* activation_bytes,
                    int* kernels_per_forward);
 
+/* Per-launch CUDA-event timing of the engine's kernels (no reference
+ * counterpart; the reference engine has no timers). While enabled, every
+ * kernel the model launches is bracketed by events on its stream. */
+int dn_model_profile(dn_model* model, int enable);
+/* Synchronise and write a JSON object {kind: {launches, ms, bytes, flops}}
+ * accumulated since the previous report (bytes/flops are algorithmic). */
+int dn_model_profile_report(dn_model* model, char* buf, size_t len);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -83,6 +83,8 @@ SIGNATURES = {
     "dn_model_forward_host": (_I, [_P, _P, _I64P, _I, _P, _P]),
     "dn_model_sync": (_I, [_P, _P]),
     "dn_model_stats": (_I, [_P, _SZP, _SZP, _IP]),
+    "dn_model_profile": (_I, [_P, _I]),
+    "dn_model_profile_report": (_I, [_P, _c.c_char_p, _c.c_size_t]),
 }
 
 
@@ -259,6 +261,18 @@ class Model:
     def sync(self, stream=None) -> None:
         """Synchronise the stream and raise if a kernel flagged a device error."""
         check(lib().dn_model_sync(self._h, stream_handle(stream)))
+
+    def profile(self, enable: bool = True) -> None:
+        """Bracket every kernel launch with CUDA events (see profile_report)."""
+        check(lib().dn_model_profile(self._h, 1 if enable else 0))
+
+    def profile_report(self) -> dict:
+        """{kind: {launches, ms, bytes, flops}} since the last report."""
+        import json
+
+        buf = ctypes.create_string_buffer(1 << 16)
+        check(lib().dn_model_profile_report(self._h, buf, len(buf)))
+        return json.loads(buf.value.decode())
 
     def stats(self) -> dict:
         wb = ctypes.c_size_t()

@@ -3,6 +3,7 @@
 // nafnet_temporal.h:11-29 of the reference) and the CLI's per-frame loop.
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <memory>
 #include <new>
 #include <string>
@@ -170,6 +171,22 @@ int dn_model_stats(const dn_model* m, size_t* weight_bytes, size_t* activation_b
     if (activation_bytes) *activation_bytes = m->eng->activation_bytes();
     if (kernels_per_forward) *kernels_per_forward = m->eng->kernels_per_forward();
     return DN_OK;
+}
+
+int dn_model_profile(dn_model* m, int enable) {
+    if (!m) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_profile: null model");
+    m->eng->set_profiling(enable != 0);
+    return DN_OK;
+}
+
+int dn_model_profile_report(dn_model* m, char* buf, size_t len) {
+    if (!m || !buf || len == 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_profile_report: bad argument");
+    return guarded([&] {
+        const std::string r = m->eng->profile_report();
+        if (r.size() + 1 > len) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_profile_report: buffer too small");
+        std::memcpy(buf, r.c_str(), r.size() + 1);
+        return DN_OK;
+    });
 }
 
 }  // extern "C"

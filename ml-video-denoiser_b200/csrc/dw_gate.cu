@@ -1,19 +1,23 @@
-// Depthwise 3x3 + bias + SimpleGate + global average pool + SCA, one pass.
+// Depthwise 3x3 + bias + SimpleGate + global average pool, then the SCA
+// matvec, as two kernels:
 //
-// Reads the conv1 output u (NHWC, 2D channels), writes the gated tensor
-// g = dw(u)[:D] * dw(u)[D:] (NHWC, D channels) and, per image, the
-// simplified-channel-attention scale s = W_sca * mean_{HW}(g) + b_sca.
-// The pool is a deterministic two-level reduction: each CTA writes its
-// per-channel partial sums, and the last CTA of an image (atomic ticket)
-// sums the partials in CTA order and evaluates the SCA 1x1 matvec.
+// dw_gate_kernel: reads the conv1 output u (NHWC, 2D channels), writes the
+//   gated tensor g = dw(u)[:D] * dw(u)[D:] (NHWC, D channels) and per-CTA
+//   per-channel partial sums of g. One thread computes one output pixel for
+//   8 channels of both gate halves: its 18 tap loads are independent, the
+//   tap weights are broadcast reads from shared memory.
+// sca_kernel: each CTA re-reduces all partial sums of its image in a fixed
+//   order (deterministic pool), then evaluates 8 outputs of
+//   s = W_sca * mean_{HW}(g) + b_sca with coalesced weight-row reads.
 //
 // Replaces the reference's grouped cudnnConvolutionForward (conv2,
 // src/models/nafnet.cu:126-130, 162), simple_gate_kernel, the serial
-// global_avg_pool_kernel (one thread per channel looping over H*W),
-// the SCA cudnn 1x1 on the pooled map and mul_channelwise's scale source
-// (src/kernels/nafnet_kernels.cu:94-141).
+// global_avg_pool_kernel, the SCA cudnn 1x1 on the pooled map and
+// mul_channelwise's scale source (src/kernels/nafnet_kernels.cu:94-141).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "kernels.h"
 #include "sm100.cuh"
@@ -24,31 +28,34 @@ namespace {
 
 constexpr int kThreads = 256;
 
-__device__ __forceinline__ void acc8(float (&a)[8], const uint4& v, const float* w) {
-    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 t = unpack_half2(u[i]);
-        a[2 * i] += t.x * w[2 * i];
-        a[2 * i + 1] += t.y * w[2 * i + 1];
-    }
+__device__ __forceinline__ void fma8(float (&a)[8], const uint4& v, const float* w) {
+    const float4 w0 = *reinterpret_cast<const float4*>(w);
+    const float4 w1 = *reinterpret_cast<const float4*>(w + 4);
+    const float2 t0 = unpack_half2(v.x), t1 = unpack_half2(v.y), t2 = unpack_half2(v.z), t3 = unpack_half2(v.w);
+    a[0] = fmaf(t0.x, w0.x, a[0]);
+    a[1] = fmaf(t0.y, w0.y, a[1]);
+    a[2] = fmaf(t1.x, w0.z, a[2]);
+    a[3] = fmaf(t1.y, w0.w, a[3]);
+    a[4] = fmaf(t2.x, w1.x, a[4]);
+    a[5] = fmaf(t2.y, w1.y, a[5]);
+    a[6] = fmaf(t3.x, w1.z, a[6]);
+    a[7] = fmaf(t3.y, w1.w, a[7]);
 }
 
-__global__ void __launch_bounds__(kThreads) dw_gate_sca_kernel(const __grid_constant__ DwParams p) {
-    // Shared: taps [9][2D], bias [2D], then the pool reduction [lanes][D].
-    extern __shared__ float sm[];
-    __shared__ bool s_last;
+__global__ void __launch_bounds__(kThreads) dw_gate_kernel(const __grid_constant__ DwParams p) {
+    // Shared: taps [9][2D], bias [2D], pool partials [lanes][D].
+    extern __shared__ __align__(16) float sm[];
     const int D = p.D;
-    const int groups = D / 8;               // 8-channel groups of the gated output
-    const int lanes = kThreads / groups;    // pixels processed concurrently
+    const int C2 = 2 * D;
+    const int groups = D / 8;
+    const int lanes = kThreads / groups;  // pixels in flight per CTA
     const int tid = threadIdx.x;
     const int cg = tid % groups;
     const int pl = tid / groups;
     const int img = blockIdx.y;
     const int HW = p.H * p.W;
-    const int C2 = 2 * D;
     float* sw = sm;
-    float* sb = sm + 9 * C2;
+    float* sb = sw + 9 * C2;
     float* red = sb + C2;
     for (int i = tid; i < 9 * C2; i += kThreads) sw[i] = p.w[i];
     for (int i = tid; i < C2; i += kThreads) sb[i] = p.b[i];
@@ -63,45 +70,43 @@ __global__ void __launch_bounds__(kThreads) dw_gate_sca_kernel(const __grid_cons
         for (int pix = blockIdx.x * lanes + pl; pix < HW; pix += stride) {
             const int y = pix / p.W;
             const int x = pix - y * p.W;
-            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            float b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            uint4 va[9], vb[9];
 #pragma unroll
-            for (int ky = 0; ky < 3; ++ky) {
-                const int yy = y + ky - 1;
-                if (yy < 0 || yy >= p.H) continue;
-#pragma unroll
-                for (int kx = 0; kx < 3; ++kx) {
-                    const int xx = x + kx - 1;
-                    if (xx < 0 || xx >= p.W) continue;
-                    const __half* src = u + (static_cast<size_t>(yy) * p.W + xx) * C2;
-                    const uint4 va = __ldg(reinterpret_cast<const uint4*>(src + c0));
-                    const uint4 vb = __ldg(reinterpret_cast<const uint4*>(src + D + c0));
-                    acc8(a, va, sw + (ky * 3 + kx) * C2 + c0);
-                    acc8(b, vb, sw + (ky * 3 + kx) * C2 + D + c0);
+            for (int t = 0; t < 9; ++t) {
+                const int yy = y + t / 3 - 1, xx = x + t % 3 - 1;
+                va[t] = make_uint4(0, 0, 0, 0);
+                vb[t] = make_uint4(0, 0, 0, 0);
+                if (yy >= 0 && yy < p.H && xx >= 0 && xx < p.W) {
+                    const __half* src = u + (static_cast<size_t>(yy) * p.W + xx) * C2 + c0;
+                    va[t] = __ldg(reinterpret_cast<const uint4*>(src));
+                    vb[t] = __ldg(reinterpret_cast<const uint4*>(src + D));
                 }
             }
-            float o[8];
+            float a[8], b[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = (a[i] + sb[c0 + i]) * (b[i] + sb[D + c0 + i]);
+            for (int i = 0; i < 8; ++i) {
+                a[i] = sb[c0 + i];
+                b[i] = sb[D + c0 + i];
+            }
+#pragma unroll
+            for (int t = 0; t < 9; ++t) {
+                fma8(a, va[t], sw + t * C2 + c0);
+                fma8(b, vb[t], sw + t * C2 + D + c0);
+            }
             uint4 ov;
-            ov.x = pack_half2(o[0], o[1]);
-            ov.y = pack_half2(o[2], o[3]);
-            ov.z = pack_half2(o[4], o[5]);
-            ov.w = pack_half2(o[6], o[7]);
+            ov.x = pack_half2(a[0] * b[0], a[1] * b[1]);
+            ov.y = pack_half2(a[2] * b[2], a[3] * b[3]);
+            ov.z = pack_half2(a[4] * b[4], a[5] * b[5]);
+            ov.w = pack_half2(a[6] * b[6], a[7] * b[7]);
             *reinterpret_cast<uint4*>(g + static_cast<size_t>(pix) * D + c0) = ov;
-            // Pool the stored (fp16-rounded) values.
             const uint32_t q[4] = {ov.x, ov.y, ov.z, ov.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float2 t = unpack_half2(q[i]);
+                const float2 t = unpack_half2(q[i]);  // pool the stored fp16 values
                 psum[2 * i] += t.x;
                 psum[2 * i + 1] += t.y;
             }
         }
-    }
-
-    // Block reduction over pixel lanes -> partials[img][block][D].
-    if (pl < lanes) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) red[pl * D + c0 + i] = psum[i];
     }
@@ -112,28 +117,43 @@ __global__ void __launch_bounds__(kThreads) dw_gate_sca_kernel(const __grid_cons
         for (int l = 0; l < lanes; ++l) s += red[l * D + c];
         part[c] = s;
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned prev = atomicAdd(p.counter + img, 1u);
-        s_last = (prev == gridDim.x - 1);
+}
+
+// grid (D / 8, N): CTA j computes s[img][8j .. 8j+8).
+__global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ DwParams p, int nb) {
+    extern __shared__ __align__(16) float sm[];
+    const int D = p.D;
+    float* mean = sm;       // [D]
+    float* red = sm + D;    // [8 warps][D]
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int img = blockIdx.y;
+    // Fixed-order pool: warp w sums CTA rows w, w+8, ...; lanes read float4
+    // channel vectors (coalesced); the 8 warp sums are added in warp order.
+    const int nvec = D / 4;
+    const float4* pp = reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(img) * nb * D);
+    for (int v = lane; v < nvec; v += 32) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+        for (int b = warp; b < nb; b += 8) {
+            const float4 x = pp[static_cast<size_t>(b) * nvec + v];
+            acc.x += x.x;
+            acc.y += x.y;
+            acc.z += x.z;
+            acc.w += x.w;
+        }
+        reinterpret_cast<float4*>(red + warp * D)[v] = acc;
     }
     __syncthreads();
-    if (!s_last) return;
-
-    // Last CTA of this image: pool in CTA order, then the SCA matvec.
-    __threadfence();
-    float* mean = red;  // reuse: D floats
-    const float inv = 1.0f / static_cast<float>(HW);
+    const float inv = 1.0f / static_cast<float>(p.H * p.W);
     for (int c = tid; c < D; c += kThreads) {
-        const float* pp = p.partials + static_cast<size_t>(img) * gridDim.x * D + c;
         float s = 0.f;
-        for (unsigned b = 0; b < gridDim.x; ++b) s += __ldcg(pp + static_cast<size_t>(b) * D);
+        for (int w = 0; w < 8; ++w) s += red[w * D + c];
         mean[c] = s * inv;
     }
     __syncthreads();
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int o = warp; o < D; o += kThreads / 32) {
+    const int o = blockIdx.x * 8 + warp;  // 8 warps -> 8 outputs
+    if (o < D) {
         const float* wr = p.sca_w + static_cast<size_t>(o) * D;
         float s = 0.f;
         for (int c = lane; c < D; c += 32) s += wr[c] * mean[c];
@@ -141,38 +161,40 @@ __global__ void __launch_bounds__(kThreads) dw_gate_sca_kernel(const __grid_cons
         for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
         if (lane == 0) p.s_out[static_cast<size_t>(img) * D + o] = s + p.sca_b[o];
     }
-    if (tid == 0) p.counter[img] = 0u;
 }
 
 }  // namespace
 
 int dw_blocks_per_img(int H, int W, int D) {
-    const int lanes = kThreads / (D / 8);
+    const int lanes = kThreads / (D / 8 > kThreads ? kThreads : D / 8);
     const long long px = static_cast<long long>(H) * W;
-    long long blocks = (px + lanes * 8 - 1) / (lanes * 8);  // ~8 pixels per thread
-    if (blocks < 1) blocks = 1;
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    return static_cast<int>(blocks);
+    const long long want = (px + lanes * 4 - 1) / (lanes * 4);  // ~4 pixels per thread
+    // The SCA pool re-reads nb x D partials per CTA: keep nb x D modest.
+    const long long cap = std::max(148LL, std::min(148LL * 4, 148LL * 4 * 64 / std::max(D, 64)));
+    return static_cast<int>(std::max(1LL, std::min(want, cap)));
 }
 
 int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s) {
     if (p.D % 8 != 0 || p.D / 8 > kThreads)
         return dn_fail(DN_ERR_UNSUPPORTED, "dw_gate: channels must be a multiple of 8 and <= 2048");
     const int lanes = kThreads / (p.D / 8);
-    const size_t smem = (static_cast<size_t>(10) * 2 * p.D + static_cast<size_t>(lanes) * p.D) *
-                        sizeof(float);
-    if (smem > 200 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "dw_gate: too many channels");
+    const size_t smem = (static_cast<size_t>(10) * 2 * p.D + static_cast<size_t>(lanes) * p.D) * sizeof(float);
+    const size_t smem2 = static_cast<size_t>(9) * p.D * sizeof(float);
+    if (smem > 200 * 1024 || smem2 > 200 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "dw_gate: too many channels");
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(dw_gate_sca_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(dw_gate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(sca_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return dn_cuda_fail(e, "dw_gate: set smem attribute");
         configured = true;
     }
-    dim3 grid(blocks_per_img, p.N);
-    dw_gate_sca_kernel<<<grid, kThreads, smem, s>>>(p);
+    dw_gate_kernel<<<dim3(blocks_per_img, p.N), kThreads, smem, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return dn_cuda_fail(e, "dw_gate: launch");
+    sca_kernel<<<dim3((p.D + 7) / 8, p.N), kThreads, smem2, s>>>(p, blocks_per_img);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return dn_cuda_fail(e, "sca: launch");
     return DN_OK;
 }
 

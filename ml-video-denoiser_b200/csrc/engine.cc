@@ -1,6 +1,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <stdexcept>
 
@@ -51,67 +52,100 @@ struct Packer {
 
 int store_nt(int n) { return std::min(128, next_pow2(std::max(16, n))); }
 
-// Pack logical W[N][K] (row-major fp32) into the tile image the GEMM kernel
-// bulk-copies: tiles [n_tile][k_chunk], each NT x KC fp16 in the no-swizzle
-// K-major core-matrix layout (8 rows x 16 B per core matrix, lbo 128 B).
-GemmW pack_gemm(Packer& pk, const std::vector<float>& W, int N, int K, int NT,
-                const std::vector<float>* bias, int n_out) {
+// Pack W[rows][K] (row-major fp32, src row per packed row, -1 = zero row)
+// into the tile image the GEMM kernel bulk-copies: tiles [n_tile][k_chunk],
+// each NT x KC fp16 in the no-swizzle K-major core-matrix layout (8 rows x
+// 16 B per core matrix, lbo 128 B). With `ln` (gamma, beta of the LayerNorm
+// that precedes the conv) the LN is folded: B = fp16(W * gamma),
+// c1[n] = sum_k B[n,k], bias'[n] = bias[n] + sum_k beta[k] W[n,k].
+struct LnFold {
+    const std::vector<float>* gamma = nullptr;
+    const std::vector<float>* beta = nullptr;
+};
+
+GemmW pack_rows(Packer& pk, const std::vector<float>& W, int K, const std::vector<int>& rows, int NT,
+                const std::vector<float>* bias, int n_out, LnFold ln = {}, int seg_c = 0) {
     GemmW g;
     g.NT = NT;
     g.K = K;
     g.n_out = n_out;
-    const int Kp = K <= 64 ? round_up(K, 16) : round_up(K, 64);
-    g.KC = std::min(64, Kp);
+    const int N = static_cast<int>(rows.size());
+    // K chunk: 16 / 32 / 64 channels (one swizzled TMA box of 32 / 64 / 128 B
+    // rows). A concat of narrower segments chunks at the segment width; 8-wide
+    // segments use the interleaved (unswizzled) A layout.
+    if (seg_c > 0 && seg_c < 64 && K > seg_c) {
+        g.KC = seg_c < 16 ? 16 : seg_c;
+        g.a_swz = seg_c < 16 ? 0 : 2 * g.KC;
+    } else {
+        g.KC = K <= 16 ? 16 : (K <= 32 ? 32 : 64);
+        // A box never wider than the source: 8-channel sources stay interleaved.
+        g.a_swz = K < g.KC ? 0 : 2 * g.KC;
+    }
+    const int Kp = round_up(K, g.KC);
     g.k_chunks = Kp / g.KC;
     g.n_tiles = (N + NT - 1) / NT;
     const uint32_t sbo = static_cast<uint32_t>(g.KC / 8) * 128u;
     const size_t tile_bytes = static_cast<size_t>(NT) * g.KC * 2;
     std::vector<uint8_t> buf(tile_bytes * g.n_tiles * g.k_chunks, 0);
-    for (int t = 0; t < g.n_tiles; ++t)
-        for (int j = 0; j < g.k_chunks; ++j) {
+    const size_t padded = static_cast<size_t>(g.n_tiles) * NT;
+    std::vector<float> bvec(padded, 0.f), c1(padded, 0.f);
+    for (int n = 0; n < N; ++n) {
+        const int src = rows[n];
+        if (src < 0) continue;
+        const int t = n / NT, r = n % NT;
+        double sum_b = 0.0, sum_c1 = 0.0;
+        for (int kk = 0; kk < K; ++kk) {
+            const float w = W[static_cast<size_t>(src) * K + kk];
+            const float wg = ln.gamma ? w * (*ln.gamma)[kk] : w;
+            const __half h = __float2half(wg);
+            sum_c1 += static_cast<double>(__half2float(h));
+            if (ln.beta) sum_b += static_cast<double>((*ln.beta)[kk]) * w;
+            const int j = kk / g.KC, k = kk % g.KC;
             uint8_t* tile = buf.data() + (static_cast<size_t>(t) * g.k_chunks + j) * tile_bytes;
-            for (int r = 0; r < NT; ++r) {
-                const int n = t * NT + r;
-                if (n >= N) break;
-                for (int k = 0; k < g.KC; ++k) {
-                    const int kk = j * g.KC + k;
-                    if (kk >= K) break;
-                    const __half h = __float2half(W[static_cast<size_t>(n) * K + kk]);
-                    std::memcpy(tile + kmajor_offset_host(r, k / 8, sbo) + (k % 8) * 2, &h, 2);
-                }
-            }
+            std::memcpy(tile + kmajor_offset_host(r, k / 8, sbo) + (k % 8) * 2, &h, 2);
         }
+        bvec[n] = (bias ? (*bias)[src] : 0.f) + static_cast<float>(sum_b);
+        c1[n] = static_cast<float>(sum_c1);
+    }
     g.bpack = pk.add(buf.data(), buf.size());
-    if (bias) {
-        std::vector<float> b(static_cast<size_t>(g.n_tiles) * NT, 0.f);
-        for (int n = 0; n < N && n < static_cast<int>(bias->size()); ++n) b[n] = (*bias)[n];
-        g.bias = pk.add_f32(b);
+    if (bias || ln.beta) {
+        g.bias = pk.add_f32(bvec);
         g.has_bias = true;
+    }
+    if (ln.gamma) {
+        g.c1 = pk.add_f32(c1);
+        g.has_c1 = true;
     }
     return g;
 }
 
+std::vector<int> iota_rows(int n) {
+    std::vector<int> r(n);
+    for (int i = 0; i < n; ++i) r[i] = i;
+    return r;
+}
+
+GemmW pack_gemm(Packer& pk, const std::vector<float>& W, int N, int K, int NT, const std::vector<float>* bias,
+                int n_out, LnFold ln = {}, int seg_c = 0) {
+    return pack_rows(pk, W, K, iota_rows(N), NT, bias, n_out, ln, seg_c);
+}
+
 // conv4 of a NAFBlock: the two SimpleGate halves are interleaved per tile so
 // that output channel c and its gate c + half land in the same tile.
-GemmW pack_gate(Packer& pk, const std::vector<float>& W, const std::vector<float>& bias, int half,
-                int K) {
+GemmW pack_gate(Packer& pk, const std::vector<float>& W, const std::vector<float>& bias, int half, int K,
+                LnFold ln = {}) {
     const int hnt = std::min(64, next_pow2(std::max(16, half)));
     const int NT = 2 * hnt;
     const int n_tiles = (half + hnt - 1) / hnt;
-    const int N = n_tiles * NT;
-    std::vector<float> Wl(static_cast<size_t>(N) * K, 0.f), bl(N, 0.f);
+    std::vector<int> rows(static_cast<size_t>(n_tiles) * NT, -1);
     for (int t = 0; t < n_tiles; ++t)
         for (int r = 0; r < hnt; ++r) {
             const int o = t * hnt + r;
             if (o >= half) break;
-            std::memcpy(&Wl[static_cast<size_t>(t * NT + r) * K], &W[static_cast<size_t>(o) * K],
-                        K * sizeof(float));
-            std::memcpy(&Wl[static_cast<size_t>(t * NT + hnt + r) * K],
-                        &W[static_cast<size_t>(half + o) * K], K * sizeof(float));
-            bl[t * NT + r] = bias[o];
-            bl[t * NT + hnt + r] = bias[half + o];
+            rows[t * NT + r] = o;
+            rows[t * NT + hnt + r] = half + o;
         }
-    return pack_gemm(pk, Wl, N, K, NT, &bl, half);
+    return pack_rows(pk, W, K, rows, NT, &bias, half, ln);
 }
 
 std::vector<int64_t> shape_of(const HostWeights& hw, const std::string& n) { return hw.entry(n).shape; }
@@ -153,6 +187,7 @@ Engine::Engine(const std::string& manifest_path, int device) : device_(device) {
 
 Engine::~Engine() {
     DeviceGuard g(device_);
+    for (auto e : prof_pool_) cudaEventDestroy(e);
     if (warena_) cudaFree(warena_);
     if (aarena_) cudaFree(aarena_);
 }
@@ -214,15 +249,17 @@ void Engine::build(const HostWeights& hw) {
         expect_shape(hw, pre + ".conv4.bias", {2 * b.ffn});
         expect_shape(hw, pre + ".conv5.weight", {C, b.ffn, 1, 1});
         expect_shape(hw, pre + ".conv5.bias", {C});
-        b.ln1w = pk.add_f32(hw.to_f32(pre + ".norm1.weight"));
-        b.ln1b = pk.add_f32(hw.to_f32(pre + ".norm1.bias"));
-        b.ln2w = pk.add_f32(hw.to_f32(pre + ".norm2.weight"));
-        b.ln2b = pk.add_f32(hw.to_f32(pre + ".norm2.bias"));
+        const auto ln1w = hw.to_f32(pre + ".norm1.weight"), ln1b = hw.to_f32(pre + ".norm1.bias");
+        const auto ln2w = hw.to_f32(pre + ".norm2.weight"), ln2b = hw.to_f32(pre + ".norm2.bias");
+        b.ln1w = pk.add_f32(ln1w);
+        b.ln1b = pk.add_f32(ln1b);
+        b.ln2w = pk.add_f32(ln2w);
+        b.ln2b = pk.add_f32(ln2b);
         b.beta = pk.add_f32(hw.to_f32(pre + ".beta"));
         b.gamma = pk.add_f32(hw.to_f32(pre + ".gamma"));
         const auto b1 = hw.to_f32(pre + ".conv1.bias");
         b.conv1 = pack_gemm(pk, hw.to_f32(pre + ".conv1.weight"), 2 * b.dw, C, store_nt(2 * b.dw), &b1,
-                            2 * b.dw);
+                            2 * b.dw, LnFold{&ln1w, &ln1b});
         {
             const auto w2 = hw.to_f32(pre + ".conv2.weight");
             std::vector<float> wt(9 * 2 * b.dw);
@@ -235,7 +272,8 @@ void Engine::build(const HostWeights& hw) {
         b.sca_b = pk.add_f32(hw.to_f32(pre + ".sca.1.bias"));
         const auto b3 = hw.to_f32(pre + ".conv3.bias");
         b.conv3 = pack_gemm(pk, hw.to_f32(pre + ".conv3.weight"), C, b.dw, store_nt(C), &b3, C);
-        b.conv4 = pack_gate(pk, hw.to_f32(pre + ".conv4.weight"), hw.to_f32(pre + ".conv4.bias"), b.ffn, C);
+        b.conv4 = pack_gate(pk, hw.to_f32(pre + ".conv4.weight"), hw.to_f32(pre + ".conv4.bias"), b.ffn, C,
+                            LnFold{&ln2w, &ln2b});
         const auto b5 = hw.to_f32(pre + ".conv5.bias");
         b.conv5 = pack_gemm(pk, hw.to_f32(pre + ".conv5.weight"), C, b.ffn, store_nt(C), &b5, C);
         return b;
@@ -310,14 +348,14 @@ void Engine::build(const HostWeights& hw) {
                         wl[static_cast<size_t>(o) * T * Cl + s * Cl + c] = w[static_cast<size_t>(o) * 2 * Cl + Cl + c] * inv;
                 }
             const auto tb = hw.to_f32(tn + ".bias");
-            tmix_.push_back(pack_gemm(pk, wl, Cl, T * Cl, store_nt(Cl), &tb, Cl));
+            tmix_.push_back(pack_gemm(pk, wl, Cl, T * Cl, store_nt(Cl), &tb, Cl, LnFold{}, Cl));
             if (info_.use_warp) {
                 const std::string on = "offset_heads." + std::to_string(l);
                 expect_shape(hw, on + ".weight", {2, 2 * Cl, 1, 1});
                 expect_shape(hw, on + ".bias", {2});
                 const auto ob = hw.to_f32(on + ".bias");
                 // 2 outputs padded to an 8-channel row (dx, dy, 0 x 6).
-                offset_heads_.push_back(pack_gemm(pk, hw.to_f32(on + ".weight"), 2, 2 * Cl, 16, &ob, 8));
+                offset_heads_.push_back(pack_gemm(pk, hw.to_f32(on + ".weight"), 2, 2 * Cl, 16, &ob, 8, LnFold{}, Cl));
             }
         }
     } else if (hw.arch().type == "nafnet_temporal") {
@@ -410,17 +448,87 @@ void Engine::plan(const Shape& s) {
 // Forward
 // ---------------------------------------------------------------------------
 
+void Engine::prof_begin(const char* kind, double bytes, double flops, cudaStream_t s) {
+    if (!profiling_) return;
+    while (prof_pool_.size() < prof_used_ + 2) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        prof_pool_.push_back(e);
+    }
+    ProfRec r{kind, bytes, flops, prof_pool_[prof_used_], prof_pool_[prof_used_ + 1]};
+    prof_used_ += 2;
+    cudaEventRecord(r.a, s);
+    prof_.push_back(r);
+}
+
+void Engine::prof_end(cudaStream_t s) {
+    if (!profiling_ || prof_.empty()) return;
+    cudaEventRecord(prof_.back().b, s);
+}
+
+std::string Engine::profile_report() {
+    DeviceGuard dg(device_);
+    cudaDeviceSynchronize();
+    struct Agg {
+        int n = 0;
+        double ms = 0, bytes = 0, flops = 0;
+    };
+    std::vector<std::pair<std::string, Agg>> agg;
+    for (const auto& r : prof_) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, r.a, r.b);
+        auto it = std::find_if(agg.begin(), agg.end(), [&](const auto& x) { return x.first == r.kind; });
+        if (it == agg.end()) {
+            agg.push_back({r.kind, Agg{}});
+            it = agg.end() - 1;
+        }
+        it->second.n += 1;
+        it->second.ms += ms;
+        it->second.bytes += r.bytes;
+        it->second.flops += r.flops;
+    }
+    prof_.clear();
+    prof_used_ = 0;
+    std::string out = "{";
+    for (size_t i = 0; i < agg.size(); ++i) {
+        char buf[256];
+        std::snprintf(buf, sizeof(buf), "%s\"%s\": {\"launches\": %d, \"ms\": %.6f, \"bytes\": %.0f, \"flops\": %.0f}",
+                      i ? ", " : "", agg[i].first.c_str(), agg[i].second.n, agg[i].second.ms, agg[i].second.bytes,
+                      agg[i].second.flops);
+        out += buf;
+    }
+    return out + "}";
+}
+
 int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cudaStream_t s) {
     p.bpack = wptr<uint8_t>(g.bpack);
     p.n_tiles = g.n_tiles;
     p.k_chunks = g.k_chunks;
     p.KC = g.KC;
+    p.a_swz = g.a_swz;
     p.K = g.K;
     p.bias = g.has_bias ? wptr<float>(g.bias) : nullptr;
+    p.ln_c1 = g.has_c1 ? wptr<float>(g.c1) : nullptr;
     p.n_out = g.n_out;
     p.err = err_;
     ++launches_;
-    return launch_gemm(p, pro, epi, amode, g.NT, s);
+    if (profiling_) {
+        const char* kind = epi == kEpiShuffleAdd ? "gemm_up_shuffle"
+                           : amode == kAS2x2     ? "gemm_down_s2"
+                           : epi == kEpiGate     ? "gemm_ln_gate"
+                           : pro == kProLayerNorm ? "gemm_ln"
+                           : pro == kProScale    ? "gemm_sca_residual"
+                           : epi == kEpiResidual ? "gemm_residual"
+                                                 : "gemm_store";
+        const double rows = p.M, n_w = static_cast<double>(g.n_tiles) * g.NT;
+        double bytes = rows * g.K * 2 + n_w * g.K * 2;
+        const double n_out = epi == kEpiShuffleAdd ? 4.0 * p.out_c : p.n_out;
+        bytes += rows * n_out * 2 * (epi == kEpiResidual || epi == kEpiShuffleAdd ? 2 : 1);
+        prof_begin(kind, bytes, 2.0 * rows * n_w * g.K, s);
+    }
+    const int rc = launch_gemm(p, pro, epi, amode, g.NT, s);
+    prof_end(s);
+    return rc;
 }
 
 static GemmParams rows_params(int nimg, int h, int w) {
@@ -447,8 +555,6 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
     p.seg_c = b.C;
     p.a_img_stride = hw * b.C;
     p.a[0] = x;
-    p.pro_w = wptr<float>(b.ln1w);
-    p.pro_b = wptr<float>(b.ln1b);
     p.out = buf_u_;
     p.out_c = 2 * b.dw;
     DN_TRY(gemm(b.conv1, kProLayerNorm, kEpiStore, kARows, p, s));
@@ -467,8 +573,11 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
     d.sca_w = wptr<float>(b.sca_w);
     d.sca_b = wptr<float>(b.sca_b);
     d.s_out = sca_s_;
-    ++launches_;
+    launches_ += 2;  // depthwise + SCA
+    prof_begin("dw_gate_sca", static_cast<double>(nimg) * hw * 3 * b.dw * 2,
+               static_cast<double>(nimg) * hw * 2 * b.dw * 9 * 2 + 2.0 * b.dw * b.dw, s);
     DN_TRY(launch_dw_gate_sca(d, dw_blocks_per_img(h, w, b.dw), s));
+    prof_end(s);
     // y = x + beta * (conv3(g * s) + b3)
     p = rows_params(nimg, h, w);
     p.seg_c = b.dw;
@@ -485,8 +594,6 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
     p.seg_c = b.C;
     p.a_img_stride = hw * b.C;
     p.a[0] = buf_y_;
-    p.pro_w = wptr<float>(b.ln2w);
-    p.pro_b = wptr<float>(b.ln2b);
     p.out = buf_t_;
     p.out_c = b.ffn;
     DN_TRY(gemm(b.conv4, kProLayerNorm, kEpiGate, kARows, p, s));
@@ -556,7 +663,10 @@ int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* 
         ip.b = wptr<float>(intro_b_);
         ip.y = enc_x_[0];
         ++launches_;
+        prof_begin("intro", static_cast<double>(nimg) * (static_cast<double>(in_c) * H * W + static_cast<double>(sh.Hp) * sh.Wp * C0) * 2,
+                   2.0 * nimg * sh.Hp * sh.Wp * C0 * in_c * 9, s);
         DN_TRY(launch_intro(ip, s));
+        prof_end(s);
         for (int l = 0; l < L; ++l) {
             const int h = sh.Hp >> l, w = sh.Wp >> l;
             DN_TRY(run_stage(levels_[l].enc, enc_x_[l], nimg, h, w, s));
@@ -605,7 +715,11 @@ int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* 
         ep.beauty_batch_stride = beauty_stride;
         ep.y = out;
         ++launches_;
-        return launch_ending(ep, s);
+        prof_begin("ending", static_cast<double>(nimg) * (static_cast<double>(sh.Hp) * sh.Wp * C0 + 6.0 * H * W) * 2,
+                   2.0 * nimg * H * W * 3 * C0 * 9, s);
+        const int rc_end = launch_ending(ep, s);
+        prof_end(s);
+        return rc_end;
     };
 
     if (!temporal) {
@@ -646,7 +760,9 @@ int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* 
                     DN_TRY(gemm(offset_heads_[l], kProNone, kEpiStore, kARows, q, s));
                     __half* wb = warp_buf_ + (si - 1) * plane;
                     ++launches_;
+                    prof_begin("warp", static_cast<double>(h) * w * (2 * Cl + 16) * 2, 8.0 * h * w * Cl, s);
                     DN_TRY(launch_warp_pixel(nb, offset_buf_, 8, wb, 1, h, w, Cl, s));
+                    prof_end(s);
                     nb = wb;
                 }
                 p.a[si++] = nb;

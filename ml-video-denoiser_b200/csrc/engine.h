@@ -20,9 +20,12 @@ namespace dnb {
 // Packed 1x1 / 2x2 conv for launch_gemm.
 struct GemmW {
     size_t bpack = 0;      // arena offset of the packed B tiles
-    size_t bias = 0;       // arena offset of the fp32 bias (packed order), or npos
+    size_t bias = 0;       // arena offset of the fp32 bias (packed order; LN fold: c2)
     bool has_bias = false;
+    size_t c1 = 0;         // LN fold: arena offset of c1 (packed order)
+    bool has_c1 = false;
     int NT = 0, KC = 0, n_tiles = 0, k_chunks = 0;
+    int a_swz = 0;         // A layout span the kernel uses (KC*2, or 0 = interleaved)
     int K = 0;             // logical K
     int n_out = 0;         // output channels the epilogue writes
 };
@@ -63,6 +66,14 @@ public:
     // Waits for `s` and returns DN_ERR_DEVICE if a kernel flagged an error
     // since the last check (the word is cleared).
     int check_device(cudaStream_t s);
+
+    // Per-launch CUDA-event timing of the engine's own kernels (off by
+    // default). Each launch is tagged with its kind and its algorithmic bytes
+    // (inputs read once + outputs written once) and FLOPs.
+    void set_profiling(bool on) { profiling_ = on; }
+    // Synchronises, then returns a JSON object: kind -> {launches, ms, bytes, flops}
+    // accumulated since the last report (which also resets the counters).
+    std::string profile_report();
 
     size_t weight_bytes() const { return warena_bytes_; }
     size_t activation_bytes() const { return aarena_bytes_; }
@@ -125,6 +136,19 @@ private:
     uint32_t* err_ = nullptr;
     int dw_blocks_max_ = 0;
     int launches_ = 0;
+
+    // profiling
+    struct ProfRec {
+        const char* kind;
+        double bytes, flops;
+        cudaEvent_t a, b;
+    };
+    void prof_begin(const char* kind, double bytes, double flops, cudaStream_t s);
+    void prof_end(cudaStream_t s);
+    bool profiling_ = false;
+    std::vector<ProfRec> prof_;
+    std::vector<cudaEvent_t> prof_pool_;
+    size_t prof_used_ = 0;
 };
 
 }  // namespace dnb

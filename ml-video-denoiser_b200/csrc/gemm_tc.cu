@@ -1,27 +1,44 @@
-// Row-panel implicit GEMM on the 5th-generation tensor cores (tcgen05).
+// Persistent, warp-specialised implicit GEMM on the 5th-generation tensor
+// cores (tcgen05):  out[M, N] = epi( pro(A)[M, K] * B[N, K]^T ).
 //
-// One CTA (4 warps) owns a 128-row x NT-column output tile. Thread t owns
-// row t end to end: it gathers its A row (1x1 pixel rows, 2x2/stride-2
-// patches, or a channel concat of up to 8 sources), applies the fused
-// prologue (LayerNorm over K, or the SCA channel scale), writes the row into
-// the no-swizzle K-major operand layout, and after the MMA reads its row of
-// the fp32 accumulator back from TMEM lane t for the fused epilogue (bias,
-// SimpleGate, beta/gamma residual, or PixelShuffle(2) scatter + skip add).
-//
-// K runs in chunks of KC (<= 64) through a 2-stage pipeline: B tiles are
-// pre-packed on the host in the exact shared-memory image and arrive by one
-// TMA bulk copy per chunk (mbarrier complete_tx); A tiles are produced by the
-// threads; one elected thread issues KC/16 tcgen05.mma (M=128, N=NT, K=16)
-// per chunk and commits them to the stage's mbarrier, which both frees the
-// stage for reuse and, for the last chunk, releases the epilogue.
+// Roles (320 threads per CTA, one CTA owns a stream of 128 x NT tiles):
+//   warp 8      TMA producer: per K-chunk, 2-D tensor-map loads of the A rows
+//               (box 8 x 128, landing directly in the no-swizzle K-major
+//               UMMA layout: LBO 2 KB between 8-wide K groups, SBO 128 B
+//               between 8-row groups) and one bulk copy of the pre-packed B
+//               tile, both completing on the stage's `raw` mbarrier.
+//   warps 0-3   transform, thread t = tile row t:
+//                 LayerNorm: accumulates the row statistics (shifted sums)
+//                   from the staged chunks while the MMA consumes them - the
+//                   LN itself is folded into the weights and the epilogue:
+//                   LN(x) W^T = rstd * (x (gW)^T - mean * c1) + c2,
+//                   c1[n] = sum_k (gW)[n,k], c2[n] = sum_k b_ln[k] W[n,k] + bias[n];
+//                 SCA scale: A[m,k] *= s[img,k] in place before the MMA;
+//                 2x2 stride-2 conv: gathers the patch rows itself.
+//   warp 9      MMA issuer: one thread issues KC/16 tcgen05.mma (M=128,
+//               N=NT, K=16) per chunk into one of two TMEM accumulators.
+//   warps 4-7   epilogue: thread t reads TMEM lane t (its row) with
+//               tcgen05.ld, applies bias / LN fold / SimpleGate / beta-gamma
+//               residual, writes a swizzled staging tile, and one thread moves
+//               the tile out with TMA tensor stores (the residual tile arrives
+//               the same way), or scatters PixelShuffle(2)+skip directly.
+// A 3-stage shared-memory ring and double-buffered accumulators overlap
+// loads, MMAs and epilogues of consecutive tiles. Every wait is bounded.
 //
 // Replaces the reference's cudnnConvolutionForward + cudnnAddTensor pair
 // (src/layers/conv2d.cu:94-150) and the separate LN / SimpleGate / SCA /
 // scaled-add / pixel-shuffle / add kernels (src/kernels/nafnet_kernels.cu
-// :54-208) that surround each 1x1 / 2x2 conv of a NAFBlock
-// (src/models/nafnet.cu:146-255).
+// :54-208) around each 1x1 / 2x2 conv of a NAFBlock (src/models/nafnet.cu
+// :146-255).
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <string>
 
 #include "kernels.h"
 #include "sm100.cuh"
@@ -31,6 +48,16 @@ namespace dnb {
 namespace {
 
 constexpr int kRows = 128;
+constexpr int kStages = 3;
+constexpr int kKC = 64;                 // shared-memory footprint is sized for KC = 64
+constexpr int kThreads = 320;
+constexpr uint32_t kALbo = kRows * 16;  // 2 KB between K-adjacent core-matrix columns
+
+struct GemmMaps {
+    CUtensorMap a[kMaxSeg];
+    CUtensorMap out;  // epilogue store (box EB x 128, swizzled)
+    CUtensorMap res;  // residual load (same geometry as out)
+};
 
 __device__ __forceinline__ void h8_to_f(const uint4& v, float (&f)[8]) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -51,58 +78,168 @@ __device__ __forceinline__ uint4 f_to_h8(const float (&f)[8]) {
     return v;
 }
 
-// Source address of the 8 channels [k, k+8) of the A row at (img, pix) of
-// the GEMM row grid.
-template <int AMODE>
-__device__ __forceinline__ const __half* a_src(const GemmParams& p, int img, int pix, int k) {
-    const int seg = k / p.seg_c;
-    const int c = k - seg * p.seg_c;
-    if (AMODE == kARows) {
-        return p.a[seg] + img * p.a_img_stride + static_cast<size_t>(pix) * p.seg_c + c;
-    } else {
-        // seg = tap (ky*2 + kx) of the 2x2 stride-2 patch
-        const int y = pix / p.Wo;
-        const int x = pix - y * p.Wo;
-        const size_t spix = static_cast<size_t>(2 * y + (seg >> 1)) * (2 * p.Wo) + 2 * x + (seg & 1);
-        return p.a[0] + img * p.a_img_stride + spix * p.seg_c + c;
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int c1, const void* src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier of the four epilogue warps.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Same barrier, returning the OR of `v` over the 128 epilogue threads (a
+// uniform decision for all of them).
+__device__ __forceinline__ bool epi_sync_or(bool v) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(out)
+        : "r"(static_cast<uint32_t>(v))
+        : "memory");
+    return out != 0;
+}
+
+// Bounded wait that also gives up as soon as another role aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              uint32_t* err, uint32_t site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 0u) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > 2000000000ull) {
+                report_error(err, site, kErrMbarTimeout);
+                *abort_flag = 1;
+                return false;
+            }
+        }
     }
 }
 
-template <int PRO, int EPI, int AMODE, int NT>
-__global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ uint64_t bar_mma[2];
-    __shared__ uint64_t bar_b[2];
-    __shared__ uint32_t tslot;
-    __shared__ int s_fail;
+// Source address of the 8 channels [k, k+8) of the 2x2/stride-2 patch of
+// output pixel `pix` of image `img`.
+__device__ __forceinline__ const __half* s2_src(const GemmParams& p, int img, int pix, int k) {
+    const int tap = k / p.seg_c;
+    const int c = k - tap * p.seg_c;
+    const int y = pix / p.Wo;
+    const int x = pix - y * p.Wo;
+    const size_t spix = static_cast<size_t>(2 * y + (tap >> 1)) * (2 * p.Wo) + 2 * x + (tap & 1);
+    return p.a[0] + img * p.a_img_stride + spix * p.seg_c + c;
+}
 
-    constexpr uint32_t kCols = NT < 32 ? 32 : NT;
+// Epilogue staging geometry: boxes of EB columns x 128 rows, TMA-swizzled
+// with a span of EB*2 bytes (32 / 64 / 128).
+template <int OUTC>
+struct Staging {
+    static constexpr int EB = OUTC < 64 ? OUTC : 64;
+    static constexpr int kBoxes = OUTC / EB;
+    static constexpr int kRowBytes = EB * 2;
+    static constexpr int kBoxBytes = kRows * kRowBytes;
+    static constexpr int kBytes = kBoxes * kBoxBytes;
+    // Byte offset of 16-byte chunk `j` (8 columns) of row r.
+    __device__ static __forceinline__ uint32_t off(int r, int j) {
+        const int box = j / (EB / 8);
+        const int jj = j - box * (EB / 8);
+        int sw;
+        if (EB == 64) sw = r & 7;
+        else if (EB == 32) sw = (r >> 1) & 3;
+        else sw = (r >> 2) & 1;
+        return box * kBoxBytes + r * kRowBytes + ((jj ^ sw) << 4);
+    }
+};
+
+template <int PRO, int EPI, int AMODE, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_ws_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ GemmMaps maps) {
+    constexpr bool kLN = (PRO == kProLayerNorm);
+    constexpr bool kWriteA = (PRO == kProScale) || (AMODE == kAS2x2);  // MMA waits for the transform
+    constexpr uint32_t kAccCols = NT < 32 ? 32 : NT;
+    constexpr uint32_t kCols = 2 * kAccCols;  // two accumulators
+    constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
+    using Stg = Staging<kOutCols>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // Swizzled TMA staging needs 1024-byte alignment: align by hand (the
+    // launch reserves 1 KB of slack).
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    __shared__ uint64_t bar_raw[kStages], bar_full[kStages], bar_empty[kStages];
+    __shared__ uint64_t bar_acc_full[2], bar_acc_empty[2], bar_st_full[2], bar_st_empty[2], bar_res;
+    __shared__ float2 s_stats[2][kRows];  // LN (mean, rstd) per tile row, double-buffered
+    __shared__ uint32_t tslot;
+    __shared__ volatile int s_abort;
+
     const int KC = p.KC;
+    const int nk = p.k_chunks;
     const uint32_t a_bytes = kRows * KC * 2;
     const uint32_t b_bytes = NT * KC * 2;
-    const uint32_t sbo = static_cast<uint32_t>(KC / 8) * 128u;
-    uint8_t* sA0 = smem;
-    uint8_t* sB0 = smem + 2 * a_bytes;
-
+    const uint32_t b_sbo = static_cast<uint32_t>(KC / 8) * 128u;
+    const uint32_t stage_bytes = kRows * kKC * 2 + NT * kKC * 2;
+    const uint32_t a_swz = static_cast<uint32_t>(p.a_swz);
+    // Byte offset of 16-byte chunk q (8 channels) of tile row r in an A stage.
+    auto a_off = [a_swz](int r, int q) -> uint32_t {
+        return a_swz ? sw_offset(r, q, a_swz) : static_cast<uint32_t>(q) * kALbo + r * 16;
+    };
+    uint8_t* stg = smem + kStages * stage_bytes;  // 1024-aligned: stage_bytes is a multiple of 1024
+    float* s_bias = reinterpret_cast<float*>(stg + Stg::kBytes);
+    float* s_rsc = s_bias + p.n_tiles * NT;
+    float* s_c1 = s_rsc + p.n_out;
+    float* s_sca = s_c1 + p.n_tiles * NT;  // SCA scale of image 0 (single-image launches)
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
-    const int n_tile = blockIdx.x % p.n_tiles;
-    const int m_tile = blockIdx.x / p.n_tiles;
-    const int row = m_tile * kRows + tid;
-    const bool row_ok = row < p.M;
-    const int img = row_ok ? row / p.hw : 0;
-    const int pix = row - img * p.hw;
+    const int lane = tid & 31;
+    const int m_tiles = (p.M + kRows - 1) / kRows;
+    const int n_tiles_total = m_tiles * p.n_tiles;
+    const bool one_img = p.M <= p.hw;
 
+    // Parameter vectors -> shared memory (c2 of the LN fold lives in s_bias).
+    for (int i = tid; i < p.n_tiles * NT; i += kThreads) {
+        s_bias[i] = p.bias ? p.bias[i] : 0.f;
+        if (kLN) s_c1[i] = p.ln_c1[i];
+    }
+    if (EPI == kEpiResidual)
+        for (int i = tid; i < p.n_out; i += kThreads) s_rsc[i] = p.res_scale[i];
+    if (PRO == kProScale && one_img)
+        for (int i = tid; i < p.K; i += kThreads) s_sca[i] = p.pro_scale[i];
     if (warp == 0) {
         tmem_alloc(&tslot, kCols);
         tmem_relinquish();
     }
     if (tid == 0) {
-        mbar_init(&bar_mma[0], 1);
-        mbar_init(&bar_mma[1], 1);
-        mbar_init(&bar_b[0], 1);
-        mbar_init(&bar_b[1], 1);
-        s_fail = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bar_raw[s], 1);
+            mbar_init(&bar_full[s], 4);
+            mbar_init(&bar_empty[s], kLN ? 5 : 1);  // LN: MMA commit + 4 statistics warps
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bar_acc_full[b], 1);
+            mbar_init(&bar_acc_empty[b], 4);
+            mbar_init(&bar_st_full[b], 4);
+            mbar_init(&bar_st_empty[b], 4);
+        }
+        mbar_init(&bar_res, 1);
+        s_abort = 0;
         fence_mbar_init();
     }
     tc_fence_before();
@@ -110,192 +247,336 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ Ge
     tc_fence_after();
     const uint32_t tmem = tslot;
 
-    // LayerNorm statistics of this row (two passes over K; the row is
-    // re-read from L1/L2 by the chunk loop below).
-    float mean = 0.f, rstd = 0.f;
-    if (PRO == kProLayerNorm && row_ok) {
-        float s = 0.f;
-        for (int k = 0; k < p.K; k += 8) {
-            float f[8];
-            h8_to_f(__ldg(reinterpret_cast<const uint4*>(a_src<AMODE>(p, img, pix, k))), f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) s += f[i];
-        }
-        mean = s / static_cast<float>(p.K);
-        float v = 0.f;
-        for (int k = 0; k < p.K; k += 8) {
-            float f[8];
-            h8_to_f(__ldg(reinterpret_cast<const uint4*>(a_src<AMODE>(p, img, pix, k))), f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float d = f[i] - mean;
-                v += d * d;
-            }
-        }
-        rstd = rsqrtf(v / static_cast<float>(p.K) + 1e-6f);
-    }
-
-    const int nk = p.k_chunks;
-    const uint32_t idesc = idesc_f16_f32(kRows, NT);
-    bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-        const int buf = j & 1;
-        uint8_t* sA = sA0 + buf * a_bytes;
-        uint8_t* sB = sB0 + buf * b_bytes;
-        if (j >= 2) {
-            // The MMAs of chunk j-2 must be done reading this stage.
-            const bool w = mbar_wait(&bar_mma[buf], ((j - 2) >> 1) & 1);
-            if (!w) report_error(p.err, 0x10, kErrMbarTimeout);
-            ok = __syncthreads_and(w) != 0;
-            if (!ok) break;
-        }
-        if (tid == 0) {
-            mbar_arrive_expect_tx(&bar_b[buf], b_bytes);
-            bulk_g2s(sB, p.bpack + (static_cast<size_t>(n_tile) * nk + j) * b_bytes, b_bytes,
-                     &bar_b[buf]);
-        }
-        // A chunk: this thread's row, KC/8 vectors of 8 channels.
-        const int k0 = j * KC;
-        uint4 v[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int k = k0 + q * 8;
-            v[q] = make_uint4(0, 0, 0, 0);
-            if (q * 8 < KC && row_ok && k < p.K)
-                v[q] = __ldg(reinterpret_cast<const uint4*>(a_src<AMODE>(p, img, pix, k)));
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            if (q * 8 >= KC) break;
-            const int k = k0 + q * 8;
-            if (PRO != kProNone && row_ok && k < p.K) {
-                float f[8];
-                h8_to_f(v[q], f);
-                if (PRO == kProLayerNorm) {
-                    const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.pro_w + k));
-                    const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.pro_w + k + 4));
-                    const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.pro_b + k));
-                    const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.pro_b + k + 4));
-                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) f[i] = (f[i] - mean) * rstd * wv[i] + bv[i];
-                } else {
-                    const float* sc = p.pro_scale + static_cast<size_t>(img) * p.K + k;
-                    const float4 s0 = __ldg(reinterpret_cast<const float4*>(sc));
-                    const float4 s1 = __ldg(reinterpret_cast<const float4*>(sc + 4));
-                    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) f[i] *= sv[i];
-                }
-                v[q] = f_to_h8(f);
-            }
-            *reinterpret_cast<uint4*>(sA + kmajor_offset(tid, q, sbo)) = v[q];
-        }
-        fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            if (!mbar_wait(&bar_b[buf], (j >> 1) & 1)) {
-                report_error(p.err, 0x11, kErrMbarTimeout);
-                s_fail = 1;
-            } else {
-                tc_fence_after();
-                const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
-                for (int s = 0; s < KC / 16; ++s) {
-                    mma_f16(tmem, sdesc_kmajor(a0 + s * 256, 128, sbo),
-                            sdesc_kmajor(b0 + s * 256, 128, sbo), idesc,
-                            (j > 0 || s > 0) ? 1u : 0u);
-                }
-            }
-            mma_commit(&bar_mma[buf]);
-        }
-    }
-
-    if (ok) {
-        const bool w = mbar_wait(&bar_mma[(nk - 1) & 1], ((nk - 1) >> 1) & 1);
-        if (!w) report_error(p.err, 0x12, kErrMbarTimeout);
-        ok = __syncthreads_and(w && s_fail == 0) != 0;
-    }
-    tc_fence_after();
-
-    if (ok) {
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-        if (EPI == kEpiGate) {
-            constexpr int kHalf = NT / 2;
-#pragma unroll 1
-            for (int c0 = 0; c0 < kHalf; c0 += 16) {
-                float va[16], vb[16];
-                tmem_ld16(lane_base + c0, va);
-                tmem_ld16(lane_base + kHalf + c0, vb);
-                tmem_ld_wait();
-                const int o0 = n_tile * kHalf + c0;
-                if (!row_ok || o0 >= p.n_out) continue;
-                const float* bias = p.bias + n_tile * NT;
-                float r[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    r[i] = (va[i] + bias[c0 + i]) * (vb[i] + bias[kHalf + c0 + i]);
-                __half* dst = p.out + static_cast<size_t>(row) * p.out_c + o0;
-#pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    if (o0 + 8 * g >= p.n_out) break;
-                    float f[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) f[i] = r[8 * g + i];
-                    *reinterpret_cast<uint4*>(dst + 8 * g) = f_to_h8(f);
-                }
-            }
-        } else {
-#pragma unroll 1
-            for (int c0 = 0; c0 < NT; c0 += 16) {
-                float va[16];
-                tmem_ld16(lane_base + c0, va);
-                tmem_ld_wait();
-                const int n0 = n_tile * NT + c0;
-                if (!row_ok || n0 >= p.n_out) continue;
-#pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    const int n = n0 + 8 * g;
-                    if (n >= p.n_out) break;
-                    float f[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        f[i] = va[8 * g + i] + (p.bias ? p.bias[n + i] : 0.f);
-                    if (EPI == kEpiStore) {
-                        *reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.out_c + n) =
-                            f_to_h8(f);
-                    } else if (EPI == kEpiResidual) {
-                        const size_t off = static_cast<size_t>(row) * p.out_c + n;
-                        float r[8];
-                        h8_to_f(*reinterpret_cast<const uint4*>(p.res + off), r);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) f[i] = r[i] + p.res_scale[n + i] * f[i];
-                        *reinterpret_cast<uint4*>(p.out + off) = f_to_h8(f);
-                    } else {  // kEpiShuffleAdd: column n -> (sub-pixel ij, channel ch)
-                        const int cout = p.out_c;
-                        const int ij = n / cout;
-                        const int ch = n - ij * cout;
-                        const int y = pix / p.Wo;
-                        const int x = pix - y * p.Wo;
-                        const size_t pix =
-                            (static_cast<size_t>(img) * (2 * p.Ho) + 2 * y + (ij >> 1)) *
-                                (2 * p.Wo) +
-                            2 * x + (ij & 1);
-                        const size_t off = pix * cout + ch;
-                        float r[8];
-                        h8_to_f(*reinterpret_cast<const uint4*>(p.skip + off), r);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) f[i] += r[i];
-                        *reinterpret_cast<uint4*>(p.out + off) = f_to_h8(f);
+    if (warp == 8) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane == 0) {
+            int it = 0;
+            for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x) {
+                const int n_tile = tile % p.n_tiles;
+                const int m0 = (tile / p.n_tiles) * kRows;
+                for (int j = 0; j < nk; ++j, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!wait_or_abort(&bar_empty[s], ph ^ 1, &s_abort, p.err, 0x20)) break;
+                    uint8_t* sa = smem + s * stage_bytes;
+                    uint8_t* sb = sa + kRows * kKC * 2;
+                    mbar_arrive_expect_tx(&bar_raw[s], (AMODE == kAS2x2 ? 0u : a_bytes) + b_bytes);
+                    bulk_g2s(sb, p.bpack + (static_cast<size_t>(n_tile) * nk + j) * b_bytes, b_bytes,
+                             &bar_raw[s]);
+                    if (AMODE != kAS2x2) {
+                        const int k0 = j * KC;
+                        if (a_swz) {
+                            // One KC-wide swizzled box (KC <= segment width).
+                            const int seg = k0 / p.seg_c;
+                            const bool in = k0 < p.K;
+                            tma_load_2d(sa, &maps.a[in ? seg : 0], in ? k0 - seg * p.seg_c : p.seg_c, m0, &bar_raw[s]);
+                        } else {
+                            for (int q = 0; q < KC / 8; ++q) {
+                                const int k = k0 + q * 8;
+                                const int seg = k < p.K ? k / p.seg_c : 0;
+                                const int kl = k < p.K ? k - seg * p.seg_c : p.seg_c;  // OOB -> zero fill
+                                tma_load_2d(sa + q * kALbo, &maps.a[seg], kl, m0, &bar_raw[s]);
+                            }
+                        }
                     }
                 }
             }
         }
+    } else if (warp == 9) {
+        // ------------------------------ MMA issuer --------------------------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(kRows, NT);
+            int it = 0, t = 0;
+            for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x, ++t) {
+                const int b = t & 1;
+                if (!wait_or_abort(&bar_acc_empty[b], ((t >> 1) & 1) ^ 1, &s_abort, p.err, 0x21)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + b * kAccCols;
+                bool ok = true;
+                for (int j = 0; j < nk; ++j, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!wait_or_abort(kWriteA ? &bar_full[s] : &bar_raw[s], ph, &s_abort, p.err, 0x22)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(smem + s * stage_bytes);
+                    const uint32_t b0 = a0 + kRows * kKC * 2;
+                    for (int k = 0; k < KC / 16; ++k) {
+                        const uint64_t ad = a_swz ? sdesc_kmajor_sw(a0 + k * 32, a_swz)
+                                                  : sdesc_kmajor(a0 + k * 2 * kALbo, kALbo, 128);
+                        mma_f16(acc, ad, sdesc_kmajor(b0 + k * 256, 128, b_sbo), idesc, (j > 0 || k > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&bar_empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&bar_acc_full[b]);
+            }
+        }
+    } else if (warp < 4) {
+        // ------------------------------ transform ---------------------------------
+        if (kLN || kWriteA) {
+            const int r = tid;  // tile row
+            int it = 0, t = 0;
+            for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x, ++t) {
+                const int row = (tile / p.n_tiles) * kRows + r;
+                const bool row_ok = row < p.M;
+                const int img = row_ok ? row / p.hw : 0;
+                const int pix = row - img * p.hw;
+                float x0 = 0.f, s1 = 0.f, s2 = 0.f;
+                bool ok = true;
+                for (int j = 0; j < nk; ++j, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!wait_or_abort(&bar_raw[s], ph, &s_abort, p.err, 0x23)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + s * stage_bytes;
+                    if (kLN) {
+                        // Shifted sums of the row (shift = its first element).
+                        for (int q = 0; q < KC / 8; ++q) {
+                            const int k = j * KC + q * 8;
+                            if (k >= p.K) break;
+                            float f[8];
+                            h8_to_f(*reinterpret_cast<const uint4*>(sa + a_off(r, q)), f);
+                            if (k == 0) x0 = f[0];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const float d = f[i] - x0;
+                                s1 += d;
+                                s2 = fmaf(d, d, s2);
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bar_empty[s]);
+                    } else if (AMODE == kAS2x2) {
+                        uint4 v[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const int k = j * KC + q * 8;
+                            v[q] = make_uint4(0, 0, 0, 0);
+                            if (q * 8 < KC && row_ok && k < p.K)
+                                v[q] = __ldg(reinterpret_cast<const uint4*>(s2_src(p, img, pix, k)));
+                        }
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            if (q * 8 < KC) *reinterpret_cast<uint4*>(sa + a_off(r, q)) = v[q];
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bar_full[s]);
+                    } else {  // SCA scale in place
+                        if (row_ok) {
+                            const float* sc = one_img ? s_sca : p.pro_scale + static_cast<size_t>(img) * p.K;
+                            for (int q = 0; q < KC / 8; ++q) {
+                                const int k = j * KC + q * 8;
+                                if (k >= p.K) break;
+                                uint4* ptr = reinterpret_cast<uint4*>(sa + a_off(r, q));
+                                float f[8];
+                                h8_to_f(*ptr, f);
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) f[i] *= sc[k + i];
+                                *ptr = f_to_h8(f);
+                            }
+                        }
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bar_full[s]);
+                    }
+                }
+                if (!ok) break;
+                if (kLN) {
+                    const int sb = t & 1;
+                    if (!wait_or_abort(&bar_st_empty[sb], ((t >> 1) & 1) ^ 1, &s_abort, p.err, 0x25)) break;
+                    const float inv = 1.0f / static_cast<float>(p.K);
+                    const float dm = s1 * inv;
+                    const float var = fmaxf(s2 * inv - dm * dm, 0.f);
+                    s_stats[sb][r] = make_float2(x0 + dm, rsqrtf(var + 1e-6f));
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bar_st_full[sb]);
+                }
+            }
+        }
     } else {
-        // Give in-flight MMAs a bounded chance to drain before TMEM is freed.
-        if (tid == 0) {
-            mbar_wait(&bar_mma[0], 0, 10000000ull);
-            mbar_wait(&bar_mma[1], 0, 10000000ull);
+        // ------------------------------ epilogue ----------------------------------
+        const int r = tid - 128;       // tile row == TMEM lane
+        const int wq = warp - 4;       // TMEM lane quarter of this warp
+        const bool leader = (r == 0);
+        const bool tma_epi = (EPI != kEpiShuffleAdd) && (p.out_c % kOutCols == 0);
+        int t = 0;
+        for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t) {
+            const int b = t & 1;
+            bool got = wait_or_abort(&bar_acc_full[b], (t >> 1) & 1, &s_abort, p.err, 0x24);
+            if (kLN && got) got = wait_or_abort(&bar_st_full[b], (t >> 1) & 1, &s_abort, p.err, 0x26);
+            if (tma_epi && leader) bulk_wait_read0();  // previous tile's store has read the staging
+            // Uniform exit decision; also the "staging is free again" barrier.
+            if (epi_sync_or(!got || s_abort)) break;
+            tc_fence_after();
+            const int n_tile = tile % p.n_tiles;
+            const int m0 = (tile / p.n_tiles) * kRows;
+            const int row = m0 + r;
+            const bool row_ok = row < p.M;
+            const int img = row_ok ? row / p.hw : 0;
+            const int pix = row - img * p.hw;
+            const uint32_t lane_base = tmem + b * kAccCols + (static_cast<uint32_t>(wq * 32) << 16);
+            float mean = 0.f, rstd = 1.f;
+            if (kLN) {
+                const float2 st = s_stats[b][r];
+                mean = st.x;
+                rstd = st.y;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar_st_empty[b]);
+            }
+            const int col0 = n_tile * kOutCols;
+            if (EPI == kEpiResidual && tma_epi) {
+                if (leader) {
+                    mbar_arrive_expect_tx(&bar_res, Stg::kBytes);
+                    for (int bx = 0; bx < Stg::kBoxes; ++bx)
+                        tma_load_2d(stg + bx * Stg::kBoxBytes, &maps.res, col0 + bx * Stg::EB, m0, &bar_res);
+                }
+                wait_or_abort(&bar_res, t & 1, &s_abort, p.err, 0x27);
+            }
+            if (EPI == kEpiShuffleAdd || !tma_epi) {
+                // Direct per-row stores (PixelShuffle scatter, or narrow outputs).
+#pragma unroll 1
+                for (int c0 = 0; c0 < kOutCols; c0 += 16) {
+                    float va[16], vb[16];
+                    tmem_ld16(lane_base + c0, va);
+                    if (EPI == kEpiGate) tmem_ld16(lane_base + NT / 2 + c0, vb);
+                    tmem_ld_wait();
+                    const int n0 = n_tile * NT + c0;
+                    const int o0 = col0 + c0;
+                    if (!row_ok || o0 >= p.n_out) continue;
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        const int n = n0 + 8 * g;
+                        const int o = o0 + 8 * g;
+                        if (o >= p.n_out) break;
+                        float f[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            float v = va[8 * g + i];
+                            if (kLN) v = rstd * (v - mean * s_c1[n + i]) + s_bias[n + i];
+                            else v += s_bias[n + i];
+                            if (EPI == kEpiGate) {
+                                const int nb2 = n + NT / 2;
+                                float w2 = vb[8 * g + i];
+                                if (kLN) w2 = rstd * (w2 - mean * s_c1[nb2 + i]) + s_bias[nb2 + i];
+                                else w2 += s_bias[nb2 + i];
+                                v *= w2;
+                            }
+                            f[i] = v;
+                        }
+                        if (EPI == kEpiShuffleAdd) {
+                            const int cout = p.out_c;
+                            const int ij = n / cout;
+                            const int ch = n - ij * cout;
+                            const int y = pix / p.Wo;
+                            const int x = pix - y * p.Wo;
+                            const size_t opix = (static_cast<size_t>(img) * (2 * p.Ho) + 2 * y + (ij >> 1)) *
+                                                    (2 * p.Wo) + 2 * x + (ij & 1);
+                            const size_t off = opix * cout + ch;
+                            float rr[8];
+                            h8_to_f(*reinterpret_cast<const uint4*>(p.skip + off), rr);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) f[i] += rr[i];
+                            *reinterpret_cast<uint4*>(p.out + off) = f_to_h8(f);
+                        } else {
+                            const size_t off = static_cast<size_t>(row) * p.out_c + o;
+                            if (EPI == kEpiResidual) {
+                                float rr[8];
+                                h8_to_f(*reinterpret_cast<const uint4*>(p.res + off), rr);
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) f[i] = rr[i] + s_rsc[o + i] * f[i];
+                            }
+                            *reinterpret_cast<uint4*>(p.out + off) = f_to_h8(f);
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+                continue;
+            }
+            // Swizzled staging tile -> TMA tensor store.
+            if (EPI == kEpiGate) {
+                constexpr int kHalf = NT / 2;
+#pragma unroll 1
+                for (int c0 = 0; c0 < kHalf; c0 += 16) {
+                    float va[16], vb[16];
+                    tmem_ld16(lane_base + c0, va);
+                    tmem_ld16(lane_base + kHalf + c0, vb);
+                    tmem_ld_wait();
+                    const int n = n_tile * NT + c0;
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        float f[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int na = n + 8 * g + i, nb2 = na + kHalf;
+                            float x1 = va[8 * g + i], x2 = vb[8 * g + i];
+                            if (kLN) {
+                                x1 = rstd * (x1 - mean * s_c1[na]) + s_bias[na];
+                                x2 = rstd * (x2 - mean * s_c1[nb2]) + s_bias[nb2];
+                            } else {
+                                x1 += s_bias[na];
+                                x2 += s_bias[nb2];
+                            }
+                            f[i] = x1 * x2;
+                        }
+                        *reinterpret_cast<uint4*>(stg + Stg::off(r, (c0 >> 3) + g)) = f_to_h8(f);
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c0 = 0; c0 < NT; c0 += 16) {
+                    float va[16];
+                    tmem_ld16(lane_base + c0, va);
+                    tmem_ld_wait();
+                    const int n = n_tile * NT + c0;
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        float f[8];
+                        uint4* sp = reinterpret_cast<uint4*>(stg + Stg::off(r, (c0 >> 3) + g));
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int nn = n + 8 * g + i;
+                            f[i] = kLN ? rstd * (va[8 * g + i] - mean * s_c1[nn]) + s_bias[nn]
+                                       : va[8 * g + i] + s_bias[nn];
+                        }
+                        if (EPI == kEpiResidual) {
+                            float rr[8];
+                            h8_to_f(*sp, rr);
+                            const int o = col0 + c0 + 8 * g;
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) f[i] = rr[i] + s_rsc[min(o + i, p.n_out - 1)] * f[i];
+                        }
+                        *sp = f_to_h8(f);
+                    }
+                }
+            }
+            // TMEM of this accumulator is no longer needed.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+            fence_async_smem();
+            epi_sync();
+            if (leader) {
+                for (int bx = 0; bx < Stg::kBoxes; ++bx)
+                    tma_store_2d(&maps.out, col0 + bx * Stg::EB, m0, stg + bx * Stg::kBoxBytes);
+                bulk_commit();
+            }
+        }
+        if (leader) bulk_wait0();
+    }
+
+    __syncthreads();
+    if (s_abort && tid == 0) {
+        // Let in-flight copies and MMAs land before the CTA's memory is released.
+        for (int s = 0; s < kStages; ++s) {
+            mbar_wait(&bar_raw[s], 0, 5000000ull);
+            mbar_wait(&bar_empty[s], 0, 5000000ull);
         }
     }
     tc_fence_before();
@@ -303,23 +584,106 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ Ge
     if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 2-D map over a [rows][cols] fp16 matrix with row stride `ld` elements and a
+// box of `box_cols` columns x 128 rows.
+int make_map(CUtensorMap* m, const void* base, long long rows, int cols, long long ld, int box_cols,
+             CUtensorMapSwizzle swz) {
+    auto fn = encode_fn();
+    if (!fn) return dn_fail(DN_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16)
+        return dn_fail(DN_ERR_INVALID_ARG, "gemm: operand must be 16-byte aligned");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), kRows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return dn_fail_str(DN_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+    return DN_OK;
+}
+
+CUtensorMapSwizzle swizzle_for(int row_bytes) {
+    return row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+           : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                             : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
+int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
 template <int PRO, int EPI, int AMODE, int NT>
 int launch_one(const GemmParams& p, cudaStream_t s) {
-    auto kern = gemm_tc_kernel<PRO, EPI, AMODE, NT>;
-    // Always reserve the KC=64 footprint: it caps residency at <= 512 TMEM
-    // columns per SM for every NT, so tcgen05.alloc never has to wait.
-    const int smem = 2 * (kRows * 64 * 2 + NT * 64 * 2);
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             smem);
+    auto kern = gemm_ws_kernel<PRO, EPI, AMODE, NT>;
+    constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
+    using Stg = Staging<kOutCols>;
+    const int params = 2 * p.n_tiles * NT + p.n_out + p.K;
+    const int smem = 1024 + kStages * (kRows * kKC * 2 + NT * kKC * 2) + Stg::kBytes + params * 4;
+    if (smem > 225 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: tile does not fit in shared memory");
+    static int configured = 0;  // largest dynamic footprint granted so far
+    if (smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return dn_cuda_fail(e, "gemm: set smem attribute");
-        configured = true;
+        configured = smem;
+    }
+    if (PRO == kProLayerNorm && !p.ln_c1) return dn_fail(DN_ERR_INVALID_ARG, "gemm: LN fold needs c1");
+    GemmMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    if (AMODE != kAS2x2) {
+        if (p.nseg > 1 && p.M != p.hw) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: concat sources need one image");
+        if (p.nseg == 1 && p.M != p.hw && p.a_img_stride != static_cast<long long>(p.hw) * p.seg_c)
+            return dn_fail(DN_ERR_UNSUPPORTED, "gemm: batched A rows must be contiguous");
+        if (p.a_swz && p.a_swz != p.KC * 2) return dn_fail(DN_ERR_INVALID_ARG, "gemm: A swizzle span must be KC*2");
+        if (p.a_swz && p.nseg > 1 && p.seg_c < p.KC)
+            return dn_fail(DN_ERR_INVALID_ARG, "gemm: swizzled concat needs KC <= segment width");
+        for (int sgi = 0; sgi < p.nseg; ++sgi) {
+            const int rc = p.a_swz ? make_map(&maps.a[sgi], p.a[sgi], p.M, p.seg_c, p.seg_c, p.KC, swizzle_for(p.a_swz))
+                                   : make_map(&maps.a[sgi], p.a[sgi], p.M, p.seg_c, p.seg_c, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (rc != DN_OK) return rc;
+        }
+    }
+    if (EPI != kEpiShuffleAdd && p.out_c % kOutCols == 0) {
+        int rc = make_map(&maps.out, p.out, p.M, p.out_c, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
+        if (rc != DN_OK) return rc;
+        if (EPI == kEpiResidual) {
+            rc = make_map(&maps.res, p.res, p.M, p.out_c, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
+            if (rc != DN_OK) return rc;
+        }
     }
     const int m_tiles = (p.M + kRows - 1) / kRows;
-    const long long grid = static_cast<long long>(m_tiles) * p.n_tiles;
-    if (grid <= 0 || grid > 0x7fffffffLL) return dn_fail(DN_ERR_INVALID_ARG, "gemm: bad grid");
-    kern<<<static_cast<unsigned>(grid), 128, smem, s>>>(p);
+    const long long tiles = static_cast<long long>(m_tiles) * p.n_tiles;
+    // TMEM: 2 accumulators of NT columns each; at most 512 columns per SM.
+    const int by_tmem = 512 / (2 * (NT < 32 ? 32 : NT));
+    const int by_smem = (227 * 1024) / (smem + 2048);
+    const int per_sm = std::max(1, std::min(by_tmem, by_smem));
+    const long long grid = std::min<long long>(tiles, static_cast<long long>(num_sms()) * per_sm);
+    kern<<<static_cast<unsigned>(grid), kThreads, smem, s>>>(p, maps);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return dn_cuda_fail(e, "gemm: launch");
     return DN_OK;
@@ -343,11 +707,13 @@ int launch_nt(const GemmParams& p, int nt, cudaStream_t s) {
 }  // namespace
 
 int launch_gemm(const GemmParams& p, int pro, int epi, int amode, int nt, cudaStream_t s) {
-    if (p.KC != 16 && p.KC != 32 && p.KC != 48 && p.KC != 64)
-        return dn_fail(DN_ERR_UNSUPPORTED, "gemm: KC must be 16/32/48/64");
+    if (p.KC != 16 && p.KC != 32 && p.KC != 64) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: KC must be 16/32/64");
+    if (p.a_swz != 0 && p.a_swz != 32 && p.a_swz != 64 && p.a_swz != 128)
+        return dn_fail(DN_ERR_UNSUPPORTED, "gemm: bad A swizzle span");
     if (p.seg_c % 8 != 0) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: channels must be a multiple of 8");
     if (p.M <= 0) return DN_OK;
-    if (epi == kEpiGate && !p.bias) return dn_fail(DN_ERR_INVALID_ARG, "gemm: gate epilogue needs a bias");
+    if (pro == kProLayerNorm && p.nseg != 1) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: LN needs one source");
+    if (p.nseg < 1 || p.nseg > kMaxSeg) return dn_fail(DN_ERR_INVALID_ARG, "gemm: bad segment count");
     // Instantiated combinations (the ones the planner emits).
     if (amode == kARows && pro == kProLayerNorm && epi == kEpiStore)
         return launch_nt<kProLayerNorm, kEpiStore, kARows>(p, nt, s);

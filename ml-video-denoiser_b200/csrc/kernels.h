@@ -16,7 +16,7 @@ namespace dnb {
 
 enum GemmPro : int {
     kProNone = 0,
-    kProLayerNorm = 1,  // per-row LayerNorm over K (eps 1e-6) then affine pro_w/pro_b
+    kProLayerNorm = 1,  // per-row LayerNorm over K (eps 1e-6), folded into B (gamma) and the epilogue
     kProScale = 2,      // A[m, k] * pro_scale[img(m) * K + k]  (SCA apply)
 };
 
@@ -42,11 +42,11 @@ struct GemmParams {
     int nseg, seg_c;           // A = concat of nseg segments of seg_c channels
     long long a_img_stride;    // elements between images of every segment source
     const __half* a[kMaxSeg];
-    const float* pro_w;        // LN gamma [K]
-    const float* pro_b;        // LN beta [K]
+    const float* ln_c1;        // LN fold: per packed column sum_k (gamma W)[n,k] (bias holds c2)
     const float* pro_scale;    // [N_img][K]
     const uint8_t* bpack;      // packed B tiles [n_tiles][k_chunks][NT x KC canonical]
     int n_tiles, k_chunks, KC;
+    int a_swz;                 // A tile layout: KC*2 (swizzled rows of that span) or 0 (8-column core-matrix columns)
     const float* bias;         // [n_tiles * NT] packed order, may be null
     __half* out;
     int out_c;                 // channels of an output pixel

@@ -162,6 +162,29 @@ __device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t saddr, uint32_t lbo, u
     return d;                             // base offset 0, layout type 0 (no swizzle)
 }
 
+// Shared-memory matrix descriptor, K-major, swizzled (the layout a TMA load
+// with CU_TENSOR_MAP_SWIZZLE_{32,64,128}B writes): rows of `row_bytes`
+// (32/64/128) with 16-byte chunks XOR-permuted within each 8-row atom.
+// SBO = 8 rows; LBO is unused for K-major swizzled operands. Advance the
+// start address by 32 bytes per K=16 step inside the row.
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw(uint32_t saddr, uint32_t row_bytes) {
+    const uint32_t layout = row_bytes == 128 ? 2u : (row_bytes == 64 ? 4u : 6u);
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1u) << 16;                           // LBO (unused)
+    d |= static_cast<uint64_t>(((8u * row_bytes) >> 4) & 0x3FFFu) << 32;  // SBO
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(layout) << 61;
+    return d;
+}
+
+// Byte offset of 16-byte chunk j of row r in a swizzled K-major tile whose
+// rows are `row_bytes` long (the TMA swizzle pattern of that span).
+__device__ __forceinline__ uint32_t sw_offset(uint32_t r, uint32_t j, uint32_t row_bytes) {
+    const uint32_t sw = row_bytes == 128 ? (r & 7u) : (row_bytes == 64 ? ((r >> 1) & 3u) : ((r >> 2) & 1u));
+    return r * row_bytes + ((j ^ sw) << 4);
+}
+
 // Instruction descriptor for tcgen05.mma kind::f16 with fp16 A/B, fp32
 // accumulate, both operands K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
