@@ -126,6 +126,11 @@ int dn_model_sync(dn_model* model, void* stream);
 int dn_model_stats(const dn_model* model, size_t* weight_bytes, size_t* activation_bytes,
                    int* kernels_per_forward);
 
+/* Select the fused two-pass NAFBlock kernels for blocks with <= 64 channels
+ * (default 1) or the per-conv kernels everywhere (0). Results agree within
+ * the parity tolerance; the switch exists for testing both paths. */
+int dn_model_set_fused(dn_model* model, int enable);
+
 /* Per-launch CUDA-event timing of the engine's kernels (no reference
  * counterpart; the reference engine has no timers). While enabled, every
  * kernel the model launches is bracketed by events on its stream. */

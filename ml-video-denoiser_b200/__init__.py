@@ -83,6 +83,7 @@ SIGNATURES = {
     "dn_model_forward_host": (_I, [_P, _P, _I64P, _I, _P, _P]),
     "dn_model_sync": (_I, [_P, _P]),
     "dn_model_stats": (_I, [_P, _SZP, _SZP, _IP]),
+    "dn_model_set_fused": (_I, [_P, _I]),
     "dn_model_profile": (_I, [_P, _I]),
     "dn_model_profile_report": (_I, [_P, _c.c_char_p, _c.c_size_t]),
 }
@@ -261,6 +262,10 @@ class Model:
     def sync(self, stream=None) -> None:
         """Synchronise the stream and raise if a kernel flagged a device error."""
         check(lib().dn_model_sync(self._h, stream_handle(stream)))
+
+    def set_fused(self, enable: bool = True) -> None:
+        """Fused two-pass NAFBlock kernels on shallow levels (default) or per-conv kernels."""
+        check(lib().dn_model_set_fused(self._h, 1 if enable else 0))
 
     def profile(self, enable: bool = True) -> None:
         """Bracket every kernel launch with CUDA events (see profile_report)."""

@@ -173,6 +173,12 @@ int dn_model_stats(const dn_model* m, size_t* weight_bytes, size_t* activation_b
     return DN_OK;
 }
 
+int dn_model_set_fused(dn_model* m, int enable) {
+    if (!m) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_set_fused: null model");
+    m->eng->set_fused(enable != 0);
+    return DN_OK;
+}
+
 int dn_model_profile(dn_model* m, int enable) {
     if (!m) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_profile: null model");
     m->eng->set_profiling(enable != 0);

@@ -174,6 +174,20 @@ int dw_blocks_per_img(int H, int W, int D) {
     return static_cast<int>(std::max(1LL, std::min(want, cap)));
 }
 
+int launch_sca(const DwParams& p, int nb, cudaStream_t s) {
+    const size_t smem2 = static_cast<size_t>(9) * p.D * sizeof(float);
+    if (smem2 > 200 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "sca: too many channels");
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(sca_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "sca: set smem attribute");
+        configured = true;
+    }
+    sca_kernel<<<dim3((p.D + 7) / 8, p.N), kThreads, smem2, s>>>(p, nb);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "sca: launch");
+}
+
 int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s) {
     if (p.D % 8 != 0 || p.D / 8 > kThreads)
         return dn_fail(DN_ERR_UNSUPPORTED, "dw_gate: channels must be a multiple of 8 and <= 2048");

@@ -5,6 +5,7 @@
 #include <cstring>
 #include <stdexcept>
 
+#include "fused_block.h"
 #include "status.h"
 
 namespace dnb {
@@ -276,6 +277,15 @@ void Engine::build(const HostWeights& hw) {
                             LnFold{&ln2w, &ln2b});
         const auto b5 = hw.to_f32(pre + ".conv5.bias");
         b.conv5 = pack_gemm(pk, hw.to_f32(pre + ".conv5.weight"), C, b.ffn, store_nt(C), &b5, C);
+        if (fused_supported(C, b.dw, b.ffn)) {
+            b.fused = true;
+            const auto b4 = hw.to_f32(pre + ".conv4.bias");
+            b.f1 = pack_gemm(pk, hw.to_f32(pre + ".conv1.weight"), 2 * b.dw, C, 2 * b.dw, &b1, 2 * b.dw,
+                             LnFold{&ln1w, &ln1b});
+            b.f3 = pack_gemm(pk, hw.to_f32(pre + ".conv3.weight"), C, b.dw, C, &b3, C);
+            b.f4 = pack_gemm(pk, hw.to_f32(pre + ".conv4.weight"), 2 * b.ffn, C, 2 * b.ffn, &b4, 2 * b.ffn);
+            b.f5 = pack_gemm(pk, hw.to_f32(pre + ".conv5.weight"), C, b.ffn, C, &b5, C);
+        }
         return b;
     };
 
@@ -399,6 +409,7 @@ void Engine::plan(const Shape& s) {
             t = std::max(t, nimg * hw * b.ffn);
             dmax = std::max(dmax, static_cast<size_t>(b.dw));
             dw_blocks_max_ = std::max(dw_blocks_max_, dw_blocks_per_img(h, w, b.dw));
+            if (b.fused) dw_blocks_max_ = std::max(dw_blocks_max_, fused_a_grid(b.C, b.dw, static_cast<int>(nimg), h, w));
         }
     };
     for (int l = 0; l < L; ++l) {
@@ -550,6 +561,64 @@ static GemmParams rows_params(int nimg, int h, int w) {
 // NAFBlock (training/models.py:166-185, src/models/nafnet.cu:146-215), in place on x.
 int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaStream_t s) {
     const long long hw = static_cast<long long>(h) * w;
+    if (b.fused && fused_enabled_ && nimg <= 8) {
+        // Pass A: LN1 + conv1 + DW3x3 + SimpleGate + pool partials.
+        FusedAParams fa{};
+        fa.x = x;
+        fa.g = buf_g_;
+        fa.N = nimg;
+        fa.H = h;
+        fa.W = w;
+        fa.w1 = wptr<uint8_t>(b.f1.bpack);
+        fa.c1 = wptr<float>(b.f1.c1);
+        fa.c2 = wptr<float>(b.f1.bias);
+        fa.dw_w = wptr<float>(b.dw_w);
+        fa.dw_b = wptr<float>(b.dw_b);
+        fa.partials = partials_;
+        fa.err = err_;
+        const int grid = fused_a_grid(b.C, b.dw, nimg, h, w);
+        launches_ += 3;
+        prof_begin("fused_block_a", static_cast<double>(nimg) * hw * (b.C + b.dw) * 2,
+                   2.0 * nimg * hw * (b.C * 2 * b.dw + 2 * b.dw * 9), s);
+        DN_TRY(launch_fused_a(fa, b.C, b.dw, grid, s));
+        prof_end(s);
+        DwParams d{};
+        d.N = nimg;
+        d.H = h;
+        d.W = w;
+        d.D = b.dw;
+        d.partials = partials_;
+        d.sca_w = wptr<float>(b.sca_w);
+        d.sca_b = wptr<float>(b.sca_b);
+        d.s_out = sca_s_;
+        prof_begin("sca", 4.0 * nimg * grid * b.dw, 2.0 * nimg * b.dw * b.dw, s);
+        DN_TRY(launch_sca(d, grid, s));
+        prof_end(s);
+        // Pass B: SCA scale + conv3 + beta residual + LN2 + conv4 + gate + conv5 + gamma residual.
+        FusedBParams fb{};
+        fb.g = buf_g_;
+        fb.x = x;
+        fb.out = x;
+        fb.M = static_cast<int>(nimg * hw);
+        fb.hw = static_cast<int>(hw);
+        fb.s = sca_s_;
+        fb.w3 = wptr<uint8_t>(b.f3.bpack);
+        fb.w4 = wptr<uint8_t>(b.f4.bpack);
+        fb.w5 = wptr<uint8_t>(b.f5.bpack);
+        fb.b3 = wptr<float>(b.f3.bias);
+        fb.beta = wptr<float>(b.beta);
+        fb.ln_w = wptr<float>(b.ln2w);
+        fb.ln_b = wptr<float>(b.ln2b);
+        fb.b4 = wptr<float>(b.f4.bias);
+        fb.b5 = wptr<float>(b.f5.bias);
+        fb.gamma = wptr<float>(b.gamma);
+        fb.err = err_;
+        prof_begin("fused_block_b", static_cast<double>(nimg) * hw * (b.dw + 2 * b.C) * 2,
+                   2.0 * nimg * hw * (b.dw * b.C + b.C * 2 * b.ffn + b.ffn * b.C), s);
+        DN_TRY(launch_fused_b(fb, b.C, b.dw, b.ffn, s));
+        prof_end(s);
+        return DN_OK;
+    }
     // u = conv1(LN1(x)) + b1
     GemmParams p = rows_params(nimg, h, w);
     p.seg_c = b.C;

@@ -36,6 +36,9 @@ struct BlockW {
     GemmW conv1, conv3, conv4, conv5;
     size_t dw_w = 0, dw_b = 0;     // fp32 [9][2dw], [2dw]
     size_t sca_w = 0, sca_b = 0;   // fp32 [dw][dw], [dw]
+    // Fused two-pass kernels (shallow levels, C <= 64): single-tile B images.
+    bool fused = false;
+    GemmW f1, f3, f4, f5;          // conv1 (LN folded), conv3, conv4, conv5
 };
 
 struct ModelInfo {
@@ -71,6 +74,8 @@ public:
     // default). Each launch is tagged with its kind and its algorithmic bytes
     // (inputs read once + outputs written once) and FLOPs.
     void set_profiling(bool on) { profiling_ = on; }
+    // Use the fused two-pass NAFBlock kernels where they apply (default on).
+    void set_fused(bool on) { fused_enabled_ = on; }
     // Synchronises, then returns a JSON object: kind -> {launches, ms, bytes, flops}
     // accumulated since the last report (which also resets the counters).
     std::string profile_report();
@@ -146,6 +151,7 @@ private:
     void prof_begin(const char* kind, double bytes, double flops, cudaStream_t s);
     void prof_end(cudaStream_t s);
     bool profiling_ = false;
+    bool fused_enabled_ = true;
     std::vector<ProfRec> prof_;
     std::vector<cudaEvent_t> prof_pool_;
     size_t prof_used_ = 0;

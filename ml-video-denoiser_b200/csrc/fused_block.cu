@@ -1,0 +1,686 @@
+// Fused NAFBlock for the HBM-bound shallow levels (C <= 64 channels), as the
+// two passes the SCA global pool forces:
+//
+// Phase A (one CTA = a stream of TH x TW output tiles):
+//   TMA loads the (TH+2) x (TW+2) halo of x (NHWC, zero outside the image)
+//   straight into the swizzled K-major UMMA layout; threads compute the
+//   LayerNorm statistics of every halo pixel; tcgen05 runs conv1 over the
+//   halo (M = 128 pixels per block, N = 2*dw, K = C) with the LN folded into
+//   the weights (B = gamma*W1) and the epilogue (rstd*(acc - mean*c1) + c2),
+//   writing u (fp16, zero outside the image = the DW zero padding) to shared
+//   memory; CUDA cores then run the 3x3 depthwise conv + bias + SimpleGate
+//   from shared memory, write g by TMA store and accumulate the per-image
+//   pool partials (deterministic order).
+// Phase B (one CTA = a stream of 128-pixel tiles): TMA brings g and x;
+//   g *= s (SCA scale) in place; tcgen05 conv3 -> y = x + beta*(acc + b3)
+//   (kept in registers) -> LayerNorm2 -> tcgen05 conv4 -> SimpleGate ->
+//   tcgen05 conv5 -> out = y + gamma*(acc + b5) -> TMA store. All three
+//   weight matrices stay resident in shared memory; the accumulators chain
+//   through TMEM.
+//
+// Per pixel this moves x (plus halo) in, g out, g and x in, x' out: the
+// two-pass minimum of 5C*2 bytes, against the ~14 passes of
+// the reference block (src/models/nafnet.cu:146-215: LN, conv1, bias, conv2,
+// bias, gate, pool, sca conv, scale, conv3, bias, scaled add, LN, conv4,
+// bias, gate, conv5, bias, scaled add).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "fused_block.h"
+#include "sm100.cuh"
+#include "status.h"
+
+namespace dnb {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();  // gemm_tc.cu
+
+namespace {
+
+constexpr int kAThreads = 256;
+constexpr int kBThreads = 128;
+
+constexpr int pow2_at_least(int v) {
+    int p = 32;
+    while (p < v) p <<= 1;
+    return p;
+}
+
+template <int C, int D>
+struct GeoA {
+    static constexpr int TH = C <= 32 ? 8 : 4;
+    static constexpr int TW = C <= 32 ? 32 : 16;
+    static constexpr int HH = TH + 2;
+    static constexpr int WW = TW + 2;
+    static constexpr int P = HH * WW;                 // halo pixels
+    static constexpr int NB = (P + 127) / 128;        // 128-row MMA blocks over the halo
+    static constexpr int N1 = 2 * D;                  // conv1 outputs
+    static constexpr int TMEM_COLS = pow2_at_least(NB * N1);
+    static constexpr int ROWB = C * 2;                // A row bytes = TMA swizzle span
+    static constexpr int A_BYTES = NB * 128 * ROWB;
+    static constexpr int U_PITCH = N1 * 2 + 16;       // padded: conflict-free DW reads
+    static constexpr int U_BYTES = ((P * U_PITCH + 1023) / 1024) * 1024;
+    static constexpr int G_BYTES = TH * TW * D * 2;
+    static constexpr int W1_BYTES = N1 * C * 2;       // one K chunk (C <= 64)
+    static constexpr int LANES = kAThreads / (2 * (D / 8)); // output pixels in flight per CTA
+    // floats: c1, c2, dw taps, dw bias, stats (2 per halo pixel), partials [8][D], reduction
+    static constexpr int F_FLOATS = N1 + N1 + 9 * N1 + N1 + 2 * P + 8 * D + LANES * D;
+    static constexpr int SMEM = 1024 + A_BYTES + U_BYTES + G_BYTES + W1_BYTES + F_FLOATS * 4;
+};
+
+template <int C, int D, int F>
+struct GeoB {
+    static constexpr int TMEM_COLS = pow2_at_least(C + 2 * F);
+    static constexpr int G_BYTES = 128 * D * 2;
+    static constexpr int X_BYTES = 128 * C * 2;
+    static constexpr int A3_BYTES = 128 * F * 2;
+    static constexpr int W3_BYTES = C * D * 2;
+    static constexpr int W4_BYTES = 2 * F * C * 2;
+    static constexpr int W5_BYTES = C * F * 2;
+    static constexpr int F_FLOATS = 6 * C + 2 * F + 8 * D;
+    static constexpr int SMEM = 1024 + G_BYTES + 3 * X_BYTES + A3_BYTES + W3_BYTES + W4_BYTES + W5_BYTES +
+                                F_FLOATS * 4;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
+}
+
+// Bounded wait; on expiry records `site` and returns false.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t site) {
+    if (mbar_wait(bar, parity)) return true;
+    report_error(err, site, kErrMbarTimeout);
+    return false;
+}
+
+// ============================== phase A =====================================
+
+template <int C, int D>
+__global__ void __launch_bounds__(kAThreads, 2)
+    fused_a_kernel(const __grid_constant__ FusedAParams p, const __grid_constant__ CUtensorMap mx,
+                   const __grid_constant__ CUtensorMap mg) {
+    using G = GeoA<C, D>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sA = smem;
+    uint8_t* sU = sA + G::A_BYTES;
+    uint8_t* sGo = sU + G::U_BYTES;
+    uint8_t* sW1 = sGo + G::G_BYTES;
+    float* sC1 = reinterpret_cast<float*>(sW1 + G::W1_BYTES);
+    float* sC2 = sC1 + G::N1;
+    float* sDw = sC2 + G::N1;       // [9][2D]
+    float* sDb = sDw + 9 * G::N1;   // [2D]
+    float2* sStat = reinterpret_cast<float2*>(sDb + G::N1);
+    float* sPart = reinterpret_cast<float*>(sStat + G::P);  // [8][D]
+    float* sRed = sPart + 8 * D;                             // [LANES][D]
+    __shared__ uint64_t bar_x, bar_w, bar_mma;
+    __shared__ uint32_t tslot;
+    __shared__ int s_fail;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tiles_x = (p.W + G::TW - 1) / G::TW;
+    const int tiles_y = (p.H + G::TH - 1) / G::TH;
+    const int per_img = tiles_x * tiles_y;
+    const int total = per_img * p.N;
+    auto decode = [&](int t, int& img, int& ty0, int& tx0) {
+        img = t / per_img;
+        const int r = t - img * per_img;
+        ty0 = (r / tiles_x) * G::TH;
+        tx0 = (r % tiles_x) * G::TW;
+    };
+
+    for (int i = tid; i < G::N1; i += kAThreads) {
+        sC1[i] = p.c1[i];
+        sC2[i] = p.c2[i];
+        sDb[i] = p.dw_b[i];
+    }
+    for (int i = tid; i < 9 * G::N1; i += kAThreads) sDw[i] = p.dw_w[i];
+    for (int i = tid; i < 8 * D; i += kAThreads) sPart[i] = 0.f;
+    if (warp == 0) {
+        tmem_alloc(&tslot, G::TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        mbar_init(&bar_x, 1);
+        mbar_init(&bar_w, 1);
+        mbar_init(&bar_mma, 1);
+        s_fail = 0;
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar_w, G::W1_BYTES);
+        bulk_g2s(sW1, p.w1, G::W1_BYTES, &bar_w);
+        if (blockIdx.x < total) {
+            int img, ty0, tx0;
+            decode(blockIdx.x, img, ty0, tx0);
+            mbar_arrive_expect_tx(&bar_x, G::P * G::ROWB);
+            tma_load_4d(sA, &mx, 0, tx0 - 1, ty0 - 1, img, &bar_x);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    const bool ok = __syncthreads_and(wait_bar(&bar_w, 0, p.err, 0x30)) != 0;
+
+    // DW thread mapping: (half, channel group) fastest, then output pixel.
+    const int half = tid & 1;
+    const int cg = (tid >> 1) % (D / 8);
+    const int pl = (tid >> 1) / (D / 8);
+    float2 dww[9][4];
+    float dwb[8];
+    {
+        const int cin = half * D + cg * 8;
+#pragma unroll
+        for (int tp = 0; tp < 9; ++tp)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                dww[tp][i] = make_float2(p.dw_w[tp * G::N1 + cin + 2 * i], p.dw_w[tp * G::N1 + cin + 2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dwb[i] = p.dw_b[cin + i];
+    }
+    float ps[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int it = 0;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+        int img, ty0, tx0;
+        decode(t, img, ty0, tx0);
+        if (!wait_bar(&bar_x, it & 1, p.err, 0x31)) s_fail = 1;
+        __syncthreads();
+        if (s_fail) break;
+        // LayerNorm statistics of the halo pixels (two passes over the row).
+        for (int r = tid; r < G::P; r += kAThreads) {
+            float s = 0.f;
+#pragma unroll
+            for (int q = 0; q < C / 8; ++q) {
+                float f[8];
+                h8_to_f(*reinterpret_cast<const uint4*>(sA + sw_offset(r, q, G::ROWB)), f);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) s += f[i];
+            }
+            const float mean = s * (1.0f / C);
+            float ss = 0.f;
+#pragma unroll
+            for (int q = 0; q < C / 8; ++q) {
+                float f[8];
+                h8_to_f(*reinterpret_cast<const uint4*>(sA + sw_offset(r, q, G::ROWB)), f);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) ss += (f[i] - mean) * (f[i] - mean);
+            }
+            sStat[r] = make_float2(mean, rsqrtf(ss * (1.0f / C) + 1e-6f));
+        }
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t idesc = idesc_f16_f32(128, G::N1);
+            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sW1);
+            for (int b = 0; b < G::NB; ++b)
+                for (int k = 0; k < C / 16; ++k)
+                    mma_f16(tmem + b * G::N1, sdesc_kmajor_sw(a0 + b * 128 * G::ROWB + k * 32, G::ROWB),
+                            sdesc_kmajor(b0 + k * 256, 128, (C / 8) * 128), idesc, k > 0 ? 1u : 0u);
+            mma_commit(&bar_mma);
+        }
+        if (!wait_bar(&bar_mma, it & 1, p.err, 0x32)) s_fail = 1;
+        tc_fence_after();
+        // The halo tile is consumed: prefetch the next one.
+        if (tid == 0 && !s_fail && t + static_cast<int>(gridDim.x) < total) {
+            int ni, ny, nx;
+            decode(t + gridDim.x, ni, ny, nx);
+            mbar_arrive_expect_tx(&bar_x, G::P * G::ROWB);
+            tma_load_4d(sA, &mx, 0, nx - 1, ny - 1, ni, &bar_x);
+        }
+        // conv1 epilogue: u = rstd*(acc - mean*c1) + c2, zero outside the image.
+        for (int b = warp >> 2; b < G::NB; b += 2) {
+            const int r = b * 128 + (warp & 3) * 32 + lane;
+            const uint32_t lb = tmem + b * G::N1 + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+            const int yy = ty0 - 1 + r / G::WW;
+            const int xx = tx0 - 1 + r % G::WW;
+            const bool in_halo = r < G::P;
+            const bool inside = in_halo && yy >= 0 && yy < p.H && xx >= 0 && xx < p.W;
+            const float2 st = in_halo ? sStat[r] : make_float2(0.f, 0.f);
+#pragma unroll 1
+            for (int c0 = 0; c0 < G::N1; c0 += 16) {
+                float v[16];
+                tmem_ld16(lb + c0, v);
+                tmem_ld_wait();
+                if (!in_halo) continue;
+#pragma unroll
+                for (int g2 = 0; g2 < 2; ++g2) {
+                    float f[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int c = c0 + 8 * g2 + i;
+                        f[i] = inside ? st.y * (v[8 * g2 + i] - st.x * sC1[c]) + sC2[c] : 0.f;
+                    }
+                    *reinterpret_cast<uint4*>(sU + r * G::U_PITCH + (c0 + 8 * g2) * 2) = f_to_h8(f);
+                }
+            }
+        }
+        tc_fence_before();
+        if (tid == 0) bulk_wait_read0();  // the previous g tile has left sGo
+        __syncthreads();
+        // Depthwise 3x3 + bias + SimpleGate from shared memory. Thread = one
+        // gate half x 8 channels (taps in registers); the halves of a gate
+        // pair are adjacent lanes and meet through one shuffle.
+        const int c0 = cg * 8;
+        const int cin = half * D + c0;
+        for (int op = pl; op < G::TH * G::TW; op += G::LANES) {
+            const int py = op / G::TW, px = op % G::TW;
+            float2 acc[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = make_float2(dwb[2 * i], dwb[2 * i + 1]);
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(
+                        sU + ((py + ky) * G::WW + px + kx) * G::U_PITCH + cin * 2);
+                    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[i] = ffma2(unpack_half2(w4[i]), dww[ky * 3 + kx][i], acc[i]);
+                }
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                o[2 * i] = acc[i].x * __shfl_xor_sync(0xffffffffu, acc[i].x, 1);
+                o[2 * i + 1] = acc[i].y * __shfl_xor_sync(0xffffffffu, acc[i].y, 1);
+            }
+            if (half == 0) {
+                const uint4 ov = f_to_h8(o);
+                *reinterpret_cast<uint4*>(sGo + (op * D + c0) * 2) = ov;
+                if (ty0 + py < p.H && tx0 + px < p.W) {
+                    float q[8];
+                    h8_to_f(ov, q);  // pool the stored fp16 values
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) ps[i] += q[i];
+                }
+            }
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tma_store_4d(&mg, 0, tx0, ty0, img, sGo);
+            bulk_commit();
+        }
+        // Flush the pool partial when the next tile belongs to another image
+        // (or this is the CTA's last tile): fixed-order reduction.
+        const int tn = t + static_cast<int>(gridDim.x);
+        if (tn >= total || tn / per_img != img) {
+            if (half == 0) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) sRed[pl * D + c0 + i] = ps[i];
+            }
+            __syncthreads();
+            for (int c = tid; c < D; c += kAThreads) {
+                float sum = 0.f;
+                for (int l = 0; l < G::LANES; ++l) sum += sRed[l * D + c];
+                sPart[img * D + c] += sum;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+            __syncthreads();
+        }
+    }
+    if (tid == 0) bulk_wait0();
+    __syncthreads();
+    for (int i = tid; i < p.N * D; i += kAThreads) {
+        const int n = i / D, c = i - n * D;
+        p.partials[(static_cast<size_t>(n) * gridDim.x + blockIdx.x) * D + c] = sPart[i];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, G::TMEM_COLS);
+}
+
+// ============================== phase B =====================================
+
+template <int C, int D, int F>
+__global__ void __launch_bounds__(kBThreads, 1)
+    fused_b_kernel(const __grid_constant__ FusedBParams p, const __grid_constant__ CUtensorMap mg,
+                   const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mo) {
+    using G = GeoB<C, D, F>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sG = smem;                  // [128][D] swizzled (span 2D)
+    uint8_t* sX = sG + G::G_BYTES;       // [128][C] swizzled (span 2C)
+    uint8_t* sA2 = sX + G::X_BYTES;      // LN2(y)
+    uint8_t* sO = sA2 + G::X_BYTES;      // output staging
+    uint8_t* sA3 = sO + G::X_BYTES;      // gated FFN (span 2F)
+    uint8_t* sW3 = sA3 + G::A3_BYTES;
+    uint8_t* sW4 = sW3 + G::W3_BYTES;
+    uint8_t* sW5 = sW4 + G::W4_BYTES;
+    float* sB3 = reinterpret_cast<float*>(sW5 + G::W5_BYTES);
+    float* sBeta = sB3 + C;
+    float* sLw = sBeta + C;
+    float* sLb = sLw + C;
+    float* sB5 = sLb + C;
+    float* sGam = sB5 + C;
+    float* sB4 = sGam + C;      // [2F]
+    float* sS = sB4 + 2 * F;    // SCA scale [8][D]
+    __shared__ uint64_t bar_w, bar_ld, bar_mma;
+    __shared__ uint32_t tslot;
+    __shared__ int s_fail;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tiles = (p.M + 127) / 128;
+    const int nimg = (p.M + p.hw - 1) / p.hw;
+    for (int i = tid; i < C; i += kBThreads) {
+        sB3[i] = p.b3[i];
+        sBeta[i] = p.beta[i];
+        sLw[i] = p.ln_w[i];
+        sLb[i] = p.ln_b[i];
+        sB5[i] = p.b5[i];
+        sGam[i] = p.gamma[i];
+    }
+    for (int i = tid; i < 2 * F; i += kBThreads) sB4[i] = p.b4[i];
+    for (int i = tid; i < nimg * D; i += kBThreads) sS[i] = p.s[i];
+    if (warp == 0) {
+        tmem_alloc(&tslot, G::TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        mbar_init(&bar_w, 1);
+        mbar_init(&bar_ld, 1);
+        mbar_init(&bar_mma, 1);
+        s_fail = 0;
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar_w, G::W3_BYTES + G::W4_BYTES + G::W5_BYTES);
+        bulk_g2s(sW3, p.w3, G::W3_BYTES, &bar_w);
+        bulk_g2s(sW4, p.w4, G::W4_BYTES, &bar_w);
+        bulk_g2s(sW5, p.w5, G::W5_BYTES, &bar_w);
+        if (blockIdx.x < tiles) {
+            mbar_arrive_expect_tx(&bar_ld, G::G_BYTES + G::X_BYTES);
+            tma_load_2d(sG, &mg, 0, blockIdx.x * 128, &bar_ld);
+            tma_load_2d(sX, &mx, 0, blockIdx.x * 128, &bar_ld);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const bool ok = __syncthreads_and(wait_bar(&bar_w, 0, p.err, 0x40)) != 0;
+    uint32_t mma_phase = 0;
+    auto mma_wait = [&](uint32_t site) {
+        if (!wait_bar(&bar_mma, mma_phase & 1, p.err, site)) s_fail = 1;
+        ++mma_phase;
+        tc_fence_after();
+    };
+
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        const int m0 = t * 128;
+        const int row = m0 + tid;
+        const int img = row < p.M ? row / p.hw : 0;
+        if (!wait_bar(&bar_ld, it & 1, p.err, 0x41)) s_fail = 1;
+        __syncthreads();
+        if (s_fail) break;
+        // SCA: g *= s in place.
+        {
+            const float* sc = sS + img * D;
+#pragma unroll
+            for (int q = 0; q < D / 8; ++q) {
+                uint4* ptr = reinterpret_cast<uint4*>(sG + sw_offset(tid, q, 2 * D));
+                float f[8];
+                h8_to_f(*ptr, f);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) f[i] *= sc[8 * q + i];
+                *ptr = f_to_h8(f);
+            }
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {  // conv3: [128 x D] x [D -> C]
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(sG), b0 = smem_u32(sW3);
+            for (int k = 0; k < D / 16; ++k)
+                mma_f16(tmem, sdesc_kmajor_sw(a0 + k * 32, 2 * D), sdesc_kmajor(b0 + k * 256, 128, (D / 8) * 128),
+                        idesc_f16_f32(128, C), k > 0 ? 1u : 0u);
+            mma_commit(&bar_mma);
+        }
+        mma_wait(0x42);
+        // y = x + beta * (acc + b3), then LayerNorm2(y) -> A of conv4.
+        float y[C];
+#pragma unroll
+        for (int c0 = 0; c0 < C; c0 += 16) {
+            float v[16];
+            tmem_ld16(lane_base + c0, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int g2 = 0; g2 < 2; ++g2) {
+                float xv[8];
+                h8_to_f(*reinterpret_cast<const uint4*>(sX + sw_offset(tid, (c0 >> 3) + g2, 2 * C)), xv);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int c = c0 + 8 * g2 + i;
+                    // round to fp16 like the stored mid-block tensor of the reference
+                    y[c] = __half2float(__float2half(xv[i] + sBeta[c] * (v[8 * g2 + i] + sB3[c])));
+                }
+            }
+        }
+        {
+            float s = 0.f;
+#pragma unroll
+            for (int c = 0; c < C; ++c) s += y[c];
+            const float mean = s * (1.0f / C);
+            float ss = 0.f;
+#pragma unroll
+            for (int c = 0; c < C; ++c) ss += (y[c] - mean) * (y[c] - mean);
+            const float rstd = rsqrtf(ss * (1.0f / C) + 1e-6f);
+#pragma unroll
+            for (int q = 0; q < C / 8; ++q) {
+                float f[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) f[i] = (y[8 * q + i] - mean) * rstd * sLw[8 * q + i] + sLb[8 * q + i];
+                *reinterpret_cast<uint4*>(sA2 + sw_offset(tid, q, 2 * C)) = f_to_h8(f);
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            // g and x of this tile are consumed: prefetch the next tile.
+            if (t + static_cast<int>(gridDim.x) < tiles) {
+                const int nm = (t + gridDim.x) * 128;
+                mbar_arrive_expect_tx(&bar_ld, G::G_BYTES + G::X_BYTES);
+                tma_load_2d(sG, &mg, 0, nm, &bar_ld);
+                tma_load_2d(sX, &mx, 0, nm, &bar_ld);
+            }
+            tc_fence_after();  // conv4: [128 x C] x [C -> 2F]
+            const uint32_t a0 = smem_u32(sA2), b0 = smem_u32(sW4);
+            for (int k = 0; k < C / 16; ++k)
+                mma_f16(tmem + C, sdesc_kmajor_sw(a0 + k * 32, 2 * C), sdesc_kmajor(b0 + k * 256, 128, (C / 8) * 128),
+                        idesc_f16_f32(128, 2 * F), k > 0 ? 1u : 0u);
+            mma_commit(&bar_mma);
+        }
+        mma_wait(0x43);
+        // SimpleGate -> A of conv5.
+#pragma unroll 1
+        for (int c0 = 0; c0 < F; c0 += 16) {
+            float va[16], vb[16];
+            tmem_ld16(lane_base + C + c0, va);
+            tmem_ld16(lane_base + C + F + c0, vb);
+            tmem_ld_wait();
+#pragma unroll
+            for (int g2 = 0; g2 < 2; ++g2) {
+                float f[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int c = c0 + 8 * g2 + i;
+                    f[i] = (va[8 * g2 + i] + sB4[c]) * (vb[8 * g2 + i] + sB4[F + c]);
+                }
+                *reinterpret_cast<uint4*>(sA3 + sw_offset(tid, (c0 >> 3) + g2, 2 * F)) = f_to_h8(f);
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        if (tid == 0) bulk_wait_read0();  // the previous output tile has left sO
+        __syncthreads();
+        if (tid == 0) {  // conv5: [128 x F] x [F -> C]
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(sA3), b0 = smem_u32(sW5);
+            for (int k = 0; k < F / 16; ++k)
+                mma_f16(tmem, sdesc_kmajor_sw(a0 + k * 32, 2 * F), sdesc_kmajor(b0 + k * 256, 128, (F / 8) * 128),
+                        idesc_f16_f32(128, C), k > 0 ? 1u : 0u);
+            mma_commit(&bar_mma);
+        }
+        mma_wait(0x44);
+        // out = y + gamma * (acc + b5)
+#pragma unroll
+        for (int c0 = 0; c0 < C; c0 += 16) {
+            float v[16];
+            tmem_ld16(lane_base + c0, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int g2 = 0; g2 < 2; ++g2) {
+                float f[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int c = c0 + 8 * g2 + i;
+                    f[i] = y[c] + sGam[c] * (v[8 * g2 + i] + sB5[c]);
+                }
+                *reinterpret_cast<uint4*>(sO + sw_offset(tid, (c0 >> 3) + g2, 2 * C)) = f_to_h8(f);
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tma_store_2d(&mo, 0, m0, sO);
+            bulk_commit();
+        }
+    }
+    if (tid == 0) bulk_wait0();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, G::TMEM_COLS);
+}
+
+// ============================== host ========================================
+
+int encode(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+           const cuuint32_t* box, CUtensorMapSwizzle swz) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return dn_fail(DN_ERR_CUDA, "fused: cuTensorMapEncodeTiled unavailable");
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return dn_fail_str(DN_ERR_CUDA, "fused: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+    return DN_OK;
+}
+
+CUtensorMapSwizzle swz_for(int bytes) {
+    return bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int d = 0;
+        cudaGetDevice(&d);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int C, int D>
+int run_a(const FusedAParams& p, int grid, cudaStream_t s) {
+    using G = GeoA<C, D>;
+    auto kern = fused_a_kernel<C, D>;
+    static bool cfg = false;
+    if (!cfg) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "fused_a: smem attribute");
+        cfg = true;
+    }
+    CUtensorMap mx, mg;
+    const cuuint64_t dx[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(p.W), static_cast<cuuint64_t>(p.H),
+                              static_cast<cuuint64_t>(p.N)};
+    const cuuint64_t sx[3] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(p.W) * C * 2,
+                              static_cast<cuuint64_t>(p.H) * p.W * C * 2};
+    const cuuint32_t bx[4] = {static_cast<cuuint32_t>(C), G::WW, G::HH, 1};
+    int rc = encode(&mx, 4, p.x, dx, sx, bx, swz_for(2 * C));
+    if (rc != DN_OK) return rc;
+    const cuuint64_t dg[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(p.W), static_cast<cuuint64_t>(p.H),
+                              static_cast<cuuint64_t>(p.N)};
+    const cuuint64_t sg[3] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(p.W) * D * 2,
+                              static_cast<cuuint64_t>(p.H) * p.W * D * 2};
+    const cuuint32_t bg[4] = {static_cast<cuuint32_t>(D), G::TW, G::TH, 1};
+    rc = encode(&mg, 4, p.g, dg, sg, bg, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != DN_OK) return rc;
+    kern<<<grid, kAThreads, G::SMEM, s>>>(p, mx, mg);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "fused_a: launch");
+}
+
+template <int C, int D, int F>
+int run_b(const FusedBParams& p, cudaStream_t s) {
+    using G = GeoB<C, D, F>;
+    auto kern = fused_b_kernel<C, D, F>;
+    static bool cfg = false;
+    if (!cfg) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "fused_b: smem attribute");
+        cfg = true;
+    }
+    CUtensorMap mg, mx, mo;
+    const cuuint32_t bD[2] = {static_cast<cuuint32_t>(D), 128};
+    const cuuint32_t bC[2] = {static_cast<cuuint32_t>(C), 128};
+    const cuuint64_t dG[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(p.M)};
+    const cuuint64_t dC[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(p.M)};
+    const cuuint64_t sG[1] = {static_cast<cuuint64_t>(D) * 2};
+    const cuuint64_t sC[1] = {static_cast<cuuint64_t>(C) * 2};
+    int rc = encode(&mg, 2, p.g, dG, sG, bD, swz_for(2 * D));
+    if (rc == DN_OK) rc = encode(&mx, 2, p.x, dC, sC, bC, swz_for(2 * C));
+    if (rc == DN_OK) rc = encode(&mo, 2, p.out, dC, sC, bC, swz_for(2 * C));
+    if (rc != DN_OK) return rc;
+    const int tiles = (p.M + 127) / 128;
+    const int per_sm = std::max(1, std::min(512 / G::TMEM_COLS, (227 * 1024) / (G::SMEM + 2048)));
+    const int grid = std::min(tiles, sm_count() * per_sm);
+    kern<<<grid, kBThreads, G::SMEM, s>>>(p, mg, mx, mo);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "fused_b: launch");
+}
+
+}  // namespace
+
+bool fused_supported(int C, int D, int F) {
+    return (C == 16 && D == 16 && (F == 16 || F == 32)) || (C == 32 && D == 32 && (F == 32 || F == 64)) ||
+           (C == 64 && D == 64 && F == 64);
+}
+
+int fused_a_grid(int C, int D, int N, int H, int W) {
+    auto geo = [&](int TH, int TW, int smem, int cols) {
+        const int tiles = N * ((H + TH - 1) / TH) * ((W + TW - 1) / TW);
+        const int per_sm = std::max(1, std::min(512 / cols, (227 * 1024) / (smem + 2048)));
+        return std::max(1, std::min(tiles, sm_count() * per_sm));
+    };
+    if (C == 16) return geo(GeoA<16, 16>::TH, GeoA<16, 16>::TW, GeoA<16, 16>::SMEM, GeoA<16, 16>::TMEM_COLS);
+    if (C == 32) return geo(GeoA<32, 32>::TH, GeoA<32, 32>::TW, GeoA<32, 32>::SMEM, GeoA<32, 32>::TMEM_COLS);
+    return geo(GeoA<64, 64>::TH, GeoA<64, 64>::TW, GeoA<64, 64>::SMEM, GeoA<64, 64>::TMEM_COLS);
+}
+
+int launch_fused_a(const FusedAParams& p, int C, int D, int grid, cudaStream_t s) {
+    if (p.N > 8) return dn_fail(DN_ERR_UNSUPPORTED, "fused_a: batch > 8");
+    if (C == 16 && D == 16) return run_a<16, 16>(p, grid, s);
+    if (C == 32 && D == 32) return run_a<32, 32>(p, grid, s);
+    if (C == 64 && D == 64) return run_a<64, 64>(p, grid, s);
+    return dn_fail(DN_ERR_UNSUPPORTED, "fused_a: channel configuration");
+}
+
+int launch_fused_b(const FusedBParams& p, int C, int D, int F, cudaStream_t s) {
+    if ((p.M + p.hw - 1) / p.hw > 8) return dn_fail(DN_ERR_UNSUPPORTED, "fused_b: batch > 8");
+    if (C == 16 && D == 16 && F == 16) return run_b<16, 16, 16>(p, s);
+    if (C == 16 && D == 16 && F == 32) return run_b<16, 16, 32>(p, s);
+    if (C == 32 && D == 32 && F == 32) return run_b<32, 32, 32>(p, s);
+    if (C == 32 && D == 32 && F == 64) return run_b<32, 32, 64>(p, s);
+    if (C == 64 && D == 64 && F == 64) return run_b<64, 64, 64>(p, s);
+    return dn_fail(DN_ERR_UNSUPPORTED, "fused_b: channel configuration");
+}
+
+}  // namespace dnb

@@ -45,6 +45,9 @@
 #include "status.h"
 
 namespace dnb {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
 namespace {
 
 constexpr int kRows = 128;
@@ -58,50 +61,6 @@ struct GemmMaps {
     CUtensorMap out;  // epilogue store (box EB x 128, swizzled)
     CUtensorMap res;  // residual load (same geometry as out)
 };
-
-__device__ __forceinline__ void h8_to_f(const uint4& v, float (&f)[8]) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 t = unpack_half2(w[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
-    }
-}
-
-__device__ __forceinline__ uint4 f_to_h8(const float (&f)[8]) {
-    uint4 v;
-    v.x = pack_half2(f[0], f[1]);
-    v.y = pack_half2(f[2], f[3]);
-    v.z = pack_half2(f[4], f[5]);
-    v.w = pack_half2(f[6], f[7]);
-    return v;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int c1, const void* src) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(c0), "r"(c1), "r"(smem_u32(src))
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() {
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 // Named barrier of the four epilogue warps.
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -588,18 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Host side
 // ---------------------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    });
-    return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 // 2-D map over a [rows][cols] fp16 matrix with row stride `ld` elements and a
 // box of `box_cols` columns x 128 rows.
@@ -705,6 +653,19 @@ int launch_nt(const GemmParams& p, int nt, cudaStream_t s) {
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
 
 int launch_gemm(const GemmParams& p, int pro, int epi, int amode, int nt, cudaStream_t s) {
     if (p.KC != 16 && p.KC != 32 && p.KC != 64) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: KC must be 16/32/64");

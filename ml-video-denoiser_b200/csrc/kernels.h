@@ -81,6 +81,8 @@ struct DwParams {
 };
 
 int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s);
+// SCA alone from existing partials [N][nb][D] (used after the fused phase A).
+int launch_sca(const DwParams& p, int nb, cudaStream_t s);
 int dw_blocks_per_img(int H, int W, int D);
 
 // ---------------------------------------------------------------------------

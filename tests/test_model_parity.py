@@ -18,29 +18,31 @@ SPATIAL = ["spatial_w16l4_64x64", "spatial_w16l4_37x53", "spatial_w32dw1_48x40",
 LEGACY = ["temporal_legacy_w8l2_t3_warp", "temporal_legacy_w8l2_t5"]
 
 
-def run_engine(pkg, path, x):
+def run_engine(pkg, path, x, fused=True):
     m = pkg.Model(path)
+    m.set_fused(fused)
     xt = torch.from_numpy(x).half().cuda()
     y = m(xt)
     m.sync()
     return y.float().cpu().numpy(), m
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "perconv"])
 @pytest.mark.parametrize("name", SPATIAL + LEGACY)
-def test_engine_matches_reference_golden(pkg, tmp_path, name):
+def test_engine_matches_reference_golden(pkg, tmp_path, name, fused):
     g = load_golden(name)
     path, _ = golden_model_dir(pkg, tmp_path, g["meta"])
-    y, _ = run_engine(pkg, path, g["x"])
+    y, _ = run_engine(pkg, path, g["x"], fused)
     err, psnr = compare(y, g["expected"])
     assert err <= MAX_ABS and psnr >= MIN_PSNR, (name, err, psnr)
 
 
-def _oracle_case(pkg, tmp_path, cfg, seed, x):
+def _oracle_case(pkg, tmp_path, cfg, seed, x, fused=True):
     synth = synth_mod(pkg)
     path, params = synth.make_model_dir(str(tmp_path), cfg, seed)
     torch.set_num_threads(min(16, os.cpu_count() or 1))
     ref = O.nafnet_forward(O.as_torch(params), torch.from_numpy(x)).numpy()
-    y, m = run_engine(pkg, path, x)
+    y, m = run_engine(pkg, path, x, fused)
     return compare(y, ref), m
 
 
@@ -52,12 +54,13 @@ def test_tiny_w16_256(pkg, tmp_path):
     assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
 
 
-def test_w32_batch2_ragged(pkg, tmp_path):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "perconv"])
+def test_w32_batch2_ragged(pkg, tmp_path, fused):
     """NAFNet-w32 architecture, batch 2, size not divisible by 16 (reflect pad + crop)."""
     synth = synth_mod(pkg)
     x = np.concatenate([synth.w32_frame(100, 150, seed=5), synth.w32_frame(100, 150, seed=6)])
     x = x.astype(np.float16).astype(np.float32)
-    (err, psnr), _ = _oracle_case(pkg, tmp_path, synth.CONFIG_W32, 1, x)
+    (err, psnr), _ = _oracle_case(pkg, tmp_path, synth.CONFIG_W32, 1, x, fused)
     assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
 
 
