@@ -1,0 +1,202 @@
+// Depthwise 3x3 + bias + SimpleGate + pool partials for the deep levels,
+// one CTA per (TH x TW output tile, 32-channel slice, image):
+//   * two TMA loads bring the (TH+2) x (TW+2) halo of both gate halves of the
+//     slice (u channels [c, c+32) and [D+c, D+c+32)) into shared memory,
+//     zero-filled outside the image (the conv's zero padding);
+//   * a thread owns one gate half x 8 channels (taps in registers) at one
+//     column and produces two vertically adjacent outputs from a 4-row
+//     sliding window; the halves of a gate pair are adjacent lanes;
+//   * the gated tile leaves by one TMA store; the tile's per-channel sums
+//     (of the stored fp16 values) go to partials[img][tile][channel].
+// Each input element crosses the memory system once (plus the 1-pixel halo),
+// instead of once per tap.
+//
+// Replaces the reference's grouped cudnnConvolutionForward (conv2) +
+// simple_gate_kernel + global_avg_pool_kernel passes (src/models/nafnet.cu
+// :162-172, src/kernels/nafnet_kernels.cu:94-126) at the deep levels.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <string>
+
+#include "kernels.h"
+#include "sm100.cuh"
+#include "status.h"
+
+namespace dnb {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+namespace {
+
+constexpr int kCS = 32;            // gated channels per CTA
+constexpr int kTH = 8, kTW = 32;   // output tile
+constexpr int kHH = kTH + 2, kWW = kTW + 2;
+constexpr int kP = kHH * kWW;      // halo pixels
+constexpr int kRowB = kCS * 2;     // 64 bytes per halo pixel and half
+constexpr int kBufB = ((kP * kRowB + 127) / 128) * 128;
+constexpr int kOutB = kTH * kTW * kCS * 2;
+constexpr int kSmem = 128 + 2 * kBufB + kOutB + kTW * kCS * 4;
+constexpr int kThreads = 256;
+
+// Lane layout inside a warp (32 lanes = 4 columns): bits 0-1 channel group,
+// bit 2 column low bit, bit 3 gate half, bit 4 column high bit. Eight
+// consecutive lanes then read 128 contiguous bytes of one half (no bank
+// conflicts) and the two halves of a gate pair are lanes l and l^8.
+__global__ void __launch_bounds__(kThreads, 2)
+    dw_tile_kernel(const __grid_constant__ DwParams p, const __grid_constant__ CUtensorMap mu,
+                   const __grid_constant__ CUtensorMap mg) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
+    uint8_t* sHalf0 = smem;
+    uint8_t* sHalf1 = smem + kBufB;
+    uint8_t* sOut = smem + 2 * kBufB;                              // [TH*TW][CS] fp16
+    float* sRed = reinterpret_cast<float*>(sOut + kOutB);          // [TW columns][CS]
+    __shared__ uint64_t bar;
+
+    const int tid = threadIdx.x;
+    const int tiles_x = (p.W + kTW - 1) / kTW;
+    const int tile = blockIdx.x;
+    const int ty0 = (tile / tiles_x) * kTH, tx0 = (tile % tiles_x) * kTW;
+    const int img = blockIdx.z;
+    const int D = p.D;
+    const int cs0 = blockIdx.y * kCS;
+
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar, 2 * kP * kRowB);
+        tma_load_4d(sHalf0, &mu, cs0, tx0 - 1, ty0 - 1, img, &bar);
+        tma_load_4d(sHalf1, &mu, D + cs0, tx0 - 1, ty0 - 1, img, &bar);
+    }
+    const int lane = tid & 31;
+    const int cg = lane & 3;
+    const int half = (lane >> 3) & 1;
+    const int px = (tid >> 5) * 4 + ((lane >> 4) << 1) + ((lane >> 2) & 1);  // 0..31
+    const int cin = half * D + cs0 + cg * 8;
+    float2 w[9][4];
+    float2 bias[4];
+#pragma unroll
+    for (int t = 0; t < 9; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            w[t][i] = make_float2(p.w[t * 2 * D + cin + 2 * i], p.w[t * 2 * D + cin + 2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) bias[i] = make_float2(p.b[cin + 2 * i], p.b[cin + 2 * i + 1]);
+    const bool ok = mbar_wait(&bar, 0);
+    if (!__syncthreads_and(ok)) {
+        if (tid == 0) report_error(p.err, 0x50, kErrMbarTimeout);
+        return;
+    }
+
+    const uint8_t* src = (half ? sHalf1 : sHalf0) + cg * 16;
+    const bool col_in = tx0 + px < p.W;
+    float ps[4] = {0, 0, 0, 0};
+#pragma unroll 1
+    for (int py = 0; py < kTH; py += 2) {
+        float2 a0[4], a1[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a0[i] = a1[i] = bias[i];
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx) {
+                const uint4 v = *reinterpret_cast<const uint4*>(src + ((py + rr) * kWW + px + kx) * kRowB);
+                const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 u = unpack_half2(q[i]);
+                    if (rr <= 2) a0[i] = ffma2(u, w[rr * 3 + kx][i], a0[i]);
+                    if (rr >= 1) a1[i] = ffma2(u, w[(rr - 1) * 3 + kx][i], a1[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int r2 = 0; r2 < 2; ++r2) {
+            // this lane keeps channels [4*half, 4*half+4) of its group
+            float o[4];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float2 lo = r2 ? a1[j] : a0[j];
+                const float2 hi = r2 ? a1[2 + j] : a0[2 + j];
+                const float2 mine = half ? hi : lo;
+                const float2 give = half ? lo : hi;
+                const float px_ = __shfl_xor_sync(0xffffffffu, give.x, 8);
+                const float py_ = __shfl_xor_sync(0xffffffffu, give.y, 8);
+                o[2 * j] = mine.x * px_;
+                o[2 * j + 1] = mine.y * py_;
+            }
+            const int oy = py + r2;
+            const uint32_t h01 = pack_half2(o[0], o[1]), h23 = pack_half2(o[2], o[3]);
+            *reinterpret_cast<uint2*>(sOut + ((oy * kTW + px) * kCS + cg * 8 + half * 4) * 2) = make_uint2(h01, h23);
+            if (col_in && ty0 + oy < p.H) {
+                const float2 f01 = unpack_half2(h01), f23 = unpack_half2(h23);
+                ps[0] += f01.x;
+                ps[1] += f01.y;
+                ps[2] += f23.x;
+                ps[3] += f23.y;
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sRed[px * kCS + cg * 8 + half * 4 + i] = ps[i];
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        tma_store_4d(&mg, cs0, tx0, ty0, img, sOut);
+        bulk_commit();
+    }
+    if (tid < kCS) {
+        float sum = 0.f;
+        for (int c = 0; c < kTW; ++c) sum += sRed[c * kCS + tid];
+        p.partials[(static_cast<size_t>(img) * gridDim.x + tile) * D + cs0 + tid] = sum;
+    }
+    if (tid == 0) bulk_wait0();
+}
+
+int encode4(CUtensorMap* m, const void* base, int C, int W, int H, int N, int box_c, int box_w, int box_h) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return dn_fail(DN_ERR_CUDA, "dw_tile: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                                static_cast<cuuint64_t>(N)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(W) * C * 2,
+                                   static_cast<cuuint64_t>(H) * W * C * 2};
+    const cuuint32_t box[4] = {static_cast<cuuint32_t>(box_c), static_cast<cuuint32_t>(box_w),
+                               static_cast<cuuint32_t>(box_h), 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return dn_fail_str(DN_ERR_CUDA, "dw_tile: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+    return DN_OK;
+}
+
+}  // namespace
+
+bool dw_tile_supported(int D) { return D % kCS == 0; }
+
+int dw_tile_blocks_per_img(int H, int W) { return ((H + kTH - 1) / kTH) * ((W + kTW - 1) / kTW); }
+
+int launch_dw_tile(const DwParams& p, cudaStream_t s) {
+    if (!dw_tile_supported(p.D)) return dn_fail(DN_ERR_UNSUPPORTED, "dw_tile: channels must be a multiple of 32");
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(dw_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: smem attribute");
+        configured = true;
+    }
+    CUtensorMap mu, mg;
+    int rc = encode4(&mu, p.u, 2 * p.D, p.W, p.H, p.N, kCS, kWW, kHH);
+    if (rc == DN_OK) rc = encode4(&mg, p.g, p.D, p.W, p.H, p.N, kCS, kTW, kTH);
+    if (rc != DN_OK) return rc;
+    const int tiles = dw_tile_blocks_per_img(p.H, p.W);
+    dw_tile_kernel<<<dim3(tiles, p.D / kCS, p.N), kThreads, kSmem, s>>>(p, mu, mg);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: launch");
+    return launch_sca(p, tiles, s);
+}
+
+}  // namespace dnb

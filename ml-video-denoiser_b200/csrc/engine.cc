@@ -409,6 +409,7 @@ void Engine::plan(const Shape& s) {
             t = std::max(t, nimg * hw * b.ffn);
             dmax = std::max(dmax, static_cast<size_t>(b.dw));
             dw_blocks_max_ = std::max(dw_blocks_max_, dw_blocks_per_img(h, w, b.dw));
+            dw_blocks_max_ = std::max(dw_blocks_max_, dw_tile_blocks_per_img(h, w));
             if (b.fused) dw_blocks_max_ = std::max(dw_blocks_max_, fused_a_grid(b.C, b.dw, static_cast<int>(nimg), h, w));
         }
     };
@@ -642,10 +643,17 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
     d.sca_w = wptr<float>(b.sca_w);
     d.sca_b = wptr<float>(b.sca_b);
     d.s_out = sca_s_;
+    d.err = err_;
     launches_ += 2;  // depthwise + SCA
-    prof_begin("dw_gate_sca", static_cast<double>(nimg) * hw * 3 * b.dw * 2,
-               static_cast<double>(nimg) * hw * 2 * b.dw * 9 * 2 + 2.0 * b.dw * b.dw, s);
-    DN_TRY(launch_dw_gate_sca(d, dw_blocks_per_img(h, w, b.dw), s));
+    if (fused_enabled_ && dw_tile_supported(b.dw)) {
+        prof_begin("dw_tile_sca", static_cast<double>(nimg) * hw * 3 * b.dw * 2,
+                   static_cast<double>(nimg) * hw * 2 * b.dw * 9 * 2 + 2.0 * b.dw * b.dw, s);
+        DN_TRY(launch_dw_tile(d, s));
+    } else {
+        prof_begin("dw_gate_sca", static_cast<double>(nimg) * hw * 3 * b.dw * 2,
+                   static_cast<double>(nimg) * hw * 2 * b.dw * 9 * 2 + 2.0 * b.dw * b.dw, s);
+        DN_TRY(launch_dw_gate_sca(d, dw_blocks_per_img(h, w, b.dw), s));
+    }
     prof_end(s);
     // y = x + beta * (conv3(g * s) + b3)
     p = rows_params(nimg, h, w);

@@ -19,7 +19,7 @@
 //   through TMEM.
 //
 // Per pixel this moves x (plus halo) in, g out, g and x in, x' out: the
-// two-pass minimum of 5C*2 bytes (SURVEY 8(d)), against the ~14 passes of
+// two-pass minimum of 5C*2 bytes, against the ~14 passes of
 // the reference block (src/models/nafnet.cu:146-215: LN, conv1, bias, conv2,
 // bias, gate, pool, sca conv, scale, conv3, bias, scaled add, LN, conv4,
 // bias, gate, conv5, bias, scaled add).
@@ -240,22 +240,28 @@ __global__ void __launch_bounds__(kAThreads, 2)
             const bool in_halo = r < G::P;
             const bool inside = in_halo && yy >= 0 && yy < p.H && xx >= 0 && xx < p.W;
             const float2 st = in_halo ? sStat[r] : make_float2(0.f, 0.f);
+            // u = rstd * acc + (c2 - rstd * mean * c1), zero outside the image.
+            const float2 rs2 = inside ? make_float2(st.y, st.y) : make_float2(0.f, 0.f);
+            const float2 nm2 = inside ? make_float2(-st.x * st.y, -st.x * st.y) : make_float2(0.f, 0.f);
+            const float2 on2 = inside ? make_float2(1.f, 1.f) : make_float2(0.f, 0.f);
 #pragma unroll 1
             for (int c0 = 0; c0 < G::N1; c0 += 16) {
                 float v[16];
                 tmem_ld16(lb + c0, v);
                 tmem_ld_wait();
                 if (!in_halo) continue;
+                uint32_t pk[8];
 #pragma unroll
-                for (int g2 = 0; g2 < 2; ++g2) {
-                    float f[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int c = c0 + 8 * g2 + i;
-                        f[i] = inside ? st.y * (v[8 * g2 + i] - st.x * sC1[c]) + sC2[c] : 0.f;
-                    }
-                    *reinterpret_cast<uint4*>(sU + r * G::U_PITCH + (c0 + 8 * g2) * 2) = f_to_h8(f);
+                for (int i = 0; i < 8; ++i) {
+                    const float2 c1 = *reinterpret_cast<const float2*>(sC1 + c0 + 2 * i);
+                    const float2 c2 = *reinterpret_cast<const float2*>(sC2 + c0 + 2 * i);
+                    const float2 k = ffma2(nm2, c1, make_float2(c2.x * on2.x, c2.y * on2.y));
+                    const float2 u = ffma2(rs2, make_float2(v[2 * i], v[2 * i + 1]), k);
+                    pk[i] = pack_half2(u.x, u.y);
                 }
+                uint4* dst = reinterpret_cast<uint4*>(sU + r * G::U_PITCH + c0 * 2);
+                dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
             }
         }
         tc_fence_before();
@@ -266,35 +272,47 @@ __global__ void __launch_bounds__(kAThreads, 2)
         // pair are adjacent lanes and meet through one shuffle.
         const int c0 = cg * 8;
         const int cin = half * D + c0;
-        for (int op = pl; op < G::TH * G::TW; op += G::LANES) {
-            const int py = op / G::TW, px = op % G::TW;
-            float2 acc[4];
+        // Work item = (column px, row pair py, py+1): input rows py-1 .. py+2
+        // stream through once, each feeding the outputs it touches.
+        for (int op = pl; op < G::TH / 2 * G::TW; op += G::LANES) {
+            const int py = (op / G::TW) * 2, px = op % G::TW;
+            float2 a0[4], a1[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = make_float2(dwb[2 * i], dwb[2 * i + 1]);
+            for (int i = 0; i < 4; ++i) a0[i] = a1[i] = make_float2(dwb[2 * i], dwb[2 * i + 1]);
 #pragma unroll
-            for (int ky = 0; ky < 3; ++ky)
+            for (int rr = 0; rr < 4; ++rr) {
 #pragma unroll
                 for (int kx = 0; kx < 3; ++kx) {
                     const uint4 v = *reinterpret_cast<const uint4*>(
-                        sU + ((py + ky) * G::WW + px + kx) * G::U_PITCH + cin * 2);
+                        sU + ((py + rr) * G::WW + px + kx) * G::U_PITCH + cin * 2);
                     const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) acc[i] = ffma2(unpack_half2(w4[i]), dww[ky * 3 + kx][i], acc[i]);
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 u = unpack_half2(w4[i]);
+                        if (rr <= 2) a0[i] = ffma2(u, dww[rr * 3 + kx][i], a0[i]);
+                        if (rr >= 1) a1[i] = ffma2(u, dww[(rr - 1) * 3 + kx][i], a1[i]);
+                    }
                 }
-            float o[8];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                o[2 * i] = acc[i].x * __shfl_xor_sync(0xffffffffu, acc[i].x, 1);
-                o[2 * i + 1] = acc[i].y * __shfl_xor_sync(0xffffffffu, acc[i].y, 1);
             }
-            if (half == 0) {
-                const uint4 ov = f_to_h8(o);
-                *reinterpret_cast<uint4*>(sGo + (op * D + c0) * 2) = ov;
-                if (ty0 + py < p.H && tx0 + px < p.W) {
-                    float q[8];
-                    h8_to_f(ov, q);  // pool the stored fp16 values
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) ps[i] += q[i];
+            for (int rowi = 0; rowi < 2; ++rowi) {
+                float o[8];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 a = rowi ? a1[i] : a0[i];
+                    o[2 * i] = a.x * __shfl_xor_sync(0xffffffffu, a.x, 1);
+                    o[2 * i + 1] = a.y * __shfl_xor_sync(0xffffffffu, a.y, 1);
+                }
+                if (half == 0) {
+                    const int oy = py + rowi;
+                    const uint4 ov = f_to_h8(o);
+                    *reinterpret_cast<uint4*>(sGo + ((oy * G::TW + px) * D + c0) * 2) = ov;
+                    if (ty0 + oy < p.H && tx0 + px < p.W) {
+                        float q[8];
+                        h8_to_f(ov, q);  // pool the stored fp16 values
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ps[i] += q[i];
+                    }
                 }
             }
         }

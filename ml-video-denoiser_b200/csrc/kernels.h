@@ -78,12 +78,17 @@ struct DwParams {
     const float* sca_w;    // [D][D] (out, in)
     const float* sca_b;    // [D]
     float* s_out;          // [N][D] channel attention scale
+    uint32_t* err;         // device error word (bounded-wait timeouts)
 };
 
 int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s);
 // SCA alone from existing partials [N][nb][D] (used after the fused phase A).
 int launch_sca(const DwParams& p, int nb, cudaStream_t s);
 int dw_blocks_per_img(int H, int W, int D);
+// TMA-tiled variant (8x32 output tiles x 32-channel slices), then SCA.
+bool dw_tile_supported(int D);
+int dw_tile_blocks_per_img(int H, int W);
+int launch_dw_tile(const DwParams& p, cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // Dense 3x3 convs at the network boundary (CUDA cores)
