@@ -64,7 +64,7 @@ _IP = _c.POINTER(_c.c_int)
 _SZP = _c.POINTER(_c.c_size_t)
 _CPP = _c.POINTER(_c.c_char_p)
 
-# name -> (restype, argtypes); every symbol of include/denoiser_b200.h.
+# name -> (restype, argtypes); every symbol of the headers in include/.
 SIGNATURES = {
     "dn_last_error": (_c.c_char_p, []),
     "dn_abi_version": (_I, []),
@@ -86,6 +86,22 @@ SIGNATURES = {
     "dn_model_set_fused": (_I, [_P, _I]),
     "dn_model_profile": (_I, [_P, _I]),
     "dn_model_profile_report": (_I, [_P, _c.c_char_p, _c.c_size_t]),
+    # include/denoiser_b200_ops.h
+    "dn_launch_reflect_pad": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "dn_launch_crop": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "dn_launch_subtract_clamp": (_I, [_P, _P, _P, _I64, _P]),
+    "dn_launch_concat_channels": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "dn_launch_extract_frame": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "dn_launch_select_prefix_channels": (_I, [_P, _P, _I, _I, _I, _I, _I, _P]),
+    "dn_launch_layer_norm_affine": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
+    "dn_launch_simple_gate": (_I, [_P, _P, _I, _I, _I, _I, _P]),
+    "dn_launch_global_avg_pool": (_I, [_P, _P, _I, _I, _I, _I, _P]),
+    "dn_launch_mul_channelwise": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "dn_launch_add": (_I, [_P, _P, _P, _I64, _P]),
+    "dn_launch_mul_scalar": (_I, [_P, _F, _P, _I64, _P]),
+    "dn_launch_scaled_add": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
+    "dn_launch_pixel_shuffle2x": (_I, [_P, _P, _I, _I, _I, _I, _P]),
+    "dn_launch_warp_bilinear": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
 }
 
 

@@ -553,12 +553,6 @@ static GemmParams rows_params(int nimg, int h, int w) {
     return p;
 }
 
-#define DN_TRY(x)                 \
-    do {                          \
-        const int _rc = (x);      \
-        if (_rc != DN_OK) return _rc; \
-    } while (0)
-
 // NAFBlock (training/models.py:166-185, src/models/nafnet.cu:146-215), in place on x.
 int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaStream_t s) {
     const long long hw = static_cast<long long>(h) * w;

@@ -17,4 +17,11 @@ int dn_fail_str(int code, const std::string& msg);
 // Records a CUDA error with context and returns DN_ERR_CUDA.
 int dn_cuda_fail(cudaError_t e, const char* where);
 
+// Returns the status of `x` from the enclosing function unless it is DN_OK.
+#define DN_TRY(x)                     \
+    do {                              \
+        const int _rc = (x);          \
+        if (_rc != DN_OK) return _rc; \
+    } while (0)
+
 }  // namespace dnb

@@ -1,13 +1,14 @@
-"""The C-ABI library loads and exports every symbol include/denoiser_b200.h declares."""
+"""The C-ABI library loads and exports every symbol the headers in include/ declare."""
 import os
 import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-HEADER = os.path.join(os.path.dirname(HERE), "include", "denoiser_b200.h")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+HEADERS = sorted(os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE) if f.endswith(".h"))
 
 
 def declared_symbols():
-    text = open(HEADER).read()
+    text = "\n".join(open(h).read() for h in HEADERS)
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(dn_[a-z0-9_]+)\s*\(", text)))
 
