@@ -79,6 +79,24 @@ int dn_launch_simple_gate(const void* input, void* output, int N, int C, int H, 
  * `stream` (cudaMallocAsync / cudaFreeAsync). */
 int dn_launch_global_avg_pool(const void* input, void* output, int N, int C, int H, int W, void* stream);
 
+/* dn_launch_global_avg_pool without any device allocation (no counterpart in
+ * the reference). For callers that must not allocate device memory: host
+ * applications that have reserved the GPU's memory for their own pool, where
+ * an allocation fails or evicts their cache, and per-frame real-time loops,
+ * where cudaMalloc/cudaFree stall the device mid-frame. The split sums go to
+ * a fixed 1 MiB array in this library's device code instead:
+ *   - limit: N*C*splits <= 262144, splits = min(128, ceil(H*W / 16384)), so
+ *     any N*C <= 2048 fits; larger sizes return DN_ERR_UNSUPPORTED;
+ *   - the first call on each device (with that device current) looks up the
+ *     array's device address once; make that first call before any stream
+ *     capture begins;
+ *   - the array is shared by every call on the device: calls whose work may
+ *     overlap on the GPU (different streams without an event between them,
+ *     or concurrent host threads) race on it and give wrong means. Order
+ *     them on one stream.
+ * Results equal dn_launch_global_avg_pool's (same plan and kernels). */
+int dn_launch_global_avg_pool_noalloc(const void* input, void* output, int N, int C, int H, int W, void* stream);
+
 /* launch_mul_channelwise (nafnet_kernels.h:47): output = input * scale[n*C + c],
  * scale (N,C) FP16. */
 int dn_launch_mul_channelwise(const void* input, const void* scale, void* output, int N, int C, int H, int W,

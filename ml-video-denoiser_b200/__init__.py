@@ -96,6 +96,7 @@ SIGNATURES = {
     "dn_launch_layer_norm_affine": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
     "dn_launch_simple_gate": (_I, [_P, _P, _I, _I, _I, _I, _P]),
     "dn_launch_global_avg_pool": (_I, [_P, _P, _I, _I, _I, _I, _P]),
+    "dn_launch_global_avg_pool_noalloc": (_I, [_P, _P, _I, _I, _I, _I, _P]),
     "dn_launch_mul_channelwise": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "dn_launch_add": (_I, [_P, _P, _P, _I64, _P]),
     "dn_launch_mul_scalar": (_I, [_P, _F, _P, _I64, _P]),

@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <mutex>
 #include <string>
 
 #include "denoiser_b200.h"
@@ -523,6 +524,36 @@ int run_rows(const RowMap& m, void* out, bool vec_ok, void* stream, const char* 
     return launched(name);
 }
 
+// ---------------------------------------------------------------------------
+// Average pool on a static scratch (dn_launch_global_avg_pool_noalloc)
+// ---------------------------------------------------------------------------
+
+// Split sums of the no-alloc pool: one array per device, part of this
+// library's device code, so it exists once the code is loaded on a device.
+constexpr int64_t kNoAllocPoolFloats = 262144;  // 1 MiB
+static __device__ __align__(256) float g_pool_scratch[kNoAllocPoolFloats];
+
+std::mutex g_pool_scratch_mu;
+float* g_pool_scratch_ptr[64];  // device address of g_pool_scratch, per device ordinal
+
+// Device address of g_pool_scratch on the calling thread's current device,
+// looked up (cudaGetSymbolAddress) by the first call on that device.
+int pool_scratch(float** out, const char* name) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return dn_cuda_fail(e, name);
+    if (dev < 0 || dev >= 64) return dn_fail_str(DN_ERR_UNSUPPORTED, std::string(name) + ": device ordinal >= 64");
+    std::lock_guard<std::mutex> lock(g_pool_scratch_mu);
+    if (!g_pool_scratch_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_pool_scratch);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "dn_launch_global_avg_pool_noalloc: cudaGetSymbolAddress");
+        g_pool_scratch_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_pool_scratch_ptr[dev];
+    return DN_OK;
+}
+
 bool any_negative(std::initializer_list<int> v) {
     for (int x : v)
         if (x < 0) return true;
@@ -714,6 +745,25 @@ int dn_launch_global_avg_pool(const void* input, void* output, int N, int C, int
     if (rc != DN_OK) return rc;
     if (e != cudaSuccess) return dn_cuda_fail(e, "dn_launch_global_avg_pool: scratch release");
     return DN_OK;
+}
+
+// Same plan and kernels as dn_launch_global_avg_pool; only the scratch
+// differs. Nothing in it needs to start at zero: the split kernel writes
+// every slot the final kernel reads, in the same call.
+int dn_launch_global_avg_pool_noalloc(const void* input, void* output, int N, int C, int H, int W, void* stream) {
+    const char* name = "dn_launch_global_avg_pool_noalloc";
+    DN_TRY(pool_check(input, output, N, C, H, W, name));
+    const PoolPlan pp = pool_plan(input, N, C, H, W);
+    if (pp.planes == 0) return DN_OK;
+    float* scratch = nullptr;
+    DN_TRY(pool_scratch(&scratch, name));
+    const int64_t need = pp.planes * pp.splits;
+    if (need > kNoAllocPoolFloats)
+        return dn_fail_str(DN_ERR_UNSUPPORTED,
+                           std::string(name) + ": N*C*splits = " + std::to_string(need) +
+                               " split sums exceed the static scratch of " + std::to_string(kNoAllocPoolFloats) +
+                               " floats (splits = min(128, ceil(H*W / 16384)))");
+    return pool_launch(pp, input, output, scratch, to_stream(stream), name);
 }
 
 int dn_launch_mul_channelwise(const void* input, const void* scale, void* output, int N, int C, int H, int W,
