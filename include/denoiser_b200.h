@@ -133,7 +133,9 @@ int dn_model_set_fused(dn_model* model, int enable);
 
 /* Per-launch CUDA-event timing of the engine's kernels (no reference
  * counterpart; the reference engine has no timers). While enabled, every
- * kernel the model launches is bracketed by events on its stream. */
+ * kernel the model launches is bracketed by events on its stream.
+ * enable: 0 off, 1 report per kernel kind, 2 per kind and shape
+ * ("kind@shape", e.g. the GEMM's M/N/K or the block's width and size). */
 int dn_model_profile(dn_model* model, int enable);
 /* Synchronise and write a JSON object {kind: {launches, ms, bytes, flops}}
  * accumulated since the previous report (bytes/flops are algorithmic). */

@@ -284,9 +284,10 @@ class Model:
         """Fused two-pass NAFBlock kernels on shallow levels (default) or per-conv kernels."""
         check(lib().dn_model_set_fused(self._h, 1 if enable else 0))
 
-    def profile(self, enable: bool = True) -> None:
-        """Bracket every kernel launch with CUDA events (see profile_report)."""
-        check(lib().dn_model_profile(self._h, 1 if enable else 0))
+    def profile(self, enable: bool = True, detail: bool = False) -> None:
+        """Bracket every kernel launch with CUDA events (see profile_report);
+        with detail, report per kernel kind and shape ("kind@shape")."""
+        check(lib().dn_model_profile(self._h, (2 if detail else 1) if enable else 0))
 
     def profile_report(self) -> dict:
         """{kind: {launches, ms, bytes, flops}} since the last report."""

@@ -181,7 +181,8 @@ int dn_model_set_fused(dn_model* m, int enable) {
 
 int dn_model_profile(dn_model* m, int enable) {
     if (!m) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_profile: null model");
-    m->eng->set_profiling(enable != 0);
+    if (enable < 0 || enable > 2) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_profile: enable must be 0, 1 or 2");
+    m->eng->set_profiling(enable);
     return DN_OK;
 }
 

@@ -119,8 +119,16 @@ __global__ void __launch_bounds__(kThreads) dw_gate_kernel(const __grid_constant
     }
 }
 
-// grid (D / 8, N): CTA j computes s[img][8j .. 8j+8).
+// grid (D / 8, N): CTA j computes s[img][8j .. 8j+8). Every lane owns
+// float4 channel vectors v = lane + 32 i (i < V, V = ceil(D / 128)) and
+// issues all of its loads before it uses any (8 / V partial rows at a time),
+// so each phase pays about one memory latency.
+constexpr int kScaVec = 8;  // D <= 32 * 4 * kScaVec = 1024
+
+template <int V>
 __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ DwParams p, int nb) {
+    constexpr int kScaVec = V;
+    constexpr int kRowsAtOnce = V >= 8 ? 1 : 8 / V;
     extern __shared__ __align__(16) float sm[];
     const int D = p.D;
     float* mean = sm;       // [D]
@@ -128,21 +136,33 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int img = blockIdx.y;
-    // Fixed-order pool: warp w sums CTA rows w, w+8, ...; lanes read float4
-    // channel vectors (coalesced); the 8 warp sums are added in warp order.
     const int nvec = D / 4;
+    // Fixed-order pool: warp w sums partial rows w, w+8, ... in order; the 8
+    // warp sums are then added in warp order.
     const float4* pp = reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(img) * nb * D);
-    for (int v = lane; v < nvec; v += 32) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-        for (int b = warp; b < nb; b += 8) {
-            const float4 x = pp[static_cast<size_t>(b) * nvec + v];
-            acc.x += x.x;
-            acc.y += x.y;
-            acc.z += x.z;
-            acc.w += x.w;
+    float4 acc[kScaVec];
+#pragma unroll
+    for (int i = 0; i < kScaVec; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll kRowsAtOnce
+    for (int b = warp; b < nb; b += 8) {
+        float4 x[kScaVec];
+#pragma unroll
+        for (int i = 0; i < kScaVec; ++i) {
+            const int v = lane + 32 * i;
+            x[i] = v < nvec ? pp[static_cast<size_t>(b) * nvec + v] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        reinterpret_cast<float4*>(red + warp * D)[v] = acc;
+#pragma unroll
+        for (int i = 0; i < kScaVec; ++i) {
+            acc[i].x += x[i].x;
+            acc[i].y += x[i].y;
+            acc[i].z += x[i].z;
+            acc[i].w += x[i].w;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kScaVec; ++i) {
+        const int v = lane + 32 * i;
+        if (v < nvec) reinterpret_cast<float4*>(red + warp * D)[v] = acc[i];
     }
     __syncthreads();
     const float inv = 1.0f / static_cast<float>(p.H * p.W);
@@ -154,9 +174,25 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
     __syncthreads();
     const int o = blockIdx.x * 8 + warp;  // 8 warps -> 8 outputs
     if (o < D) {
-        const float* wr = p.sca_w + static_cast<size_t>(o) * D;
+        const float4* wr = reinterpret_cast<const float4*>(p.sca_w + static_cast<size_t>(o) * D);
+        float4 w[kScaVec];
+#pragma unroll
+        for (int i = 0; i < kScaVec; ++i) {
+            const int v = lane + 32 * i;
+            w[i] = v < nvec ? wr[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         float s = 0.f;
-        for (int c = lane; c < D; c += 32) s += wr[c] * mean[c];
+#pragma unroll
+        for (int i = 0; i < kScaVec; ++i) {
+            const int v = lane + 32 * i;
+            if (v < nvec) {
+                const float4 m = reinterpret_cast<const float4*>(mean)[v];
+                s = fmaf(w[i].x, m.x, s);
+                s = fmaf(w[i].y, m.y, s);
+                s = fmaf(w[i].z, m.z, s);
+                s = fmaf(w[i].w, m.w, s);
+            }
+        }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
         if (lane == 0) p.s_out[static_cast<size_t>(img) * D + o] = s + p.sca_b[o];
@@ -174,23 +210,33 @@ int dw_blocks_per_img(int H, int W, int D) {
     return static_cast<int>(std::max(1LL, std::min(want, cap)));
 }
 
-int launch_sca(const DwParams& p, int nb, cudaStream_t s) {
-    const size_t smem2 = static_cast<size_t>(9) * p.D * sizeof(float);
-    if (smem2 > 200 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "sca: too many channels");
+template <int V>
+int launch_sca_v(const DwParams& p, int nb, cudaStream_t s) {
+    const size_t smem = static_cast<size_t>(9) * p.D * sizeof(float);
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(sca_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(sca_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
         if (e != cudaSuccess) return dn_cuda_fail(e, "sca: set smem attribute");
         configured = true;
     }
-    sca_kernel<<<dim3((p.D + 7) / 8, p.N), kThreads, smem2, s>>>(p, nb);
+    sca_kernel<V><<<dim3((p.D + 7) / 8, p.N), kThreads, smem, s>>>(p, nb);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "sca: launch");
 }
 
+int launch_sca(const DwParams& p, int nb, cudaStream_t s) {
+    if (p.D % 4 != 0 || p.D > 32 * 4 * kScaVec)
+        return dn_fail(DN_ERR_UNSUPPORTED, "sca: channels must be a multiple of 4 and <= 1024");
+    const int nvec = p.D / 4;
+    if (nvec <= 32) return launch_sca_v<1>(p, nb, s);
+    if (nvec <= 64) return launch_sca_v<2>(p, nb, s);
+    if (nvec <= 128) return launch_sca_v<4>(p, nb, s);
+    return launch_sca_v<8>(p, nb, s);
+}
+
 int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s) {
-    if (p.D % 8 != 0 || p.D / 8 > kThreads)
-        return dn_fail(DN_ERR_UNSUPPORTED, "dw_gate: channels must be a multiple of 8 and <= 2048");
+    if (p.D % 8 != 0 || p.D > 32 * 4 * kScaVec)
+        return dn_fail(DN_ERR_UNSUPPORTED, "dw_gate: channels must be a multiple of 8 and <= 1024");
     const int lanes = kThreads / (p.D / 8);
     const size_t smem = (static_cast<size_t>(10) * 2 * p.D + static_cast<size_t>(lanes) * p.D) * sizeof(float);
     const size_t smem2 = static_cast<size_t>(9) * p.D * sizeof(float);
@@ -198,18 +244,13 @@ int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s) {
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(dw_gate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(sca_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return dn_cuda_fail(e, "dw_gate: set smem attribute");
         configured = true;
     }
     dw_gate_kernel<<<dim3(blocks_per_img, p.N), kThreads, smem, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return dn_cuda_fail(e, "dw_gate: launch");
-    sca_kernel<<<dim3((p.D + 7) / 8, p.N), kThreads, smem2, s>>>(p, blocks_per_img);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return dn_cuda_fail(e, "sca: launch");
-    return DN_OK;
+    return launch_sca(p, blocks_per_img, s);
 }
 
 }  // namespace dnb

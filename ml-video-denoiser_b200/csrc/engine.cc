@@ -51,7 +51,10 @@ struct Packer {
     size_t add_f32(const std::vector<float>& v) { return add(v.data(), v.size() * sizeof(float)); }
 };
 
-int store_nt(int n) { return std::min(128, next_pow2(std::max(16, n))); }
+// N tile of a GEMM writing n columns: up to 256 wide, which halves the
+// shared-memory operand traffic per MMA against 128 (the tensor core reads
+// A once per 256 output columns).
+int store_nt(int n) { return std::min(256, next_pow2(std::max(16, n))); }
 
 // Pack W[rows][K] (row-major fp32, src row per packed row, -1 = zero row)
 // into the tile image the GEMM kernel bulk-copies: tiles [n_tile][k_chunk],
@@ -135,7 +138,7 @@ GemmW pack_gemm(Packer& pk, const std::vector<float>& W, int N, int K, int NT, c
 // that output channel c and its gate c + half land in the same tile.
 GemmW pack_gate(Packer& pk, const std::vector<float>& W, const std::vector<float>& bias, int half, int K,
                 LnFold ln = {}) {
-    const int hnt = std::min(64, next_pow2(std::max(16, half)));
+    const int hnt = std::min(128, next_pow2(std::max(16, half)));
     const int NT = 2 * hnt;
     const int n_tiles = (half + hnt - 1) / hnt;
     std::vector<int> rows(static_cast<size_t>(n_tiles) * NT, -1);
@@ -467,7 +470,9 @@ void Engine::prof_begin(const char* kind, double bytes, double flops, cudaStream
         cudaEventCreate(&e);
         prof_pool_.push_back(e);
     }
-    ProfRec r{kind, bytes, flops, prof_pool_[prof_used_], prof_pool_[prof_used_ + 1]};
+    std::string key = kind;
+    if (prof_detail_ && !prof_tag_.empty()) key += "@" + prof_tag_;
+    ProfRec r{key, bytes, flops, prof_pool_[prof_used_], prof_pool_[prof_used_ + 1]};
     prof_used_ += 2;
     cudaEventRecord(r.a, s);
     prof_.push_back(r);
@@ -536,7 +541,11 @@ int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cuda
         double bytes = rows * g.K * 2 + n_w * g.K * 2;
         const double n_out = epi == kEpiShuffleAdd ? 4.0 * p.out_c : p.n_out;
         bytes += rows * n_out * 2 * (epi == kEpiResidual || epi == kEpiShuffleAdd ? 2 : 1);
+        const std::string block_tag = prof_tag_;
+        if (prof_detail_)
+            prof_tag_ = "M" + std::to_string(p.M) + "_N" + std::to_string(g.n_tiles * g.NT) + "_K" + std::to_string(g.K);
         prof_begin(kind, bytes, 2.0 * rows * n_w * g.K, s);
+        prof_tag_ = block_tag;
     }
     const int rc = launch_gemm(p, pro, epi, amode, g.NT, s);
     prof_end(s);
@@ -555,6 +564,7 @@ static GemmParams rows_params(int nimg, int h, int w) {
 
 // NAFBlock (training/models.py:166-185, src/models/nafnet.cu:146-215), in place on x.
 int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaStream_t s) {
+    if (prof_detail_) prof_tag_ = "C" + std::to_string(b.C) + "_" + std::to_string(h) + "x" + std::to_string(w);
     const long long hw = static_cast<long long>(h) * w;
     if (b.fused && fused_enabled_ && nimg <= 8) {
         // Pass A: LN1 + conv1 + DW3x3 + SimpleGate + pool partials.

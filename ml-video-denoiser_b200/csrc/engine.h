@@ -73,7 +73,11 @@ public:
     // Per-launch CUDA-event timing of the engine's own kernels (off by
     // default). Each launch is tagged with its kind and its algorithmic bytes
     // (inputs read once + outputs written once) and FLOPs.
-    void set_profiling(bool on) { profiling_ = on; }
+    // 0 off, 1 per kernel kind, 2 per kind and shape ("kind@shape")
+    void set_profiling(int mode) {
+        profiling_ = mode != 0;
+        prof_detail_ = mode == 2;
+    }
     // Use the fused two-pass NAFBlock kernels where they apply (default on).
     void set_fused(bool on) { fused_enabled_ = on; }
     // Synchronises, then returns a JSON object: kind -> {launches, ms, bytes, flops}
@@ -144,13 +148,15 @@ private:
 
     // profiling
     struct ProfRec {
-        const char* kind;
+        std::string kind;
         double bytes, flops;
         cudaEvent_t a, b;
     };
     void prof_begin(const char* kind, double bytes, double flops, cudaStream_t s);
     void prof_end(cudaStream_t s);
     bool profiling_ = false;
+    bool prof_detail_ = false;
+    std::string prof_tag_;  // shape suffix of the next prof_begin in detail mode
     bool fused_enabled_ = true;
     std::vector<ProfRec> prof_;
     std::vector<cudaEvent_t> prof_pool_;

@@ -53,7 +53,7 @@ namespace {
 constexpr int kRows = 128;
 constexpr int kStages = 3;
 constexpr int kKC = 64;                 // shared-memory footprint is sized for KC = 64
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
 constexpr uint32_t kALbo = kRows * 16;  // 2 KB between K-adjacent core-matrix columns
 
 struct GemmMaps {
@@ -62,17 +62,17 @@ struct GemmMaps {
     CUtensorMap res;  // residual load (same geometry as out)
 };
 
-// Named barrier of the four epilogue warps.
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of the eight epilogue warps.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-// Same barrier, returning the OR of `v` over the 128 epilogue threads (a
+// Same barrier, returning the OR of `v` over the 256 epilogue threads (a
 // uniform decision for all of them).
 __device__ __forceinline__ bool epi_sync_or(bool v) {
     uint32_t out;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, 1, 128, p;\n\t"
+        "bar.red.or.pred q, 1, 256, p;\n\t"
         "selp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(out)
         : "r"(static_cast<uint32_t>(v))
@@ -130,6 +130,22 @@ struct Staging {
     }
 };
 
+// Dynamic shared memory of one instantiation: the stage ring, the epilogue
+// staging tile (none for the PixelShuffle scatter, which stores directly)
+// and the parameter vectors it uses.
+template <int PRO, int EPI, int NT>
+struct SmemPlan {
+    static constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
+    static constexpr int kStgBytes = (EPI == kEpiShuffleAdd) ? 0 : Staging<kOutCols>::kBytes;
+    static int param_floats(const GemmParams& p) {
+        return p.n_tiles * NT * (PRO == kProLayerNorm ? 2 : 1) + (EPI == kEpiResidual ? p.n_out : 0) +
+               (PRO == kProScale ? p.K : 0);
+    }
+    static int bytes(const GemmParams& p) {
+        return 1024 + kStages * (kRows * kKC * 2 + NT * kKC * 2) + kStgBytes + param_floats(p) * 4;
+    }
+};
+
 template <int PRO, int EPI, int AMODE, int NT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ws_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ GemmMaps maps) {
@@ -161,10 +177,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         return a_swz ? sw_offset(r, q, a_swz) : static_cast<uint32_t>(q) * kALbo + r * 16;
     };
     uint8_t* stg = smem + kStages * stage_bytes;  // 1024-aligned: stage_bytes is a multiple of 1024
-    float* s_bias = reinterpret_cast<float*>(stg + Stg::kBytes);
-    float* s_rsc = s_bias + p.n_tiles * NT;
-    float* s_c1 = s_rsc + p.n_out;
-    float* s_sca = s_c1 + p.n_tiles * NT;  // SCA scale of image 0 (single-image launches)
+    float* s_bias = reinterpret_cast<float*>(stg + SmemPlan<PRO, EPI, NT>::kStgBytes);
+    float* s_c1 = s_bias + p.n_tiles * NT;                                   // LN fold only
+    float* s_rsc = s_c1 + (kLN ? p.n_tiles * NT : 0);                        // residual only
+    float* s_sca = s_rsc + (EPI == kEpiResidual ? p.n_out : 0);             // SCA scale of image 0
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
@@ -193,9 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bar_acc_full[b], 1);
-            mbar_init(&bar_acc_empty[b], 4);
+            mbar_init(&bar_acc_empty[b], 8);
             mbar_init(&bar_st_full[b], 4);
-            mbar_init(&bar_st_empty[b], 4);
+            mbar_init(&bar_st_empty[b], 8);
         }
         mbar_init(&bar_res, 1);
         s_abort = 0;
@@ -206,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tslot;
 
-    if (warp == 8) {
+    if (warp == 12) {
         // ------------------------------ TMA producer ------------------------------
         if (lane == 0) {
             int it = 0;
@@ -241,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == 13) {
         // ------------------------------ MMA issuer --------------------------------
         if (lane == 0) {
             const uint32_t idesc = idesc_f16_f32(kRows, NT);
@@ -294,20 +310,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* sa = smem + s * stage_bytes;
                     if (kLN) {
-                        // Shifted sums of the row (shift = its first element).
-                        for (int q = 0; q < KC / 8; ++q) {
-                            const int k = j * KC + q * 8;
-                            if (k >= p.K) break;
-                            float f[8];
-                            h8_to_f(*reinterpret_cast<const uint4*>(sa + a_off(r, q)), f);
-                            if (k == 0) x0 = f[0];
+                        // Shifted sums of the row (shift = its first element):
+                        // every load first, then two independent packed chains.
+                        const int nq = min(KC, p.K - j * KC) >> 3;
+                        uint4 v[8];
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const float d = f[i] - x0;
-                                s1 += d;
-                                s2 = fmaf(d, d, s2);
+                        for (int q = 0; q < 8; ++q)
+                            if (q < nq) v[q] = *reinterpret_cast<const uint4*>(sa + a_off(r, q));
+                        if (j == 0) x0 = unpack_half2(v[0].x).x;
+                        const float2 nx = make_float2(-x0, -x0), one = make_float2(1.f, 1.f);
+                        float2 a1[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                        float2 a2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            if (q < nq) {
+                                const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    const float2 d = ffma2(unpack_half2(w[i]), one, nx);
+                                    a1[i & 1] = ffma2(d, one, a1[i & 1]);
+                                    a2[i & 1] = ffma2(d, d, a2[i & 1]);
+                                }
                             }
                         }
+                        s1 += (a1[0].x + a1[0].y) + (a1[1].x + a1[1].y);
+                        s2 += (a2[0].x + a2[0].y) + (a2[1].x + a2[1].y);
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&bar_empty[s]);
                     } else if (AMODE == kAS2x2) {
@@ -359,9 +386,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------ epilogue ----------------------------------
-        const int r = tid - 128;       // tile row == TMEM lane
-        const int wq = warp - 4;       // TMEM lane quarter of this warp
-        const bool leader = (r == 0);
+        // Warps 4-11: warp w reads TMEM lanes 32*(w%4).. (its tile rows) and
+        // column half (w-4)/4 of the tile (all columns if the tile is narrow).
+        const int wq = warp & 3;                 // TMEM lane quarter of this warp
+        const int r = wq * 32 + lane;            // tile row == TMEM lane
+        const int ch = (warp - 4) >> 2;          // column group
+        const bool leader = (tid == 128);
+        // [lo, hi) of a span of `cols` columns for this warp's group (spans
+        // narrower than 32 stay with group 0)
+        auto span = [ch](int cols, int& lo, int& hi) {
+            if (cols >= 32) {
+                lo = ch * (cols / 2);
+                hi = lo + cols / 2;
+            } else {
+                lo = 0;
+                hi = ch == 0 ? cols : 0;
+            }
+        };
         const bool tma_epi = (EPI != kEpiShuffleAdd) && (p.out_c % kOutCols == 0);
         int t = 0;
         for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t) {
@@ -398,8 +439,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (EPI == kEpiShuffleAdd || !tma_epi) {
                 // Direct per-row stores (PixelShuffle scatter, or narrow outputs).
+                int c_lo, c_hi;
+                span(kOutCols, c_lo, c_hi);
 #pragma unroll 1
-                for (int c0 = 0; c0 < kOutCols; c0 += 16) {
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                     float va[16], vb[16];
                     tmem_ld16(lane_base + c0, va);
                     if (EPI == kEpiGate) tmem_ld16(lane_base + NT / 2 + c0, vb);
@@ -458,11 +501,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
                 continue;
             }
-            // Swizzled staging tile -> TMA tensor store.
+            // Swizzled staging tile -> TMA tensor store. Per 8 columns:
+            // LN fold  y = rstd * acc + (c2 - rstd * mean * c1), else y = acc + bias,
+            // in packed f32x2 arithmetic with float4 parameter loads.
+            const float2 one2 = make_float2(1.f, 1.f);
+            const float2 rs2 = make_float2(rstd, rstd);
+            const float2 nm2 = make_float2(-rstd * mean, -rstd * mean);
+            // 8 columns starting at n: acc (8 values) -> bias/LN-folded values
+            auto fold8 = [&](const float* acc, int n, float2 (&y)[4]) {
+                const float4 b0 = *reinterpret_cast<const float4*>(s_bias + n);
+                const float4 b1 = *reinterpret_cast<const float4*>(s_bias + n + 4);
+                const float2 bb[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                                      make_float2(b1.z, b1.w)};
+                if (kLN) {
+                    const float4 k0 = *reinterpret_cast<const float4*>(s_c1 + n);
+                    const float4 k1 = *reinterpret_cast<const float4*>(s_c1 + n + 4);
+                    const float2 cc[4] = {make_float2(k0.x, k0.y), make_float2(k0.z, k0.w), make_float2(k1.x, k1.y),
+                                          make_float2(k1.z, k1.w)};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        y[i] = ffma2(rs2, make_float2(acc[2 * i], acc[2 * i + 1]), ffma2(nm2, cc[i], bb[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) y[i] = ffma2(make_float2(acc[2 * i], acc[2 * i + 1]), one2, bb[i]);
+                }
+            };
             if (EPI == kEpiGate) {
                 constexpr int kHalf = NT / 2;
+                int c_lo, c_hi;
+                span(kHalf, c_lo, c_hi);
 #pragma unroll 1
-                for (int c0 = 0; c0 < kHalf; c0 += 16) {
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                     float va[16], vb[16];
                     tmem_ld16(lane_base + c0, va);
                     tmem_ld16(lane_base + kHalf + c0, vb);
@@ -470,48 +539,59 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int n = n_tile * NT + c0;
 #pragma unroll
                     for (int g = 0; g < 2; ++g) {
-                        float f[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int na = n + 8 * g + i, nb2 = na + kHalf;
-                            float x1 = va[8 * g + i], x2 = vb[8 * g + i];
-                            if (kLN) {
-                                x1 = rstd * (x1 - mean * s_c1[na]) + s_bias[na];
-                                x2 = rstd * (x2 - mean * s_c1[nb2]) + s_bias[nb2];
-                            } else {
-                                x1 += s_bias[na];
-                                x2 += s_bias[nb2];
-                            }
-                            f[i] = x1 * x2;
-                        }
-                        *reinterpret_cast<uint4*>(stg + Stg::off(r, (c0 >> 3) + g)) = f_to_h8(f);
+                        float2 x1[4], x2[4];
+                        fold8(va + 8 * g, n + 8 * g, x1);
+                        fold8(vb + 8 * g, n + kHalf + 8 * g, x2);
+                        uint4 o;
+                        const float2 z = make_float2(0.f, 0.f);
+                        const float2 p0 = ffma2(x1[0], x2[0], z), p1 = ffma2(x1[1], x2[1], z);
+                        const float2 p2 = ffma2(x1[2], x2[2], z), p3 = ffma2(x1[3], x2[3], z);
+                        o.x = pack_half2(p0.x, p0.y);
+                        o.y = pack_half2(p1.x, p1.y);
+                        o.z = pack_half2(p2.x, p2.y);
+                        o.w = pack_half2(p3.x, p3.y);
+                        *reinterpret_cast<uint4*>(stg + Stg::off(r, (c0 >> 3) + g)) = o;
                     }
                 }
             } else {
+                constexpr int kStep = NT >= 64 ? 32 : 16;
+                int c_lo, c_hi;
+                span(NT, c_lo, c_hi);
 #pragma unroll 1
-                for (int c0 = 0; c0 < NT; c0 += 16) {
-                    float va[16];
-                    tmem_ld16(lane_base + c0, va);
+                for (int c0 = c_lo; c0 < c_hi; c0 += kStep) {
+                    float va[32];
+                    tmem_ld16(lane_base + c0, *reinterpret_cast<float(*)[16]>(va));
+                    if (kStep == 32) tmem_ld16(lane_base + c0 + 16, *reinterpret_cast<float(*)[16]>(va + 16));
                     tmem_ld_wait();
                     const int n = n_tile * NT + c0;
 #pragma unroll
-                    for (int g = 0; g < 2; ++g) {
-                        float f[8];
+                    for (int g = 0; g < kStep / 8; ++g) {
+                        float2 y[4];
+                        fold8(va + 8 * g, n + 8 * g, y);
                         uint4* sp = reinterpret_cast<uint4*>(stg + Stg::off(r, (c0 >> 3) + g));
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int nn = n + 8 * g + i;
-                            f[i] = kLN ? rstd * (va[8 * g + i] - mean * s_c1[nn]) + s_bias[nn]
-                                       : va[8 * g + i] + s_bias[nn];
-                        }
                         if (EPI == kEpiResidual) {
-                            float rr[8];
-                            h8_to_f(*sp, rr);
+                            const uint4 rv = *sp;
+                            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
                             const int o = col0 + c0 + 8 * g;
+                            float2 sc[4];
+                            if (o + 8 <= p.n_out) {
+                                const float4 q0 = *reinterpret_cast<const float4*>(s_rsc + o);
+                                const float4 q1 = *reinterpret_cast<const float4*>(s_rsc + o + 4);
+                                sc[0] = make_float2(q0.x, q0.y);
+                                sc[1] = make_float2(q0.z, q0.w);
+                                sc[2] = make_float2(q1.x, q1.y);
+                                sc[3] = make_float2(q1.z, q1.w);
+                            } else {
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) f[i] = rr[i] + s_rsc[min(o + i, p.n_out - 1)] * f[i];
+                                for (int i = 0; i < 4; ++i)
+                                    sc[i] = make_float2(s_rsc[min(o + 2 * i, p.n_out - 1)],
+                                                        s_rsc[min(o + 2 * i + 1, p.n_out - 1)]);
+                            }
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) y[i] = ffma2(sc[i], y[i], unpack_half2(rw[i]));
                         }
-                        *sp = f_to_h8(f);
+                        *sp = make_uint4(pack_half2(y[0].x, y[0].y), pack_half2(y[1].x, y[1].y),
+                                         pack_half2(y[2].x, y[2].y), pack_half2(y[3].x, y[3].y));
                     }
                 }
             }
@@ -591,8 +671,7 @@ int launch_one(const GemmParams& p, cudaStream_t s) {
     auto kern = gemm_ws_kernel<PRO, EPI, AMODE, NT>;
     constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
     using Stg = Staging<kOutCols>;
-    const int params = 2 * p.n_tiles * NT + p.n_out + p.K;
-    const int smem = 1024 + kStages * (kRows * kKC * 2 + NT * kKC * 2) + Stg::kBytes + params * 4;
+    const int smem = SmemPlan<PRO, EPI, NT>::bytes(p);
     if (smem > 225 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: tile does not fit in shared memory");
     static int configured = 0;  // largest dynamic footprint granted so far
     if (smem > configured) {

@@ -7,7 +7,7 @@
 
 #include <string>
 
-#include "../../include/denoiser_b200.h"
+#include "denoiser_b200.h"
 
 namespace dnb {
 
