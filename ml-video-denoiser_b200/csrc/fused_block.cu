@@ -3,14 +3,16 @@
 //
 // Phase A (one CTA = a stream of TH x TW output tiles):
 //   TMA loads the (TH+2) x (TW+2) halo of x (NHWC, zero outside the image)
-//   straight into the swizzled K-major UMMA layout; threads compute the
-//   LayerNorm statistics of every halo pixel; tcgen05 runs conv1 over the
-//   halo (M = 128 pixels per block, N = 2*dw, K = C) with the LN folded into
-//   the weights (B = gamma*W1) and the epilogue (rstd*(acc - mean*c1) + c2),
-//   writing u (fp16, zero outside the image = the DW zero padding) to shared
-//   memory; CUDA cores then run the 3x3 depthwise conv + bias + SimpleGate
-//   from shared memory, write g by TMA store and accumulate the per-image
-//   pool partials (deterministic order).
+//   straight into the swizzled K-major UMMA layout; one thread per halo pixel
+//   normalises it in place (LayerNorm without the affine, FP32 statistics,
+//   FP16 result as in the reference); tcgen05 runs conv1 over the halo
+//   (M = 128 pixels per block, N = 2*dw, K = C) with the affine folded into
+//   the weights (B = gamma*W1, bias' = b1 + W1 beta), and all eight warps
+//   move u = acc + bias' (zero outside the image = the DW zero padding) to
+//   shared memory; CUDA cores then run the 3x3 depthwise conv + bias +
+//   SimpleGate (a thread owns 4 channels of one gate half and a 2 x 4 block
+//   of outputs, so each loaded u vector feeds up to 6 outputs), write g by
+//   TMA store and accumulate the per-image pool partials (deterministic).
 // Phase B (one CTA = a stream of 128-pixel tiles): TMA brings g and x;
 //   g *= s (SCA scale) in place; tcgen05 conv3 -> y = x + beta*(acc + b3)
 //   (kept in registers) -> LayerNorm2 -> tcgen05 conv4 -> SimpleGate ->
@@ -67,10 +69,14 @@ struct GeoA {
     static constexpr int U_BYTES = ((P * U_PITCH + 1023) / 1024) * 1024;
     static constexpr int G_BYTES = TH * TW * D * 2;
     static constexpr int W1_BYTES = N1 * C * 2;       // one K chunk (C <= 64)
-    static constexpr int LANES = kAThreads / (2 * (D / 8)); // output pixels in flight per CTA
-    // floats: c1, c2, dw taps, dw bias, stats (2 per halo pixel), partials [8][D], reduction
-    static constexpr int F_FLOATS = N1 + N1 + 9 * N1 + N1 + 2 * P + 8 * D + LANES * D;
+    // depthwise: thread = (gate half, 4-channel group, slot); slot = 2 x 4 output block
+    static constexpr int CG = D / 4;
+    static constexpr int SLOTS = kAThreads / (2 * CG);
+    static constexpr int NBLK = (TH / 2) * (TW / 4);
+    // floats: bias' [2D], pool partials [8][D], pool reduction [2*SLOTS][D]
+    static constexpr int F_FLOATS = N1 + 8 * D + 2 * SLOTS * D;
     static constexpr int SMEM = 1024 + A_BYTES + U_BYTES + G_BYTES + W1_BYTES + F_FLOATS * 4;
+    static_assert(TH % 2 == 0 && TW % 4 == 0, "2 x 4 output blocks");
 };
 
 template <int C, int D, int F>
@@ -111,13 +117,9 @@ __global__ void __launch_bounds__(kAThreads, 2)
     uint8_t* sU = sA + G::A_BYTES;
     uint8_t* sGo = sU + G::U_BYTES;
     uint8_t* sW1 = sGo + G::G_BYTES;
-    float* sC1 = reinterpret_cast<float*>(sW1 + G::W1_BYTES);
-    float* sC2 = sC1 + G::N1;
-    float* sDw = sC2 + G::N1;       // [9][2D]
-    float* sDb = sDw + 9 * G::N1;   // [2D]
-    float2* sStat = reinterpret_cast<float2*>(sDb + G::N1);
-    float* sPart = reinterpret_cast<float*>(sStat + G::P);  // [8][D]
-    float* sRed = sPart + 8 * D;                             // [LANES][D]
+    float* sC2 = reinterpret_cast<float*>(sW1 + G::W1_BYTES);  // [2D]
+    float* sPart = sC2 + G::N1;                                 // [8][D]
+    float* sRed = sPart + 8 * D;                                // [2*SLOTS][D]
     __shared__ uint64_t bar_x, bar_w, bar_mma;
     __shared__ uint32_t tslot;
     __shared__ int s_fail;
@@ -134,12 +136,7 @@ __global__ void __launch_bounds__(kAThreads, 2)
         tx0 = (r % tiles_x) * G::TW;
     };
 
-    for (int i = tid; i < G::N1; i += kAThreads) {
-        sC1[i] = p.c1[i];
-        sC2[i] = p.c2[i];
-        sDb[i] = p.dw_b[i];
-    }
-    for (int i = tid; i < 9 * G::N1; i += kAThreads) sDw[i] = p.dw_w[i];
+    for (int i = tid; i < G::N1; i += kAThreads) sC2[i] = p.c2[i];
     for (int i = tid; i < 8 * D; i += kAThreads) sPart[i] = 0.f;
     if (warp == 0) {
         tmem_alloc(&tslot, G::TMEM_COLS);
@@ -166,23 +163,23 @@ __global__ void __launch_bounds__(kAThreads, 2)
     const uint32_t tmem = tslot;
     const bool ok = __syncthreads_and(wait_bar(&bar_w, 0, p.err, 0x30)) != 0;
 
-    // DW thread mapping: (half, channel group) fastest, then output pixel.
+    // Depthwise mapping: gate half fastest (pairs meet through one shuffle),
+    // then 4-channel group, then block slot.
     const int half = tid & 1;
-    const int cg = (tid >> 1) % (D / 8);
-    const int pl = (tid >> 1) / (D / 8);
-    float2 dww[9][4];
-    float dwb[8];
-    {
-        const int cin = half * D + cg * 8;
+    const int cg = (tid >> 1) % G::CG;
+    const int slot = (tid >> 1) / G::CG;
+    const int cin = half * D + cg * 4;
+    float2 dww[9][2];
+    float2 dwb[2];
 #pragma unroll
-        for (int tp = 0; tp < 9; ++tp)
+    for (int tp = 0; tp < 9; ++tp)
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                dww[tp][i] = make_float2(p.dw_w[tp * G::N1 + cin + 2 * i], p.dw_w[tp * G::N1 + cin + 2 * i + 1]);
+        for (int i = 0; i < 2; ++i)
+            dww[tp][i] = make_float2(p.dw_w[tp * G::N1 + cin + 2 * i], p.dw_w[tp * G::N1 + cin + 2 * i + 1]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dwb[i] = p.dw_b[cin + i];
-    }
-    float ps[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i < 2; ++i) dwb[i] = make_float2(p.dw_b[cin + 2 * i], p.dw_b[cin + 2 * i + 1]);
+    float ps[4] = {0.f, 0.f, 0.f, 0.f};
+
     int it = 0;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         int img, ty0, tx0;
@@ -190,27 +187,45 @@ __global__ void __launch_bounds__(kAThreads, 2)
         if (!wait_bar(&bar_x, it & 1, p.err, 0x31)) s_fail = 1;
         __syncthreads();
         if (s_fail) break;
-        // LayerNorm statistics of the halo pixels (two passes over the row).
+        // (1) LayerNorm (no affine) of every halo pixel, in place: the row is
+        // read once into registers; statistics are shifted sums (shift = its
+        // first element) in two packed chains.
         for (int r = tid; r < G::P; r += kAThreads) {
-            float s = 0.f;
+            uint4 v[C / 8];
+#pragma unroll
+            for (int q = 0; q < C / 8; ++q) v[q] = *reinterpret_cast<const uint4*>(sA + sw_offset(r, q, G::ROWB));
+            const float x0 = unpack_half2(v[0].x).x;
+            const float2 nx = make_float2(-x0, -x0), one = make_float2(1.f, 1.f);
+            float2 a1[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            float2 a2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
             for (int q = 0; q < C / 8; ++q) {
-                float f[8];
-                h8_to_f(*reinterpret_cast<const uint4*>(sA + sw_offset(r, q, G::ROWB)), f);
+                const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) s += f[i];
+                for (int i = 0; i < 4; ++i) {
+                    const float2 d = ffma2(unpack_half2(w[i]), one, nx);
+                    a1[i & 1] = ffma2(d, one, a1[i & 1]);
+                    a2[i & 1] = ffma2(d, d, a2[i & 1]);
+                }
             }
-            const float mean = s * (1.0f / C);
-            float ss = 0.f;
+            const float dm = ((a1[0].x + a1[0].y) + (a1[1].x + a1[1].y)) * (1.0f / C);
+            const float var = fmaxf(((a2[0].x + a2[0].y) + (a2[1].x + a2[1].y)) * (1.0f / C) - dm * dm, 0.f);
+            const float rstd = rsqrtf(var + 1e-6f);
+            const float2 rs2 = make_float2(rstd, rstd);
+            const float2 sh2 = make_float2(-(x0 + dm) * rstd, -(x0 + dm) * rstd);
 #pragma unroll
             for (int q = 0; q < C / 8; ++q) {
-                float f[8];
-                h8_to_f(*reinterpret_cast<const uint4*>(sA + sw_offset(r, q, G::ROWB)), f);
+                const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+                uint32_t o[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) ss += (f[i] - mean) * (f[i] - mean);
+                for (int i = 0; i < 4; ++i) {
+                    const float2 y = ffma2(unpack_half2(w[i]), rs2, sh2);
+                    o[i] = pack_half2(y.x, y.y);
+                }
+                *reinterpret_cast<uint4*>(sA + sw_offset(r, q, G::ROWB)) = make_uint4(o[0], o[1], o[2], o[3]);
             }
-            sStat[r] = make_float2(mean, rsqrtf(ss * (1.0f / C) + 1e-6f));
         }
+        fence_async_smem();  // the normalised rows feed the tensor core (async proxy)
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
@@ -226,38 +241,33 @@ __global__ void __launch_bounds__(kAThreads, 2)
         tc_fence_after();
         // The halo tile is consumed: prefetch the next one.
         if (tid == 0 && !s_fail && t + static_cast<int>(gridDim.x) < total) {
-            int ni, ny, nx;
-            decode(t + gridDim.x, ni, ny, nx);
+            int ni, ny, nx2;
+            decode(t + gridDim.x, ni, ny, nx2);
             mbar_arrive_expect_tx(&bar_x, G::P * G::ROWB);
-            tma_load_4d(sA, &mx, 0, nx - 1, ny - 1, ni, &bar_x);
+            tma_load_4d(sA, &mx, 0, nx2 - 1, ny - 1, ni, &bar_x);
         }
-        // conv1 epilogue: u = rstd*(acc - mean*c1) + c2, zero outside the image.
-        for (int b = warp >> 2; b < G::NB; b += 2) {
-            const int r = b * 128 + (warp & 3) * 32 + lane;
-            const uint32_t lb = tmem + b * G::N1 + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-            const int yy = ty0 - 1 + r / G::WW;
-            const int xx = tx0 - 1 + r % G::WW;
-            const bool in_halo = r < G::P;
-            const bool inside = in_halo && yy >= 0 && yy < p.H && xx >= 0 && xx < p.W;
-            const float2 st = in_halo ? sStat[r] : make_float2(0.f, 0.f);
-            // u = rstd * acc + (c2 - rstd * mean * c1), zero outside the image.
-            const float2 rs2 = inside ? make_float2(st.y, st.y) : make_float2(0.f, 0.f);
-            const float2 nm2 = inside ? make_float2(-st.x * st.y, -st.x * st.y) : make_float2(0.f, 0.f);
-            const float2 on2 = inside ? make_float2(1.f, 1.f) : make_float2(0.f, 0.f);
-#pragma unroll 1
-            for (int c0 = 0; c0 < G::N1; c0 += 16) {
+        // (2) conv1 epilogue over all eight warps: warp w reads TMEM lane
+        // quarter w%4 and every other 16-column chunk: u = acc + bias',
+        // zero outside the image.
+        {
+            constexpr int CH = G::N1 / 16;
+            const int q4 = warp & 3;
+            for (int j = warp >> 2; j < G::NB * CH; j += 2) {
+                const int b = j / CH, c0 = (j - b * CH) * 16;
+                const int r = b * 128 + q4 * 32 + lane;
                 float v[16];
-                tmem_ld16(lb + c0, v);
+                tmem_ld16(tmem + b * G::N1 + c0 + (static_cast<uint32_t>(q4 * 32) << 16), v);
                 tmem_ld_wait();
-                if (!in_halo) continue;
+                if (r >= G::P) continue;
+                const int yy = ty0 - 1 + r / G::WW;
+                const int xx = tx0 - 1 + r % G::WW;
+                const bool inside = yy >= 0 && yy < p.H && xx >= 0 && xx < p.W;
                 uint32_t pk[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float2 c1 = *reinterpret_cast<const float2*>(sC1 + c0 + 2 * i);
-                    const float2 c2 = *reinterpret_cast<const float2*>(sC2 + c0 + 2 * i);
-                    const float2 k = ffma2(nm2, c1, make_float2(c2.x * on2.x, c2.y * on2.y));
-                    const float2 u = ffma2(rs2, make_float2(v[2 * i], v[2 * i + 1]), k);
-                    pk[i] = pack_half2(u.x, u.y);
+                for (int i = 0; i < 4; ++i) {
+                    const float4 c = *reinterpret_cast<const float4*>(sC2 + c0 + 4 * i);
+                    pk[2 * i] = inside ? pack_half2(v[4 * i] + c.x, v[4 * i + 1] + c.y) : 0u;
+                    pk[2 * i + 1] = inside ? pack_half2(v[4 * i + 2] + c.z, v[4 * i + 3] + c.w) : 0u;
                 }
                 uint4* dst = reinterpret_cast<uint4*>(sU + r * G::U_PITCH + c0 * 2);
                 dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -267,54 +277,67 @@ __global__ void __launch_bounds__(kAThreads, 2)
         tc_fence_before();
         if (tid == 0) bulk_wait_read0();  // the previous g tile has left sGo
         __syncthreads();
-        // Depthwise 3x3 + bias + SimpleGate from shared memory. Thread = one
-        // gate half x 8 channels (taps in registers); the halves of a gate
-        // pair are adjacent lanes and meet through one shuffle.
-        const int c0 = cg * 8;
-        const int cin = half * D + c0;
-        // Work item = (column px, row pair py, py+1): input rows py-1 .. py+2
-        // stream through once, each feeding the outputs it touches.
-        for (int op = pl; op < G::TH / 2 * G::TW; op += G::LANES) {
-            const int py = (op / G::TW) * 2, px = op % G::TW;
-            float2 a0[4], a1[4];
+        // (3) Depthwise 3x3 + bias + SimpleGate. Block = output rows by, by+1 x
+        // columns bx .. bx+3: halo rows by .. by+3 x columns bx .. bx+5 stream
+        // through once; each loaded vector feeds every output it touches.
+        for (int blk = slot; blk < G::NBLK; blk += G::SLOTS) {
+            const int by = (blk / (G::TW / 4)) * 2, bx = (blk % (G::TW / 4)) * 4;
+            float2 acc[2][4][2];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a0[i] = a1[i] = make_float2(dwb[2 * i], dwb[2 * i + 1]);
+            for (int ro = 0; ro < 2; ++ro)
+#pragma unroll
+                for (int oc = 0; oc < 4; ++oc) {
+                    acc[ro][oc][0] = dwb[0];
+                    acc[ro][oc][1] = dwb[1];
+                }
 #pragma unroll
             for (int rr = 0; rr < 4; ++rr) {
+                float2 in[6][2];
+                const uint8_t* row = sU + ((by + rr) * G::WW + bx) * G::U_PITCH + cin * 2;
 #pragma unroll
-                for (int kx = 0; kx < 3; ++kx) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(
-                        sU + ((py + rr) * G::WW + px + kx) * G::U_PITCH + cin * 2);
-                    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+                for (int cc = 0; cc < 6; ++cc) {
+                    const uint2 u2 = *reinterpret_cast<const uint2*>(row + cc * G::U_PITCH);
+                    in[cc][0] = unpack_half2(u2.x);
+                    in[cc][1] = unpack_half2(u2.y);
+                }
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 u = unpack_half2(w4[i]);
-                        if (rr <= 2) a0[i] = ffma2(u, dww[rr * 3 + kx][i], a0[i]);
-                        if (rr >= 1) a1[i] = ffma2(u, dww[(rr - 1) * 3 + kx][i], a1[i]);
+                for (int oc = 0; oc < 4; ++oc)
+#pragma unroll
+                    for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            if (rr <= 2) acc[0][oc][i] = ffma2(in[oc + kx][i], dww[rr * 3 + kx][i], acc[0][oc][i]);
+                            if (rr >= 1)
+                                acc[1][oc][i] = ffma2(in[oc + kx][i], dww[(rr - 1) * 3 + kx][i], acc[1][oc][i]);
+                        }
+            }
+            // Gate: this lane stores columns 2*half, 2*half+1 of both rows;
+            // it hands the partner the other two columns' values.
+#pragma unroll
+            for (int ro = 0; ro < 2; ++ro)
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int oy = by + ro, ox = bx + 2 * half + k;
+                    float2 prod[2];
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const float2 lo = acc[ro][k][i], hi = acc[ro][2 + k][i];
+                        const float2 mine = half ? hi : lo;
+                        const float2 give = half ? lo : hi;
+                        const float gx = __shfl_xor_sync(0xffffffffu, give.x, 1);
+                        const float gy = __shfl_xor_sync(0xffffffffu, give.y, 1);
+                        prod[i] = make_float2(mine.x * gx, mine.y * gy);
+                    }
+                    const uint32_t h01 = pack_half2(prod[0].x, prod[0].y), h23 = pack_half2(prod[1].x, prod[1].y);
+                    *reinterpret_cast<uint2*>(sGo + ((oy * G::TW + ox) * D + cg * 4) * 2) = make_uint2(h01, h23);
+                    if (ty0 + oy < p.H && tx0 + ox < p.W) {  // pool the stored fp16 values
+                        const float2 f01 = unpack_half2(h01), f23 = unpack_half2(h23);
+                        ps[0] += f01.x;
+                        ps[1] += f01.y;
+                        ps[2] += f23.x;
+                        ps[3] += f23.y;
                     }
                 }
-            }
-#pragma unroll
-            for (int rowi = 0; rowi < 2; ++rowi) {
-                float o[8];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 a = rowi ? a1[i] : a0[i];
-                    o[2 * i] = a.x * __shfl_xor_sync(0xffffffffu, a.x, 1);
-                    o[2 * i + 1] = a.y * __shfl_xor_sync(0xffffffffu, a.y, 1);
-                }
-                if (half == 0) {
-                    const int oy = py + rowi;
-                    const uint4 ov = f_to_h8(o);
-                    *reinterpret_cast<uint4*>(sGo + ((oy * G::TW + px) * D + c0) * 2) = ov;
-                    if (ty0 + oy < p.H && tx0 + px < p.W) {
-                        float q[8];
-                        h8_to_f(ov, q);  // pool the stored fp16 values
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) ps[i] += q[i];
-                    }
-                }
-            }
         }
         fence_async_smem();
         __syncthreads();
@@ -326,18 +349,16 @@ __global__ void __launch_bounds__(kAThreads, 2)
         // (or this is the CTA's last tile): fixed-order reduction.
         const int tn = t + static_cast<int>(gridDim.x);
         if (tn >= total || tn / per_img != img) {
-            if (half == 0) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) sRed[pl * D + c0 + i] = ps[i];
-            }
+            for (int i = 0; i < 4; ++i) sRed[(slot * 2 + half) * D + cg * 4 + i] = ps[i];
             __syncthreads();
             for (int c = tid; c < D; c += kAThreads) {
                 float sum = 0.f;
-                for (int l = 0; l < G::LANES; ++l) sum += sRed[l * D + c];
+                for (int l = 0; l < 2 * G::SLOTS; ++l) sum += sRed[l * D + c];
                 sPart[img * D + c] += sum;
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+            for (int i = 0; i < 4; ++i) ps[i] = 0.f;
             __syncthreads();
         }
     }
