@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "sm100.cuh"
 #include "status.h"
 
@@ -49,10 +50,12 @@ __global__ void __launch_bounds__(256) intro_kernel(const __grid_constant__ Intr
     const int tid = threadIdx.x;
     const int K = Cin * 9;
     const int Kp = (K + 3) & ~3;
+    pdl_trigger();
     for (int i = tid; i < C0 * Kp; i += 256) {
         const int o = i / Kp, k = i - o * Kp;
         sw[i] = k < K ? p.w[o * K + k] : 0.f;
     }
+    pdl_wait();
     const int area = (kTile + 2) * (kTile + 2);
     for (int i = tid; i < Cin * area; i += 256) {
         const int c = i / area;
@@ -131,7 +134,9 @@ __global__ void __launch_bounds__(256) ending_kernel(const __grid_constant__ End
     const int img = blockIdx.z;
     const int ty0 = blockIdx.y * kTile, tx0 = blockIdx.x * kTile;
     const int tid = threadIdx.x;
+    pdl_trigger();
     for (int i = tid; i < 27 * C0; i += 256) sw[i] = p.w[i];
+    pdl_wait();
     const __half* xin = p.x + static_cast<size_t>(img) * p.Hp * p.Wp * C0;
     const int vec = C0 / 8;
     for (int i = tid; i < area * vec; i += 256) {
@@ -192,7 +197,8 @@ int launch_intro(const IntroParams& p, cudaStream_t s) {
         configured = true;
     }
     dim3 grid((p.Wp + kTile - 1) / kTile, (p.Hp + kTile - 1) / kTile, p.N);
-    intro_kernel<<<grid, 256, smem, s>>>(p);
+    const cudaError_t le = launch_pdl(intro_kernel, grid, dim3(256), smem, s, p);
+    if (le != cudaSuccess) return dn_cuda_fail(le, "intro: launch");
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "intro: launch");
 }
@@ -210,7 +216,8 @@ int launch_ending(const EndingParams& p, cudaStream_t s) {
         configured = true;
     }
     dim3 grid((p.W + kTile - 1) / kTile, (p.H + kTile - 1) / kTile, p.N);
-    ending_kernel<<<grid, 256, smem, s>>>(p);
+    const cudaError_t le = launch_pdl(ending_kernel, grid, dim3(256), smem, s, p);
+    if (le != cudaSuccess) return dn_cuda_fail(le, "ending: launch");
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "ending: launch");
 }

@@ -20,6 +20,7 @@
 #include <algorithm>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "sm100.cuh"
 #include "status.h"
 
@@ -57,9 +58,11 @@ __global__ void __launch_bounds__(kThreads) dw_gate_kernel(const __grid_constant
     float* sw = sm;
     float* sb = sw + 9 * C2;
     float* red = sb + C2;
+    pdl_trigger();
     for (int i = tid; i < 9 * C2; i += kThreads) sw[i] = p.w[i];
     for (int i = tid; i < C2; i += kThreads) sb[i] = p.b[i];
     __syncthreads();
+    pdl_wait();
     const __half* u = p.u + static_cast<size_t>(img) * HW * C2;
     __half* g = p.g + static_cast<size_t>(img) * HW * D;
     const int c0 = cg * 8;
@@ -137,6 +140,17 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
     const int warp = tid >> 5, lane = tid & 31;
     const int img = blockIdx.y;
     const int nvec = D / 4;
+    pdl_trigger();
+    // The weight row of this warp's output (constant) loads before the wait.
+    const int o = blockIdx.x * 8 + warp;  // 8 warps -> 8 outputs
+    float4 w[kScaVec];
+#pragma unroll
+    for (int i = 0; i < kScaVec; ++i) {
+        const int v = lane + 32 * i;
+        w[i] = (o < D && v < nvec) ? reinterpret_cast<const float4*>(p.sca_w + static_cast<size_t>(o) * D)[v]
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    pdl_wait();
     // Fixed-order pool: warp w sums partial rows w, w+8, ... in order; the 8
     // warp sums are then added in warp order.
     const float4* pp = reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(img) * nb * D);
@@ -172,15 +186,7 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
         mean[c] = s * inv;
     }
     __syncthreads();
-    const int o = blockIdx.x * 8 + warp;  // 8 warps -> 8 outputs
     if (o < D) {
-        const float4* wr = reinterpret_cast<const float4*>(p.sca_w + static_cast<size_t>(o) * D);
-        float4 w[kScaVec];
-#pragma unroll
-        for (int i = 0; i < kScaVec; ++i) {
-            const int v = lane + 32 * i;
-            w[i] = v < nvec ? wr[v] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
         float s = 0.f;
 #pragma unroll
         for (int i = 0; i < kScaVec; ++i) {
@@ -219,8 +225,7 @@ int launch_sca_v(const DwParams& p, int nb, cudaStream_t s) {
         if (e != cudaSuccess) return dn_cuda_fail(e, "sca: set smem attribute");
         configured = true;
     }
-    sca_kernel<V><<<dim3((p.D + 7) / 8, p.N), kThreads, smem, s>>>(p, nb);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(sca_kernel<V>, dim3((p.D + 7) / 8, p.N), dim3(kThreads), smem, s, p, nb);
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "sca: launch");
 }
 
@@ -247,8 +252,7 @@ int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s) {
         if (e != cudaSuccess) return dn_cuda_fail(e, "dw_gate: set smem attribute");
         configured = true;
     }
-    dw_gate_kernel<<<dim3(blocks_per_img, p.N), kThreads, smem, s>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(dw_gate_kernel, dim3(blocks_per_img, p.N), dim3(kThreads), smem, s, p);
     if (e != cudaSuccess) return dn_cuda_fail(e, "dw_gate: launch");
     return launch_sca(p, blocks_per_img, s);
 }

@@ -22,6 +22,7 @@
 #include <string>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "sm100.cuh"
 #include "status.h"
 
@@ -64,12 +65,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int D = p.D;
     const int cs0 = blockIdx.y * kCS;
 
+    pdl_trigger();
     if (tid == 0) {
         mbar_init(&bar, 1);
         fence_mbar_init();
-        mbar_arrive_expect_tx(&bar, 2 * kP * kRowB);
-        tma_load_4d(sHalf0, &mu, cs0, tx0 - 1, ty0 - 1, img, &bar);
-        tma_load_4d(sHalf1, &mu, D + cs0, tx0 - 1, ty0 - 1, img, &bar);
     }
     const int lane = tid & 31;
     const int cg = lane & 3;
@@ -85,6 +84,13 @@ __global__ void __launch_bounds__(kThreads, 2)
             w[t][i] = make_float2(p.w[t * 2 * D + cin + 2 * i], p.w[t * 2 * D + cin + 2 * i + 1]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) bias[i] = make_float2(p.b[cin + 2 * i], p.b[cin + 2 * i + 1]);
+    __syncthreads();  // barrier initialised before anyone waits on it
+    pdl_wait();
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&bar, 2 * kP * kRowB);
+        tma_load_4d(sHalf0, &mu, cs0, tx0 - 1, ty0 - 1, img, &bar);
+        tma_load_4d(sHalf1, &mu, D + cs0, tx0 - 1, ty0 - 1, img, &bar);
+    }
     const bool ok = mbar_wait(&bar, 0);
     if (!__syncthreads_and(ok)) {
         if (tid == 0) report_error(p.err, 0x50, kErrMbarTimeout);
@@ -193,8 +199,7 @@ int launch_dw_tile(const DwParams& p, cudaStream_t s) {
     if (rc == DN_OK) rc = encode4(&mg, p.g, p.D, p.W, p.H, p.N, kCS, kTW, kTH);
     if (rc != DN_OK) return rc;
     const int tiles = dw_tile_blocks_per_img(p.H, p.W);
-    dw_tile_kernel<<<dim3(tiles, p.D / kCS, p.N), kThreads, kSmem, s>>>(p, mu, mg);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(dw_tile_kernel, dim3(tiles, p.D / kCS, p.N), dim3(kThreads), kSmem, s, p, mu, mg);
     if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: launch");
     return launch_sca(p, tiles, s);
 }

@@ -35,6 +35,7 @@
 #include <string>
 
 #include "fused_block.h"
+#include "launch.cuh"
 #include "sm100.cuh"
 #include "status.h"
 
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(kAThreads, 2)
         tx0 = (r % tiles_x) * G::TW;
     };
 
+    pdl_trigger();
     for (int i = tid; i < G::N1; i += kAThreads) sC2[i] = p.c2[i];
     for (int i = tid; i < 8 * D; i += kAThreads) sPart[i] = 0.f;
     if (warp == 0) {
@@ -150,17 +152,18 @@ __global__ void __launch_bounds__(kAThreads, 2)
         fence_mbar_init();
         mbar_arrive_expect_tx(&bar_w, G::W1_BYTES);
         bulk_g2s(sW1, p.w1, G::W1_BYTES, &bar_w);
-        if (blockIdx.x < total) {
-            int img, ty0, tx0;
-            decode(blockIdx.x, img, ty0, tx0);
-            mbar_arrive_expect_tx(&bar_x, G::P * G::ROWB);
-            tma_load_4d(sA, &mx, 0, tx0 - 1, ty0 - 1, img, &bar_x);
-        }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    pdl_wait();  // x was written by the previous kernel
+    if (tid == 0 && blockIdx.x < total) {
+        int img, ty0, tx0;
+        decode(blockIdx.x, img, ty0, tx0);
+        mbar_arrive_expect_tx(&bar_x, G::P * G::ROWB);
+        tma_load_4d(sA, &mx, 0, tx0 - 1, ty0 - 1, img, &bar_x);
+    }
     const bool ok = __syncthreads_and(wait_bar(&bar_w, 0, p.err, 0x30)) != 0;
 
     // Depthwise mapping: gate half fastest (pairs meet through one shuffle),
@@ -413,8 +416,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
         sB5[i] = p.b5[i];
         sGam[i] = p.gamma[i];
     }
+    pdl_trigger();
     for (int i = tid; i < 2 * F; i += kBThreads) sB4[i] = p.b4[i];
-    for (int i = tid; i < nimg * D; i += kBThreads) sS[i] = p.s[i];
     if (warp == 0) {
         tmem_alloc(&tslot, G::TMEM_COLS);
         tmem_relinquish();
@@ -429,16 +432,18 @@ __global__ void __launch_bounds__(kBThreads, 1)
         bulk_g2s(sW3, p.w3, G::W3_BYTES, &bar_w);
         bulk_g2s(sW4, p.w4, G::W4_BYTES, &bar_w);
         bulk_g2s(sW5, p.w5, G::W5_BYTES, &bar_w);
-        if (blockIdx.x < tiles) {
-            mbar_arrive_expect_tx(&bar_ld, G::G_BYTES + G::X_BYTES);
-            tma_load_2d(sG, &mg, 0, blockIdx.x * 128, &bar_ld);
-            tma_load_2d(sX, &mx, 0, blockIdx.x * 128, &bar_ld);
-        }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    pdl_wait();  // g, x and the SCA scale come from earlier kernels
+    for (int i = tid; i < nimg * D; i += kBThreads) sS[i] = p.s[i];
+    if (tid == 0 && blockIdx.x < tiles) {
+        mbar_arrive_expect_tx(&bar_ld, G::G_BYTES + G::X_BYTES);
+        tma_load_2d(sG, &mg, 0, blockIdx.x * 128, &bar_ld);
+        tma_load_2d(sX, &mx, 0, blockIdx.x * 128, &bar_ld);
+    }
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const bool ok = __syncthreads_and(wait_bar(&bar_w, 0, p.err, 0x40)) != 0;
     uint32_t mma_phase = 0;
@@ -652,8 +657,7 @@ int run_a(const FusedAParams& p, int grid, cudaStream_t s) {
     const cuuint32_t bg[4] = {static_cast<cuuint32_t>(D), G::TW, G::TH, 1};
     rc = encode(&mg, 4, p.g, dg, sg, bg, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != DN_OK) return rc;
-    kern<<<grid, kAThreads, G::SMEM, s>>>(p, mx, mg);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kAThreads), G::SMEM, s, p, mx, mg);
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "fused_a: launch");
 }
 
@@ -681,8 +685,7 @@ int run_b(const FusedBParams& p, cudaStream_t s) {
     const int tiles = (p.M + 127) / 128;
     const int per_sm = std::max(1, std::min(512 / G::TMEM_COLS, (227 * 1024) / (G::SMEM + 2048)));
     const int grid = std::min(tiles, sm_count() * per_sm);
-    kern<<<grid, kBThreads, G::SMEM, s>>>(p, mg, mx, mo);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kBThreads), G::SMEM, s, p, mg, mx, mo);
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "fused_b: launch");
 }
 

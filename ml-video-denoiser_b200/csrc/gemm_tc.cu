@@ -41,6 +41,7 @@
 #include <string>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "sm100.cuh"
 #include "status.h"
 
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_tiles_total = m_tiles * p.n_tiles;
     const bool one_img = p.M <= p.hw;
 
+    pdl_trigger();
     // Parameter vectors -> shared memory (c2 of the LN fold lives in s_bias).
     for (int i = tid; i < p.n_tiles * NT; i += kThreads) {
         s_bias[i] = p.bias ? p.bias[i] : 0.f;
@@ -195,8 +197,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (EPI == kEpiResidual)
         for (int i = tid; i < p.n_out; i += kThreads) s_rsc[i] = p.res_scale[i];
-    if (PRO == kProScale && one_img)
-        for (int i = tid; i < p.K; i += kThreads) s_sca[i] = p.pro_scale[i];
     if (warp == 0) {
         tmem_alloc(&tslot, kCols);
         tmem_relinquish();
@@ -221,6 +221,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    // Everything above touched only weights; activations (A, the residual,
+    // the SCA scale) were written by earlier kernels.
+    pdl_wait();
+    if (PRO == kProScale && one_img) {
+        for (int i = tid; i < p.K; i += kThreads) s_sca[i] = p.pro_scale[i];
+        __syncthreads();
+    }
 
     if (warp == 12) {
         // ------------------------------ TMA producer ------------------------------
@@ -710,8 +717,7 @@ int launch_one(const GemmParams& p, cudaStream_t s) {
     const int by_smem = (227 * 1024) / (smem + 2048);
     const int per_sm = std::max(1, std::min(by_tmem, by_smem));
     const long long grid = std::min<long long>(tiles, static_cast<long long>(num_sms()) * per_sm);
-    kern<<<static_cast<unsigned>(grid), kThreads, smem, s>>>(p, maps);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem, s, p, maps);
     if (e != cudaSuccess) return dn_cuda_fail(e, "gemm: launch");
     return DN_OK;
 }

@@ -1,0 +1,38 @@
+// Kernel launches with programmatic dependent launch (PDL).
+//
+// Every kernel of the forward is launched with programmatic stream
+// serialisation: the next kernel in the stream may start as soon as every
+// CTA of the current one has executed pdl_trigger(), so its launch and its
+// prologue (weight loads, shared-memory set-up, TMEM allocation, barrier
+// init) overlap the tail of the current kernel. Each kernel calls
+// pdl_wait() before it reads anything an earlier kernel wrote and before
+// its first global write; pdl_wait() returns once the preceding kernel has
+// completed and its writes are visible (so ordering stays transitive along
+// the stream).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <utility>
+
+namespace dnb {
+
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+}  // namespace dnb

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "sm100.cuh"
 #include "status.h"
 
@@ -16,6 +17,8 @@ namespace {
 __global__ void warp_pixel_kernel(const __half* __restrict__ feat, const __half* __restrict__ off,
                                   int off_stride, __half* __restrict__ out, int nimg, int H, int W,
                                   int C) {
+    pdl_trigger();
+    pdl_wait();
     const int groups = C / 8;
     const long long total = static_cast<long long>(nimg) * H * W * groups;
     const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -64,8 +67,7 @@ int launch_warp_pixel(const __half* feat, const __half* off, int off_stride, __h
     if (C % 8 != 0) return dn_fail(DN_ERR_UNSUPPORTED, "warp: channels must be a multiple of 8");
     const long long total = static_cast<long long>(nimg) * H * W * (C / 8);
     const int blocks = static_cast<int>((total + 255) / 256);
-    warp_pixel_kernel<<<blocks, 256, 0, s>>>(feat, off, off_stride, out, nimg, H, W, C);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(warp_pixel_kernel, dim3(blocks), dim3(256), 0, s, feat, off, off_stride, out, nimg, H, W, C);
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "warp: launch");
 }
 
