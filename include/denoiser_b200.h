@@ -85,7 +85,7 @@ int dn_weights_arch(const dn_weights* weights, char* type_buf, int type_buf_len,
 typedef struct dn_model dn_model;
 
 typedef struct dn_model_info {
-    int kind;            /* 0 NAFNet, 1 NAFNetTemporal (C++ engine design) */
+    int kind;            /* 0 NAFNet, 1 NAFNetTemporal (C++ engine design), 2 NAFNetTemporal (PyTorch design: bottleneck_mix, temporal_mix.N.0, 3-layer offset heads) */
     int in_channels;     /* NAFNet::in_channels()                           */
     int num_levels;      /* NAFNet::num_levels()                            */
     int base_channels;

@@ -123,6 +123,16 @@ int dn_launch_pixel_shuffle2x(const void* input, void* output, int N, int C_in, 
 int dn_launch_warp_bilinear(const void* feat, const void* offset, void* output, int N, int C, int H, int W,
                             void* stream);
 
+/* UpsampleLayer::forward (include/denoiser/layers/upsample.h:19-26): output
+ * (N,C,H*s,W*s) = bilinear upsampling of input (N,C,H,W) by the integer
+ * factor s = scale_factor, with the reference kernel's coordinate rule
+ * (src/layers/upsample.cu:10-45): source (o + 0.5)/s - 0.5, low corner
+ * clamped to 0 with the weight from the unclamped coordinate, high corner
+ * clamped to the edge. DN_ERR_INVALID_ARG for scale_factor <= 0 (the
+ * reference throws std::invalid_argument). */
+int dn_upsample_bilinear(const void* input, void* output, int N, int C, int H, int W, int scale_factor,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -103,6 +103,7 @@ SIGNATURES = {
     "dn_launch_scaled_add": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
     "dn_launch_pixel_shuffle2x": (_I, [_P, _P, _I, _I, _I, _I, _P]),
     "dn_launch_warp_bilinear": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "dn_upsample_bilinear": (_I, [_P, _P, _I, _I, _I, _I, _I, _P]),
 }
 
 

@@ -11,7 +11,8 @@
 namespace dnb {
 
 int launch_warp_pixel(const __half* feat, const __half* off, int off_stride, __half* out, int nimg,
-                      int H, int W, int C, cudaStream_t s);
+                      int H, int W, int C, float sx, float sy, cudaStream_t s);
+int launch_dw_pair(const __half* a, const __half* b, const float* w, __half* out, int H, int W, int C, cudaStream_t s);
 
 namespace {
 
@@ -337,8 +338,54 @@ void Engine::build(const HostWeights& hw) {
     // Temporal models.
     const bool legacy = hw.contains("temporal_mix.0.weight");
     const bool pyt = hw.contains("temporal_mix.0.0.weight");
-    if (pyt) throw FormatError("NAFNetTemporal (bottleneck_mix / temporal_mix.N.0 export) is not supported by this build");
-    if (legacy) {
+    // NAFBlocks of a mix stage: root.1, root.2, ... (root.0 is the 1x1 conv).
+    auto mix_blocks = [&](const std::string& root, int Cl) {
+        std::vector<BlockW> v;
+        for (int i = 1; hw.contains(root + "." + std::to_string(i) + ".conv1.weight"); ++i)
+            v.push_back(block(root + "." + std::to_string(i), Cl));
+        return v;
+    };
+    if (pyt) {
+        info_.kind = 2;
+        const auto& s0 = hw.entry("temporal_mix.0.0.weight").shape;
+        if (s0.size() != 4 || s0[1] % C0 != 0) throw FormatError("temporal_mix.0.0.weight: unexpected shape");
+        const int T = static_cast<int>(s0[1] / C0);
+        if (T < 2) throw FormatError("temporal model needs num_frames >= 2");
+        if (T > kMaxSeg) throw FormatError("temporal model: num_frames > 8 is not supported");
+        info_.num_frames = T;
+        info_.use_warp = hw.contains("offset_heads.0.0.weight") ? 1 : 0;
+        const int Cd = levels_[levels - 1].C * 2;
+        expect_shape(hw, "bottleneck_mix.0.weight", {Cd, static_cast<int64_t>(T) * Cd, 1, 1});
+        expect_shape(hw, "bottleneck_mix.0.bias", {Cd});
+        const auto bb = hw.to_f32("bottleneck_mix.0.bias");
+        bneck_ = pack_gemm(pk, hw.to_f32("bottleneck_mix.0.weight"), Cd, T * Cd, store_nt(Cd), &bb, Cd, LnFold{}, Cd);
+        bneck_blocks_ = mix_blocks("bottleneck_mix", Cd);
+        for (int l = 0; l < levels; ++l) {
+            const int Cl = levels_[l].C;
+            const std::string tn = "temporal_mix." + std::to_string(l);
+            expect_shape(hw, tn + ".0.weight", {Cl, static_cast<int64_t>(T) * Cl, 1, 1});
+            expect_shape(hw, tn + ".0.bias", {Cl});
+            const auto tb = hw.to_f32(tn + ".0.bias");
+            tmix_.push_back(pack_gemm(pk, hw.to_f32(tn + ".0.weight"), Cl, T * Cl, store_nt(Cl), &tb, Cl, LnFold{}, Cl));
+            tmix_blocks_.push_back(mix_blocks(tn, Cl));
+            if (info_.use_warp) {
+                const std::string on = "offset_heads." + std::to_string(l);
+                expect_shape(hw, on + ".0.weight", {2 * Cl, 1, 3, 3});
+                expect_shape(hw, on + ".1.weight", {Cl, 2 * Cl, 1, 1});
+                expect_shape(hw, on + ".3.weight", {2, Cl, 1, 1});
+                expect_shape(hw, on + ".3.bias", {2});
+                const auto w0 = hw.to_f32(on + ".0.weight");
+                std::vector<float> wt(9 * 2 * Cl);
+                for (int c = 0; c < 2 * Cl; ++c)
+                    for (int t = 0; t < 9; ++t) wt[t * 2 * Cl + c] = w0[c * 9 + t];
+                oh_dw_.push_back(pk.add_f32(wt));
+                oh_pw1_.push_back(pack_gemm(pk, hw.to_f32(on + ".1.weight"), Cl, 2 * Cl, store_nt(Cl), nullptr, Cl));
+                const auto b3 = hw.to_f32(on + ".3.bias");
+                // 2 outputs padded to an 8-channel row (dx, dy, 0 x 6).
+                oh_pw2_.push_back(pack_gemm(pk, hw.to_f32(on + ".3.weight"), 2, Cl, 16, &b3, 8));
+            }
+        }
+    } else if (legacy) {
         info_.kind = 1;
         const int T = hw.arch().num_frames > 0 ? hw.arch().num_frames : 3;
         if (T < 2) throw FormatError("temporal model needs num_frames >= 2");
@@ -430,6 +477,10 @@ void Engine::plan(const Shape& s) {
     const int Cm = levels_[L - 1].C * 2;
     req.push_back({n_enc * hwm * Cm * 2, reinterpret_cast<void**>(&mid_x_)});
     account(middle_, 1 * (temporal ? 1 : n_enc), hm, wm);
+    if (info_.kind == 2) {
+        account(bneck_blocks_, 1, hm, wm);
+        for (int l = 0; l < L; ++l) account(tmix_blocks_[l], 1, s.Hp >> l, s.Wp >> l);
+    }
     req.push_back({u * 2, reinterpret_cast<void**>(&buf_u_)});
     req.push_back({g * 2, reinterpret_cast<void**>(&buf_g_)});
     req.push_back({y * 2, reinterpret_cast<void**>(&buf_y_)});
@@ -438,6 +489,14 @@ void Engine::plan(const Shape& s) {
         const size_t hw0 = static_cast<size_t>(s.Hp) * s.Wp;
         req.push_back({static_cast<size_t>(s.T) * hw0 * levels_[0].C * 2, reinterpret_cast<void**>(&warp_buf_)});
         req.push_back({hw0 * 8 * 2, reinterpret_cast<void**>(&offset_buf_)});
+    }
+    if (info_.kind == 2) {
+        req.push_back({hwm * Cm * 2, reinterpret_cast<void**>(&bneck_x_)});
+        if (info_.use_warp) {
+            const size_t hw0 = static_cast<size_t>(s.Hp) * s.Wp;
+            req.push_back({hw0 * 2 * levels_[0].C * 2, reinterpret_cast<void**>(&oh_d_)});
+            req.push_back({hw0 * levels_[0].C * 2, reinterpret_cast<void**>(&oh_h_)});
+        }
     }
     req.push_back({n_enc * dw_blocks_max_ * dmax * 4, reinterpret_cast<void**>(&partials_)});
     req.push_back({n_enc * 4, reinterpret_cast<void**>(&counters_)});
@@ -808,6 +867,77 @@ int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* 
         return decode(mid_x_, N, enc_x_, x, C * H * W, y);
     }
 
+    if (info_.kind == 2) {
+        // PyTorch NAFNetTemporal (training/models.py:738-808): every frame
+        // through the shared encoder (a batch of T images); bottleneck_mix
+        // over the T deep features, middle, per level temporal_mix over the
+        // T skips (neighbours warped by their offset head when present),
+        // decoder on the fused skips.
+        const int ref = T / 2;
+        const int hm = sh.Hp >> L, wm = sh.Wp >> L;
+        const size_t mplane = static_cast<size_t>(hm) * wm * levels_[L - 1].C * 2;
+        for (int n = 0; n < N; ++n) {
+            const __half* clip = x + static_cast<size_t>(n) * T * C * H * W;
+            DN_TRY(encode(clip, T));
+            GemmParams p = rows_params(1, hm, wm);
+            p.seg_c = levels_[L - 1].C * 2;
+            p.nseg = T;
+            for (int t = 0; t < T; ++t) p.a[t] = mid_x_ + t * mplane;
+            p.out = bneck_x_;
+            p.out_c = p.seg_c;
+            DN_TRY(gemm(bneck_, kProNone, kEpiStore, kARows, p, s));
+            DN_TRY(run_stage(bneck_blocks_, bneck_x_, 1, hm, wm, s));
+            for (int l = 0; l < L; ++l) {
+                const int h = sh.Hp >> l, w = sh.Wp >> l, Cl = levels_[l].C;
+                const size_t plane = static_cast<size_t>(h) * w * Cl;
+                const __half* rf = enc_x_[l] + ref * plane;
+                GemmParams q = rows_params(1, h, w);
+                q.seg_c = Cl;
+                q.nseg = T;
+                int wi = 0;
+                for (int t = 0; t < T; ++t) {
+                    const __half* f = enc_x_[l] + t * plane;
+                    if (info_.use_warp && t != ref) {
+                        // offset head: DW 3x3 over [ref, f] -> PW -> ReLU -> PW -> (dx, dy)
+                        ++launches_;
+                        prof_begin("offset_dw", static_cast<double>(h) * w * 6 * Cl * 2, 36.0 * h * w * Cl, s);
+                        DN_TRY(launch_dw_pair(rf, f, wptr<float>(oh_dw_[l]), oh_d_, h, w, Cl, s));
+                        prof_end(s);
+                        GemmParams o = rows_params(1, h, w);
+                        o.seg_c = 2 * Cl;
+                        o.a[0] = oh_d_;
+                        o.out = oh_h_;
+                        o.out_c = Cl;
+                        o.relu = 1;
+                        DN_TRY(gemm(oh_pw1_[l], kProNone, kEpiStore, kARows, o, s));
+                        o = rows_params(1, h, w);
+                        o.seg_c = Cl;
+                        o.a[0] = oh_h_;
+                        o.out = offset_buf_;
+                        o.out_c = 8;
+                        DN_TRY(gemm(oh_pw2_[l], kProNone, kEpiStore, kARows, o, s));
+                        __half* wb = warp_buf_ + wi * plane;
+                        ++wi;
+                        ++launches_;
+                        prof_begin("warp", static_cast<double>(h) * w * (2 * Cl + 16) * 2, 8.0 * h * w * Cl, s);
+                        DN_TRY(launch_warp_pixel(f, offset_buf_, 8, wb, 1, h, w, Cl, static_cast<float>(w - 1) / w,
+                                                 static_cast<float>(h - 1) / h, s));
+                        prof_end(s);
+                        f = wb;
+                    }
+                    q.a[t] = f;
+                }
+                q.out = fused_skip_[l];
+                q.out_c = Cl;
+                DN_TRY(gemm(tmix_[l], kProNone, kEpiStore, kARows, q, s));
+                DN_TRY(run_stage(tmix_blocks_[l], fused_skip_[l], 1, h, w, s));
+            }
+            const __half* beauty = clip + static_cast<size_t>(ref) * C * H * W;
+            DN_TRY(decode(bneck_x_, 1, fused_skip_, beauty, C * H * W, y + static_cast<size_t>(n) * 3 * H * W));
+        }
+        return DN_OK;
+    }
+
     // Temporal model of the C++ engine (nafnet_temporal.cu:363-503): every
     // frame of the clip through the shared encoder (as a batch of T images),
     // middle on the reference frame, per-level fused skip
@@ -842,7 +972,7 @@ int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* 
                     __half* wb = warp_buf_ + (si - 1) * plane;
                     ++launches_;
                     prof_begin("warp", static_cast<double>(h) * w * (2 * Cl + 16) * 2, 8.0 * h * w * Cl, s);
-                    DN_TRY(launch_warp_pixel(nb, offset_buf_, 8, wb, 1, h, w, Cl, s));
+                    DN_TRY(launch_warp_pixel(nb, offset_buf_, 8, wb, 1, h, w, Cl, 1.f, 1.f, s));
                     prof_end(s);
                     nb = wb;
                 }

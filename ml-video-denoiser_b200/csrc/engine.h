@@ -128,6 +128,15 @@ private:
     // and optional offset heads (1x1, 2C -> 2).
     std::vector<GemmW> tmix_;
     std::vector<GemmW> offset_heads_;
+    // temporal (PyTorch design, training/models.py:651-808): bottleneck_mix
+    // (T*C -> C 1x1 + NAFBlocks) on the T deep features, per level
+    // temporal_mix (T*C -> C 1x1 + NAFBlocks) on the T skips, and optional
+    // offset heads (DW 3x3 -> PW 2C->C -> ReLU -> PW C->2) with grid_sample warp.
+    GemmW bneck_;
+    std::vector<BlockW> bneck_blocks_;
+    std::vector<std::vector<BlockW>> tmix_blocks_;
+    std::vector<size_t> oh_dw_;               // fp32 [9][2C] per level
+    std::vector<GemmW> oh_pw1_, oh_pw2_;
 
     // activations
     Shape shape_{};
@@ -138,7 +147,10 @@ private:
     __half *buf_u_ = nullptr, *buf_g_ = nullptr, *buf_y_ = nullptr, *buf_t_ = nullptr;
     std::vector<__half*> fused_skip_;     // temporal: fused skip per level
     __half* warp_buf_ = nullptr;          // temporal: warped neighbours [T-1][...]
-    __half* offset_buf_ = nullptr;        // temporal: offsets [HW][16]
+    __half* offset_buf_ = nullptr;        // temporal: offsets [HW][8]
+    __half* bneck_x_ = nullptr;           // temporal (PyTorch design): fused deep feature
+    __half* oh_d_ = nullptr;              // offset head: depthwise output [HW][2C]
+    __half* oh_h_ = nullptr;              // offset head: hidden layer [HW][C]
     float* partials_ = nullptr;
     unsigned* counters_ = nullptr;
     float* sca_s_ = nullptr;

@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 else w2 += s_bias[nb2 + i];
                                 v *= w2;
                             }
-                            f[i] = v;
+                            f[i] = (EPI == kEpiStore && p.relu) ? fmaxf(v, 0.f) : v;
                         }
                         if (EPI == kEpiShuffleAdd) {
                             const int cout = p.out_c;
@@ -575,6 +575,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int g = 0; g < kStep / 8; ++g) {
                         float2 y[4];
                         fold8(va + 8 * g, n + 8 * g, y);
+                        if (EPI == kEpiStore && p.relu) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) y[i] = make_float2(fmaxf(y[i].x, 0.f), fmaxf(y[i].y, 0.f));
+                        }
                         uint4* sp = reinterpret_cast<uint4*>(stg + Stg::off(r, (c0 >> 3) + g));
                         if (EPI == kEpiResidual) {
                             const uint4 rv = *sp;

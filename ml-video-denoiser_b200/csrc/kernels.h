@@ -55,6 +55,7 @@ struct GemmParams {
     const float* res_scale;    // [n_out]
     const __half* skip;        // shuffle-add skip (layout of out)
     uint32_t* err;
+    int relu;                  // store epilogue: max(y, 0) (offset-head hidden layer)
 };
 
 // NT in {16, 32, 64, 128, 256}

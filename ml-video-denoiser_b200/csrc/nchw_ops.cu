@@ -457,6 +457,44 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // ---------------------------------------------------------------------------
+// Bilinear upsampling by an integer factor (UpsampleLayer's kernel,
+// src/layers/upsample.cu:10-45): source coordinate (o + 0.5) / s - 0.5, the
+// low corner clamped to >= 0 but the weight taken from the unclamped
+// coordinate, so the first output row/column extrapolates slightly (as the
+// reference does); the high corner is clamped to the last row/column.
+// One thread = one output element; consecutive threads write consecutive
+// columns.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads)
+    upsample_kernel(const __half* __restrict__ in, __half* __restrict__ out, int H, int W, int Ho, int Wo,
+                    float scale, int64_t total) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int wo = static_cast<int>(i % Wo);
+        const int64_t r = i / Wo;
+        const int ho = static_cast<int>(r % Ho);
+        const int64_t plane = r / Ho;
+        const float hf = (static_cast<float>(ho) + 0.5f) / scale - 0.5f;
+        const float wf = (static_cast<float>(wo) + 0.5f) / scale - 0.5f;
+        const int h0 = max(0, static_cast<int>(floorf(hf)));
+        const int w0 = max(0, static_cast<int>(floorf(wf)));
+        const int h1 = min(h0 + 1, H - 1);
+        const int w1 = min(w0 + 1, W - 1);
+        const float dh = hf - static_cast<float>(h0);
+        const float dw = wf - static_cast<float>(w0);
+        const __half* src = in + plane * H * W;
+        const float v00 = __half2float(src[static_cast<int64_t>(h0) * W + w0]);
+        const float v01 = __half2float(src[static_cast<int64_t>(h0) * W + w1]);
+        const float v10 = __half2float(src[static_cast<int64_t>(h1) * W + w0]);
+        const float v11 = __half2float(src[static_cast<int64_t>(h1) * W + w1]);
+        const float val = v00 * (1.f - dh) * (1.f - dw) + v01 * (1.f - dh) * dw + v10 * dh * (1.f - dw) +
+                          v11 * dh * dw;
+        out[i] = __float2half(val);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Row copies (pad / crop / extract / prefix / concat): one warp per row
 // ---------------------------------------------------------------------------
 
@@ -801,6 +839,21 @@ int dn_launch_pixel_shuffle2x(const void* input, void* output, int N, int C_in, 
         shuffle_kernel<false><<<grid_for(total, kThreads), kThreads, 0, to_stream(stream)>>>(hin, hout, Cout, H, W,
                                                                                             total);
     return launched("dn_launch_pixel_shuffle2x");
+}
+
+int dn_upsample_bilinear(const void* input, void* output, int N, int C, int H, int W, int scale_factor,
+                         void* stream) {
+    if (scale_factor <= 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_upsample_bilinear: scale_factor must be > 0");
+    if (any_negative({N, C, H, W})) return dn_fail(DN_ERR_INVALID_ARG, "dn_upsample_bilinear: negative size");
+    const int64_t Ho = static_cast<int64_t>(H) * scale_factor, Wo = static_cast<int64_t>(W) * scale_factor;
+    if (Ho > 0x7fffffff || Wo > 0x7fffffff) return dn_fail(DN_ERR_INVALID_ARG, "dn_upsample_bilinear: output too large");
+    const int64_t total = static_cast<int64_t>(N) * C * Ho * Wo;
+    if (total == 0) return DN_OK;
+    if (!input || !output) return dn_fail(DN_ERR_INVALID_ARG, "dn_upsample_bilinear: null pointer");
+    upsample_kernel<<<grid_for(total, kThreads), kThreads, 0, to_stream(stream)>>>(
+        static_cast<const __half*>(input), static_cast<__half*>(output), H, W, static_cast<int>(Ho),
+        static_cast<int>(Wo), static_cast<float>(scale_factor), total);
+    return launched("dn_upsample_bilinear");
 }
 
 int dn_launch_warp_bilinear(const void* feat, const void* offset, void* output, int N, int C, int H, int W,

@@ -79,5 +79,10 @@ def launch_pixel_shuffle2x(input, output, N, C_in, H, W, stream=None):
     check(lib().dn_launch_pixel_shuffle2x(_p(input), _p(output), N, C_in, H, W, _s(stream)))
 
 
+def upsample_bilinear(input, output, N, C, H, W, scale_factor=2, stream=None):
+    """UpsampleLayer::forward on an existing output buffer (N, C, H*s, W*s)."""
+    check(lib().dn_upsample_bilinear(_p(input), _p(output), N, C, H, W, scale_factor, _s(stream)))
+
+
 def launch_warp_bilinear(feat, offset, output, N, C, H, W, stream=None):
     check(lib().dn_launch_warp_bilinear(_p(feat), _p(offset), _p(output), N, C, H, W, _s(stream)))

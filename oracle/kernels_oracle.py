@@ -28,6 +28,8 @@ kernels do (``__half2float`` / ``__float2half``).
 * ``scaled_add``              src/kernels/nafnet_kernels.cu:165-180
 * ``pixel_shuffle2x``         src/kernels/nafnet_kernels.cu:182-208
 * ``warp_bilinear``           src/kernels/nafnet_kernels.cu:210-262
+* ``upsample_bilinear``       src/layers/upsample.cu:10-45 (UpsampleLayer's
+                              kernel: unclamped weights at the low border)
 
 The restatements are pinned against torch's own CPU operators (F.pad
 reflect, F.pixel_shuffle, channel LayerNorm, mean, grid arithmetic) in
@@ -180,3 +182,27 @@ def warp_bilinear(feat, offset):
         val = (v00 * (one - wy) * (one - wx) + v01 * (one - wy) * wx + v10 * wy * (one - wx) + v11 * wy * wx)
         out[n] = val.astype(F16)
     return out
+
+
+def upsample_bilinear(x, scale: int):
+    """upsample.cu:24-44: src = (o + 0.5) / s - 0.5; low corner max(0, floor(src)),
+    high corner min(low + 1, size - 1); weights from the unclamped src."""
+    f = _f(x)
+    N, C, H, W = f.shape
+    ho = np.arange(H * scale, dtype=F32)
+    wo = np.arange(W * scale, dtype=F32)
+    hf = ((ho + F32(0.5)) / F32(scale) - F32(0.5)).astype(F32)
+    wf = ((wo + F32(0.5)) / F32(scale) - F32(0.5)).astype(F32)
+    h0 = np.maximum(0, np.floor(hf).astype(np.int64))
+    w0 = np.maximum(0, np.floor(wf).astype(np.int64))
+    h1 = np.minimum(h0 + 1, H - 1)
+    w1 = np.minimum(w0 + 1, W - 1)
+    dh = (hf - h0.astype(F32)).astype(F32)[:, None]
+    dw = (wf - w0.astype(F32)).astype(F32)[None, :]
+    one = F32(1)
+    v00 = f[:, :, h0[:, None], w0[None, :]]
+    v01 = f[:, :, h0[:, None], w1[None, :]]
+    v10 = f[:, :, h1[:, None], w0[None, :]]
+    v11 = f[:, :, h1[:, None], w1[None, :]]
+    val = v00 * (one - dh) * (one - dw) + v01 * (one - dh) * dw + v10 * dh * (one - dw) + v11 * dh * dw
+    return val.astype(F16)

@@ -91,3 +91,21 @@ def test_elementwise_and_copies():
     s = rng_half((2, 3), 13)
     want = (torch.from_numpy(a).float() * torch.from_numpy(s).float()[:, :, None, None]).half().numpy()
     assert np.array_equal(ko.mul_channelwise(a, s), want)
+
+
+def test_upsample_matches_torch_away_from_the_low_border():
+    # The reference kernel extrapolates on the first output row/column
+    # (unclamped weight); elsewhere it is PyTorch's align_corners=False bilinear.
+    x = rng_half((1, 3, 7, 9), 14)
+    want = F.interpolate(torch.from_numpy(x).float(), scale_factor=2, mode="bilinear",
+                         align_corners=False).half().numpy()
+    got = ko.upsample_bilinear(x, 2)
+    assert got.shape == want.shape
+    assert ulp_close(got[:, :, 1:, 1:], want[:, :, 1:, 1:], ulps=1)
+    # first output row: source row -0.25 -> weights 1.25 / -0.25 on input rows 0 / 1
+    # (columns from 1 on, where the horizontal weights are PyTorch's)
+    def hrow(r):
+        return F.interpolate(torch.from_numpy(x[:, :, r:r + 1, :]).float(), scale_factor=(1, 2),
+                             mode="bilinear", align_corners=False).numpy()[:, :, 0, :]
+    expect = 1.25 * hrow(0) - 0.25 * hrow(1)
+    assert np.allclose(got[:, :, 0, 1:].astype(np.float32), expect[:, :, 1:], atol=2e-3)

@@ -16,6 +16,7 @@ pytestmark = pytest.mark.gpu
 
 SPATIAL = ["spatial_w16l4_64x64", "spatial_w16l4_37x53", "spatial_w32dw1_48x40", "spatial_w8_9ch_dw2_30x44"]
 LEGACY = ["temporal_legacy_w8l2_t3_warp", "temporal_legacy_w8l2_t5"]
+PYTORCH_TEMPORAL = ["temporal_py_w8l2_t3_warp", "temporal_py_w8l2_t5"]
 
 
 def run_engine(pkg, path, x, fused=True):
@@ -28,7 +29,7 @@ def run_engine(pkg, path, x, fused=True):
 
 
 @pytest.mark.parametrize("fused", [True, False], ids=["fused", "perconv"])
-@pytest.mark.parametrize("name", SPATIAL + LEGACY)
+@pytest.mark.parametrize("name", SPATIAL + LEGACY + PYTORCH_TEMPORAL)
 def test_engine_matches_reference_golden(pkg, tmp_path, name, fused):
     g = load_golden(name)
     path, _ = golden_model_dir(pkg, tmp_path, g["meta"])

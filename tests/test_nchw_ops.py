@@ -216,3 +216,19 @@ def test_invalid_arguments_raise(K, pkg):
         K.launch_global_avg_pool(t, t, 1, 2, 0, 4)
     with pytest.raises(pkg.InvalidArgumentError):
         K.launch_simple_gate(None, t, 1, 1, 4, 4)
+
+
+@pytest.mark.parametrize("shape,scale", [((1, 8, 17, 23), 2), ((2, 3, 5, 7), 3), ((1, 32, 135, 240), 2)])
+def test_upsample_bilinear(K, shape, scale):
+    N, C, H, W = shape
+    x = rng_half(shape, 20)
+    out = empty((N, C, H * scale, W * scale))
+    K.upsample_bilinear(dev(x), out, N, C, H, W, scale)
+    ok, nbad = ulp_close(host(out), ko.upsample_bilinear(x, scale), ulps=1)
+    assert ok, nbad
+
+
+def test_upsample_rejects_bad_scale(K, pkg):
+    t = empty((16,))
+    with pytest.raises(pkg.InvalidArgumentError):
+        K.upsample_bilinear(t, t, 1, 1, 2, 2, 0)
