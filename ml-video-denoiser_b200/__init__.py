@@ -104,6 +104,13 @@ SIGNATURES = {
     "dn_launch_pixel_shuffle2x": (_I, [_P, _P, _I, _I, _I, _I, _P]),
     "dn_launch_warp_bilinear": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "dn_upsample_bilinear": (_I, [_P, _P, _I, _I, _I, _I, _I, _P]),
+    # include/denoiser_b200_layers.h
+    "dn_dcn_create": (_I, [_P, _c.c_char_p, _c.c_char_p, _I, _I, _I, _I, _I, _PP]),
+    "dn_dcn_destroy": (_I, [_P]),
+    "dn_dcn_info": (_I, [_P, _IP, _IP, _IP, _IP, _IP]),
+    "dn_dcn_output_size": (_I, [_P, _I, _I, _IP, _IP]),
+    "dn_dcn_forward": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P]),
+    "dn_dcn_sync": (_I, [_P, _P]),
 }
 
 

@@ -6,14 +6,12 @@
 #include <memory>
 #include <new>
 
+#include "capi_internal.h"
 #include "manifest.h"
 #include "status.h"
 
 using namespace dnb;
 
-struct dn_weights {
-    std::unique_ptr<HostWeights> hw;
-};
 
 extern "C" {
 
