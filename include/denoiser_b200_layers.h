@@ -1,6 +1,6 @@
 /*
- * denoiser_b200_layers.h — C-ABI of the stand-alone layers of the reference's
- * include/denoiser/layers/ that are not part of a model forward.
+ * denoiser_b200_layers.h — C-ABI of the stand-alone convolution layers of the
+ * reference's include/denoiser/layers/ (the model forwards use the engine).
  *
  * Tensors are device pointers to FP16 NCHW data; `stream` is a cudaStream_t
  * (NULL = legacy default stream). Every function returns DN_OK or a negative
@@ -45,6 +45,34 @@ int dn_dcn_forward(dn_dcn* layer, const void* input, const void* offsets, const 
                    int W_in, void* output, void* stream);
 /* Synchronise `stream` and report a device-side error of the layer's kernel. */
 int dn_dcn_sync(dn_dcn* layer, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Conv2dLayer (include/denoiser/layers/conv2d.h:44-63): regular convolution
+ * with symmetric zero padding, stride, dilation and groups, weight
+ * (Cout, Cin/groups, kH, kW) and optional bias (Cout) from the store. One
+ * implicit-GEMM kernel on the tensor cores per 256 output channels (FP32
+ * accumulation), bias fused; the reference runs cuDNN plus a bias pass.
+ * ------------------------------------------------------------------------ */
+typedef struct dn_conv2d dn_conv2d;
+
+/* Conv2dLayer(store, weight_name, bias_name, pad, stride, dilation, groups)
+ * (src/layers/conv2d.cu:16-92); bias_name NULL = std::nullopt. Errors as for
+ * dn_dcn_create (DN_ERR_INVALID_ARG when Cout is not divisible by groups). */
+int dn_conv2d_create(const dn_weights* store, const char* weight_name, const char* bias_name, int pad, int stride,
+                     int dilation, int groups, int device, dn_conv2d** out);
+int dn_conv2d_destroy(dn_conv2d* layer);
+/* out_channels(), in_channels() (= weight dim 1, per group), kernel_h(),
+ * kernel_w(), groups(). */
+int dn_conv2d_info(const dn_conv2d* layer, int* out_channels, int* in_channels, int* kernel_h, int* kernel_w,
+                   int* groups);
+int dn_conv2d_output_size(const dn_conv2d* layer, int H_in, int W_in, int* H_out, int* W_out);
+/* Conv2dLayer::forward (conv2d.cu:94-150): input (N, C, H, W) with
+ * C = in_channels * groups -> output (N, Cout, Ho, Wo), asynchronous on
+ * `stream`; calls on one layer must not overlap (the layer keeps an NHWC
+ * copy of the input). */
+int dn_conv2d_forward(dn_conv2d* layer, const void* input, int N, int C, int H_in, int W_in, void* output,
+                      void* stream);
+int dn_conv2d_sync(dn_conv2d* layer, void* stream);
 
 #ifdef __cplusplus
 }

@@ -111,6 +111,12 @@ SIGNATURES = {
     "dn_dcn_output_size": (_I, [_P, _I, _I, _IP, _IP]),
     "dn_dcn_forward": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "dn_dcn_sync": (_I, [_P, _P]),
+    "dn_conv2d_create": (_I, [_P, _c.c_char_p, _c.c_char_p, _I, _I, _I, _I, _I, _PP]),
+    "dn_conv2d_destroy": (_I, [_P]),
+    "dn_conv2d_info": (_I, [_P, _IP, _IP, _IP, _IP, _IP]),
+    "dn_conv2d_output_size": (_I, [_P, _I, _I, _IP, _IP]),
+    "dn_conv2d_forward": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
+    "dn_conv2d_sync": (_I, [_P, _P]),
 }
 
 

@@ -1,4 +1,9 @@
-// Modulated deformable 3x3 convolution (DCNv2) as one fused implicit GEMM:
+// Stand-alone convolution layers as one fused implicit GEMM each:
+// DeformConv2dLayer (modulated deformable convolution, DCNv2) and
+// Conv2dLayer (regular convolution with any kernel, padding, stride,
+// dilation and groups).
+//
+// Deformable:
 //   out[n, o, y, x] = bias[o] + sum_{g, k, c} W[o, g*cpg + c, k] *
 //                     bilinear(in[n, g*cpg + c], p(y, x, k) + off[n, g, k]) * sigmoid(mask[n, g, k])
 //
@@ -21,6 +26,14 @@
 // pixels of one output plane). Sampling rule (bilinear_sample,
 // deform_im2col.cuh:34-69): zero when h < -1, h > H, w < -1 or w > W;
 // corners outside the image contribute zero.
+//
+// Regular (Conv2dLayer::forward, src/layers/conv2d.cu:94-150, a cuDNN
+// convolution plus a bias pass in the reference): the same kernel with
+// integer sample points, so an A-tile item is one vector copy from the NHWC
+// input (zero outside the image). K runs over (block of cpg input channels,
+// tap, channel); a grouped convolution packs B block-diagonally (weights of
+// input channels outside an output's group are zero), and more than 256
+// output channels run as 256-wide slabs over the same NHWC copy.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -49,9 +62,10 @@ struct DcnParams {
     const __half* off;   // [N][2*dg*KK][Ho][Wo] (dy, dx per (group, tap))
     const __half* msk;   // [N][dg*KK][Ho][Wo] (pre-sigmoid)
     __half* out;         // [N][Cout][Ho][Wo]
-    const uint8_t* bpack;  // [k_chunks][NT x 64] no-swizzle K-major tiles
+    const uint8_t* bpack;  // [k_chunks][NT x 64] no-swizzle K-major tiles (this launch's output slab)
     const float* bias;     // [NT] (zero padded)
     int N, H, W, Ho, Wo, Cin, Cout;
+    int cout_base;         // first output channel of this launch's slab
     int kw, KK, pad, stride, dil, dg, cpg, k_chunks;
     uint32_t* err;
 };
@@ -113,8 +127,12 @@ __device__ __forceinline__ typename Vec<VEC>::T pack_vec(const float (&f)[VEC]) 
     return v;
 }
 
-template <int NT, int VEC>
-__global__ void __launch_bounds__(kThreads, 1) dcn_kernel(const __grid_constant__ DcnParams p) {
+// DEFORM: modulated deformable sampling. Otherwise a regular convolution:
+// the sample points are integer, so each item copies one vector of the NHWC
+// input (zero outside the image = zero padding); `dg` then counts blocks of
+// `cpg` input channels and B is block-diagonal for grouped convolutions.
+template <int NT, int VEC, bool DEFORM>
+__global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant__ DcnParams p) {
     constexpr int kBBytes = NT * kKC * 2;
     constexpr uint32_t kCols = NT < 32 ? 32 : NT;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -177,7 +195,26 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_kernel(const __grid_constant_
                 const int m = tile * 128 + r;
                 float wts[4] = {0.f, 0.f, 0.f, 0.f};
                 const __half* corner[4] = {nullptr, nullptr, nullptr, nullptr};
-                if (m < M && gk < combos) {
+                if (!DEFORM && m < M && gk < combos) {
+                    const int n = m / HWo;
+                    const int pix = m - n * HWo;
+                    const int ho = pix / p.Wo, wo = pix - ho * p.Wo;
+                    const int g = gk / p.KK, k = gk - g * p.KK;
+                    const int ki = k / p.kw, kj = k - ki * p.kw;
+                    const int yy = ho * p.stride - p.pad + ki * p.dil;
+                    const int xx = wo * p.stride - p.pad + kj * p.dil;
+                    const bool in = yy >= 0 && yy < p.H && xx >= 0 && xx < p.W;
+                    const __half* src =
+                        p.xt + ((static_cast<size_t>(n) * p.H + (in ? yy : 0)) * p.W + (in ? xx : 0)) * p.Cin + g * p.cpg;
+                    for (int v0 = 0; v0 < p.cpg; v0 += VEC) {
+                        typename Vec<VEC>::T v{};
+                        if (in) v = *reinterpret_cast<const typename Vec<VEC>::T*>(src + v0);
+                        const int kk = lc * p.cpg + v0;
+                        *reinterpret_cast<typename Vec<VEC>::T*>(sA[s] + sw_offset(r, kk >> 3, 128) + (kk & 7) * 2) = v;
+                    }
+                    continue;
+                }
+                if (DEFORM && m < M && gk < combos) {
                     const int n = m / HWo;
                     const int pix = m - n * HWo;
                     const int ho = pix / p.Wo, wo = pix - ho * p.Wo;
@@ -273,7 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_kernel(const __grid_constant_
             const int c_lo = NT >= 32 ? half * (NT / 2) : (half == 0 ? 0 : NT);
             const int c_hi = NT >= 32 ? c_lo + NT / 2 : (half == 0 ? NT : NT);
             const int n = m / HWo, pix = m - n * HWo;
-            __half* orow = p.out + static_cast<size_t>(n) * p.Cout * HWo + pix;
+            __half* orow = p.out + (static_cast<size_t>(n) * p.Cout + p.cout_base) * HWo + pix;
+            const int cmax = p.Cout - p.cout_base;  // channels of this slab that exist
             for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                 float v[16];
                 tmem_ld16(tmem + c0 + (static_cast<uint32_t>(q4 * 32) << 16), v);
@@ -281,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) dcn_kernel(const __grid_constant_
                 if (m < M) {
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
-                        if (c0 + e < p.Cout) orow[static_cast<size_t>(c0 + e) * HWo] = __float2half(v[e] + sBias[c0 + e]);
+                        if (c0 + e < cmax) orow[static_cast<size_t>(c0 + e) * HWo] = __float2half(v[e] + sBias[c0 + e]);
                 }
             }
         }
@@ -337,12 +375,12 @@ struct dn_dcn {
 
 namespace {
 
-template <int NT, int VEC>
-int run_dcn(const DcnParams& p, int device, cudaStream_t s) {
+template <int NT, int VEC, bool DEFORM>
+int run_conv(const DcnParams& p, int device, cudaStream_t s) {
     constexpr int smem = 1024 + 2 * kABytes + 2 * NT * kKC * 2 + NT * 4;
     static bool configured[64] = {};
     if (device >= 0 && device < 64 && !configured[device]) {
-        cudaError_t e = cudaFuncSetAttribute(dcn_kernel<NT, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(conv_kernel<NT, VEC, DEFORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return dn_cuda_fail(e, "dcn: smem attribute");
         configured[device] = true;
     }
@@ -350,16 +388,27 @@ int run_dcn(const DcnParams& p, int device, cudaStream_t s) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     const int tiles = (p.N * p.Ho * p.Wo + 127) / 128;
     const int grid = std::max(1, std::min(tiles, sms));
-    cudaError_t e = launch_pdl(dcn_kernel<NT, VEC>, dim3(grid), dim3(kThreads), smem, s, p);
-    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "dcn: launch");
+    cudaError_t e = launch_pdl(conv_kernel<NT, VEC, DEFORM>, dim3(grid), dim3(kThreads), smem, s, p);
+    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "conv: launch");
 }
 
-template <int NT>
-int run_dcn_vec(const DcnParams& p, int device, cudaStream_t s) {
-    if (p.cpg % 8 == 0) return run_dcn<NT, 8>(p, device, s);
-    if (p.cpg % 4 == 0) return run_dcn<NT, 4>(p, device, s);
-    if (p.cpg % 2 == 0) return run_dcn<NT, 2>(p, device, s);
-    return run_dcn<NT, 1>(p, device, s);
+template <int NT, bool DEFORM>
+int run_conv_vec(const DcnParams& p, int device, cudaStream_t s) {
+    if (p.cpg % 8 == 0) return run_conv<NT, 8, DEFORM>(p, device, s);
+    if (p.cpg % 4 == 0) return run_conv<NT, 4, DEFORM>(p, device, s);
+    if (p.cpg % 2 == 0) return run_conv<NT, 2, DEFORM>(p, device, s);
+    return run_conv<NT, 1, DEFORM>(p, device, s);
+}
+
+template <bool DEFORM>
+int run_conv_nt(const DcnParams& p, int nt, int device, cudaStream_t s) {
+    switch (nt) {
+        case 16: return run_conv_vec<16, DEFORM>(p, device, s);
+        case 32: return run_conv_vec<32, DEFORM>(p, device, s);
+        case 64: return run_conv_vec<64, DEFORM>(p, device, s);
+        case 128: return run_conv_vec<128, DEFORM>(p, device, s);
+        default: return run_conv_vec<256, DEFORM>(p, device, s);
+    }
 }
 
 struct DevGuard {
@@ -535,13 +584,8 @@ int dn_dcn_forward(dn_dcn* L, const void* input, const void* offsets, const void
     p.cpg = L->cpg;
     p.k_chunks = L->k_chunks;
     p.err = L->err;
-    switch (L->NT) {
-        case 16: return run_dcn_vec<16>(p, L->device, s);
-        case 32: return run_dcn_vec<32>(p, L->device, s);
-        case 64: return run_dcn_vec<64>(p, L->device, s);
-        case 128: return run_dcn_vec<128>(p, L->device, s);
-        default: return run_dcn_vec<256>(p, L->device, s);
-    }
+    p.cout_base = 0;
+    return run_conv_nt<true>(p, L->NT, L->device, s);
 }
 
 int dn_dcn_sync(dn_dcn* L, void* stream) {
@@ -555,6 +599,205 @@ int dn_dcn_sync(dn_dcn* L, void* stream) {
     if (word) {
         cudaMemset(L->err, 0, 4);
         return dn_fail_str(DN_ERR_DEVICE, "dcn kernel reported device error word " + std::to_string(word));
+    }
+    return DN_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Conv2dLayer
+// ---------------------------------------------------------------------------
+
+struct dn_conv2d {
+    int device = 0;
+    int cout = 0, cin_g = 0, cin = 0, kh = 0, kw = 0, pad = 1, stride = 1, dil = 1, groups = 1;
+    int cb = 0, nblk = 0, NT = 0, slabs = 0, k_chunks = 0;
+    uint8_t* bpack = nullptr;  // device: [slabs][k_chunks][NT x 64] packed weights
+    float* bias = nullptr;     // device: [slabs * NT]
+    __half* xt = nullptr;      // device: NHWC copy of the input (grown on demand)
+    size_t xt_bytes = 0;
+    uint32_t* err = nullptr;
+};
+
+extern "C" {
+
+int dn_conv2d_create(const dn_weights* store, const char* weight_name, const char* bias_name, int pad, int stride,
+                     int dilation, int groups, int device, dn_conv2d** out) {
+    if (!store || !weight_name || !out) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_create: null argument");
+    *out = nullptr;
+    if (pad < 0 || stride <= 0 || dilation <= 0 || groups <= 0)
+        return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_create: bad pad/stride/dilation/groups");
+    try {
+        const HostWeights& hw = *store->hw;
+        if (!hw.contains(weight_name)) return dn_fail_str(DN_ERR_NOT_FOUND, std::string("weight not found: ") + weight_name);
+        if (bias_name && !hw.contains(bias_name))
+            return dn_fail_str(DN_ERR_NOT_FOUND, std::string("weight not found: ") + bias_name);
+        const auto& sh = hw.entry(weight_name).shape;
+        if (sh.size() != 4)
+            return dn_fail_str(DN_ERR_FORMAT, "Conv2dLayer: weight must be 4-D, got " + std::to_string(sh.size()) + "-D");
+        auto L = std::make_unique<dn_conv2d>();
+        L->device = device;
+        L->cout = static_cast<int>(sh[0]);
+        L->cin_g = static_cast<int>(sh[1]);
+        L->kh = static_cast<int>(sh[2]);
+        L->kw = static_cast<int>(sh[3]);
+        L->pad = pad;
+        L->stride = stride;
+        L->dil = dilation;
+        L->groups = groups;
+        if (L->cout % groups != 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_create: out_channels % groups != 0");
+        L->cin = L->cin_g * groups;
+        L->cb = kKC;
+        while (L->cin % L->cb != 0) L->cb >>= 1;  // largest power of two dividing Cin and 64
+        L->nblk = L->cin / L->cb;
+        const int KK = L->kh * L->kw;
+        L->k_chunks = (L->cin * KK + kKC - 1) / kKC;
+        L->NT = std::min(256, std::max(16, next_pow2(L->cout)));
+        L->slabs = (L->cout + L->NT - 1) / L->NT;
+        const auto w = hw.to_f32(weight_name);
+        const size_t tile = static_cast<size_t>(L->NT) * kKC * 2;
+        const size_t slab_bytes = tile * L->k_chunks;
+        std::vector<uint8_t> pk(slab_bytes * L->slabs, 0);
+        const int cout_g = L->cout / groups;
+        for (int o = 0; o < L->cout; ++o) {
+            const int sl = o / L->NT, ol = o % L->NT, grp = o / cout_g;
+            for (int cl = 0; cl < L->cin_g; ++cl) {
+                const int ci = grp * L->cin_g + cl;
+                for (int k = 0; k < KK; ++k) {
+                    const int kidx = ((ci / L->cb) * KK + k) * L->cb + (ci % L->cb);
+                    const __half h = __float2half(w[(static_cast<size_t>(o) * L->cin_g + cl) * KK + k]);
+                    const int j = kidx / kKC, kk = kidx % kKC;
+                    const size_t offb = static_cast<size_t>(ol >> 3) * 1024 + (kk / 8) * 128 + (ol & 7) * 16 + (kk % 8) * 2;
+                    std::memcpy(pk.data() + sl * slab_bytes + j * tile + offb, &h, 2);
+                }
+            }
+        }
+        std::vector<float> b(static_cast<size_t>(L->slabs) * L->NT, 0.f);
+        if (bias_name) {
+            const auto bv = hw.to_f32(bias_name);
+            if (static_cast<int>(bv.size()) != L->cout) return dn_fail(DN_ERR_FORMAT, "dn_conv2d_create: bias size");
+            for (int o = 0; o < L->cout; ++o) b[o] = __half2float(__float2half(bv[o]));
+        }
+        DevGuard dg(device);
+        cudaError_t e = cudaMalloc(&L->bpack, pk.size());
+        if (e == cudaSuccess) e = cudaMalloc(&L->bias, b.size() * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&L->err, 4);
+        if (e == cudaSuccess) e = cudaMemcpy(L->bpack, pk.data(), pk.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(L->bias, b.data(), b.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemset(L->err, 0, 4);
+        if (e != cudaSuccess) {
+            cudaFree(L->bpack);
+            cudaFree(L->bias);
+            cudaFree(L->err);
+            return dn_cuda_fail(e, "dn_conv2d_create: upload");
+        }
+        *out = L.release();
+        return DN_OK;
+    } catch (const std::exception& ex) {
+        return dn_fail_str(DN_ERR_FORMAT, ex.what());
+    }
+}
+
+int dn_conv2d_destroy(dn_conv2d* L) {
+    if (!L) return DN_OK;
+    DevGuard dg(L->device);
+    cudaFree(L->bpack);
+    cudaFree(L->bias);
+    cudaFree(L->xt);
+    cudaFree(L->err);
+    delete L;
+    return DN_OK;
+}
+
+int dn_conv2d_info(const dn_conv2d* L, int* out_channels, int* in_channels, int* kernel_h, int* kernel_w,
+                   int* groups) {
+    if (!L) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_info: null layer");
+    if (out_channels) *out_channels = L->cout;
+    if (in_channels) *in_channels = L->cin_g;
+    if (kernel_h) *kernel_h = L->kh;
+    if (kernel_w) *kernel_w = L->kw;
+    if (groups) *groups = L->groups;
+    return DN_OK;
+}
+
+int dn_conv2d_output_size(const dn_conv2d* L, int H_in, int W_in, int* H_out, int* W_out) {
+    if (!L || !H_out || !W_out) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_output_size: null argument");
+    *H_out = (H_in + 2 * L->pad - L->dil * (L->kh - 1) - 1) / L->stride + 1;
+    *W_out = (W_in + 2 * L->pad - L->dil * (L->kw - 1) - 1) / L->stride + 1;
+    return DN_OK;
+}
+
+int dn_conv2d_forward(dn_conv2d* L, const void* input, int N, int C, int H_in, int W_in, void* output, void* stream) {
+    if (!L || !input || !output) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_forward: null argument");
+    if (N <= 0 || H_in <= 0 || W_in <= 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_forward: empty input");
+    if (C != L->cin)
+        return dn_fail_str(DN_ERR_INVALID_ARG, "dn_conv2d_forward: input has " + std::to_string(C) +
+                                                   " channels, the layer expects " + std::to_string(L->cin));
+    int Ho = 0, Wo = 0;
+    dn_conv2d_output_size(L, H_in, W_in, &Ho, &Wo);
+    if (Ho <= 0 || Wo <= 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_forward: output would be empty");
+    if (static_cast<long long>(N) * H_in * W_in * L->cin > (1LL << 31) ||
+        static_cast<long long>(N) * Ho * Wo > (1LL << 31))
+        return dn_fail(DN_ERR_UNSUPPORTED, "dn_conv2d_forward: input too large");
+    DevGuard dg(L->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t need = static_cast<size_t>(N) * H_in * W_in * L->cin * 2;
+    if (need > L->xt_bytes) {
+        cudaError_t e = cudaStreamSynchronize(s);  // the old copy may still be read
+        if (e == cudaSuccess) {
+            cudaFree(L->xt);
+            L->xt = nullptr;
+            L->xt_bytes = 0;
+            e = cudaMalloc(&L->xt, need);
+        }
+        if (e != cudaSuccess) return dn_cuda_fail(e, "dn_conv2d_forward: NHWC buffer");
+        L->xt_bytes = need;
+    }
+    const int HW = H_in * W_in;
+    cudaError_t e = launch_pdl(to_nhwc_kernel, dim3((HW + 31) / 32, (L->cin + 31) / 32, N), dim3(32, 8), 0, s,
+                               static_cast<const __half*>(input), L->xt, L->cin, HW);
+    if (e != cudaSuccess) return dn_cuda_fail(e, "dn_conv2d_forward: transpose launch");
+    DcnParams p{};
+    p.xt = L->xt;
+    p.out = static_cast<__half*>(output);
+    p.N = N;
+    p.H = H_in;
+    p.W = W_in;
+    p.Ho = Ho;
+    p.Wo = Wo;
+    p.Cin = L->cin;
+    p.Cout = L->cout;
+    p.kw = L->kw;
+    p.KK = L->kh * L->kw;
+    p.pad = L->pad;
+    p.stride = L->stride;
+    p.dil = L->dil;
+    p.dg = L->nblk;
+    p.cpg = L->cb;
+    p.k_chunks = L->k_chunks;
+    p.err = L->err;
+    const size_t slab_bytes = static_cast<size_t>(L->NT) * kKC * 2 * L->k_chunks;
+    for (int sl = 0; sl < L->slabs; ++sl) {
+        p.bpack = L->bpack + sl * slab_bytes;
+        p.bias = L->bias + sl * L->NT;
+        p.cout_base = sl * L->NT;
+        DN_TRY(run_conv_nt<false>(p, L->NT, L->device, s));
+    }
+    return DN_OK;
+}
+
+int dn_conv2d_sync(dn_conv2d* L, void* stream) {
+    if (!L) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_sync: null layer");
+    DevGuard dg(L->device);
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return dn_cuda_fail(e, "dn_conv2d_sync");
+    uint32_t word = 0;
+    e = cudaMemcpy(&word, L->err, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return dn_cuda_fail(e, "dn_conv2d_sync: error word");
+    if (word) {
+        cudaMemset(L->err, 0, 4);
+        return dn_fail_str(DN_ERR_DEVICE, "conv kernel reported device error word " + std::to_string(word));
     }
     return DN_OK;
 }
