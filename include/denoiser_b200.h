@@ -74,6 +74,15 @@ int dn_weights_name(const dn_weights* weights, int index, const char** name);
 /* Manifest::Architecture fields (weight_loader.h:30-39). */
 int dn_weights_arch(const dn_weights* weights, char* type_buf, int type_buf_len, int* base_channels,
                     int* num_levels, int* in_channels, int* num_frames, int* use_warp);
+/* Manifest::version and default dtype (0 float32, 1 float16), the
+ * architecture's enc_channels (up to max_enc, count in *n_enc) and
+ * out_channels. Strings stay valid until dn_weights_close. */
+int dn_weights_meta(const dn_weights* weights, const char** version, int* dtype, int* enc_channels, int max_enc,
+                    int* n_enc, int* out_channels);
+/* LayerEntry::file of `name` (relative to the manifest directory). */
+int dn_weights_file(const dn_weights* weights, const char* name, const char** file);
+/* Path of the manifest the store was opened from. */
+const char* dn_weights_path(const dn_weights* weights);
 
 /* ------------------------------------------------------------------------
  * Models: NAFNet (spatial) and NAFNetTemporal, architecture discovered from

@@ -76,6 +76,9 @@ SIGNATURES = {
     "dn_weights_info": (_I, [_P, _c.c_char_p, _I64P, _IP, _IP, _PP]),
     "dn_weights_name": (_I, [_P, _I, _CPP]),
     "dn_weights_arch": (_I, [_P, _c.c_char_p, _I, _IP, _IP, _IP, _IP, _IP]),
+    "dn_weights_meta": (_I, [_P, _CPP, _IP, _IP, _I, _IP, _IP]),
+    "dn_weights_file": (_I, [_P, _c.c_char_p, _CPP]),
+    "dn_weights_path": (_c.c_char_p, [_P]),
     "dn_model_create": (_I, [_c.c_char_p, _I, _PP]),
     "dn_model_destroy": (_I, [_P]),
     "dn_model_get_info": (_I, [_P, _c.POINTER(ModelInfo)]),

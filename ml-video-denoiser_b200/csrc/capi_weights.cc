@@ -84,4 +84,26 @@ int dn_weights_arch(const dn_weights* w, char* type_buf, int type_buf_len, int* 
     return DN_OK;
 }
 
+int dn_weights_meta(const dn_weights* w, const char** version, int* dtype, int* enc_channels, int max_enc,
+                    int* n_enc, int* out_channels) {
+    if (!w) return dn_fail(DN_ERR_INVALID_ARG, "dn_weights_meta: null handle");
+    const ManifestArch& a = w->hw->arch();
+    if (version) *version = w->hw->version().c_str();
+    if (dtype) *dtype = w->hw->dtype() == WDType::F16 ? 1 : 0;
+    if (n_enc) *n_enc = static_cast<int>(a.enc_channels.size());
+    if (enc_channels)
+        for (int i = 0; i < max_enc && i < static_cast<int>(a.enc_channels.size()); ++i) enc_channels[i] = a.enc_channels[i];
+    if (out_channels) *out_channels = a.out_channels;
+    return DN_OK;
+}
+
+int dn_weights_file(const dn_weights* w, const char* name, const char** file) {
+    if (!w || !name || !file) return dn_fail(DN_ERR_INVALID_ARG, "dn_weights_file: null argument");
+    if (!w->hw->contains(name)) return dn_fail_str(DN_ERR_NOT_FOUND, std::string("weight not found: ") + name);
+    *file = w->hw->entry(name).file.c_str();
+    return DN_OK;
+}
+
+const char* dn_weights_path(const dn_weights* w) { return w ? w->hw->path().c_str() : ""; }
+
 }  // extern "C"

@@ -1,0 +1,155 @@
+// Exercises the C++ API mirror (include/denoiser/) the way the reference's
+// own C++ tests and CLI use the reference headers.
+//   api_test host <manifest>            : host-only checks (no GPU calls)
+//   api_test gpu  <conv_manifest> <model_manifest> <x.bin> <y_ref.bin> N C H W
+// Exit code 0 = pass; failures print one line and exit 1.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "denoiser/kernels/model_kernels.h"
+#include "denoiser/kernels/nafnet_kernels.h"
+#include "denoiser/layers/conv2d.h"
+#include "denoiser/layers/deform_conv2d.h"
+#include "denoiser/layers/upsample.h"
+#include "denoiser/models/nafnet.h"
+#include "denoiser/models/nafnet_temporal.h"
+#include "denoiser/tensor.h"
+#include "denoiser/weight_loader.h"
+
+using namespace denoiser;
+
+#define EXPECT(c)                                                      \
+    do {                                                               \
+        if (!(c)) {                                                    \
+            std::fprintf(stderr, "FAILED %s:%d: %s\n", __FILE__, __LINE__, #c); \
+            return 1;                                                  \
+        }                                                              \
+    } while (0)
+
+template <class E, class F>
+bool throws(F&& f) {
+    try {
+        f();
+    } catch (const E&) {
+        return true;
+    } catch (...) {
+        return false;
+    }
+    return false;
+}
+
+static std::vector<char> read_file(const std::string& p) {
+    std::ifstream f(p, std::ios::binary);
+    return std::vector<char>((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+}
+
+static int host_checks(const std::string& manifest) {
+    EXPECT(throws<std::runtime_error>([] { WeightStore s("/nonexistent/manifest.json"); }));
+    WeightStore store(manifest);
+    EXPECT(store.contains("conv1x1.weight"));
+    EXPECT(!store.contains("nope"));
+    EXPECT(store.manifest().layers.size() == 3);
+    EXPECT(store.manifest().layers[0].name == "conv1x1.weight");
+    EXPECT(store.manifest().layers[0].shape == std::vector<int64_t>({1, 1, 1, 1}));
+    EXPECT(store.manifest().layers[0].dtype == DType::kFloat16);
+    EXPECT(!store.manifest().layers[0].file.empty());
+    EXPECT(store.manifest().architecture.type == "nafnet_residual");
+    EXPECT(store.manifest().version == "1.0");
+    EXPECT(throws<std::invalid_argument>([] { UpsampleLayer u(0); }));
+    EXPECT(dtype_size(DType::kFloat16) == 2 && dtype_size(DType::kFloat32) == 4);
+    std::printf("host ok\n");
+    return 0;
+}
+
+static std::vector<float> to_floats(const Tensor& t) {
+    std::vector<__half> h(static_cast<size_t>(t.numel()));
+    t.to_host(h.data());
+    std::vector<float> f(h.size());
+    for (size_t i = 0; i < h.size(); ++i) f[i] = __half2float(h[i]);
+    return f;
+}
+
+static Tensor from_floats(const std::vector<float>& v, std::vector<int64_t> shape) {
+    std::vector<__half> h(v.size());
+    for (size_t i = 0; i < v.size(); ++i) h[i] = __float2half(v[i]);
+    return Tensor::from_host(h.data(), std::move(shape), DType::kFloat16);
+}
+
+static int gpu_checks(char** a) {
+    // Tensor semantics
+    auto t = from_floats({1, 2, 3, 4, 5, 6, 7, 8}, {1, 2, 2, 2});
+    EXPECT(t.numel() == 8 && t.nbytes() == 16 && t.channels() == 2 && t.shape_str() == "(1, 2, 2, 2)");
+    auto c = t.clone();
+    auto s1 = c.slice_channels(1, 2);
+    EXPECT(s1.channels() == 1 && to_floats(s1) == std::vector<float>({5, 6, 7, 8}));
+    EXPECT(throws<std::out_of_range>([&] { (void)t.slice_channels(1, 3); }));
+    EXPECT(throws<std::invalid_argument>([] { (void)Tensor::empty({1, 0}, DType::kFloat16); }));
+    EXPECT(throws<std::runtime_error>([] { Tensor e; std::vector<char> b(4); e.to_host(b.data()); }));
+    Tensor moved = std::move(c);
+    EXPECT(moved.is_valid() && !c.is_valid());
+
+    // Conv2dLayer: the reference's known answers (tests/test_conv2d.cc:154-212)
+    WeightStore cs(a[2]);
+    Conv2dLayer conv(cs, "conv1x1.weight", "conv1x1.bias", 0);
+    EXPECT(conv.out_channels() == 1 && conv.in_channels() == 1 && conv.kernel_h() == 1 && conv.kernel_w() == 1);
+    auto y = to_floats(conv.forward(from_floats({1, 2, 3, 4, 5, 6, 7, 8, 9}, {1, 1, 3, 3})));
+    for (int i = 0; i < 9; ++i) EXPECT(std::fabs(y[i] - (2.f * (i + 1) + 1.f)) < 1e-2f);
+    Conv2dLayer multi(cs, "conv_multi.weight", std::nullopt, 0);
+    auto ym = to_floats(multi.forward(from_floats({1, 2, 3, 4}, {1, 1, 2, 2})));
+    for (int i = 0; i < 4; ++i) EXPECT(std::fabs(ym[i] - (i + 1)) < 1e-2f && std::fabs(ym[4 + i] + (i + 1)) < 1e-2f);
+    std::vector<float> ones(9, 1.f);
+    auto f32 = Tensor::from_host(ones.data(), {1, 1, 3, 3}, DType::kFloat32);
+    EXPECT(throws<std::runtime_error>([&] { (void)conv.forward(f32); }));
+    EXPECT(throws<std::out_of_range>([&] { Conv2dLayer bad(cs, "missing.weight"); }));
+    EXPECT(conv.forward(from_floats(ones, {1, 1, 3, 3})).height() == 3);
+    Conv2dLayer padded(cs, "conv1x1.weight", std::nullopt, 1);
+    EXPECT(padded.forward(from_floats(ones, {1, 1, 3, 3})).height() == 5);
+
+    // UpsampleLayer shape and a constant field
+    UpsampleLayer up(2);
+    auto u = to_floats(up.forward(from_floats(std::vector<float>(12, 3.f), {1, 1, 3, 4})));
+    EXPECT(u.size() == 48);
+    for (float v : u) EXPECT(std::fabs(v - 3.f) < 1e-3f);
+
+    // Kernel launchers
+    auto p = Tensor::empty({1, 2, 2, 2}, DType::kFloat16);
+    kernels::launch_add(t.data_f16(), t.data_f16(), p.data_f16(), 8, nullptr);
+    auto pv = to_floats(p);
+    for (int i = 0; i < 8; ++i) EXPECT(pv[i] == 2.f * (i + 1));
+    EXPECT(throws<std::invalid_argument>([&] { kernels::launch_crop(t.data_f16(), p.data_f16(), 1, 2, 2, 2, 3, 3, nullptr); }));
+
+    // NAFNet through the mirror == the engine output computed by the caller
+    WeightStore ms(a[3]);
+    NAFNet net(ms);
+    EXPECT(throws<std::runtime_error>([&] { NAFNetTemporal bad(ms); }));
+    const int N = std::atoi(a[6]), C = std::atoi(a[7]), H = std::atoi(a[8]), W = std::atoi(a[9]);
+    EXPECT(net.in_channels() == 3 && net.num_levels() == static_cast<int>(net.enc_channels().size()));
+    auto xb = read_file(a[4]);
+    auto rb = read_file(a[5]);
+    EXPECT(xb.size() == static_cast<size_t>(N) * C * H * W * 2);
+    auto x = Tensor::from_host(xb.data(), {N, C, H, W}, DType::kFloat16);
+    auto out = net.forward(x);
+    EXPECT(out.channels() == 3 && out.height() == H && out.width() == W);
+    std::vector<char> ob(out.nbytes());
+    out.to_host(ob.data());
+    EXPECT(rb.size() == ob.size() && std::memcmp(rb.data(), ob.data(), ob.size()) == 0);
+    std::printf("gpu ok\n");
+    return 0;
+}
+
+int main(int argc, char** argv) {
+    try {
+        if (argc >= 3 && std::string(argv[1]) == "host") return host_checks(argv[2]);
+        if (argc >= 10 && std::string(argv[1]) == "gpu") return gpu_checks(argv);
+    } catch (const std::exception& e) {
+        std::fprintf(stderr, "FAILED: unexpected exception: %s\n", e.what());
+        return 1;
+    }
+    std::fprintf(stderr, "usage: api_test host <manifest> | gpu <conv_manifest> <model_manifest> <x> <y> N C H W\n");
+    return 2;
+}
