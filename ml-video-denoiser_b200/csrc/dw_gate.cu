@@ -131,11 +131,10 @@ constexpr int kScaVec = 8;  // D <= 32 * 4 * kScaVec = 1024
 template <int V>
 __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ DwParams p, int nb) {
     constexpr int kScaVec = V;
-    constexpr int kRowsAtOnce = V >= 8 ? 1 : 8 / V;
     extern __shared__ __align__(16) float sm[];
     const int D = p.D;
     float* mean = sm;       // [D]
-    float* red = sm + D;    // [8 warps][D]
+    float* red = sm + D;    // [stripes][D], stripes * D = 4 * kThreads floats
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int img = blockIdx.y;
@@ -151,38 +150,41 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     pdl_wait();
-    // Fixed-order pool: warp w sums partial rows w, w+8, ... in order; the 8
-    // warp sums are then added in warp order.
+    // Fixed-order pool over all 256 threads: thread (stripe, v) sums the
+    // float4 channel vector v of partial rows stripe, stripe + stripes, ...
+    // (four loads in flight); the stripe sums are then added in stripe order.
     const float4* pp = reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(img) * nb * D);
-    float4 acc[kScaVec];
+    const int stripes = kThreads / nvec;
+    const int v = tid % nvec, stripe = tid / nvec;
+    if (stripe < stripes) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        int b = stripe;
+        for (; b + 3 * stripes < nb; b += 4 * stripes) {
+            float4 x[4];
 #pragma unroll
-    for (int i = 0; i < kScaVec; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll kRowsAtOnce
-    for (int b = warp; b < nb; b += 8) {
-        float4 x[kScaVec];
+            for (int u = 0; u < 4; ++u) x[u] = pp[static_cast<size_t>(b + u * stripes) * nvec + v];
 #pragma unroll
-        for (int i = 0; i < kScaVec; ++i) {
-            const int v = lane + 32 * i;
-            x[i] = v < nvec ? pp[static_cast<size_t>(b) * nvec + v] : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int u = 0; u < 4; ++u) {
+                acc.x += x[u].x;
+                acc.y += x[u].y;
+                acc.z += x[u].z;
+                acc.w += x[u].w;
+            }
         }
-#pragma unroll
-        for (int i = 0; i < kScaVec; ++i) {
-            acc[i].x += x[i].x;
-            acc[i].y += x[i].y;
-            acc[i].z += x[i].z;
-            acc[i].w += x[i].w;
+        for (; b < nb; b += stripes) {
+            const float4 x = pp[static_cast<size_t>(b) * nvec + v];
+            acc.x += x.x;
+            acc.y += x.y;
+            acc.z += x.z;
+            acc.w += x.w;
         }
-    }
-#pragma unroll
-    for (int i = 0; i < kScaVec; ++i) {
-        const int v = lane + 32 * i;
-        if (v < nvec) reinterpret_cast<float4*>(red + warp * D)[v] = acc[i];
+        reinterpret_cast<float4*>(red + stripe * D)[v] = acc;
     }
     __syncthreads();
     const float inv = 1.0f / static_cast<float>(p.H * p.W);
     for (int c = tid; c < D; c += kThreads) {
         float s = 0.f;
-        for (int w = 0; w < 8; ++w) s += red[w * D + c];
+        for (int st = 0; st < stripes; ++st) s += red[st * D + c];
         mean[c] = s * inv;
     }
     __syncthreads();
@@ -218,7 +220,7 @@ int dw_blocks_per_img(int H, int W, int D) {
 
 template <int V>
 int launch_sca_v(const DwParams& p, int nb, cudaStream_t s) {
-    const size_t smem = static_cast<size_t>(9) * p.D * sizeof(float);
+    const size_t smem = (static_cast<size_t>(p.D) + 4 * kThreads) * sizeof(float);
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(sca_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);

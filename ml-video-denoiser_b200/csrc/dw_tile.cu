@@ -1,5 +1,8 @@
-// Depthwise 3x3 + bias + SimpleGate + pool partials for the deep levels,
-// one CTA per (TH x TW output tile, 32-channel slice, image):
+// Depthwise 3x3 + bias + SimpleGate + pool partials for the deep levels.
+// A persistent CTA owns one 32-channel slice of one image and walks that
+// image's TH x TW output tiles; two halo buffers let the TMA load of the
+// tile after next overlap the current tile's math, and the slice's taps stay
+// in registers for the whole walk. Per tile:
 //   * two TMA loads bring the (TH+2) x (TW+2) halo of both gate halves of the
 //     slice (u channels [c, c+32) and [D+c, D+c+32)) into shared memory,
 //     zero-filled outside the image (the conv's zero padding);
@@ -19,6 +22,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <string>
 
 #include "kernels.h"
@@ -39,7 +43,7 @@ constexpr int kP = kHH * kWW;      // halo pixels
 constexpr int kRowB = kCS * 2;     // 64 bytes per halo pixel and half
 constexpr int kBufB = ((kP * kRowB + 127) / 128) * 128;
 constexpr int kOutB = kTH * kTW * kCS * 2;
-constexpr int kSmem = 128 + 2 * kBufB + kOutB + kTW * kCS * 4;
+constexpr int kSmem = 128 + 4 * kBufB + kOutB + kTW * kCS * 4;  // 2 halo buffers x 2 gate halves
 constexpr int kThreads = 256;
 
 // Lane layout inside a warp (32 lanes = 4 columns): bits 0-1 channel group,
@@ -51,23 +55,21 @@ __global__ void __launch_bounds__(kThreads, 2)
                    const __grid_constant__ CUtensorMap mg) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
-    uint8_t* sHalf0 = smem;
-    uint8_t* sHalf1 = smem + kBufB;
-    uint8_t* sOut = smem + 2 * kBufB;                              // [TH*TW][CS] fp16
+    uint8_t* sOut = smem + 4 * kBufB;                              // [TH*TW][CS] fp16
     float* sRed = reinterpret_cast<float*>(sOut + kOutB);          // [TW columns][CS]
-    __shared__ uint64_t bar;
+    __shared__ uint64_t bar[2];
 
     const int tid = threadIdx.x;
     const int tiles_x = (p.W + kTW - 1) / kTW;
-    const int tile = blockIdx.x;
-    const int ty0 = (tile / tiles_x) * kTH, tx0 = (tile % tiles_x) * kTW;
+    const int ntiles = tiles_x * ((p.H + kTH - 1) / kTH);
     const int img = blockIdx.z;
     const int D = p.D;
     const int cs0 = blockIdx.y * kCS;
 
     pdl_trigger();
     if (tid == 0) {
-        mbar_init(&bar, 1);
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
         fence_mbar_init();
     }
     const int lane = tid & 31;
@@ -84,80 +86,94 @@ __global__ void __launch_bounds__(kThreads, 2)
             w[t][i] = make_float2(p.w[t * 2 * D + cin + 2 * i], p.w[t * 2 * D + cin + 2 * i + 1]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) bias[i] = make_float2(p.b[cin + 2 * i], p.b[cin + 2 * i + 1]);
-    __syncthreads();  // barrier initialised before anyone waits on it
+    __syncthreads();  // barriers initialised before anyone waits on them
     pdl_wait();
+    // Halo of tile t (both gate halves) into buffer b.
+    auto load = [&](int t, int b) {
+        const int ty0 = (t / tiles_x) * kTH, tx0 = (t % tiles_x) * kTW;
+        uint8_t* dst = smem + b * 2 * kBufB;
+        mbar_arrive_expect_tx(&bar[b], 2 * kP * kRowB);
+        tma_load_4d(dst, &mu, cs0, tx0 - 1, ty0 - 1, img, &bar[b]);
+        tma_load_4d(dst + kBufB, &mu, D + cs0, tx0 - 1, ty0 - 1, img, &bar[b]);
+    };
     if (tid == 0) {
-        mbar_arrive_expect_tx(&bar, 2 * kP * kRowB);
-        tma_load_4d(sHalf0, &mu, cs0, tx0 - 1, ty0 - 1, img, &bar);
-        tma_load_4d(sHalf1, &mu, D + cs0, tx0 - 1, ty0 - 1, img, &bar);
-    }
-    const bool ok = mbar_wait(&bar, 0);
-    if (!__syncthreads_and(ok)) {
-        if (tid == 0) report_error(p.err, 0x50, kErrMbarTimeout);
-        return;
+        if (static_cast<int>(blockIdx.x) < ntiles) load(blockIdx.x, 0);
+        if (static_cast<int>(blockIdx.x + gridDim.x) < ntiles) load(blockIdx.x + gridDim.x, 1);
     }
 
-    const uint8_t* src = (half ? sHalf1 : sHalf0) + cg * 16;
-    const bool col_in = tx0 + px < p.W;
-    float ps[4] = {0, 0, 0, 0};
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int b = it & 1;
+        const int ty0 = (t / tiles_x) * kTH, tx0 = (t % tiles_x) * kTW;
+        if (tid == 0) bulk_wait_read0();  // the previous tile's store has read sOut
+        const bool ok = mbar_wait(&bar[b], (it >> 1) & 1);
+        if (!__syncthreads_and(ok)) {
+            if (tid == 0) report_error(p.err, 0x50, kErrMbarTimeout);
+            break;
+        }
+        const uint8_t* src = smem + b * 2 * kBufB + half * kBufB + cg * 16;
+        const bool col_in = tx0 + px < p.W;
+        float ps[4] = {0, 0, 0, 0};
 #pragma unroll 1
-    for (int py = 0; py < kTH; py += 2) {
-        float2 a0[4], a1[4];
+        for (int py = 0; py < kTH; py += 2) {
+            float2 a0[4], a1[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a0[i] = a1[i] = bias[i];
+            for (int i = 0; i < 4; ++i) a0[i] = a1[i] = bias[i];
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
+            for (int rr = 0; rr < 4; ++rr) {
 #pragma unroll
-            for (int kx = 0; kx < 3; ++kx) {
-                const uint4 v = *reinterpret_cast<const uint4*>(src + ((py + rr) * kWW + px + kx) * kRowB);
-                const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+                for (int kx = 0; kx < 3; ++kx) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(src + ((py + rr) * kWW + px + kx) * kRowB);
+                    const uint32_t q[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 u = unpack_half2(q[i]);
-                    if (rr <= 2) a0[i] = ffma2(u, w[rr * 3 + kx][i], a0[i]);
-                    if (rr >= 1) a1[i] = ffma2(u, w[(rr - 1) * 3 + kx][i], a1[i]);
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 u = unpack_half2(q[i]);
+                        if (rr <= 2) a0[i] = ffma2(u, w[rr * 3 + kx][i], a0[i]);
+                        if (rr >= 1) a1[i] = ffma2(u, w[(rr - 1) * 3 + kx][i], a1[i]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r2 = 0; r2 < 2; ++r2) {
+                // this lane keeps channels [4*half, 4*half+4) of its group
+                float o[4];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const float2 lo = r2 ? a1[j] : a0[j];
+                    const float2 hi = r2 ? a1[2 + j] : a0[2 + j];
+                    const float2 mine = half ? hi : lo;
+                    const float2 give = half ? lo : hi;
+                    const float gx = __shfl_xor_sync(0xffffffffu, give.x, 8);
+                    const float gy = __shfl_xor_sync(0xffffffffu, give.y, 8);
+                    o[2 * j] = mine.x * gx;
+                    o[2 * j + 1] = mine.y * gy;
+                }
+                const int oy = py + r2;
+                const uint32_t h01 = pack_half2(o[0], o[1]), h23 = pack_half2(o[2], o[3]);
+                *reinterpret_cast<uint2*>(sOut + ((oy * kTW + px) * kCS + cg * 8 + half * 4) * 2) = make_uint2(h01, h23);
+                if (col_in && ty0 + oy < p.H) {
+                    const float2 f01 = unpack_half2(h01), f23 = unpack_half2(h23);
+                    ps[0] += f01.x;
+                    ps[1] += f01.y;
+                    ps[2] += f23.x;
+                    ps[3] += f23.y;
                 }
             }
         }
 #pragma unroll
-        for (int r2 = 0; r2 < 2; ++r2) {
-            // this lane keeps channels [4*half, 4*half+4) of its group
-            float o[4];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const float2 lo = r2 ? a1[j] : a0[j];
-                const float2 hi = r2 ? a1[2 + j] : a0[2 + j];
-                const float2 mine = half ? hi : lo;
-                const float2 give = half ? lo : hi;
-                const float px_ = __shfl_xor_sync(0xffffffffu, give.x, 8);
-                const float py_ = __shfl_xor_sync(0xffffffffu, give.y, 8);
-                o[2 * j] = mine.x * px_;
-                o[2 * j + 1] = mine.y * py_;
-            }
-            const int oy = py + r2;
-            const uint32_t h01 = pack_half2(o[0], o[1]), h23 = pack_half2(o[2], o[3]);
-            *reinterpret_cast<uint2*>(sOut + ((oy * kTW + px) * kCS + cg * 8 + half * 4) * 2) = make_uint2(h01, h23);
-            if (col_in && ty0 + oy < p.H) {
-                const float2 f01 = unpack_half2(h01), f23 = unpack_half2(h23);
-                ps[0] += f01.x;
-                ps[1] += f01.y;
-                ps[2] += f23.x;
-                ps[3] += f23.y;
-            }
+        for (int i = 0; i < 4; ++i) sRed[px * kCS + cg * 8 + half * 4 + i] = ps[i];
+        fence_async_smem();
+        __syncthreads();  // every thread is done with halo buffer b, sOut and sRed are complete
+        if (tid == 0) {
+            tma_store_4d(&mg, cs0, tx0, ty0, img, sOut);
+            bulk_commit();
+            if (t + 2 * static_cast<int>(gridDim.x) < ntiles) load(t + 2 * gridDim.x, b);
         }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sRed[px * kCS + cg * 8 + half * 4 + i] = ps[i];
-    fence_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-        tma_store_4d(&mg, cs0, tx0, ty0, img, sOut);
-        bulk_commit();
-    }
-    if (tid < kCS) {
-        float sum = 0.f;
-        for (int c = 0; c < kTW; ++c) sum += sRed[c * kCS + tid];
-        p.partials[(static_cast<size_t>(img) * gridDim.x + tile) * D + cs0 + tid] = sum;
+        if (tid < kCS) {
+            float sum = 0.f;
+            for (int c = 0; c < kTW; ++c) sum += sRed[c * kCS + tid];
+            p.partials[(static_cast<size_t>(img) * ntiles + t) * D + cs0 + tid] = sum;
+        }
     }
     if (tid == 0) bulk_wait0();
 }
@@ -199,7 +215,12 @@ int launch_dw_tile(const DwParams& p, cudaStream_t s) {
     if (rc == DN_OK) rc = encode4(&mg, p.g, p.D, p.W, p.H, p.N, kCS, kTW, kTH);
     if (rc != DN_OK) return rc;
     const int tiles = dw_tile_blocks_per_img(p.H, p.W);
-    cudaError_t e = launch_pdl(dw_tile_kernel, dim3(tiles, p.D / kCS, p.N), dim3(kThreads), kSmem, s, p, mu, mg);
+    // About two CTAs per SM in total; each walks ceil(tiles / grid_x) tiles.
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int per = (p.D / kCS) * p.N;
+    const int gx = std::max(1, std::min(tiles, (2 * sms + per - 1) / per));
+    cudaError_t e = launch_pdl(dw_tile_kernel, dim3(gx, p.D / kCS, p.N), dim3(kThreads), kSmem, s, p, mu, mg);
     if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: launch");
     return launch_sca(p, tiles, s);
 }
