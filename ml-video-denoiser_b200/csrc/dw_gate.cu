@@ -204,6 +204,27 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
         if (lane == 0) p.s_out[static_cast<size_t>(img) * D + o] = s + p.sca_b[o];
+        if (lane == 0) red[warp] = s + p.sca_b[o];  // red[] is no longer read: keep this CTA's s there
+    }
+    if (p.bdst == nullptr) return;
+    // Fold s[8j .. 8j+8) into the conv3 B columns of this CTA's 8 channels:
+    // one 16-byte chunk per output row.
+    __syncthreads();
+    const int k0 = blockIdx.x * 8;
+    const int kc = k0 / p.b_kc, kq = (k0 % p.b_kc) / 8;
+    const size_t tile_b = static_cast<size_t>(p.b_nt) * p.b_kc * 2;
+    const uint32_t sbo = static_cast<uint32_t>(p.b_kc / 8) * 128u;
+    float sc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sc[i] = (k0 + i < D) ? red[i] : 0.f;
+    for (int n = tid; n < p.b_rows; n += kThreads) {
+        const int nt = n / p.b_nt, nl = n - nt * p.b_nt;
+        const size_t off = (static_cast<size_t>(nt) * p.b_kchunks + kc) * tile_b + (nl >> 3) * sbo + kq * 128 + (nl & 7) * 16;
+        float f[8];
+        h8_to_f(*reinterpret_cast<const uint4*>(p.bsrc + off), f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] *= sc[i];
+        *reinterpret_cast<uint4*>(p.bdst + off) = f_to_h8(f);
     }
 }
 

@@ -501,6 +501,21 @@ void Engine::plan(const Shape& s) {
     req.push_back({n_enc * dw_blocks_max_ * dmax * 4, reinterpret_cast<void**>(&partials_)});
     req.push_back({n_enc * 4, reinterpret_cast<void**>(&counters_)});
     req.push_back({n_enc * dmax * 4, reinterpret_cast<void**>(&sca_s_)});
+    {
+        size_t b3 = 0;
+        auto acc_b3 = [&](const std::vector<BlockW>& bl) {
+            for (const auto& b : bl)
+                b3 = std::max(b3, static_cast<size_t>(b.conv3.n_tiles) * b.conv3.k_chunks * b.conv3.NT * b.conv3.KC * 2);
+        };
+        for (int l = 0; l < L; ++l) {
+            acc_b3(levels_[l].enc);
+            acc_b3(levels_[l].dec);
+        }
+        acc_b3(middle_);
+        acc_b3(bneck_blocks_);
+        for (const auto& tb : tmix_blocks_) acc_b3(tb);
+        req.push_back({b3, reinterpret_cast<void**>(&b3s_)});
+    }
     req.push_back({256, reinterpret_cast<void**>(&err_)});
     size_t total = 0;
     for (auto& r : req) total = align256(total) + align256(r.first);
@@ -576,8 +591,9 @@ std::string Engine::profile_report() {
     return out + "}";
 }
 
-int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cudaStream_t s) {
-    p.bpack = wptr<uint8_t>(g.bpack);
+int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cudaStream_t s,
+                 const uint8_t* bpack_override) {
+    p.bpack = bpack_override ? bpack_override : wptr<uint8_t>(g.bpack);
     p.n_tiles = g.n_tiles;
     p.k_chunks = g.k_chunks;
     p.KC = g.KC;
@@ -707,6 +723,17 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
     d.sca_b = wptr<float>(b.sca_b);
     d.s_out = sca_s_;
     d.err = err_;
+    // Single image: the SCA kernel also writes conv3's B with s folded in,
+    // so conv3 needs no in-place scaling of A.
+    const bool fold_sca = fused_enabled_ && nimg == 1 && b3s_ != nullptr;
+    if (fold_sca) {
+        d.bsrc = wptr<uint8_t>(b.conv3.bpack);
+        d.bdst = b3s_;
+        d.b_rows = b.C;
+        d.b_nt = b.conv3.NT;
+        d.b_kc = b.conv3.KC;
+        d.b_kchunks = b.conv3.k_chunks;
+    }
     launches_ += 2;  // depthwise + SCA
     if (fused_enabled_ && dw_tile_supported(b.dw)) {
         prof_begin("dw_tile_sca", static_cast<double>(nimg) * hw * 3 * b.dw * 2,
@@ -728,7 +755,10 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
     p.out_c = b.C;
     p.res = x;
     p.res_scale = wptr<float>(b.beta);
-    DN_TRY(gemm(b.conv3, kProScale, kEpiResidual, kARows, p, s));
+    if (fold_sca)
+        DN_TRY(gemm(b.conv3, kProNone, kEpiResidual, kARows, p, s, b3s_));  // s folded into B by the SCA kernel
+    else
+        DN_TRY(gemm(b.conv3, kProScale, kEpiResidual, kARows, p, s));
     // t = SG(conv4(LN2(y)) + b4)
     p = rows_params(nimg, h, w);
     p.seg_c = b.C;

@@ -106,7 +106,8 @@ private:
     void plan(const Shape& s);
     int run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaStream_t s);
     int run_stage(const std::vector<BlockW>& blocks, __half* x, int nimg, int h, int w, cudaStream_t s);
-    int gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cudaStream_t s);
+    int gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cudaStream_t s,
+             const uint8_t* bpack_override = nullptr);
 
     template <class T>
     const T* wptr(size_t off) const {
@@ -154,6 +155,7 @@ private:
     float* partials_ = nullptr;
     unsigned* counters_ = nullptr;
     float* sca_s_ = nullptr;
+    uint8_t* b3s_ = nullptr;              // conv3 B with the SCA scale folded in (single image)
     uint32_t* err_ = nullptr;
     int dw_blocks_max_ = 0;
     int launches_ = 0;

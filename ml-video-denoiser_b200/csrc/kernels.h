@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 namespace dnb {
 
@@ -80,6 +81,13 @@ struct DwParams {
     const float* sca_b;    // [D]
     float* s_out;          // [N][D] channel attention scale
     uint32_t* err;         // device error word (bounded-wait timeouts)
+    // Optional (single image): write bdst = bsrc with column k scaled by
+    // s[k], i.e. the packed conv3 B operand with the SCA scale folded in
+    // (layout of launch_gemm: tiles [n_tile][k_chunk] of NT x KC, no-swizzle
+    // K-major core matrices); b_rows = conv3 output channels.
+    const uint8_t* bsrc;
+    uint8_t* bdst;
+    int b_rows, b_nt, b_kc, b_kchunks;
 };
 
 int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s);
