@@ -126,6 +126,23 @@ int dn_model_forward(dn_model* model, const void* x, const int64_t* shape, int n
 int dn_model_forward_host(dn_model* model, const void* x_host, const int64_t* shape, int ndim,
                           void* y_host, void* stream);
 
+/* Temporal models over a frame sequence with a frame cache (no reference
+ * counterpart: the reference CLI rebuilds and re-encodes a T-frame clip for
+ * every output frame, cli/main.cc:260-267). The model keeps the encoder
+ * features of T frames in slots 0 .. T-1:
+ *   dn_model_encode_frame  runs the encoder on one (1, C, H, W) frame into
+ *                          `slot`;
+ *   dn_model_decode_window denoises the window whose frame t sits in
+ *                          slots[t] (edge replication = a repeated slot),
+ *                          with `beauty` = the (1, C, H, W) reference frame,
+ *                          into y (1, 3, H, W).
+ * A sequence then encodes every frame once (frame f in slot f % T) instead of
+ * T times. The slots stay valid while the frame size does not change.
+ * DN_ERR_INVALID_ARG for spatial models or slots outside [0, T). */
+int dn_model_encode_frame(dn_model* model, const void* frame, int C, int H, int W, int slot, void* stream);
+int dn_model_decode_window(dn_model* model, const int* slots, int T, const void* beauty, int C, int H, int W,
+                           void* y, void* stream);
+
 /* Synchronise `stream`; DN_ERR_DEVICE if a kernel reported a device-side
  * error (e.g. a bounded wait that expired) since the last check. */
 int dn_model_sync(dn_model* model, void* stream);

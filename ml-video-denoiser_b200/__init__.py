@@ -84,6 +84,8 @@ SIGNATURES = {
     "dn_model_get_info": (_I, [_P, _c.POINTER(ModelInfo)]),
     "dn_model_forward": (_I, [_P, _P, _I64P, _I, _P, _P]),
     "dn_model_forward_host": (_I, [_P, _P, _I64P, _I, _P, _P]),
+    "dn_model_encode_frame": (_I, [_P, _P, _I, _I, _I, _I, _P]),
+    "dn_model_decode_window": (_I, [_P, _IP, _I, _P, _I, _I, _I, _P, _P]),
     "dn_model_sync": (_I, [_P, _P]),
     "dn_model_stats": (_I, [_P, _SZP, _SZP, _IP]),
     "dn_model_set_fused": (_I, [_P, _I]),
@@ -292,6 +294,25 @@ class Model:
         sh = (ctypes.c_int64 * len(shape))(*shape)
         check(lib().dn_model_forward_host(self._h, ctypes.c_void_p(x_ptr), sh, len(shape),
                                           ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream_ptr)))
+
+    def encode_frame(self, frame, slot: int, stream=None) -> None:
+        """Temporal models: encoder features of one (1, C, H, W) frame into cache slot `slot`."""
+        _, c, h, w = frame.shape
+        check(lib().dn_model_encode_frame(self._h, ctypes.c_void_p(frame.data_ptr()), c, h, w, slot,
+                                          stream_handle(stream)))
+
+    def decode_window(self, slots, beauty, out=None, stream=None):
+        """Temporal models: denoise the window whose frame t is in slots[t];
+        beauty = the (1, C, H, W) reference frame. Returns (1, 3, H, W)."""
+        import torch
+
+        _, c, h, w = beauty.shape
+        if out is None:
+            out = torch.empty(1, 3, h, w, dtype=torch.float16, device=beauty.device)
+        arr = (ctypes.c_int * len(slots))(*slots)
+        check(lib().dn_model_decode_window(self._h, arr, len(slots), ctypes.c_void_p(beauty.data_ptr()), c, h, w,
+                                           ctypes.c_void_p(out.data_ptr()), stream_handle(stream)))
+        return out
 
     def sync(self, stream=None) -> None:
         """Synchronise the stream and raise if a kernel flagged a device error."""

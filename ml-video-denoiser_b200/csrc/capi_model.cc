@@ -118,6 +118,24 @@ int dn_model_forward(dn_model* m, const void* x, const int64_t* shape, int ndim,
     });
 }
 
+int dn_model_encode_frame(dn_model* m, const void* frame, int C, int H, int W, int slot, void* stream) {
+    if (!m || !frame) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_encode_frame: null argument");
+    return guarded([&] {
+        return m->eng->encode_frame(static_cast<const __half*>(frame), C, H, W, slot, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int dn_model_decode_window(dn_model* m, const int* slots, int T, const void* beauty, int C, int H, int W, void* y,
+                           void* stream) {
+    if (!m || !slots || !beauty || !y) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_decode_window: null argument");
+    if (T != m->eng->info().num_frames)
+        return dn_fail(DN_ERR_INVALID_ARG, "dn_model_decode_window: T differs from the model's num_frames");
+    return guarded([&] {
+        return m->eng->decode_window(slots, static_cast<const __half*>(beauty), C, H, W, static_cast<__half*>(y),
+                                     static_cast<cudaStream_t>(stream));
+    });
+}
+
 int dn_model_forward_host(dn_model* m, const void* x_host, const int64_t* shape, int ndim, void* y_host,
                           void* stream) {
     if (!m || !x_host || !y_host) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_forward_host: null argument");

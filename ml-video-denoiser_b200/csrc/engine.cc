@@ -490,8 +490,8 @@ void Engine::plan(const Shape& s) {
         req.push_back({static_cast<size_t>(s.T) * hw0 * levels_[0].C * 2, reinterpret_cast<void**>(&warp_buf_)});
         req.push_back({hw0 * 8 * 2, reinterpret_cast<void**>(&offset_buf_)});
     }
+    if (temporal) req.push_back({hwm * Cm * 2, reinterpret_cast<void**>(&bneck_x_)});
     if (info_.kind == 2) {
-        req.push_back({hwm * Cm * 2, reinterpret_cast<void**>(&bneck_x_)});
         if (info_.use_warp) {
             const size_t hw0 = static_cast<size_t>(s.Hp) * s.Wp;
             req.push_back({hw0 * 2 * levels_[0].C * 2, reinterpret_cast<void**>(&oh_d_)});
@@ -785,18 +785,17 @@ int Engine::run_stage(const std::vector<BlockW>& blocks, __half* x, int nimg, in
     return DN_OK;
 }
 
-int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* y, cudaStream_t s) {
-    if (!x || !y) return dn_fail(DN_ERR_INVALID_ARG, "forward: null pointer");
+// Shape of an input of N images (clips of T frames) of C x H x W, padded to
+// the model's multiple; DN_OK or an error for shapes the engine rejects.
+int Engine::make_shape(int N, int T, int C, int H, int W, Shape& sh) {
     if (N <= 0 || H <= 0 || W <= 0) return dn_fail(DN_ERR_INVALID_ARG, "forward: empty input");
     if (C < info_.in_channels)
         return dn_fail(DN_ERR_INVALID_ARG, "forward: input has fewer channels than model expects");
     if (C < 3) return dn_fail(DN_ERR_INVALID_ARG, "forward: expected at least 3 input channels");
-    const bool temporal = info_.kind != 0;
-    if (temporal && T != info_.num_frames) return dn_fail(DN_ERR_INVALID_ARG, "forward: frame count mismatch");
-    if (!temporal && T != 1) return dn_fail(DN_ERR_INVALID_ARG, "forward: spatial model takes 4-D input");
     const int m = pad_multiple_;
-    Shape sh;
-    sh.N = N;
+    // Temporal models process one clip at a time: the arena (and with it the
+    // frame cache of encode_frame) does not depend on N.
+    sh.N = info_.kind != 0 ? 1 : N;
     sh.T = T;
     sh.H = H;
     sh.W = W;
@@ -806,218 +805,269 @@ int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* 
         return dn_fail(DN_ERR_INVALID_ARG, "forward: frame smaller than the reflect padding it needs");
     if (static_cast<long long>(N) * T * sh.Hp * sh.Wp > (1LL << 30))
         return dn_fail(DN_ERR_UNSUPPORTED, "forward: input too large");
-    DeviceGuard dg(device_);
     try {
         plan(sh);
     } catch (const std::exception& e) {
         return dn_fail(DN_ERR_CUDA, e.what());
     }
-    launches_ = 0;
+    return DN_OK;
+}
+
+// Intro + encoder over `nimg` NCHW images (image stride in_stride) into
+// encoder slots slot0 .. slot0 + nimg - 1: the per-level features land in
+// enc_x_[l] + slot * plane_l and the deep features in mid_x_ + slot * mplane.
+int Engine::encode_into(const __half* src, int nimg, int in_stride, int slot0, cudaStream_t s) {
+    const Shape& sh = shape_;
     const int L = info_.num_levels;
     const int C0 = info_.base_channels;
     const int in_c = info_.in_channels;
-
-    // Encoder over n_enc images (the frames of one clip for temporal models).
-    auto encode = [&](const __half* src, int nimg) -> int {
-        IntroParams ip{};
-        ip.x = src;
-        ip.N = nimg;
-        ip.Cin = in_c;
-        ip.H = H;
-        ip.W = W;
-        ip.Hp = sh.Hp;
-        ip.Wp = sh.Wp;
-        ip.C0 = C0;
-        ip.in_batch_stride = C * H * W;
-        ip.w = wptr<float>(intro_w_);
-        ip.b = wptr<float>(intro_b_);
-        ip.y = enc_x_[0];
-        ++launches_;
-        prof_begin("intro", static_cast<double>(nimg) * (static_cast<double>(in_c) * H * W + static_cast<double>(sh.Hp) * sh.Wp * C0) * 2,
-                   2.0 * nimg * sh.Hp * sh.Wp * C0 * in_c * 9, s);
-        DN_TRY(launch_intro(ip, s));
-        prof_end(s);
-        for (int l = 0; l < L; ++l) {
-            const int h = sh.Hp >> l, w = sh.Wp >> l;
-            DN_TRY(run_stage(levels_[l].enc, enc_x_[l], nimg, h, w, s));
-            GemmParams p = rows_params(nimg, h / 2, w / 2);
-            p.seg_c = levels_[l].C;
-            p.a_img_stride = static_cast<long long>(h) * w * levels_[l].C;
-            p.a[0] = enc_x_[l];
-            p.out = (l + 1 < L) ? enc_x_[l + 1] : mid_x_;
-            p.out_c = 2 * levels_[l].C;
-            DN_TRY(gemm(levels_[l].down, kProNone, kEpiStore, kAS2x2, p, s));
-        }
-        return DN_OK;
+    const int H = sh.H, W = sh.W;
+    auto slot_ptr = [&](__half* base, int l) {
+        const size_t plane = static_cast<size_t>(sh.Hp >> l) * (sh.Wp >> l) * (l < L ? levels_[l].C : levels_[L - 1].C * 2);
+        return base + static_cast<size_t>(slot0) * plane;
     };
-    // Middle + decoder on n images with the given per-level skips.
-    auto decode = [&](__half* xm, int nimg, const std::vector<__half*>& skips, const __half* beauty,
-                      int beauty_stride, __half* out) -> int {
-        const int hm = sh.Hp >> L, wm = sh.Wp >> L;
-        DN_TRY(run_stage(middle_, xm, nimg, hm, wm, s));
-        const __half* cur = xm;
-        for (int d = 0; d < L; ++d) {
-            const int lev = L - 1 - d;
-            const int h = sh.Hp >> (lev + 1), w = sh.Wp >> (lev + 1);
-            const int Cin = levels_[lev].C * 2;
-            GemmParams p = rows_params(nimg, h, w);
-            p.seg_c = Cin;
-            p.a_img_stride = static_cast<long long>(h) * w * Cin;
-            p.a[0] = cur;
-            p.out = dec_x_[lev];
-            p.out_c = levels_[lev].C;
-            p.skip = skips[lev];
-            DN_TRY(gemm(levels_[lev].up, kProNone, kEpiShuffleAdd, kARows, p, s));
-            DN_TRY(run_stage(levels_[lev].dec, dec_x_[lev], nimg, 2 * h, 2 * w, s));
-            cur = dec_x_[lev];
-        }
-        EndingParams ep{};
-        ep.x = dec_x_[0];
-        ep.N = nimg;
-        ep.Hp = sh.Hp;
-        ep.Wp = sh.Wp;
-        ep.C0 = C0;
-        ep.H = H;
-        ep.W = W;
-        ep.w = wptr<float>(ending_w_);
-        ep.b = wptr<float>(ending_b_);
-        ep.beauty = beauty;
-        ep.beauty_batch_stride = beauty_stride;
-        ep.y = out;
-        ++launches_;
-        prof_begin("ending", static_cast<double>(nimg) * (static_cast<double>(sh.Hp) * sh.Wp * C0 + 6.0 * H * W) * 2,
-                   2.0 * nimg * H * W * 3 * C0 * 9, s);
-        const int rc_end = launch_ending(ep, s);
-        prof_end(s);
-        return rc_end;
-    };
-
-    if (!temporal) {
-        DN_TRY(encode(x, N));
-        return decode(mid_x_, N, enc_x_, x, C * H * W, y);
+    IntroParams ip{};
+    ip.x = src;
+    ip.N = nimg;
+    ip.Cin = in_c;
+    ip.H = H;
+    ip.W = W;
+    ip.Hp = sh.Hp;
+    ip.Wp = sh.Wp;
+    ip.C0 = C0;
+    ip.in_batch_stride = in_stride;
+    ip.w = wptr<float>(intro_w_);
+    ip.b = wptr<float>(intro_b_);
+    ip.y = slot_ptr(enc_x_[0], 0);
+    ++launches_;
+    prof_begin("intro", static_cast<double>(nimg) * (static_cast<double>(in_c) * H * W + static_cast<double>(sh.Hp) * sh.Wp * C0) * 2,
+               2.0 * nimg * sh.Hp * sh.Wp * C0 * in_c * 9, s);
+    DN_TRY(launch_intro(ip, s));
+    prof_end(s);
+    for (int l = 0; l < L; ++l) {
+        const int h = sh.Hp >> l, w = sh.Wp >> l;
+        __half* xl = slot_ptr(enc_x_[l], l);
+        DN_TRY(run_stage(levels_[l].enc, xl, nimg, h, w, s));
+        GemmParams p = rows_params(nimg, h / 2, w / 2);
+        p.seg_c = levels_[l].C;
+        p.a_img_stride = static_cast<long long>(h) * w * levels_[l].C;
+        p.a[0] = xl;
+        p.out = (l + 1 < L) ? slot_ptr(enc_x_[l + 1], l + 1) : slot_ptr(mid_x_, L);
+        p.out_c = 2 * levels_[l].C;
+        DN_TRY(gemm(levels_[l].down, kProNone, kEpiStore, kAS2x2, p, s));
     }
+    return DN_OK;
+}
 
-    if (info_.kind == 2) {
-        // PyTorch NAFNetTemporal (training/models.py:738-808): every frame
-        // through the shared encoder (a batch of T images); bottleneck_mix
-        // over the T deep features, middle, per level temporal_mix over the
-        // T skips (neighbours warped by their offset head when present),
-        // decoder on the fused skips.
-        const int ref = T / 2;
-        const int hm = sh.Hp >> L, wm = sh.Wp >> L;
-        const size_t mplane = static_cast<size_t>(hm) * wm * levels_[L - 1].C * 2;
-        for (int n = 0; n < N; ++n) {
-            const __half* clip = x + static_cast<size_t>(n) * T * C * H * W;
-            DN_TRY(encode(clip, T));
-            GemmParams p = rows_params(1, hm, wm);
-            p.seg_c = levels_[L - 1].C * 2;
-            p.nseg = T;
-            for (int t = 0; t < T; ++t) p.a[t] = mid_x_ + t * mplane;
-            p.out = bneck_x_;
-            p.out_c = p.seg_c;
-            DN_TRY(gemm(bneck_, kProNone, kEpiStore, kARows, p, s));
-            DN_TRY(run_stage(bneck_blocks_, bneck_x_, 1, hm, wm, s));
-            for (int l = 0; l < L; ++l) {
-                const int h = sh.Hp >> l, w = sh.Wp >> l, Cl = levels_[l].C;
-                const size_t plane = static_cast<size_t>(h) * w * Cl;
-                const __half* rf = enc_x_[l] + ref * plane;
-                GemmParams q = rows_params(1, h, w);
-                q.seg_c = Cl;
-                q.nseg = T;
-                int wi = 0;
-                for (int t = 0; t < T; ++t) {
-                    const __half* f = enc_x_[l] + t * plane;
-                    if (info_.use_warp && t != ref) {
-                        // offset head: DW 3x3 over [ref, f] -> PW -> ReLU -> PW -> (dx, dy)
-                        ++launches_;
-                        prof_begin("offset_dw", static_cast<double>(h) * w * 6 * Cl * 2, 36.0 * h * w * Cl, s);
-                        DN_TRY(launch_dw_pair(rf, f, wptr<float>(oh_dw_[l]), oh_d_, h, w, Cl, s));
-                        prof_end(s);
-                        GemmParams o = rows_params(1, h, w);
-                        o.seg_c = 2 * Cl;
-                        o.a[0] = oh_d_;
-                        o.out = oh_h_;
-                        o.out_c = Cl;
-                        o.relu = 1;
-                        DN_TRY(gemm(oh_pw1_[l], kProNone, kEpiStore, kARows, o, s));
-                        o = rows_params(1, h, w);
-                        o.seg_c = Cl;
-                        o.a[0] = oh_h_;
-                        o.out = offset_buf_;
-                        o.out_c = 8;
-                        DN_TRY(gemm(oh_pw2_[l], kProNone, kEpiStore, kARows, o, s));
-                        __half* wb = warp_buf_ + wi * plane;
-                        ++wi;
-                        ++launches_;
-                        prof_begin("warp", static_cast<double>(h) * w * (2 * Cl + 16) * 2, 8.0 * h * w * Cl, s);
-                        DN_TRY(launch_warp_pixel(f, offset_buf_, 8, wb, 1, h, w, Cl, static_cast<float>(w - 1) / w,
-                                                 static_cast<float>(h - 1) / h, s));
-                        prof_end(s);
-                        f = wb;
-                    }
-                    q.a[t] = f;
-                }
-                q.out = fused_skip_[l];
-                q.out_c = Cl;
-                DN_TRY(gemm(tmix_[l], kProNone, kEpiStore, kARows, q, s));
-                DN_TRY(run_stage(tmix_blocks_[l], fused_skip_[l], 1, h, w, s));
-            }
-            const __half* beauty = clip + static_cast<size_t>(ref) * C * H * W;
-            DN_TRY(decode(bneck_x_, 1, fused_skip_, beauty, C * H * W, y + static_cast<size_t>(n) * 3 * H * W));
-        }
-        return DN_OK;
+// Middle + decoder + ending on `nimg` images from the deep features xm (in
+// place) and the per-level skips; out = beauty + residual, NCHW.
+int Engine::decode_from(__half* xm, int nimg, const std::vector<__half*>& skips, const __half* beauty,
+                        int beauty_stride, __half* out, cudaStream_t s) {
+    const Shape& sh = shape_;
+    const int L = info_.num_levels;
+    const int C0 = info_.base_channels;
+    const int H = sh.H, W = sh.W;
+    const int hm = sh.Hp >> L, wm = sh.Wp >> L;
+    DN_TRY(run_stage(middle_, xm, nimg, hm, wm, s));
+    const __half* cur = xm;
+    for (int d = 0; d < L; ++d) {
+        const int lev = L - 1 - d;
+        const int h = sh.Hp >> (lev + 1), w = sh.Wp >> (lev + 1);
+        const int Cin = levels_[lev].C * 2;
+        GemmParams p = rows_params(nimg, h, w);
+        p.seg_c = Cin;
+        p.a_img_stride = static_cast<long long>(h) * w * Cin;
+        p.a[0] = cur;
+        p.out = dec_x_[lev];
+        p.out_c = levels_[lev].C;
+        p.skip = skips[lev];
+        DN_TRY(gemm(levels_[lev].up, kProNone, kEpiShuffleAdd, kARows, p, s));
+        DN_TRY(run_stage(levels_[lev].dec, dec_x_[lev], nimg, 2 * h, 2 * w, s));
+        cur = dec_x_[lev];
     }
+    EndingParams ep{};
+    ep.x = dec_x_[0];
+    ep.N = nimg;
+    ep.Hp = sh.Hp;
+    ep.Wp = sh.Wp;
+    ep.C0 = C0;
+    ep.H = H;
+    ep.W = W;
+    ep.w = wptr<float>(ending_w_);
+    ep.b = wptr<float>(ending_b_);
+    ep.beauty = beauty;
+    ep.beauty_batch_stride = beauty_stride;
+    ep.y = out;
+    ++launches_;
+    prof_begin("ending", static_cast<double>(nimg) * (static_cast<double>(sh.Hp) * sh.Wp * C0 + 6.0 * H * W) * 2,
+               2.0 * nimg * H * W * 3 * C0 * 9, s);
+    const int rc_end = launch_ending(ep, s);
+    prof_end(s);
+    return rc_end;
+}
 
-    // Temporal model of the C++ engine (nafnet_temporal.cu:363-503): every
-    // frame of the clip through the shared encoder (as a batch of T images),
-    // middle on the reference frame, per-level fused skip
-    // temporal_mix(concat(ref, mean_t warp?(nbr_t))), then the decoder.
+// Temporal tail of one clip whose frame t sits in encoder slot slots[t]:
+// the temporal fusion of the skips (and, in the PyTorch design, of the deep
+// features), middle, decoder and ending; beauty = the reference frame. The
+// slots are only read, so they can be reused for the next window.
+int Engine::temporal_tail(const int* slots, const __half* beauty, int beauty_stride, __half* y, cudaStream_t s) {
+    const Shape& sh = shape_;
+    const int L = info_.num_levels;
+    const int T = info_.num_frames;
     const int ref = T / 2;
-    for (int n = 0; n < N; ++n) {
-        const __half* clip = x + static_cast<size_t>(n) * T * C * H * W;
-        DN_TRY(encode(clip, T));
+    const int hm = sh.Hp >> L, wm = sh.Wp >> L;
+    const size_t mplane = static_cast<size_t>(hm) * wm * levels_[L - 1].C * 2;
+    if (info_.kind == 2) {
+        // PyTorch NAFNetTemporal (training/models.py:738-808): bottleneck_mix
+        // over the T deep features, middle, per level temporal_mix over the T
+        // skips (neighbours warped by their offset head when present).
+        GemmParams p = rows_params(1, hm, wm);
+        p.seg_c = levels_[L - 1].C * 2;
+        p.nseg = T;
+        for (int t = 0; t < T; ++t) p.a[t] = mid_x_ + slots[t] * mplane;
+        p.out = bneck_x_;
+        p.out_c = p.seg_c;
+        DN_TRY(gemm(bneck_, kProNone, kEpiStore, kARows, p, s));
+        DN_TRY(run_stage(bneck_blocks_, bneck_x_, 1, hm, wm, s));
         for (int l = 0; l < L; ++l) {
             const int h = sh.Hp >> l, w = sh.Wp >> l, Cl = levels_[l].C;
             const size_t plane = static_cast<size_t>(h) * w * Cl;
-            const __half* rf = enc_x_[l] + ref * plane;
-            GemmParams p = rows_params(1, h, w);
-            p.seg_c = Cl;
-            p.a_img_stride = 0;
-            p.nseg = T;
-            p.a[0] = rf;
-            int si = 1;
+            const __half* rf = enc_x_[l] + slots[ref] * plane;
+            GemmParams q = rows_params(1, h, w);
+            q.seg_c = Cl;
+            q.nseg = T;
+            int wi = 0;
             for (int t = 0; t < T; ++t) {
-                if (t == ref) continue;
-                const __half* nb = enc_x_[l] + t * plane;
-                if (info_.use_warp) {
-                    GemmParams q = rows_params(1, h, w);
-                    q.seg_c = Cl;
-                    q.a_img_stride = 0;
-                    q.nseg = 2;
-                    q.a[0] = rf;
-                    q.a[1] = nb;
-                    q.out = offset_buf_;
-                    q.out_c = 8;
-                    DN_TRY(gemm(offset_heads_[l], kProNone, kEpiStore, kARows, q, s));
-                    __half* wb = warp_buf_ + (si - 1) * plane;
+                const __half* f = enc_x_[l] + slots[t] * plane;
+                if (info_.use_warp && t != ref) {
+                    // offset head: DW 3x3 over [ref, f] -> PW -> ReLU -> PW -> (dx, dy)
+                    ++launches_;
+                    prof_begin("offset_dw", static_cast<double>(h) * w * 6 * Cl * 2, 36.0 * h * w * Cl, s);
+                    DN_TRY(launch_dw_pair(rf, f, wptr<float>(oh_dw_[l]), oh_d_, h, w, Cl, s));
+                    prof_end(s);
+                    GemmParams o = rows_params(1, h, w);
+                    o.seg_c = 2 * Cl;
+                    o.a[0] = oh_d_;
+                    o.out = oh_h_;
+                    o.out_c = Cl;
+                    o.relu = 1;
+                    DN_TRY(gemm(oh_pw1_[l], kProNone, kEpiStore, kARows, o, s));
+                    o = rows_params(1, h, w);
+                    o.seg_c = Cl;
+                    o.a[0] = oh_h_;
+                    o.out = offset_buf_;
+                    o.out_c = 8;
+                    DN_TRY(gemm(oh_pw2_[l], kProNone, kEpiStore, kARows, o, s));
+                    __half* wb = warp_buf_ + wi * plane;
+                    ++wi;
                     ++launches_;
                     prof_begin("warp", static_cast<double>(h) * w * (2 * Cl + 16) * 2, 8.0 * h * w * Cl, s);
-                    DN_TRY(launch_warp_pixel(nb, offset_buf_, 8, wb, 1, h, w, Cl, 1.f, 1.f, s));
+                    DN_TRY(launch_warp_pixel(f, offset_buf_, 8, wb, 1, h, w, Cl, static_cast<float>(w - 1) / w,
+                                             static_cast<float>(h - 1) / h, s));
                     prof_end(s);
-                    nb = wb;
+                    f = wb;
                 }
-                p.a[si++] = nb;
+                q.a[t] = f;
             }
-            p.out = fused_skip_[l];
-            p.out_c = Cl;
-            DN_TRY(gemm(tmix_[l], kProNone, kEpiStore, kARows, p, s));
+            q.out = fused_skip_[l];
+            q.out_c = Cl;
+            DN_TRY(gemm(tmix_[l], kProNone, kEpiStore, kARows, q, s));
+            DN_TRY(run_stage(tmix_blocks_[l], fused_skip_[l], 1, h, w, s));
         }
-        const size_t mplane = static_cast<size_t>(sh.Hp >> L) * (sh.Wp >> L) * levels_[L - 1].C * 2;
-        const __half* beauty = clip + static_cast<size_t>(ref) * C * H * W;
-        DN_TRY(decode(mid_x_ + ref * mplane, 1, fused_skip_, beauty, C * H * W,
-                      y + static_cast<size_t>(n) * 3 * H * W));
+        return decode_from(bneck_x_, 1, fused_skip_, beauty, beauty_stride, y, s);
+    }
+    // Temporal model of the C++ engine (nafnet_temporal.cu:363-503): middle on
+    // the reference frame's deep feature (a copy: the middle runs in place),
+    // per-level fused skip temporal_mix(concat(ref, mean_t warp?(nbr_t))).
+    for (int l = 0; l < L; ++l) {
+        const int h = sh.Hp >> l, w = sh.Wp >> l, Cl = levels_[l].C;
+        const size_t plane = static_cast<size_t>(h) * w * Cl;
+        const __half* rf = enc_x_[l] + slots[ref] * plane;
+        GemmParams p = rows_params(1, h, w);
+        p.seg_c = Cl;
+        p.a_img_stride = 0;
+        p.nseg = T;
+        p.a[0] = rf;
+        int si = 1;
+        for (int t = 0; t < T; ++t) {
+            if (t == ref) continue;
+            const __half* nb = enc_x_[l] + slots[t] * plane;
+            if (info_.use_warp) {
+                GemmParams q = rows_params(1, h, w);
+                q.seg_c = Cl;
+                q.a_img_stride = 0;
+                q.nseg = 2;
+                q.a[0] = rf;
+                q.a[1] = nb;
+                q.out = offset_buf_;
+                q.out_c = 8;
+                DN_TRY(gemm(offset_heads_[l], kProNone, kEpiStore, kARows, q, s));
+                __half* wb = warp_buf_ + (si - 1) * plane;
+                ++launches_;
+                prof_begin("warp", static_cast<double>(h) * w * (2 * Cl + 16) * 2, 8.0 * h * w * Cl, s);
+                DN_TRY(launch_warp_pixel(nb, offset_buf_, 8, wb, 1, h, w, Cl, 1.f, 1.f, s));
+                prof_end(s);
+                nb = wb;
+            }
+            p.a[si++] = nb;
+        }
+        p.out = fused_skip_[l];
+        p.out_c = Cl;
+        DN_TRY(gemm(tmix_[l], kProNone, kEpiStore, kARows, p, s));
+    }
+    cudaError_t e = cudaMemcpyAsync(bneck_x_, mid_x_ + slots[ref] * mplane, mplane * 2, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return dn_cuda_fail(e, "temporal: reference deep feature copy");
+    return decode_from(bneck_x_, 1, fused_skip_, beauty, beauty_stride, y, s);
+}
+
+int Engine::forward(const __half* x, int N, int T, int C, int H, int W, __half* y, cudaStream_t s) {
+    if (!x || !y) return dn_fail(DN_ERR_INVALID_ARG, "forward: null pointer");
+    const bool temporal = info_.kind != 0;
+    if (temporal && T != info_.num_frames) return dn_fail(DN_ERR_INVALID_ARG, "forward: frame count mismatch");
+    if (!temporal && T != 1) return dn_fail(DN_ERR_INVALID_ARG, "forward: spatial model takes 4-D input");
+    DeviceGuard dg(device_);
+    Shape sh;
+    DN_TRY(make_shape(N, T, C, H, W, sh));
+    launches_ = 0;
+    if (!temporal) {
+        DN_TRY(encode_into(x, N, C * H * W, 0, s));
+        return decode_from(mid_x_, N, enc_x_, x, C * H * W, y, s);
+    }
+    // Every frame of a clip through the shared encoder as one batch of T
+    // images (slots 0 .. T-1), then the temporal tail on those slots.
+    std::vector<int> slots(T);
+    for (int t = 0; t < T; ++t) slots[t] = t;
+    const int ref = T / 2;
+    for (int n = 0; n < N; ++n) {
+        const __half* clip = x + static_cast<size_t>(n) * T * C * H * W;
+        DN_TRY(encode_into(clip, T, C * H * W, 0, s));
+        DN_TRY(temporal_tail(slots.data(), clip + static_cast<size_t>(ref) * C * H * W, C * H * W,
+                             y + static_cast<size_t>(n) * 3 * H * W, s));
     }
     return DN_OK;
+}
+
+int Engine::encode_frame(const __half* frame, int C, int H, int W, int slot, cudaStream_t s) {
+    if (!frame) return dn_fail(DN_ERR_INVALID_ARG, "encode_frame: null pointer");
+    if (info_.kind == 0) return dn_fail(DN_ERR_INVALID_ARG, "encode_frame: spatial models have no frame cache");
+    if (slot < 0 || slot >= info_.num_frames) return dn_fail(DN_ERR_INVALID_ARG, "encode_frame: slot outside [0, T)");
+    DeviceGuard dg(device_);
+    Shape sh;
+    DN_TRY(make_shape(1, info_.num_frames, C, H, W, sh));
+    launches_ = 0;
+    return encode_into(frame, 1, C * H * W, slot, s);
+}
+
+int Engine::decode_window(const int* slots, const __half* beauty, int C, int H, int W, __half* y, cudaStream_t s) {
+    if (!slots || !beauty || !y) return dn_fail(DN_ERR_INVALID_ARG, "decode_window: null pointer");
+    if (info_.kind == 0) return dn_fail(DN_ERR_INVALID_ARG, "decode_window: spatial models have no frame cache");
+    for (int t = 0; t < info_.num_frames; ++t)
+        if (slots[t] < 0 || slots[t] >= info_.num_frames)
+            return dn_fail(DN_ERR_INVALID_ARG, "decode_window: slot outside [0, T)");
+    DeviceGuard dg(device_);
+    Shape sh;
+    DN_TRY(make_shape(1, info_.num_frames, C, H, W, sh));
+    return temporal_tail(slots, beauty, C * H * W, y, s);
 }
 
 int Engine::check_device(cudaStream_t s) {

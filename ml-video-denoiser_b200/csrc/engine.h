@@ -66,6 +66,14 @@ public:
     // Returns DN_OK or a DN_ERR_* code (message via dn_last_error).
     int forward(const __half* x, int N, int T, int C, int H, int W, __half* y, cudaStream_t s);
 
+    // Temporal models, one sequence frame at a time: encode_frame runs the
+    // encoder on one (1, C, H, W) frame into cache slot `slot` (0 .. T-1);
+    // decode_window denoises the window whose frame t is in slots[t], with
+    // `beauty` = the (1, C, H, W) reference frame. A sequence then encodes
+    // every frame once instead of T times.
+    int encode_frame(const __half* frame, int C, int H, int W, int slot, cudaStream_t s);
+    int decode_window(const int* slots, const __half* beauty, int C, int H, int W, __half* y, cudaStream_t s);
+
     // Waits for `s` and returns DN_ERR_DEVICE if a kernel flagged an error
     // since the last check (the word is cleared).
     int check_device(cudaStream_t s);
@@ -104,6 +112,11 @@ private:
 
     void build(const HostWeights& hw);
     void plan(const Shape& s);
+    int make_shape(int N, int T, int C, int H, int W, Shape& sh);
+    int encode_into(const __half* src, int nimg, int in_stride, int slot0, cudaStream_t s);
+    int decode_from(__half* xm, int nimg, const std::vector<__half*>& skips, const __half* beauty, int beauty_stride,
+                    __half* out, cudaStream_t s);
+    int temporal_tail(const int* slots, const __half* beauty, int beauty_stride, __half* y, cudaStream_t s);
     int run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaStream_t s);
     int run_stage(const std::vector<BlockW>& blocks, __half* x, int nimg, int h, int w, cudaStream_t s);
     int gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cudaStream_t s,

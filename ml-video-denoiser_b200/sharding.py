@@ -59,25 +59,43 @@ def plan(n_frames: int, world: int, num_frames: int = 1) -> list[dict]:
     return out
 
 
-def denoise_segment(model, frames, n_frames: int, world: int, rank: int, num_frames: int = 1, stream=None):
+def denoise_segment(model, frames, n_frames: int, world: int, rank: int, num_frames: int = 1, stream=None,
+                    cache: bool = True):
     """Denoise this rank's segment on its device.
 
     `model` is a ``Model`` (spatial when num_frames == 1, else temporal with
     that window); `frames(i)` returns frame i as a (C, H, W) FP16 CUDA tensor.
     Returns the list of (frame index, (3, H, W) output) for the segment.
-    Each frame is loaded once; a temporal clip is assembled from the loaded
-    frames on the device."""
+
+    Temporal models use the engine's frame cache (``cache=True``): frame f is
+    encoded once into slot f % T (distinct frames of one window never share a
+    slot) and each output decodes its window from the slots, so the encoder
+    runs once per loaded frame instead of T times per output. With
+    ``cache=False`` every window is assembled as a (1, T, C, H, W) clip."""
     import torch
 
     s, e = segment(n_frames, world, rank)
-    loads = needed_frames(n_frames, world, rank, num_frames)
-    cache = {f: frames(f) for f in loads}
     results = []
+    if num_frames == 1:
+        for i in range(s, e):
+            y = model(frames(i).unsqueeze(0).contiguous(), stream=stream)
+            results.append((i, y[0]))
+        return results
+    if not cache:
+        loads = needed_frames(n_frames, world, rank, num_frames)
+        held = {f: frames(f) for f in loads}
+        for i in range(s, e):
+            x = torch.stack([held[f] for f in window(i, num_frames, n_frames)], dim=0).unsqueeze(0)
+            results.append((i, model(x.contiguous(), stream=stream)[0]))
+        return results
+    T = num_frames
+    in_slot = [-1] * T  # frame index held by each slot
     for i in range(s, e):
-        if num_frames == 1:
-            x = cache[i].unsqueeze(0)
-        else:
-            x = torch.stack([cache[f] for f in window(i, num_frames, n_frames)], dim=0).unsqueeze(0)
-        y = model(x.contiguous(), stream=stream)
+        win = window(i, T, n_frames)
+        for f in win:
+            if in_slot[f % T] != f:
+                model.encode_frame(frames(f).unsqueeze(0).contiguous(), f % T, stream=stream)
+                in_slot[f % T] = f
+        y = model.decode_window([f % T for f in win], frames(i).unsqueeze(0).contiguous(), stream=stream)
         results.append((i, y[0]))
     return results

@@ -112,11 +112,41 @@ def test_sharded_temporal_engine_equals_single_rank(pkg, S, tmp_path):
     n, H, W = 7, 36, 44
     rng = np.random.default_rng(5)
     seq = [torch.from_numpy(rng.uniform(0, 1, (3, H, W)).astype(np.float16)).cuda() for _ in range(n)]
-    whole = dict(S.denoise_segment(m, lambda i: seq[i], n, 1, 0, 3))
+    whole = {i: y.clone() for i, y in S.denoise_segment(m, lambda i: seq[i], n, 1, 0, 3, cache=False)}
     parts = {}
     for r in range(3):
-        parts.update({i: y.clone() for i, y in S.denoise_segment(m, lambda i: seq[i], n, 3, r, 3)})
+        parts.update({i: y.clone() for i, y in S.denoise_segment(m, lambda i: seq[i], n, 3, r, 3, cache=False)})
     torch.cuda.synchronize()
     assert sorted(parts) == list(range(n))
     for i in range(n):
         assert torch.equal(parts[i], whole[i]), i
+    # the frame cache (each frame encoded once) gives the same frames: the
+    # per-frame encoder pools over one image instead of a batch of T, so the
+    # pool sums group differently and agree to FP32 rounding
+    cached = {}
+    for r in range(3):
+        cached.update({i: y.clone() for i, y in S.denoise_segment(m, lambda i: seq[i], n, 3, r, 3, cache=True)})
+    m.sync()
+    for i in range(n):
+        assert float((cached[i].float() - whole[i].float()).abs().max()) <= 2e-3, i
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind,T", [("legacy", 3), ("py", 5)])
+def test_frame_cache_matches_clip_forward(pkg, S, tmp_path, kind, T):
+    import torch
+
+    synth = importlib.import_module(pkg.__name__ + ".synth")
+    cfg = synth.NAFConfig(base_channels=8, enc_blocks=(1, 1), middle_blocks=1, dec_blocks=(1, 1))
+    path, _ = synth.make_model_dir(str(tmp_path), cfg, 4, kind, T, True)
+    m = pkg.Model(path)
+    n, H, W = 9, 30, 42
+    rng = np.random.default_rng(6)
+    seq = [torch.from_numpy(rng.uniform(0, 1, (3, H, W)).astype(np.float16)).cuda() for _ in range(n)]
+    ref = {i: y.clone() for i, y in S.denoise_segment(m, lambda i: seq[i], n, 1, 0, T, cache=False)}
+    got = {i: y.clone() for i, y in S.denoise_segment(m, lambda i: seq[i], n, 1, 0, T, cache=True)}
+    m.sync()
+    for i in range(n):
+        assert float((got[i].float() - ref[i].float()).abs().max()) <= 2e-3, i
+    with pytest.raises(pkg.InvalidArgumentError):
+        m.encode_frame(seq[0].unsqueeze(0), T)
