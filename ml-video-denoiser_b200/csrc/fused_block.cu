@@ -90,7 +90,8 @@ struct GeoB {
     static constexpr int W4_BYTES = 2 * F * C * 2;
     static constexpr int W5_BYTES = C * F * 2;
     static constexpr int F_FLOATS = 6 * C + 2 * F + 8 * D;
-    static constexpr int SMEM = 1024 + G_BYTES + 3 * X_BYTES + A3_BYTES + W3_BYTES + W4_BYTES + W5_BYTES +
+    // x, LN2(y) (which doubles as the output staging tile once conv4 has read it)
+    static constexpr int SMEM = 1024 + G_BYTES + 2 * X_BYTES + A3_BYTES + W3_BYTES + W4_BYTES + W5_BYTES +
                                 F_FLOATS * 4;
 };
 
@@ -388,8 +389,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
     uint8_t* sG = smem;                  // [128][D] swizzled (span 2D)
     uint8_t* sX = sG + G::G_BYTES;       // [128][C] swizzled (span 2C)
     uint8_t* sA2 = sX + G::X_BYTES;      // LN2(y)
-    uint8_t* sO = sA2 + G::X_BYTES;      // output staging
-    uint8_t* sA3 = sO + G::X_BYTES;      // gated FFN (span 2F)
+    uint8_t* sO = sA2;                   // output staging: LN2(y) is dead once conv4 has read it
+    uint8_t* sA3 = sA2 + G::X_BYTES;     // gated FFN (span 2F)
     uint8_t* sW3 = sA3 + G::A3_BYTES;
     uint8_t* sW4 = sW3 + G::W3_BYTES;
     uint8_t* sW5 = sW4 + G::W4_BYTES;
@@ -475,6 +476,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
             }
         }
         fence_async_smem();
+        if (tid == 0) bulk_wait_read0();  // the previous output tile has left sO (= sA2, written below)
         __syncthreads();
         if (tid == 0) {  // conv3: [128 x D] x [D -> C]
             tc_fence_after();
