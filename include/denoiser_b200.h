@@ -152,9 +152,11 @@ int dn_model_sync(dn_model* model, void* stream);
 int dn_model_stats(const dn_model* model, size_t* weight_bytes, size_t* activation_bytes,
                    int* kernels_per_forward);
 
-/* Select the fused two-pass NAFBlock kernels for blocks with <= 64 channels
- * (default 1) or the per-conv kernels everywhere (0). Results agree within
- * the parity tolerance; the switch exists for testing both paths. */
+/* Select the fused NAFBlock kernels (default 1): both passes for blocks with
+ * <= 64 channels, the single-kernel second pass for 128- and 256-channel
+ * blocks of a single-image forward; or the per-conv kernels everywhere (0).
+ * Results agree within the parity tolerance; the switch exists for testing
+ * both paths. */
 int dn_model_set_fused(dn_model* model, int enable);
 
 /* Per-launch CUDA-event timing of the engine's kernels (no reference

@@ -1,0 +1,529 @@
+// Second pass of a deep NAFBlock (C = 128 or 256 channels) in one kernel:
+//
+//   y   = x + beta * (g (W3 diag(s))^T + b3)          conv3, SCA scale in W3
+//   h   = SimpleGate(LN2(y) W4^T + b4)                 LN2 folded into W4
+//   out = y + gamma * (h W5^T + b5)                    conv5
+//
+// the tail of the reference block (src/models/nafnet.cu:176-215:
+// scaled add, LayerNorm, conv4, bias, gate, conv5, bias, scaled add;
+// training/models.py:178-185), which the separate-GEMM path runs as three
+// launches with y and h round-tripping through memory.
+//
+// One CTA (320 threads) owns a stream of 128-pixel tiles:
+//   warp 0   producer: walks the tile's operand units - 16 KB slices of
+//            [128 x 64] fp16 - through an R-deep shared-memory ring: g and x
+//            boxes by TMA (128-byte swizzle), weight slices by bulk copy from
+//            the engine's pre-packed GEMM images (no swizzle, K-major).
+//   warp 1   MMA issuer: conv3 into TMEM columns [0, C); conv4 per 64-channel
+//            gate chunk j (a and b halves side by side, N = 128) into one of
+//            two TMEM buffers at [C, C + 256); conv5 accumulating into [0, C)
+//            (conv3's columns are free by then) with the gated chunk as A.
+//            Issue order conv4_0, conv4_1, conv5_0, conv4_2, conv5_1, ... so
+//            the next conv4 overlaps the epilogue of the current chunk.
+//   warps 2-9 epilogue, two threads per tile row (a TMEM lane) splitting its
+//            columns: (1) y -> sY (fp16, the swizzled A of conv4) and the
+//            LN2 statistics of the fp16 y (pairs merged with Chan's formula);
+//            (2) per chunk h = (rstd*acc_a + c2a - rstd*mean*c1a) *
+//            (rstd*acc_b + ...) -> sH[j % 2]; (3) out = y + gamma*(acc + b5)
+//            written over y in sY, then TMA-stored.
+// Per pixel this reads g and x and writes out (the 3C*2-byte minimum for the
+// pass, D = C); weights stream from L2 once per tile. Every wait is bounded.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+
+#include "fused_block.h"
+#include "launch.cuh"
+#include "sm100.cuh"
+#include "status.h"
+
+namespace dnb {
+
+namespace {
+
+constexpr int kDThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-9 epilogue
+constexpr int kUnit = 16384;     // one ring unit: [128 rows x 64] fp16
+
+template <int C, int D, int F>
+struct GeoD {
+    static constexpr int R = C >= 256 ? 6 : 8;            // ring units
+    static constexpr int KD = D / 64;                     // conv3 K chunks
+    static constexpr int KC4 = C / 64;                    // conv4 K chunks
+    static constexpr int J = F / 64;                      // gate chunks
+    static constexpr int NH = C / 128;                    // 128-column slices of a C-wide output
+    static constexpr int U3 = KD * (1 + NH);              // conv3 units: A box + NH weight slices per chunk
+    static constexpr int UX = C / 64;                     // x boxes
+    static constexpr int U = U3 + UX + J * KC4 + J * NH;  // units per tile
+    static constexpr int Y_BYTES = 128 * C * 2;
+    static constexpr int H_BYTES = 128 * 64 * 2;
+    static constexpr int P_FLOATS = 4 * C + 4 * F;        // b3, beta, gamma, b5, c1[2F], c2[2F]
+    static constexpr int SMEM = 1024 + Y_BYTES + 2 * H_BYTES + R * kUnit + P_FLOATS * 4;
+    static constexpr int TMEM_COLS = 512;                 // C + 2 x 128 <= 512
+    static_assert(C + 256 <= 512, "TMEM: conv3/conv5 accumulator + two gate-chunk buffers");
+    static_assert(D % 64 == 0 && F % 128 == 0 && C % 128 == 0, "tile geometry");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
+}
+
+__device__ __forceinline__ void epi_sync() { named_sync(1, 256); }
+__device__ __forceinline__ bool epi_sync_or(bool v) { return named_sync_or(1, 256, v); }
+
+template <int C, int D, int F>
+__global__ void __launch_bounds__(kDThreads, 1)
+    deep_b_kernel(const __grid_constant__ DeepBParams p, const __grid_constant__ CUtensorMap mg,
+                  const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mo) {
+    using G = GeoD<C, D, F>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sY = smem;                   // C/64 boxes [128 x 64], 128-byte swizzle: y, then out
+    uint8_t* sH = sY + G::Y_BYTES;        // 2 gate chunks [128 x 64], same layout
+    uint8_t* ring = sH + 2 * G::H_BYTES;  // R units
+    float* sB3 = reinterpret_cast<float*>(ring + G::R * kUnit);
+    float* sBeta = sB3 + C;
+    float* sGam = sBeta + C;
+    float* sB5 = sGam + C;
+    float* sC1 = sB5 + C;  // [2F], conv4 packed order
+    float* sC2 = sC1 + 2 * F;
+    __shared__ uint64_t full[G::R], empty[G::R];
+    __shared__ uint64_t acc3_full, y_ready, acc5_full, acc_free, mma_done;
+    __shared__ uint64_t acc4_full[2], acc4_empty[2], h_full[2], h_empty[2];
+    __shared__ float2 s_stat[2][128];
+    __shared__ uint32_t tslot;
+    __shared__ volatile int s_abort;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tiles = (p.M + 127) / 128;
+
+    pdl_trigger();
+    for (int i = tid; i < C; i += kDThreads) {
+        sB3[i] = p.b3[i];
+        sBeta[i] = p.beta[i];
+        sGam[i] = p.gamma[i];
+        sB5[i] = p.b5[i];
+    }
+    for (int i = tid; i < 2 * F; i += kDThreads) {
+        sC1[i] = p.c1[i];
+        sC2[i] = p.c2[i];
+    }
+    if (warp == 0) {
+        tmem_alloc(&tslot, G::TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (tid == 32) {
+        for (int s = 0; s < G::R; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&acc3_full, 1);
+        mbar_init(&y_ready, 1);
+        mbar_init(&acc5_full, 1);
+        mbar_init(&acc_free, 1);
+        mbar_init(&mma_done, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc4_full[b], 1);
+            mbar_init(&acc4_empty[b], 1);
+            mbar_init(&h_full[b], 1);
+            mbar_init(&h_empty[b], 1);
+        }
+        s_abort = 0;
+        fence_mbar_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    pdl_wait();  // g, x and the SCA-scaled conv3 image come from earlier kernels
+
+    if (warp == 0) {
+        // ------------------------------ producer ---------------------------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            // Next ring slot, once free, armed for `bytes`; nullptr on abort.
+            auto slot = [&](uint32_t bytes, uint64_t*& bar) -> uint8_t* {
+                const uint32_t s = it % G::R, ph = (it / G::R) & 1u;
+                ++it;
+                if (!wait_or_abort(&empty[s], ph ^ 1u, &s_abort, p.err, 0x50)) {
+                    ok = false;
+                    return nullptr;
+                }
+                bar = &full[s];
+                mbar_arrive_expect_tx(bar, bytes);
+                return ring + s * kUnit;
+            };
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = t * 128;
+                uint64_t* bar = nullptr;
+                uint8_t* u;
+                for (int kk = 0; kk < G::KD && ok; ++kk) {
+                    if (!(u = slot(kUnit, bar))) break;
+                    tma_load_2d(u, &mg, kk * 64, m0, bar);
+                    for (int h = 0; h < G::NH && ok; ++h) {
+                        if (!(u = slot(kUnit, bar))) break;
+                        bulk_g2s(u, p.w3 + static_cast<size_t>(kk) * C * 128 + h * kUnit, kUnit, bar);
+                    }
+                }
+                for (int kk = 0; kk < C / 64 && ok; ++kk) {
+                    if (!(u = slot(kUnit, bar))) break;
+                    tma_load_2d(u, &mx, kk * 64, m0, bar);
+                }
+                // conv4 chunk j: rows [64(j%2), +64) (a) and [128 + 64(j%2), +64)
+                // (b) of packed tile j/2, per K chunk: two contiguous 8 KB slices.
+                auto c4 = [&](int j) {
+                    const uint8_t* src = p.w4 + static_cast<size_t>(j >> 1) * G::KC4 * 32768 + (j & 1) * 8192;
+                    for (int kk = 0; kk < G::KC4 && ok; ++kk) {
+                        if (!(u = slot(kUnit, bar))) return;
+                        bulk_g2s(u, src + kk * 32768, 8192, bar);
+                        bulk_g2s(u + 8192, src + kk * 32768 + 16384, 8192, bar);
+                    }
+                };
+                // conv5 chunk j: K chunk j of the [C x F] image, in 128-row slices.
+                auto c5 = [&](int j) {
+                    for (int h = 0; h < G::NH && ok; ++h) {
+                        if (!(u = slot(kUnit, bar))) return;
+                        bulk_g2s(u, p.w5 + static_cast<size_t>(j) * C * 128 + h * kUnit, kUnit, bar);
+                    }
+                };
+                c4(0);
+                for (int j = 1; j < G::J && ok; ++j) {
+                    c4(j);
+                    c5(j - 1);
+                }
+                c5(G::J - 1);
+            }
+            if (!ok) {
+                // Let the copies already issued land before the CTA's memory is released.
+                const uint32_t lo = it > static_cast<uint32_t>(G::R) ? it - G::R : 0u;
+                for (uint32_t v = lo; v + 1 < it; ++v) mbar_wait(&full[v % G::R], (v / G::R) & 1u, 5000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer -------------------------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(128, 128);
+            uint32_t it = 0, n4 = 0;
+            bool ok = true;
+            auto take = [&](uint32_t site) -> uint32_t {
+                const uint32_t s = it % G::R, ph = (it / G::R) & 1u;
+                ++it;
+                if (ok && !wait_or_abort(&full[s], ph, &s_abort, p.err, site)) ok = false;
+                return s;
+            };
+            auto bdesc = [&](uint32_t s, int k) { return sdesc_kmajor(smem_u32(ring + s * kUnit) + k * 256, 128, 1024); };
+            int tl = 0;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tl) {
+                if (!wait_or_abort(&acc_free, (tl & 1) ^ 1, &s_abort, p.err, 0x51)) break;
+                tc_fence_after();
+                // conv3: [128 x D] x [D -> C]
+                for (int kk = 0; kk < G::KD && ok; ++kk) {
+                    const uint32_t sa = take(0x52);
+                    uint32_t sb[G::NH];
+#pragma unroll
+                    for (int h = 0; h < G::NH; ++h) sb[h] = take(0x52);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(ring + sa * kUnit);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+#pragma unroll
+                        for (int h = 0; h < G::NH; ++h)
+                            mma_f16(tmem + h * 128, sdesc_kmajor_sw(a0 + k * 32, 128), bdesc(sb[h], k), idesc,
+                                    (kk | k) ? 1u : 0u);
+                    mma_commit(&empty[sa]);
+#pragma unroll
+                    for (int h = 0; h < G::NH; ++h) mma_commit(&empty[sb[h]]);
+                }
+                if (!ok) break;
+                mma_commit(&acc3_full);
+                it += C / 64;  // the x boxes go to the epilogue
+                if (!wait_or_abort(&y_ready, tl & 1, &s_abort, p.err, 0x53)) break;
+                tc_fence_after();
+                auto c4 = [&](int j) {
+                    const uint32_t u4 = n4 + j, b = u4 & 1u;
+                    if (!wait_or_abort(&acc4_empty[b], ((u4 >> 1) & 1u) ^ 1u, &s_abort, p.err, 0x54)) {
+                        ok = false;
+                        return;
+                    }
+                    tc_fence_after();
+                    for (int kk = 0; kk < G::KC4; ++kk) {
+                        const uint32_t s = take(0x55);
+                        if (!ok) return;
+                        tc_fence_after();
+                        const uint32_t a0 = smem_u32(sY + kk * kUnit);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f16(tmem + C + b * 128, sdesc_kmajor_sw(a0 + k * 32, 128), bdesc(s, k), idesc,
+                                    (kk | k) ? 1u : 0u);
+                        mma_commit(&empty[s]);
+                    }
+                    mma_commit(&acc4_full[b]);
+                };
+                auto c5 = [&](int j) {
+                    const uint32_t u4 = n4 + j, b = u4 & 1u;
+                    if (!wait_or_abort(&h_full[b], (u4 >> 1) & 1u, &s_abort, p.err, 0x56)) {
+                        ok = false;
+                        return;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sH + b * G::H_BYTES);
+                    for (int h = 0; h < G::NH; ++h) {
+                        const uint32_t s = take(0x57);
+                        if (!ok) return;
+                        tc_fence_after();
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f16(tmem + h * 128, sdesc_kmajor_sw(a0 + k * 32, 128), bdesc(s, k), idesc,
+                                    (j | k) ? 1u : 0u);
+                        mma_commit(&empty[s]);
+                    }
+                    mma_commit(&h_empty[b]);
+                };
+                c4(0);
+                for (int j = 1; j < G::J && ok; ++j) {
+                    c4(j);
+                    if (ok) c5(j - 1);
+                }
+                if (ok) c5(G::J - 1);
+                if (!ok) break;
+                mma_commit(&acc5_full);
+                n4 += G::J;
+            }
+            // Every MMA of this CTA has completed before TMEM is released.
+            mma_commit(&mma_done);
+            mbar_wait(&mma_done, 0, 5000000ull);
+        }
+    } else {
+        // ------------------------------ epilogue ---------------------------------
+        const int q = warp & 3;            // TMEM lane quarter of this warp
+        const int half = (warp - 2) >> 2;  // column half of the tile row
+        const int r = q * 32 + lane;       // tile row == TMEM lane
+        const bool leader = (tid == 64);
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        constexpr int CH = C / 2;
+        const int cb = half * CH;
+        const float2 one2 = make_float2(1.f, 1.f);
+        uint32_t it_base = 0, n4 = 0;
+        int tl = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tl, it_base += G::U) {
+            const int m0 = t * 128;
+            // (1) y = x + beta * (acc + b3) -> sY; LN2 statistics of the fp16 y.
+            bool ok = wait_or_abort(&acc3_full, tl & 1, &s_abort, p.err, 0x58);
+            for (int kk = 0; kk < C / 64 && ok; ++kk) {
+                const uint32_t v = it_base + G::U3 + kk;
+                ok = wait_or_abort(&full[v % G::R], (v / G::R) & 1u, &s_abort, p.err, 0x59);
+            }
+            if (leader) bulk_wait_read0();  // the previous tile's output has left sY
+            if (epi_sync_or(!ok)) break;
+            tc_fence_after();
+            float sh = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll 1
+            for (int c0 = cb; c0 < cb + CH; c0 += 16) {
+                float v[16];
+                tmem_ld16(lane_base + c0, v);
+                tmem_ld_wait();
+                const uint8_t* xu = ring + ((it_base + G::U3 + (c0 >> 6)) % G::R) * kUnit;
+                uint8_t* yb = sY + (c0 >> 6) * kUnit;
+#pragma unroll
+                for (int g2 = 0; g2 < 2; ++g2) {
+                    const uint32_t off = sw_offset(r, ((c0 & 63) >> 3) + g2, 128);
+                    const uint4 xv = *reinterpret_cast<const uint4*>(xu + off);
+                    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+                    const int c = c0 + 8 * g2;
+                    const float4 bb0 = *reinterpret_cast<const float4*>(sB3 + c);
+                    const float4 bb1 = *reinterpret_cast<const float4*>(sB3 + c + 4);
+                    const float4 be0 = *reinterpret_cast<const float4*>(sBeta + c);
+                    const float4 be1 = *reinterpret_cast<const float4*>(sBeta + c + 4);
+                    const float2 bb[4] = {make_float2(bb0.x, bb0.y), make_float2(bb0.z, bb0.w),
+                                          make_float2(bb1.x, bb1.y), make_float2(bb1.z, bb1.w)};
+                    const float2 be[4] = {make_float2(be0.x, be0.y), make_float2(be0.z, be0.w),
+                                          make_float2(be1.x, be1.y), make_float2(be1.z, be1.w)};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 a = ffma2(make_float2(v[8 * g2 + 2 * i], v[8 * g2 + 2 * i + 1]), one2, bb[i]);
+                        const float2 y = ffma2(be[i], a, unpack_half2(xw[i]));
+                        o[i] = pack_half2(y.x, y.y);
+                        const float2 yr = unpack_half2(o[i]);  // statistics of the stored fp16 y
+                        if (c0 == cb && g2 == 0 && i == 0) sh = yr.x;
+                        const float d0 = yr.x - sh, d1 = yr.y - sh;
+                        s1 += d0 + d1;
+                        s2 = fmaf(d0, d0, fmaf(d1, d1, s2));
+                    }
+                    *reinterpret_cast<uint4*>(yb + off) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            const float m_h = sh + s1 * (1.0f / CH);
+            const float M2 = fmaxf(s2 - s1 * s1 * (1.0f / CH), 0.f);
+            s_stat[half][r] = make_float2(m_h, M2);
+            fence_async_smem();  // y is conv4's A (async proxy)
+            tc_fence_before();
+            epi_sync();
+            const float2 other = s_stat[half ^ 1][r];
+            const float mean = 0.5f * (m_h + other.x);
+            const float dm = m_h - other.x;
+            const float var = (M2 + other.y + dm * dm * (0.25f * C)) * (1.0f / C);
+            const float rstd = rsqrtf(var + 1e-6f);
+            if (leader) {
+                mbar_arrive(&y_ready);
+                for (int kk = 0; kk < C / 64; ++kk) mbar_arrive(&empty[(it_base + G::U3 + kk) % G::R]);
+            }
+            // (2) gate chunks: h = (LN-folded a) * (LN-folded b) -> sH[j % 2].
+            const float2 rs2 = make_float2(rstd, rstd), nm2 = make_float2(-rstd * mean, -rstd * mean);
+            auto fold8 = [&](const float* acc, int n, float2 (&out)[4]) {
+                const float4 k0 = *reinterpret_cast<const float4*>(sC1 + n);
+                const float4 k1 = *reinterpret_cast<const float4*>(sC1 + n + 4);
+                const float4 q0 = *reinterpret_cast<const float4*>(sC2 + n);
+                const float4 q1 = *reinterpret_cast<const float4*>(sC2 + n + 4);
+                const float2 kc[4] = {make_float2(k0.x, k0.y), make_float2(k0.z, k0.w), make_float2(k1.x, k1.y),
+                                      make_float2(k1.z, k1.w)};
+                const float2 qc[4] = {make_float2(q0.x, q0.y), make_float2(q0.z, q0.w), make_float2(q1.x, q1.y),
+                                      make_float2(q1.z, q1.w)};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    out[i] = ffma2(rs2, make_float2(acc[2 * i], acc[2 * i + 1]), ffma2(nm2, kc[i], qc[i]));
+            };
+            for (int j = 0; j < G::J && ok; ++j) {
+                const uint32_t u4 = n4 + j, b = u4 & 1u;
+                bool got = wait_or_abort(&acc4_full[b], (u4 >> 1) & 1u, &s_abort, p.err, 0x5a);
+                if (got) got = wait_or_abort(&h_empty[b], ((u4 >> 1) & 1u) ^ 1u, &s_abort, p.err, 0x5b);
+                if (epi_sync_or(!got)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int pa = (j >> 1) * 256 + (j & 1) * 64;  // packed index of gate channel 64j
+                uint8_t* hb = sH + b * G::H_BYTES;
+#pragma unroll
+                for (int cc = half * 32; cc < half * 32 + 32; cc += 16) {
+                    float va[16], vb[16];
+                    tmem_ld16(lane_base + C + b * 128 + cc, va);
+                    tmem_ld16(lane_base + C + b * 128 + 64 + cc, vb);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int g2 = 0; g2 < 2; ++g2) {
+                        float2 xa[4], xb[4];
+                        fold8(va + 8 * g2, pa + cc + 8 * g2, xa);
+                        fold8(vb + 8 * g2, pa + 128 + cc + 8 * g2, xb);
+                        const float2 z = make_float2(0.f, 0.f);
+                        uint32_t o[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float2 pr = ffma2(xa[i], xb[i], z);
+                            o[i] = pack_half2(pr.x, pr.y);
+                        }
+                        *reinterpret_cast<uint4*>(hb + sw_offset(r, (cc >> 3) + g2, 128)) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+                fence_async_smem();
+                tc_fence_before();
+                epi_sync();
+                if (leader) {
+                    mbar_arrive(&acc4_empty[b]);
+                    mbar_arrive(&h_full[b]);
+                }
+            }
+            if (!ok) break;
+            n4 += G::J;
+            // (3) out = y + gamma * (acc + b5), over y in sY, then TMA store.
+            ok = wait_or_abort(&acc5_full, tl & 1, &s_abort, p.err, 0x5c);
+            if (epi_sync_or(!ok)) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c0 = cb; c0 < cb + CH; c0 += 16) {
+                float v[16];
+                tmem_ld16(lane_base + c0, v);
+                tmem_ld_wait();
+                uint8_t* yb = sY + (c0 >> 6) * kUnit;
+#pragma unroll
+                for (int g2 = 0; g2 < 2; ++g2) {
+                    uint4* ptr = reinterpret_cast<uint4*>(yb + sw_offset(r, ((c0 & 63) >> 3) + g2, 128));
+                    const uint4 yv = *ptr;
+                    const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+                    const int c = c0 + 8 * g2;
+                    const float4 bb0 = *reinterpret_cast<const float4*>(sB5 + c);
+                    const float4 bb1 = *reinterpret_cast<const float4*>(sB5 + c + 4);
+                    const float4 ga0 = *reinterpret_cast<const float4*>(sGam + c);
+                    const float4 ga1 = *reinterpret_cast<const float4*>(sGam + c + 4);
+                    const float2 bb[4] = {make_float2(bb0.x, bb0.y), make_float2(bb0.z, bb0.w),
+                                          make_float2(bb1.x, bb1.y), make_float2(bb1.z, bb1.w)};
+                    const float2 ga[4] = {make_float2(ga0.x, ga0.y), make_float2(ga0.z, ga0.w),
+                                          make_float2(ga1.x, ga1.y), make_float2(ga1.z, ga1.w)};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 a = ffma2(make_float2(v[8 * g2 + 2 * i], v[8 * g2 + 2 * i + 1]), one2, bb[i]);
+                        const float2 y = ffma2(ga[i], a, unpack_half2(yw[i]));
+                        o[i] = pack_half2(y.x, y.y);
+                    }
+                    *ptr = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            epi_sync();
+            if (leader) {
+                mbar_arrive(&acc_free);
+                for (int bx = 0; bx < C / 64; ++bx) tma_store_2d(&mo, bx * 64, m0, sY + bx * kUnit);
+                bulk_commit();
+            }
+        }
+        if (leader) bulk_wait0();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, G::TMEM_COLS);
+}
+
+template <int C, int D, int F>
+int run_deep_b(const DeepBParams& p, cudaStream_t s) {
+    using G = GeoD<C, D, F>;
+    auto kern = deep_b_kernel<C, D, F>;
+    static bool cfg = false;
+    if (!cfg) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "deep_b: smem attribute");
+        cfg = true;
+    }
+    CUtensorMap mg, mx, mo;
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint64_t dG[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(p.M)};
+    const cuuint64_t dC[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(p.M)};
+    const cuuint64_t sG[1] = {static_cast<cuuint64_t>(D) * 2};
+    const cuuint64_t sC[1] = {static_cast<cuuint64_t>(C) * 2};
+    int rc = encode_f16_map(&mg, 2, p.g, dG, sG, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == DN_OK) rc = encode_f16_map(&mx, 2, p.x, dC, sC, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == DN_OK) rc = encode_f16_map(&mo, 2, p.out, dC, sC, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != DN_OK) return rc;
+    const int tiles = (p.M + 127) / 128;
+    const int grid = std::min(tiles, sm_count());
+    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kDThreads), G::SMEM, s, p, mg, mx, mo);
+    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "deep_b: launch");
+}
+
+}  // namespace
+
+bool deep_b_supported(int C, int D, int F) {
+    return (C == 128 || C == 256) && (D == C || D == 2 * C) && (F == C || F == 2 * C);
+}
+
+int launch_deep_b(const DeepBParams& p, int C, int D, int F, cudaStream_t s) {
+    if (p.M <= 0) return dn_fail(DN_ERR_INVALID_ARG, "deep_b: empty input");
+    if (C == 128 && D == 128 && F == 128) return run_deep_b<128, 128, 128>(p, s);
+    if (C == 128 && D == 128 && F == 256) return run_deep_b<128, 128, 256>(p, s);
+    if (C == 128 && D == 256 && F == 128) return run_deep_b<128, 256, 128>(p, s);
+    if (C == 128 && D == 256 && F == 256) return run_deep_b<128, 256, 256>(p, s);
+    if (C == 256 && D == 256 && F == 256) return run_deep_b<256, 256, 256>(p, s);
+    if (C == 256 && D == 256 && F == 512) return run_deep_b<256, 256, 512>(p, s);
+    if (C == 256 && D == 512 && F == 256) return run_deep_b<256, 512, 256>(p, s);
+    if (C == 256 && D == 512 && F == 512) return run_deep_b<256, 512, 512>(p, s);
+    return dn_fail(DN_ERR_UNSUPPORTED, "deep_b: channel configuration");
+}
+
+}  // namespace dnb

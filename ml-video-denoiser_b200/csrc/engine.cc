@@ -627,6 +627,16 @@ int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cuda
     return rc;
 }
 
+// The deep second-pass kernel reads the GEMM tile images directly: conv3 and
+// conv5 as single N tiles of K chunk 64, conv4 as 256-row tiles (two
+// 128-channel gate halves) of K chunk 64.
+static bool deep_b_layout_ok(const BlockW& b) {
+    return b.conv3.n_tiles == 1 && b.conv3.NT == b.C && b.conv3.KC == 64 && b.conv3.k_chunks * 64 == b.dw &&
+           b.conv4.NT == 256 && b.conv4.KC == 64 && b.conv4.n_tiles * 128 == b.ffn && b.conv4.has_c1 &&
+           b.conv5.n_tiles == 1 && b.conv5.NT == b.C && b.conv5.KC == 64 && b.conv5.k_chunks * 64 == b.ffn &&
+           b.conv3.has_bias && b.conv5.has_bias;
+}
+
 static GemmParams rows_params(int nimg, int h, int w) {
     GemmParams p{};
     p.M = nimg * h * w;
@@ -745,6 +755,31 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
         DN_TRY(launch_dw_gate_sca(d, dw_blocks_per_img(h, w, b.dw), s));
     }
     prof_end(s);
+    if (fold_sca && deep_b_supported(b.C, b.dw, b.ffn) && deep_b_layout_ok(b)) {
+        // conv3 + beta residual + LN2 + conv4 + gate + conv5 + gamma residual
+        // in one kernel; y and the gated tensor stay on chip.
+        DeepBParams q{};
+        q.g = buf_g_;
+        q.x = x;
+        q.out = x;
+        q.M = static_cast<int>(hw);
+        q.w3 = b3s_;
+        q.w4 = wptr<uint8_t>(b.conv4.bpack);
+        q.w5 = wptr<uint8_t>(b.conv5.bpack);
+        q.b3 = wptr<float>(b.conv3.bias);
+        q.beta = wptr<float>(b.beta);
+        q.c1 = wptr<float>(b.conv4.c1);
+        q.c2 = wptr<float>(b.conv4.bias);
+        q.b5 = wptr<float>(b.conv5.bias);
+        q.gamma = wptr<float>(b.gamma);
+        q.err = err_;
+        ++launches_;
+        prof_begin("deep_block_b", static_cast<double>(hw) * (b.dw + 2 * b.C) * 2,
+                   2.0 * hw * (b.dw * b.C + b.C * 2 * b.ffn + b.ffn * b.C), s);
+        DN_TRY(launch_deep_b(q, b.C, b.dw, b.ffn, s));
+        prof_end(s);
+        return DN_OK;
+    }
     // y = x + beta * (conv3(g * s) + b3)
     p = rows_params(nimg, h, w);
     p.seg_c = b.dw;

@@ -606,8 +606,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
 
 // ============================== host ========================================
 
-int encode(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
-           const cuuint32_t* box, CUtensorMapSwizzle swz) {
+}  // namespace
+
+int encode_f16_map(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                   const cuuint32_t* box, CUtensorMapSwizzle swz) {
     auto fn = tensor_map_encoder();
     if (!fn) return dn_fail(DN_ERR_CUDA, "fused: cuTensorMapEncodeTiled unavailable");
     cuuint32_t es[5] = {1, 1, 1, 1, 1};
@@ -619,10 +621,6 @@ int encode(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, c
     return DN_OK;
 }
 
-CUtensorMapSwizzle swz_for(int bytes) {
-    return bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-}
-
 int sm_count() {
     static int n = 0;
     if (!n) {
@@ -632,6 +630,12 @@ int sm_count() {
         if (n <= 0) n = 148;
     }
     return n;
+}
+
+namespace {
+
+CUtensorMapSwizzle swz_for(int bytes) {
+    return bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
 }
 
 template <int C, int D>
@@ -650,14 +654,14 @@ int run_a(const FusedAParams& p, int grid, cudaStream_t s) {
     const cuuint64_t sx[3] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(p.W) * C * 2,
                               static_cast<cuuint64_t>(p.H) * p.W * C * 2};
     const cuuint32_t bx[4] = {static_cast<cuuint32_t>(C), G::WW, G::HH, 1};
-    int rc = encode(&mx, 4, p.x, dx, sx, bx, swz_for(2 * C));
+    int rc = encode_f16_map(&mx, 4, p.x, dx, sx, bx, swz_for(2 * C));
     if (rc != DN_OK) return rc;
     const cuuint64_t dg[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(p.W), static_cast<cuuint64_t>(p.H),
                               static_cast<cuuint64_t>(p.N)};
     const cuuint64_t sg[3] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(p.W) * D * 2,
                               static_cast<cuuint64_t>(p.H) * p.W * D * 2};
     const cuuint32_t bg[4] = {static_cast<cuuint32_t>(D), G::TW, G::TH, 1};
-    rc = encode(&mg, 4, p.g, dg, sg, bg, CU_TENSOR_MAP_SWIZZLE_NONE);
+    rc = encode_f16_map(&mg, 4, p.g, dg, sg, bg, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != DN_OK) return rc;
     cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kAThreads), G::SMEM, s, p, mx, mg);
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "fused_a: launch");
@@ -680,9 +684,9 @@ int run_b(const FusedBParams& p, cudaStream_t s) {
     const cuuint64_t dC[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(p.M)};
     const cuuint64_t sG[1] = {static_cast<cuuint64_t>(D) * 2};
     const cuuint64_t sC[1] = {static_cast<cuuint64_t>(C) * 2};
-    int rc = encode(&mg, 2, p.g, dG, sG, bD, swz_for(2 * D));
-    if (rc == DN_OK) rc = encode(&mx, 2, p.x, dC, sC, bC, swz_for(2 * C));
-    if (rc == DN_OK) rc = encode(&mo, 2, p.out, dC, sC, bC, swz_for(2 * C));
+    int rc = encode_f16_map(&mg, 2, p.g, dG, sG, bD, swz_for(2 * D));
+    if (rc == DN_OK) rc = encode_f16_map(&mx, 2, p.x, dC, sC, bC, swz_for(2 * C));
+    if (rc == DN_OK) rc = encode_f16_map(&mo, 2, p.out, dC, sC, bC, swz_for(2 * C));
     if (rc != DN_OK) return rc;
     const int tiles = (p.M + 127) / 128;
     const int per_sm = std::max(1, std::min(512 / G::TMEM_COLS, (227 * 1024) / (G::SMEM + 2048)));

@@ -1,6 +1,9 @@
-// Fused NAFBlock kernels for the shallow levels (C <= 64); see fused_block.cu.
+// Fused NAFBlock kernels: both passes for the shallow levels (C <= 64,
+// fused_block.cu) and the second pass for the deep levels (C = 128 / 256,
+// deep_block.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -38,5 +41,30 @@ bool fused_supported(int C, int D, int F);
 int fused_a_grid(int C, int D, int N, int H, int W);
 int launch_fused_a(const FusedAParams& p, int C, int D, int grid, cudaStream_t s);
 int launch_fused_b(const FusedBParams& p, int C, int D, int F, cudaStream_t s);
+
+// Second pass of a deep NAFBlock on one image, in place on x:
+// y = x + beta * (g (W3 diag(s))^T + b3); h = SimpleGate(LN2(y) W4^T + b4);
+// out = y + gamma * (h W5^T + b5). The B operands are the engine's GEMM tile
+// images (KC = 64): w3 = the SCA-scaled conv3 image ([C x D], one N tile),
+// w4 = conv4 packed with the gate halves interleaved per 128-channel tile and
+// LN2 folded (c1, c2 in that packed order), w5 = conv5 ([C x F], one N tile).
+struct DeepBParams {
+    const __half* g;        // [M, D]
+    const __half* x;        // [M, C]
+    __half* out;            // [M, C] (may alias x)
+    int M;
+    const uint8_t *w3, *w4, *w5;
+    const float *b3, *beta, *c1, *c2, *b5, *gamma;
+    uint32_t* err;
+};
+
+bool deep_b_supported(int C, int D, int F);
+int launch_deep_b(const DeepBParams& p, int C, int D, int F, cudaStream_t s);
+
+// Shared host helpers: FP16 tensor map (tiled, no interleave, L2 promotion
+// 128 B, zero fill) and the device's SM count.
+int encode_f16_map(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                   const cuuint32_t* box, CUtensorMapSwizzle swz);
+int sm_count();
 
 }  // namespace dnb

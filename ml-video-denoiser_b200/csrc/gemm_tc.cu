@@ -64,40 +64,11 @@ struct GemmMaps {
 };
 
 // Named barrier of the eight epilogue warps.
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void epi_sync() { named_sync(1, 256); }
 
 // Same barrier, returning the OR of `v` over the 256 epilogue threads (a
 // uniform decision for all of them).
-__device__ __forceinline__ bool epi_sync_or(bool v) {
-    uint32_t out;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, 1, 256, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(out)
-        : "r"(static_cast<uint32_t>(v))
-        : "memory");
-    return out != 0;
-}
-
-// Bounded wait that also gives up as soon as another role aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                              uint32_t* err, uint32_t site) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63u) == 0u) {
-            if (*abort_flag) return false;
-            if (globaltimer_ns() - t0 > 2000000000ull) {
-                report_error(err, site, kErrMbarTimeout);
-                *abort_flag = 1;
-                return false;
-            }
-        }
-    }
-}
+__device__ __forceinline__ bool epi_sync_or(bool v) { return named_sync_or(1, 256, v); }
 
 // Source address of the 8 channels [k, k+8) of the 2x2/stride-2 patch of
 // output pixel `pix` of image `img`.

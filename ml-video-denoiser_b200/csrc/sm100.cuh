@@ -71,6 +71,46 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
 }
 
+// Bounded wait shared by the roles of a warp-specialised kernel: gives up
+// as soon as another role has set `abort_flag`, and on its own timeout
+// records `site` in the error word and sets the flag for the others.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              uint32_t* err, uint32_t site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 0u) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > 2000000000ull) {
+                report_error(err, site, kErrMbarTimeout);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Named barrier `id` over `n` threads (a multiple of 32).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Same barrier, returning the OR of `v` over its threads (a decision that is
+// uniform across them).
+__device__ __forceinline__ bool named_sync_or(uint32_t id, uint32_t n, bool v) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(out)
+        : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(n)
+        : "memory");
+    return out != 0;
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                  "r"(bytes)

@@ -65,6 +65,23 @@ def test_w32_batch2_ragged(pkg, tmp_path, fused):
     assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
 
 
+def test_w32_single_image_deep_second_pass(pkg, tmp_path):
+    """Single image, so the 128- and 256-channel blocks run their second pass
+    as one kernel (conv3 -> LN2/conv4/gate -> conv5); 200x328 leaves partial
+    128-pixel tiles at both levels (50x82 and 25x41). Both engine paths meet
+    the oracle bar and agree with each other."""
+    synth = synth_mod(pkg)
+    x = synth.w32_frame(200, 328, seed=9).astype(np.float16).astype(np.float32)
+    (err, psnr), m = _oracle_case(pkg, tmp_path, synth.CONFIG_W32, 2, x, True)
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+    m.set_fused(False)
+    y_ref = m(torch.from_numpy(x).half().cuda())
+    m.set_fused(True)
+    y_fused = m(torch.from_numpy(x).half().cuda())
+    m.sync()
+    assert float((y_fused.float() - y_ref.float()).abs().max()) <= 2e-3
+
+
 def test_w32_1080p(pkg, tmp_path):
     """NAFNet-w32 on one 1080p Poisson-Gaussian frame (the benchmark workload)."""
     synth = synth_mod(pkg)
