@@ -20,7 +20,10 @@
 namespace dnb {
 namespace {
 
-constexpr int kTile = 16;  // 16x16 output pixels per CTA, 256 threads
+constexpr int kTH = 8, kTW = 32;        // output tile; 128 threads, two pixels each
+constexpr int kHH = kTH + 2, kWW = kTW + 2;
+constexpr int kArea = kHH * kWW;        // halo pixels
+constexpr int kThreads = 128;
 
 __device__ __forceinline__ float finite_or_zero(float v) {
     return (isnan(v) || isinf(v)) ? 0.f : v;
@@ -28,166 +31,214 @@ __device__ __forceinline__ float finite_or_zero(float v) {
 
 __device__ __forceinline__ int reflect_hi(int i, int n) { return i < n ? i : 2 * (n - 1) - i; }
 
-__device__ __forceinline__ void h8_to_f(const uint4& v, float (&f)[8]) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+// Thread t owns pixels (t / 16, t % 16) and (t / 16, t % 16 + 16) of the
+// tile: the lanes of a warp read consecutive halo pixels (conflict-free
+// shared-memory reads) and both pixels share every broadcast weight load.
+
+// Intro: one pass per group of NP output-channel pairs (2*NP channels).
+// acc pair (o, o+1) of pixel q += (v, v) * (w[k][o], w[k][o+1]) in packed
+// fp32 FMAs; weights are broadcast float4 reads of sw[k][C0].
+template <int NP>
+__device__ __forceinline__ void intro_group(const float* sx, const float* sw, const float* bias, int Cin, int C0,
+                                            int o0, int ly, int lx, __half* dst0, __half* dst1, bool st0, bool st1) {
+    float2 acc[2][NP];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 t = unpack_half2(w[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
+    for (int j = 0; j < NP; ++j) acc[0][j] = acc[1][j] = make_float2(bias[o0 + 2 * j], bias[o0 + 2 * j + 1]);
+    for (int c = 0; c < Cin; ++c) {
+        const float* xc = sx + c * kArea;
+#pragma unroll
+        for (int t = 0; t < 9; ++t) {
+            const int r = (ly + t / 3) * kWW + lx + t % 3;
+            const float v0 = xc[r], v1 = xc[r + 16];
+            const float2 a = make_float2(v0, v0), b = make_float2(v1, v1);
+            const float4* wr = reinterpret_cast<const float4*>(sw + (c * 9 + t) * C0 + o0);
+#pragma unroll
+            for (int j = 0; j < NP / 2; ++j) {
+                const float4 w4 = wr[j];
+                const float2 wa = make_float2(w4.x, w4.y), wb = make_float2(w4.z, w4.w);
+                acc[0][2 * j] = ffma2(a, wa, acc[0][2 * j]);
+                acc[0][2 * j + 1] = ffma2(a, wb, acc[0][2 * j + 1]);
+                acc[1][2 * j] = ffma2(b, wa, acc[1][2 * j]);
+                acc[1][2 * j + 1] = ffma2(b, wb, acc[1][2 * j + 1]);
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        if (!(q ? st1 : st0)) continue;
+        __half* d = (q ? dst1 : dst0) + o0;
+#pragma unroll
+        for (int j = 0; j < NP; j += 4) {
+            uint4 ov;
+            ov.x = pack_half2(acc[q][j].x, acc[q][j].y);
+            ov.y = pack_half2(acc[q][j + 1].x, acc[q][j + 1].y);
+            ov.z = pack_half2(acc[q][j + 2].x, acc[q][j + 2].y);
+            ov.w = pack_half2(acc[q][j + 3].x, acc[q][j + 3].y);
+            *reinterpret_cast<uint4*>(d + 2 * j) = ov;
+        }
     }
 }
 
-// One thread = one output pixel, all C0 outputs (in groups of 8).
-__global__ void __launch_bounds__(256) intro_kernel(const __grid_constant__ IntroParams p) {
-    extern __shared__ float sm[];
+__global__ void __launch_bounds__(kThreads) intro_kernel(const __grid_constant__ IntroParams p) {
+    extern __shared__ __align__(16) float sm[];
     const int Cin = p.Cin, C0 = p.C0;
-    float* sx = sm;                                   // [Cin][18][18]
-    float* sw = sx + Cin * (kTile + 2) * (kTile + 2);  // [C0][Kp] (Kp = Cin*9 rounded to 4)
+    float* sw = sm;                   // [Cin*9][C0]
+    float* sb = sw + Cin * 9 * C0;    // [C0]
+    float* sx = sb + C0;              // [Cin][kHH][kWW]
     const int img = blockIdx.z;
-    const int ty0 = blockIdx.y * kTile, tx0 = blockIdx.x * kTile;
+    const int ty0 = blockIdx.y * kTH, tx0 = blockIdx.x * kTW;
     const __half* x = p.x + static_cast<size_t>(img) * p.in_batch_stride;
     const int tid = threadIdx.x;
-    const int K = Cin * 9;
-    const int Kp = (K + 3) & ~3;
     pdl_trigger();
-    for (int i = tid; i < C0 * Kp; i += 256) {
-        const int o = i / Kp, k = i - o * Kp;
-        sw[i] = k < K ? p.w[o * K + k] : 0.f;
+    for (int i = tid; i < Cin * 9 * C0; i += kThreads) {
+        const int k = i / C0, o = i - k * C0;
+        sw[i] = p.w[o * Cin * 9 + k];
     }
+    for (int i = tid; i < C0; i += kThreads) sb[i] = p.b[i];
     pdl_wait();
-    const int area = (kTile + 2) * (kTile + 2);
-    for (int i = tid; i < Cin * area; i += 256) {
-        const int c = i / area;
-        const int r = i - c * area;
-        const int yy = ty0 + r / (kTile + 2) - 1;  // coordinate in the padded frame
-        const int xx = tx0 + r % (kTile + 2) - 1;
-        float v = 0.f;  // conv zero padding outside the padded frame
-        if (yy >= 0 && yy < p.Hp && xx >= 0 && xx < p.Wp) {
-            const int sy = reflect_hi(yy, p.H);
-            const int sx2 = reflect_hi(xx, p.W);
-            v = finite_or_zero(__half2float(x[(static_cast<size_t>(c) * p.H + sy) * p.W + sx2]));
+    // Halo staging in batches of kBatch loads per thread, all issued before
+    // any is used (one memory latency per batch).
+    constexpr int kBatch = 12;
+    for (int base = tid; base < Cin * kArea; base += kBatch * kThreads) {
+        __half hv[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int i = base + j * kThreads;
+            hv[j] = __float2half(0.f);  // conv zero padding outside the padded frame
+            if (i < Cin * kArea) {
+                const int c = i / kArea;
+                const int r = i - c * kArea;
+                const int yy = ty0 + r / kWW - 1;  // coordinate in the padded frame
+                const int xx = tx0 + r % kWW - 1;
+                if (yy >= 0 && yy < p.Hp && xx >= 0 && xx < p.Wp)
+                    hv[j] = x[(static_cast<size_t>(c) * p.H + reflect_hi(yy, p.H)) * p.W + reflect_hi(xx, p.W)];
+            }
         }
-        sx[i] = v;
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int i = base + j * kThreads;
+            if (i < Cin * kArea) sx[i] = finite_or_zero(__half2float(hv[j]));
+        }
     }
     __syncthreads();
-    const int ly = tid / kTile, lx = tid % kTile;
-    const int oy = ty0 + ly, ox = tx0 + lx;
-    if (oy >= p.Hp || ox >= p.Wp) return;
-    __half* dst = p.y + ((static_cast<size_t>(img) * p.Hp + oy) * p.Wp + ox) * C0;
-    // The patch (Cin x 3 x 3) in registers; weight rows are broadcast reads.
-    constexpr int kMaxK = 36;  // up to 4 input channels per pass
-    for (int cbase = 0; cbase < Cin; cbase += 4) {
-        const int cn = min(4, Cin - cbase);
-        float v[kMaxK];
-#pragma unroll
-        for (int i = 0; i < kMaxK; ++i) {
-            const int c = cbase + i / 9;
-            const int t = i % 9;
-            v[i] = (i < cn * 9) ? sx[c * area + (ly + t / 3) * (kTile + 2) + lx + t % 3] : 0.f;
-        }
-        for (int o0 = 0; o0 < C0; o0 += 8) {
-            float acc[8];
-            if (cbase == 0) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] = p.b[o0 + i];
-            } else {
-                float prev[8];
-                h8_to_f(*reinterpret_cast<const uint4*>(dst + o0), prev);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] = prev[i];
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                // cbase * 9 is a multiple of 4: 16-byte aligned broadcast reads.
-                const float4* wr = reinterpret_cast<const float4*>(sw + (o0 + i) * Kp + cbase * 9);
-#pragma unroll
-                for (int k4 = 0; k4 < kMaxK / 4; ++k4) {
-                    if (4 * k4 >= cn * 9) break;
-                    const float4 w4 = wr[k4];
-                    acc[i] = fmaf(v[4 * k4], w4.x, acc[i]);
-                    acc[i] = fmaf(v[4 * k4 + 1], w4.y, acc[i]);
-                    acc[i] = fmaf(v[4 * k4 + 2], w4.z, acc[i]);
-                    acc[i] = fmaf(v[4 * k4 + 3], w4.w, acc[i]);
-                }
-            }
-            uint4 ov;
-            ov.x = pack_half2(acc[0], acc[1]);
-            ov.y = pack_half2(acc[2], acc[3]);
-            ov.z = pack_half2(acc[4], acc[5]);
-            ov.w = pack_half2(acc[6], acc[7]);
-            *reinterpret_cast<uint4*>(dst + o0) = ov;
-        }
-    }
+    const int ly = tid >> 4, lx = tid & 15;
+    const int oy = ty0 + ly, ox0 = tx0 + lx;
+    if (oy >= p.Hp) return;
+    __half* row = p.y + (static_cast<size_t>(img) * p.Hp + oy) * p.Wp * C0;
+    __half* d0 = row + static_cast<size_t>(ox0) * C0;
+    __half* d1 = row + static_cast<size_t>(ox0 + 16) * C0;
+    const bool st0 = ox0 < p.Wp, st1 = ox0 + 16 < p.Wp;
+    int o0 = 0;
+    for (; o0 + 16 <= C0; o0 += 16) intro_group<8>(sx, sw, sb, Cin, C0, o0, ly, lx, d0, d1, st0, st1);
+    if (o0 < C0) intro_group<4>(sx, sw, sb, Cin, C0, o0, ly, lx, d0, d1, st0, st1);
 }
 
-// One thread = one output pixel of the cropped frame, 3 outputs.
-__global__ void __launch_bounds__(256) ending_kernel(const __grid_constant__ EndingParams p) {
-    extern __shared__ float sm[];
+// Ending: the halo tile of the NHWC features staged once as fp32 (pixel
+// stride C0 + 4 floats: consecutive lanes hit distinct 16-byte bank groups);
+// per tap and 4 channels, three broadcast float4 weight reads (one per output)
+// and one float4 input read per pixel feed six packed FMAs whose two lanes
+// accumulate the even and odd channels.
+__global__ void __launch_bounds__(kThreads) ending_kernel(const __grid_constant__ EndingParams p) {
+    extern __shared__ __align__(16) float sm[];
     const int C0 = p.C0;
-    const int area = (kTile + 2) * (kTile + 2);
-    float* sw = sm;               // [3][9][C0]
-    // NHWC tile with a padded pixel stride (C0 + 2 halves: an odd number of
-    // 32-bit words) so that lanes on neighbouring pixels hit distinct banks.
-    const int ps = C0 + 2;
-    __half* sx = reinterpret_cast<__half*>(sw + 27 * C0);  // [18*18][ps]
+    const int ps = C0 + 4;
+    float* sw = sm;                   // [9 taps][C0/4][3 outputs][4]
+    float* sx = sw + 27 * C0;         // [kArea][ps]
     const int img = blockIdx.z;
-    const int ty0 = blockIdx.y * kTile, tx0 = blockIdx.x * kTile;
+    const int ty0 = blockIdx.y * kTH, tx0 = blockIdx.x * kTW;
     const int tid = threadIdx.x;
     pdl_trigger();
-    for (int i = tid; i < 27 * C0; i += 256) sw[i] = p.w[i];
+    for (int i = tid; i < 27 * C0; i += kThreads) {
+        const int t = i / (3 * C0);
+        const int r = i - t * 3 * C0;
+        const int c4 = r / 12, o = (r / 4) % 3, e = r % 4;
+        sw[i] = p.w[(o * 9 + t) * C0 + 4 * c4 + e];
+    }
     pdl_wait();
     const __half* xin = p.x + static_cast<size_t>(img) * p.Hp * p.Wp * C0;
+    // Halo staging in batches of kBatch 16-byte loads per thread, all issued
+    // before any is converted (one memory latency per batch).
+    constexpr int kBatch = 12;
     const int vec = C0 / 8;
-    for (int i = tid; i < area * vec; i += 256) {
-        const int r = i / vec;
-        const int q = i - r * vec;
-        const int yy = ty0 + r / (kTile + 2) - 1;
-        const int xx = tx0 + r % (kTile + 2) - 1;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (yy >= 0 && yy < p.Hp && xx >= 0 && xx < p.Wp)
-            v = __ldg(reinterpret_cast<const uint4*>(xin + (static_cast<size_t>(yy) * p.Wp + xx) * C0) + q);
-        uint32_t* d = reinterpret_cast<uint32_t*>(sx + static_cast<size_t>(r) * ps + q * 8);
-        d[0] = v.x;
-        d[1] = v.y;
-        d[2] = v.z;
-        d[3] = v.w;
-    }
-    __syncthreads();
-    const int ly = tid / kTile, lx = tid % kTile;
-    const int oy = ty0 + ly, ox = tx0 + lx;
-    if (oy >= p.H || ox >= p.W) return;
-    float acc[3] = {p.b[0], p.b[1], p.b[2]};
+    for (int base = tid; base < kArea * vec; base += kBatch * kThreads) {
+        uint4 v[kBatch];
 #pragma unroll
-    for (int ky = 0; ky < 3; ++ky)
-#pragma unroll
-        for (int kx = 0; kx < 3; ++kx) {
-            const __half* px = sx + static_cast<size_t>((ly + ky) * (kTile + 2) + lx + kx) * ps;
-            const float* w0 = sw + (0 * 9 + ky * 3 + kx) * C0;
-            const float* w1 = sw + (1 * 9 + ky * 3 + kx) * C0;
-            const float* w2 = sw + (2 * 9 + ky * 3 + kx) * C0;
-            for (int c = 0; c < C0; c += 2) {
-                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(px + c));
-                acc[0] += v.x * w0[c] + v.y * w0[c + 1];
-                acc[1] += v.x * w1[c] + v.y * w1[c + 1];
-                acc[2] += v.x * w2[c] + v.y * w2[c + 1];
+        for (int j = 0; j < kBatch; ++j) {
+            const int i = base + j * kThreads;
+            v[j] = make_uint4(0, 0, 0, 0);
+            if (i < kArea * vec) {
+                const int r = i / vec;
+                const int q = i - r * vec;
+                const int yy = ty0 + r / kWW - 1;
+                const int xx = tx0 + r % kWW - 1;
+                if (yy >= 0 && yy < p.Hp && xx >= 0 && xx < p.Wp)
+                    v[j] = __ldg(reinterpret_cast<const uint4*>(xin + (static_cast<size_t>(yy) * p.Wp + xx) * C0) + q);
             }
         }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int i = base + j * kThreads;
+            if (i >= kArea * vec) break;
+            const int r = i / vec;
+            const int q = i - r * vec;
+            float f[8];
+            h8_to_f(v[j], f);
+            float4* d = reinterpret_cast<float4*>(sx + static_cast<size_t>(r) * ps + q * 8);
+            d[0] = make_float4(f[0], f[1], f[2], f[3]);
+            d[1] = make_float4(f[4], f[5], f[6], f[7]);
+        }
+    }
+    __syncthreads();
+    const int ly = tid >> 4, lx = tid & 15;
+    const int oy = ty0 + ly;
+    if (oy >= p.H) return;
+    float2 acc[2][3];
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int o = 0; o < 3; ++o) acc[q][o] = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int t = 0; t < 9; ++t) {
+        const float* x0 = sx + static_cast<size_t>((ly + t / 3) * kWW + lx + t % 3) * ps;
+        const float* x1 = x0 + 16 * ps;
+        const float4* wt = reinterpret_cast<const float4*>(sw + t * 3 * C0);
+#pragma unroll 4
+        for (int c4 = 0; c4 < C0 / 4; ++c4) {
+            const float4 a = *reinterpret_cast<const float4*>(x0 + 4 * c4);
+            const float4 b = *reinterpret_cast<const float4*>(x1 + 4 * c4);
+#pragma unroll
+            for (int o = 0; o < 3; ++o) {
+                const float4 w = wt[c4 * 3 + o];
+                const float2 w01 = make_float2(w.x, w.y), w23 = make_float2(w.z, w.w);
+                acc[0][o] = ffma2(make_float2(a.x, a.y), w01, acc[0][o]);
+                acc[0][o] = ffma2(make_float2(a.z, a.w), w23, acc[0][o]);
+                acc[1][o] = ffma2(make_float2(b.x, b.y), w01, acc[1][o]);
+                acc[1][o] = ffma2(make_float2(b.z, b.w), w23, acc[1][o]);
+            }
+        }
+    }
     const size_t plane = static_cast<size_t>(p.H) * p.W;
     const __half* beauty = p.beauty + static_cast<size_t>(img) * p.beauty_batch_stride;
     __half* out = p.y + static_cast<size_t>(img) * 3 * plane;
-    const size_t o = static_cast<size_t>(oy) * p.W + ox;
 #pragma unroll
-    for (int c = 0; c < 3; ++c)
-        out[c * plane + o] = __float2half(finite_or_zero(__half2float(beauty[c * plane + o])) + acc[c]);
+    for (int q = 0; q < 2; ++q) {
+        const int ox = tx0 + lx + 16 * q;
+        if (ox >= p.W) continue;
+        const size_t o = static_cast<size_t>(oy) * p.W + ox;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float r = (acc[q][c].x + acc[q][c].y) + p.b[c];
+            out[c * plane + o] = __float2half(finite_or_zero(__half2float(beauty[c * plane + o])) + r);
+        }
+    }
 }
 
 }  // namespace
 
 int launch_intro(const IntroParams& p, cudaStream_t s) {
     if (p.C0 % 8 != 0) return dn_fail(DN_ERR_UNSUPPORTED, "intro: base channels must be a multiple of 8");
-    const size_t smem = (static_cast<size_t>(p.Cin) * (kTile + 2) * (kTile + 2) +
-                         static_cast<size_t>(p.C0) * ((p.Cin * 9 + 3) & ~3)) * sizeof(float);
+    const size_t smem = (static_cast<size_t>(p.Cin) * kArea + static_cast<size_t>(p.C0) * (p.Cin * 9 + 1)) *
+                        sizeof(float);
     if (smem > 200 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "intro: too many channels");
     static bool configured = false;
     if (!configured) {
@@ -196,8 +247,8 @@ int launch_intro(const IntroParams& p, cudaStream_t s) {
         if (e != cudaSuccess) return dn_cuda_fail(e, "intro: set smem attribute");
         configured = true;
     }
-    dim3 grid((p.Wp + kTile - 1) / kTile, (p.Hp + kTile - 1) / kTile, p.N);
-    const cudaError_t le = launch_pdl(intro_kernel, grid, dim3(256), smem, s, p);
+    dim3 grid((p.Wp + kTW - 1) / kTW, (p.Hp + kTH - 1) / kTH, p.N);
+    const cudaError_t le = launch_pdl(intro_kernel, grid, dim3(kThreads), smem, s, p);
     if (le != cudaSuccess) return dn_cuda_fail(le, "intro: launch");
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "intro: launch");
@@ -205,8 +256,7 @@ int launch_intro(const IntroParams& p, cudaStream_t s) {
 
 int launch_ending(const EndingParams& p, cudaStream_t s) {
     if (p.C0 % 8 != 0) return dn_fail(DN_ERR_UNSUPPORTED, "ending: base channels must be a multiple of 8");
-    const size_t smem = static_cast<size_t>(27) * p.C0 * sizeof(float) +
-                        static_cast<size_t>((kTile + 2) * (kTile + 2)) * (p.C0 + 2) * sizeof(__half);
+    const size_t smem = (static_cast<size_t>(27) * p.C0 + static_cast<size_t>(kArea) * (p.C0 + 4)) * sizeof(float);
     if (smem > 200 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "ending: too many channels");
     static bool configured = false;
     if (!configured) {
@@ -215,8 +265,8 @@ int launch_ending(const EndingParams& p, cudaStream_t s) {
         if (e != cudaSuccess) return dn_cuda_fail(e, "ending: set smem attribute");
         configured = true;
     }
-    dim3 grid((p.W + kTile - 1) / kTile, (p.H + kTile - 1) / kTile, p.N);
-    const cudaError_t le = launch_pdl(ending_kernel, grid, dim3(256), smem, s, p);
+    dim3 grid((p.W + kTW - 1) / kTW, (p.H + kTH - 1) / kTH, p.N);
+    const cudaError_t le = launch_pdl(ending_kernel, grid, dim3(kThreads), smem, s, p);
     if (le != cudaSuccess) return dn_cuda_fail(le, "ending: launch");
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "ending: launch");

@@ -9,15 +9,19 @@
 // training/models.py:178-185), which the separate-GEMM path runs as three
 // launches with y and h round-tripping through memory.
 //
-// One CTA (320 threads) owns a stream of 128-pixel tiles:
-//   warp 0   producer: walks the tile's operand units - 16 KB slices of
-//            [128 x 64] fp16 - through an R-deep shared-memory ring: g and x
-//            boxes by TMA (128-byte swizzle), weight slices by bulk copy from
-//            the engine's pre-packed GEMM images (no swizzle, K-major).
+// One CTA (416 threads) owns a stream of 128-pixel tiles:
+//   warps 0, 10-12  producers: walk the tile's operand units - 16 KB slices
+//            of [128 x 64] fp16 - through an R-deep shared-memory ring, unit v
+//            issued by producer v % 4 (a single issuing thread sustains only
+//            about one copy in flight): g and x boxes by TMA (128-byte
+//            swizzle), weight slices by bulk copy from the engine's
+//            pre-packed GEMM images (no swizzle, K-major).
 //   warp 1   MMA issuer: conv3 into TMEM columns [0, C); conv4 per 64-channel
 //            gate chunk j (a and b halves side by side, N = 128) into one of
-//            two TMEM buffers at [C, C + 256); conv5 accumulating into [0, C)
-//            (conv3's columns are free by then) with the gated chunk as A.
+//            two TMEM buffers at [C, C + 256); conv5, with the gated chunk as
+//            A, accumulating into its own columns [C + 256, 2C + 256) when
+//            they fit (C = 128: the next tile's conv3 then overlaps this
+//            tile's last epilogue), else into conv3's (free by then).
 //            Issue order conv4_0, conv4_1, conv5_0, conv4_2, conv5_1, ... so
 //            the next conv4 overlaps the epilogue of the current chunk.
 //   warps 2-9 epilogue, two threads per tile row (a TMEM lane) splitting its
@@ -44,7 +48,8 @@ namespace dnb {
 
 namespace {
 
-constexpr int kDThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-9 epilogue
+constexpr int kDThreads = 416;   // warps 0, 10-12 producers, warp 1 MMA, warps 2-9 epilogue
+constexpr int kProd = 4;         // producer warps
 constexpr int kUnit = 16384;     // one ring unit: [128 rows x 64] fp16
 
 template <int C, int D, int F>
@@ -62,6 +67,8 @@ struct GeoD {
     static constexpr int P_FLOATS = 4 * C + 4 * F;        // b3, beta, gamma, b5, c1[2F], c2[2F]
     static constexpr int SMEM = 1024 + Y_BYTES + 2 * H_BYTES + R * kUnit + P_FLOATS * 4;
     static constexpr int TMEM_COLS = 512;                 // C + 2 x 128 <= 512
+    static constexpr bool kSplit = 2 * C + 256 <= 512;    // conv5 has columns of its own
+    static constexpr int ACC5 = kSplit ? C + 256 : 0;     // conv5 accumulator column
     static_assert(C + 256 <= 512, "TMEM: conv3/conv5 accumulator + two gate-chunk buffers");
     static_assert(D % 64 == 0 && F % 128 == 0 && C % 128 == 0, "tile geometry");
     static_assert(SMEM <= 227 * 1024, "shared memory");
@@ -140,15 +147,22 @@ __global__ void __launch_bounds__(kDThreads, 1)
     const uint32_t tmem = tslot;
     pdl_wait();  // g, x and the SCA-scaled conv3 image come from earlier kernels
 
-    if (warp == 0) {
-        // ------------------------------ producer ---------------------------------
+    if (warp == 0 || warp >= 10) {
+        // ------------------------------ producers --------------------------------
+        // Unit v of the tile sequence is issued by producer v % kProd: one
+        // issuing thread keeps only about one copy in flight, so four warps
+        // stream the ring.
+        const int pk = warp == 0 ? 0 : warp - 9;
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            // Next ring slot, once free, armed for `bytes`; nullptr on abort.
+            // Claims sequence unit `it`: the slot, once free, armed for `bytes`;
+            // nullptr if another producer issues this unit (or on abort, with
+            // `ok` cleared).
             auto slot = [&](uint32_t bytes, uint64_t*& bar) -> uint8_t* {
-                const uint32_t s = it % G::R, ph = (it / G::R) & 1u;
-                ++it;
+                const uint32_t v = it++;
+                if (static_cast<int>(v % kProd) != pk) return nullptr;
+                const uint32_t s = v % G::R, ph = (v / G::R) & 1u;
                 if (!wait_or_abort(&empty[s], ph ^ 1u, &s_abort, p.err, 0x50)) {
                     ok = false;
                     return nullptr;
@@ -162,33 +176,28 @@ __global__ void __launch_bounds__(kDThreads, 1)
                 uint64_t* bar = nullptr;
                 uint8_t* u;
                 for (int kk = 0; kk < G::KD && ok; ++kk) {
-                    if (!(u = slot(kUnit, bar))) break;
-                    tma_load_2d(u, &mg, kk * 64, m0, bar);
-                    for (int h = 0; h < G::NH && ok; ++h) {
-                        if (!(u = slot(kUnit, bar))) break;
-                        bulk_g2s(u, p.w3 + static_cast<size_t>(kk) * C * 128 + h * kUnit, kUnit, bar);
-                    }
+                    if ((u = slot(kUnit, bar))) tma_load_2d(u, &mg, kk * 64, m0, bar);
+                    for (int h = 0; h < G::NH && ok; ++h)
+                        if ((u = slot(kUnit, bar)))
+                            bulk_g2s(u, p.w3 + static_cast<size_t>(kk) * C * 128 + h * kUnit, kUnit, bar);
                 }
-                for (int kk = 0; kk < C / 64 && ok; ++kk) {
-                    if (!(u = slot(kUnit, bar))) break;
-                    tma_load_2d(u, &mx, kk * 64, m0, bar);
-                }
+                for (int kk = 0; kk < C / 64 && ok; ++kk)
+                    if ((u = slot(kUnit, bar))) tma_load_2d(u, &mx, kk * 64, m0, bar);
                 // conv4 chunk j: rows [64(j%2), +64) (a) and [128 + 64(j%2), +64)
                 // (b) of packed tile j/2, per K chunk: two contiguous 8 KB slices.
                 auto c4 = [&](int j) {
                     const uint8_t* src = p.w4 + static_cast<size_t>(j >> 1) * G::KC4 * 32768 + (j & 1) * 8192;
-                    for (int kk = 0; kk < G::KC4 && ok; ++kk) {
-                        if (!(u = slot(kUnit, bar))) return;
-                        bulk_g2s(u, src + kk * 32768, 8192, bar);
-                        bulk_g2s(u + 8192, src + kk * 32768 + 16384, 8192, bar);
-                    }
+                    for (int kk = 0; kk < G::KC4 && ok; ++kk)
+                        if ((u = slot(kUnit, bar))) {
+                            bulk_g2s(u, src + kk * 32768, 8192, bar);
+                            bulk_g2s(u + 8192, src + kk * 32768 + 16384, 8192, bar);
+                        }
                 };
                 // conv5 chunk j: K chunk j of the [C x F] image, in 128-row slices.
                 auto c5 = [&](int j) {
-                    for (int h = 0; h < G::NH && ok; ++h) {
-                        if (!(u = slot(kUnit, bar))) return;
-                        bulk_g2s(u, p.w5 + static_cast<size_t>(j) * C * 128 + h * kUnit, kUnit, bar);
-                    }
+                    for (int h = 0; h < G::NH && ok; ++h)
+                        if ((u = slot(kUnit, bar)))
+                            bulk_g2s(u, p.w5 + static_cast<size_t>(j) * C * 128 + h * kUnit, kUnit, bar);
                 };
                 c4(0);
                 for (int j = 1; j < G::J && ok; ++j) {
@@ -200,7 +209,8 @@ __global__ void __launch_bounds__(kDThreads, 1)
             if (!ok) {
                 // Let the copies already issued land before the CTA's memory is released.
                 const uint32_t lo = it > static_cast<uint32_t>(G::R) ? it - G::R : 0u;
-                for (uint32_t v = lo; v + 1 < it; ++v) mbar_wait(&full[v % G::R], (v / G::R) & 1u, 5000000ull);
+                for (uint32_t v = lo; v + 1 < it; ++v)
+                    if (static_cast<int>(v % kProd) == pk) mbar_wait(&full[v % G::R], (v / G::R) & 1u, 5000000ull);
             }
         }
     } else if (warp == 1) {
@@ -218,7 +228,9 @@ __global__ void __launch_bounds__(kDThreads, 1)
             auto bdesc = [&](uint32_t s, int k) { return sdesc_kmajor(smem_u32(ring + s * kUnit) + k * 256, 128, 1024); };
             int tl = 0;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tl) {
-                if (!wait_or_abort(&acc_free, (tl & 1) ^ 1, &s_abort, p.err, 0x51)) break;
+                // conv3 overwrites [0, C): with a shared accumulator the
+                // previous tile's output epilogue must have drained it.
+                if (!G::kSplit && !wait_or_abort(&acc_free, (tl & 1) ^ 1, &s_abort, p.err, 0x51)) break;
                 tc_fence_after();
                 // conv3: [128 x D] x [D -> C]
                 for (int kk = 0; kk < G::KD && ok; ++kk) {
@@ -266,6 +278,12 @@ __global__ void __launch_bounds__(kDThreads, 1)
                 };
                 auto c5 = [&](int j) {
                     const uint32_t u4 = n4 + j, b = u4 & 1u;
+                    // Own conv5 columns: the previous tile's output epilogue
+                    // must have drained them before the first chunk overwrites.
+                    if (G::kSplit && j == 0 && !wait_or_abort(&acc_free, (tl & 1) ^ 1, &s_abort, p.err, 0x51)) {
+                        ok = false;
+                        return;
+                    }
                     if (!wait_or_abort(&h_full[b], (u4 >> 1) & 1u, &s_abort, p.err, 0x56)) {
                         ok = false;
                         return;
@@ -278,7 +296,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
                         tc_fence_after();
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            mma_f16(tmem + h * 128, sdesc_kmajor_sw(a0 + k * 32, 128), bdesc(s, k), idesc,
+                            mma_f16(tmem + G::ACC5 + h * 128, sdesc_kmajor_sw(a0 + k * 32, 128), bdesc(s, k), idesc,
                                     (j | k) ? 1u : 0u);
                         mma_commit(&empty[s]);
                     }
@@ -438,7 +456,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
 #pragma unroll 1
             for (int c0 = cb; c0 < cb + CH; c0 += 16) {
                 float v[16];
-                tmem_ld16(lane_base + c0, v);
+                tmem_ld16(lane_base + G::ACC5 + c0, v);
                 tmem_ld_wait();
                 uint8_t* yb = sY + (c0 >> 6) * kUnit;
 #pragma unroll

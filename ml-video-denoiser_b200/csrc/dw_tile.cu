@@ -10,7 +10,9 @@
 //     column and produces two vertically adjacent outputs from a 4-row
 //     sliding window; the halves of a gate pair are adjacent lanes;
 //   * the gated tile leaves by one TMA store; the tile's per-channel sums
-//     (of the stored fp16 values) go to partials[img][tile][channel].
+//     (of the stored fp16 values) add, in the CTA's fixed tile order, to the
+//     CTA's running sums, written once to partials[img][blockIdx.x][channel]
+//     (one pool row per CTA keeps the SCA kernel's re-reduction short).
 // Each input element crosses the memory system once (plus the 1-pixel halo),
 // instead of once per tap.
 //
@@ -101,6 +103,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (static_cast<int>(blockIdx.x + gridDim.x) < ntiles) load(blockIdx.x + gridDim.x, 1);
     }
 
+    float cta_sum = 0.f;  // threads tid < kCS: running pool sum of channel cs0 + tid
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int b = it & 1;
@@ -172,9 +175,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (tid < kCS) {
             float sum = 0.f;
             for (int c = 0; c < kTW; ++c) sum += sRed[c * kCS + tid];
-            p.partials[(static_cast<size_t>(img) * ntiles + t) * D + cs0 + tid] = sum;
+            cta_sum += sum;
         }
     }
+    if (tid < kCS) p.partials[(static_cast<size_t>(img) * gridDim.x + blockIdx.x) * D + cs0 + tid] = cta_sum;
     if (tid == 0) bulk_wait0();
 }
 
@@ -222,7 +226,7 @@ int launch_dw_tile(const DwParams& p, cudaStream_t s) {
     const int gx = std::max(1, std::min(tiles, (2 * sms + per - 1) / per));
     cudaError_t e = launch_pdl(dw_tile_kernel, dim3(gx, p.D / kCS, p.N), dim3(kThreads), kSmem, s, p, mu, mg);
     if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: launch");
-    return launch_sca(p, tiles, s);
+    return launch_sca(p, gx, s);
 }
 
 }  // namespace dnb

@@ -1,12 +1,14 @@
 // Persistent, warp-specialised implicit GEMM on the 5th-generation tensor
 // cores (tcgen05):  out[M, N] = epi( pro(A)[M, K] * B[N, K]^T ).
 //
-// Roles (320 threads per CTA, one CTA owns a stream of 128 x NT tiles):
-//   warp 8      TMA producer: per K-chunk, 2-D tensor-map loads of the A rows
-//               (box 8 x 128, landing directly in the no-swizzle K-major
-//               UMMA layout: LBO 2 KB between 8-wide K groups, SBO 128 B
-//               between 8-row groups) and one bulk copy of the pre-packed B
-//               tile, both completing on the stage's `raw` mbarrier.
+// Roles (480 threads per CTA, one CTA owns a stream of 128 x NT tiles):
+//   warp 12     A producer: per K-chunk, 2-D tensor-map loads of the A rows
+//               (one 128-byte-swizzled box of KC channels, or 8-channel boxes
+//               landing directly in the no-swizzle K-major UMMA layout: LBO
+//               2 KB between 8-wide K groups, SBO 128 B between 8-row groups).
+//   warp 14     B producer: one bulk copy of the pre-packed B tile per
+//               K-chunk. Both arrive on the stage's `raw` mbarrier; two
+//               issuing threads keep two copies in flight per stage.
 //   warps 0-3   transform, thread t = tile row t:
 //                 LayerNorm: accumulates the row statistics (shifted sums)
 //                   from the staged chunks while the MMA consumes them - the
@@ -15,13 +17,14 @@
 //                   c1[n] = sum_k (gW)[n,k], c2[n] = sum_k b_ln[k] W[n,k] + bias[n];
 //                 SCA scale: A[m,k] *= s[img,k] in place before the MMA;
 //                 2x2 stride-2 conv: gathers the patch rows itself.
-//   warp 9      MMA issuer: one thread issues KC/16 tcgen05.mma (M=128,
+//   warp 13     MMA issuer: one thread issues KC/16 tcgen05.mma (M=128,
 //               N=NT, K=16) per chunk into one of two TMEM accumulators.
-//   warps 4-7   epilogue: thread t reads TMEM lane t (its row) with
-//               tcgen05.ld, applies bias / LN fold / SimpleGate / beta-gamma
-//               residual, writes a swizzled staging tile, and one thread moves
-//               the tile out with TMA tensor stores (the residual tile arrives
-//               the same way), or scatters PixelShuffle(2)+skip directly.
+//   warps 4-11  epilogue: warp w reads TMEM lanes 32*(w%4) (its tile rows)
+//               and one column half with tcgen05.ld, applies bias / LN fold /
+//               SimpleGate / beta-gamma residual, writes a swizzled staging
+//               tile, and one thread moves the tile out with TMA tensor stores
+//               (the residual tile arrives the same way), or scatters
+//               PixelShuffle(2)+skip directly.
 // A 3-stage shared-memory ring and double-buffered accumulators overlap
 // loads, MMAs and epilogues of consecutive tiles. Every wait is bounded.
 //
@@ -54,7 +57,7 @@ namespace {
 constexpr int kRows = 128;
 constexpr int kStages = 3;
 constexpr int kKC = 64;                 // shared-memory footprint is sized for KC = 64
-constexpr int kThreads = 448;
+constexpr int kThreads = 480;
 constexpr uint32_t kALbo = kRows * 16;  // 2 KB between K-adjacent core-matrix columns
 
 struct GemmMaps {
@@ -174,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&bar_raw[s], 1);
+            mbar_init(&bar_raw[s], 2);  // the A and the B producer
             mbar_init(&bar_full[s], 4);
             mbar_init(&bar_empty[s], kLN ? 5 : 1);  // LN: MMA commit + 4 statistics warps
         }
@@ -200,8 +203,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncthreads();
     }
 
-    if (warp == 12) {
-        // ------------------------------ TMA producer ------------------------------
+    if (warp == 12 || warp == 14) {
+        // ------------------------------ TMA producers -----------------------------
+        // Warp 12 loads the A rows, warp 14 the B tile of each stage: one
+        // issuing thread sustains about one copy per microsecond-scale copy
+        // latency, so the two operands stream from separate threads.
+        const bool is_b = (warp == 14);
         if (lane == 0) {
             int it = 0;
             for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x) {
@@ -213,9 +220,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!wait_or_abort(&bar_empty[s], ph ^ 1, &s_abort, p.err, 0x20)) break;
                     uint8_t* sa = smem + s * stage_bytes;
                     uint8_t* sb = sa + kRows * kKC * 2;
-                    mbar_arrive_expect_tx(&bar_raw[s], (AMODE == kAS2x2 ? 0u : a_bytes) + b_bytes);
-                    bulk_g2s(sb, p.bpack + (static_cast<size_t>(n_tile) * nk + j) * b_bytes, b_bytes,
-                             &bar_raw[s]);
+                    if (is_b) {
+                        mbar_arrive_expect_tx(&bar_raw[s], b_bytes);
+                        bulk_g2s(sb, p.bpack + (static_cast<size_t>(n_tile) * nk + j) * b_bytes, b_bytes,
+                                 &bar_raw[s]);
+                        continue;
+                    }
+                    mbar_arrive_expect_tx(&bar_raw[s], AMODE == kAS2x2 ? 0u : a_bytes);
                     if (AMODE != kAS2x2) {
                         const int k0 = j * KC;
                         if (a_swz) {
