@@ -283,6 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kLN || kWriteA) {
             const int r = tid;  // tile row
             int it = 0, t = 0;
+            int s2_prev = -1;  // 2x2 gather: stage whose copies are still in flight
             for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x, ++t) {
                 const int row = (tile / p.n_tiles) * kRows + r;
                 const bool row_ok = row < p.M;
@@ -327,20 +328,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&bar_empty[s]);
                     } else if (AMODE == kAS2x2) {
-                        uint4 v[8];
+                        // Gather this stage's patch rows with cp.async (zero fill
+                        // outside), then release the previous stage once its copies
+                        // have landed: one stage of gathers stays in flight.
 #pragma unroll
                         for (int q = 0; q < 8; ++q) {
                             const int k = j * KC + q * 8;
-                            v[q] = make_uint4(0, 0, 0, 0);
-                            if (q * 8 < KC && row_ok && k < p.K)
-                                v[q] = __ldg(reinterpret_cast<const uint4*>(s2_src(p, img, pix, k)));
+                            if (q * 8 < KC) {
+                                const bool valid = row_ok && k < p.K;
+                                cp_async16_zfill(sa + a_off(r, q), valid ? s2_src(p, img, pix, k) : p.a[0], valid);
+                            }
                         }
-#pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            if (q * 8 < KC) *reinterpret_cast<uint4*>(sa + a_off(r, q)) = v[q];
-                        fence_async_smem();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&bar_full[s]);
+                        cp_async_commit();
+                        if (s2_prev >= 0) {
+                            cp_async_wait<1>();
+                            fence_async_smem();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&bar_full[s2_prev]);
+                        }
+                        s2_prev = s;
                     } else {  // SCA scale in place
                         if (row_ok) {
                             const float* sc = one_img ? s_sca : p.pro_scale + static_cast<size_t>(img) * p.K;
@@ -371,6 +377,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&bar_st_full[sb]);
                 }
+            }
+            if (AMODE == kAS2x2) {
+                // Release the last gathered stage (and let every copy land).
+                cp_async_wait<0>();
+                fence_async_smem();
+                __syncwarp();
+                if (s2_prev >= 0 && lane == 0 && !s_abort) mbar_arrive(&bar_full[s2_prev]);
             }
         }
     } else {
@@ -426,8 +439,60 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 wait_or_abort(&bar_res, t & 1, &s_abort, p.err, 0x27);
             }
-            if (EPI == kEpiShuffleAdd || !tma_epi) {
-                // Direct per-row stores (PixelShuffle scatter, or narrow outputs).
+            if (EPI == kEpiShuffleAdd) {
+                // PixelShuffle(2) scatter + skip: column n = ij * cout + ch of input
+                // pixel (y, x) lands at output pixel (2y + ij/2, 2x + ij%2),
+                // channel ch. The skip vectors of 8 column groups are loaded
+                // before any is used (one memory latency per 64 columns).
+                int c_lo, c_hi;
+                span(kOutCols, c_lo, c_hi);
+                const int cout = p.out_c;
+                const int y = pix / p.Wo;
+                const int x = pix - y * p.Wo;
+                auto soff = [&](int n) -> size_t {
+                    const int ij = n / cout;
+                    const int ch = n - ij * cout;
+                    const size_t opix = (static_cast<size_t>(img) * (2 * p.Ho) + 2 * y + (ij >> 1)) * (2 * p.Wo) +
+                                        2 * x + (ij & 1);
+                    return opix * cout + ch;
+                };
+#pragma unroll 1
+                for (int cb = c_lo; cb < c_hi; cb += 64) {
+                    uint4 sk[8];
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        const int c = cb + 8 * g;
+                        sk[g] = make_uint4(0, 0, 0, 0);
+                        if (row_ok && c < c_hi && col0 + c < p.n_out)
+                            sk[g] = __ldg(reinterpret_cast<const uint4*>(p.skip + soff(n_tile * NT + c)));
+                    }
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        const int c0 = cb + 16 * h;
+                        if (c0 >= c_hi) break;  // uniform across the warp
+                        float va[16];
+                        tmem_ld16(lane_base + c0, va);
+                        tmem_ld_wait();
+                        if (!row_ok) continue;
+#pragma unroll
+                        for (int g = 0; g < 2; ++g) {
+                            const int n = n_tile * NT + c0 + 8 * g;
+                            if (col0 + c0 + 8 * g >= p.n_out) break;
+                            float f[8], rr[8];
+                            h8_to_f(sk[2 * h + g], rr);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) f[i] = va[8 * g + i] + s_bias[n + i] + rr[i];
+                            *reinterpret_cast<uint4*>(p.out + soff(n)) = f_to_h8(f);
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+                continue;
+            }
+            if (!tma_epi) {
+                // Direct per-row stores (outputs narrower than a staging box).
                 int c_lo, c_hi;
                 span(kOutCols, c_lo, c_hi);
 #pragma unroll 1
@@ -459,30 +524,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                             f[i] = (EPI == kEpiStore && p.relu) ? fmaxf(v, 0.f) : v;
                         }
-                        if (EPI == kEpiShuffleAdd) {
-                            const int cout = p.out_c;
-                            const int ij = n / cout;
-                            const int ch = n - ij * cout;
-                            const int y = pix / p.Wo;
-                            const int x = pix - y * p.Wo;
-                            const size_t opix = (static_cast<size_t>(img) * (2 * p.Ho) + 2 * y + (ij >> 1)) *
-                                                    (2 * p.Wo) + 2 * x + (ij & 1);
-                            const size_t off = opix * cout + ch;
+                        const size_t off = static_cast<size_t>(row) * p.out_c + o;
+                        if (EPI == kEpiResidual) {
                             float rr[8];
-                            h8_to_f(*reinterpret_cast<const uint4*>(p.skip + off), rr);
+                            h8_to_f(*reinterpret_cast<const uint4*>(p.res + off), rr);
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) f[i] += rr[i];
-                            *reinterpret_cast<uint4*>(p.out + off) = f_to_h8(f);
-                        } else {
-                            const size_t off = static_cast<size_t>(row) * p.out_c + o;
-                            if (EPI == kEpiResidual) {
-                                float rr[8];
-                                h8_to_f(*reinterpret_cast<const uint4*>(p.res + off), rr);
-#pragma unroll
-                                for (int i = 0; i < 8; ++i) f[i] = rr[i] + s_rsc[o + i] * f[i];
-                            }
-                            *reinterpret_cast<uint4*>(p.out + off) = f_to_h8(f);
+                            for (int i = 0; i < 8; ++i) f[i] = rr[i] + s_rsc[o + i] * f[i];
                         }
+                        *reinterpret_cast<uint4*>(p.out + off) = f_to_h8(f);
                     }
                 }
                 tc_fence_before();
