@@ -281,6 +281,17 @@ void Engine::build(const HostWeights& hw) {
                             LnFold{&ln2w, &ln2b});
         const auto b5 = hw.to_f32(pre + ".conv5.bias");
         b.conv5 = pack_gemm(pk, hw.to_f32(pre + ".conv5.weight"), C, b.ffn, store_nt(C), &b5, C);
+        if (deep_b_supported(C, b.dw, b.ffn)) {
+            std::vector<int> rows(static_cast<size_t>(b.ffn / 64) * 128);
+            for (int j = 0; j < b.ffn / 64; ++j)
+                for (int r = 0; r < 64; ++r) {
+                    rows[j * 128 + r] = 64 * j + r;
+                    rows[j * 128 + 64 + r] = b.ffn + 64 * j + r;
+                }
+            const auto b4 = hw.to_f32(pre + ".conv4.bias");
+            b.d4 = pack_rows(pk, hw.to_f32(pre + ".conv4.weight"), C, rows, 128, &b4, b.ffn, LnFold{&ln2w, &ln2b});
+            b.deep = true;
+        }
         if (fused_supported(C, b.dw, b.ffn)) {
             b.fused = true;
             const auto b4 = hw.to_f32(pre + ".conv4.bias");
@@ -631,10 +642,10 @@ int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cuda
 // conv5 as single N tiles of K chunk 64, conv4 as 256-row tiles (two
 // 128-channel gate halves) of K chunk 64.
 static bool deep_b_layout_ok(const BlockW& b) {
-    return b.conv3.n_tiles == 1 && b.conv3.NT == b.C && b.conv3.KC == 64 && b.conv3.k_chunks * 64 == b.dw &&
-           b.conv4.NT == 256 && b.conv4.KC == 64 && b.conv4.n_tiles * 128 == b.ffn && b.conv4.has_c1 &&
-           b.conv5.n_tiles == 1 && b.conv5.NT == b.C && b.conv5.KC == 64 && b.conv5.k_chunks * 64 == b.ffn &&
-           b.conv3.has_bias && b.conv5.has_bias;
+    return b.deep && b.conv3.n_tiles == 1 && b.conv3.NT == b.C && b.conv3.KC == 64 && b.conv3.k_chunks * 64 == b.dw &&
+           b.d4.NT == 128 && b.d4.KC == 64 && b.d4.n_tiles * 64 == b.ffn && b.d4.k_chunks * 64 == b.C &&
+           b.d4.has_c1 && b.d4.has_bias && b.conv5.n_tiles == 1 && b.conv5.NT == b.C && b.conv5.KC == 64 &&
+           b.conv5.k_chunks * 64 == b.ffn && b.conv3.has_bias && b.conv5.has_bias;
 }
 
 static GemmParams rows_params(int nimg, int h, int w) {
@@ -764,12 +775,12 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
         q.out = x;
         q.M = static_cast<int>(hw);
         q.w3 = b3s_;
-        q.w4 = wptr<uint8_t>(b.conv4.bpack);
+        q.w4 = wptr<uint8_t>(b.d4.bpack);
         q.w5 = wptr<uint8_t>(b.conv5.bpack);
         q.b3 = wptr<float>(b.conv3.bias);
         q.beta = wptr<float>(b.beta);
-        q.c1 = wptr<float>(b.conv4.c1);
-        q.c2 = wptr<float>(b.conv4.bias);
+        q.c1 = wptr<float>(b.d4.c1);
+        q.c2 = wptr<float>(b.d4.bias);
         q.b5 = wptr<float>(b.conv5.bias);
         q.gamma = wptr<float>(b.gamma);
         q.err = err_;

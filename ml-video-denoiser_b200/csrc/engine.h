@@ -39,6 +39,10 @@ struct BlockW {
     // Fused two-pass kernels (shallow levels, C <= 64): single-tile B images.
     bool fused = false;
     GemmW f1, f3, f4, f5;          // conv1 (LN folded), conv3, conv4, conv5
+    // Single-kernel second pass (C = D = F = 128 / 256): conv4 with LN2 folded
+    // as 128-row tiles [64 a rows | 64 b rows] per 64-channel gate chunk.
+    bool deep = false;
+    GemmW d4;
 };
 
 struct ModelInfo {

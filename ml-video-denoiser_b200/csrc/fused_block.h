@@ -44,10 +44,11 @@ int launch_fused_b(const FusedBParams& p, int C, int D, int F, cudaStream_t s);
 
 // Second pass of a deep NAFBlock on one image, in place on x:
 // y = x + beta * (g (W3 diag(s))^T + b3); h = SimpleGate(LN2(y) W4^T + b4);
-// out = y + gamma * (h W5^T + b5). The B operands are the engine's GEMM tile
-// images (KC = 64): w3 = the SCA-scaled conv3 image ([C x D], one N tile),
-// w4 = conv4 packed with the gate halves interleaved per 128-channel tile and
-// LN2 folded (c1, c2 in that packed order), w5 = conv5 ([C x F], one N tile).
+// out = y + gamma * (h W5^T + b5), for C = D = F = 128 or 256. The B operands
+// are the engine's tile images (K chunks of 64): w3 = the SCA-scaled conv3
+// image ([C x D], one N tile), w4 = conv4 with LN2 folded as 128-row tiles
+// [64 a rows | 64 b rows] per 64-channel gate chunk (c1, c2 in that packed
+// order), w5 = conv5 ([C x F], one N tile).
 struct DeepBParams {
     const __half* g;        // [M, D]
     const __half* x;        // [M, C]
