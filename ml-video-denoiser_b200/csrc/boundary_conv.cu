@@ -133,101 +133,102 @@ __global__ void __launch_bounds__(kThreads) intro_kernel(const __grid_constant__
     if (o0 < C0) intro_group<4>(sx, sw, sb, Cin, C0, o0, ly, lx, d0, d1, st0, st1);
 }
 
-// Ending: the halo tile of the NHWC features staged once as fp32 (pixel
-// stride C0 + 4 floats: consecutive lanes hit distinct 16-byte bank groups);
-// per tap and 4 channels, three broadcast float4 weight reads (one per output)
-// and one float4 input read per pixel feed six packed FMAs whose two lanes
-// accumulate the even and odd channels.
+// Ending: output tile 16 x 32; thread = one column x 4 output rows, so per
+// tap column kx and 8 channels it loads the 6 halo rows it needs once and
+// uses them for all 3 tap rows, and every broadcast weight read serves 4
+// pixels. The halo of the NHWC features is staged as fp16 by cp.async (zero
+// fill outside the padded map; pixel stride C0 + 8 halves: consecutive lanes
+// hit distinct 16-byte bank groups). Packed FMAs accumulate even and odd
+// channels in the two lanes.
+constexpr int kETH = 16, kETW = 32;
+constexpr int kEWW = kETW + 2;
+constexpr int kEArea = (kETH + 2) * kEWW;
+
 __global__ void __launch_bounds__(kThreads) ending_kernel(const __grid_constant__ EndingParams p) {
     extern __shared__ __align__(16) float sm[];
     const int C0 = p.C0;
-    const int ps = C0 + 4;
-    float* sw = sm;                   // [9 taps][C0/4][3 outputs][4]
-    float* sx = sw + 27 * C0;         // [kArea][ps]
+    const int ps = C0 + 8;                                  // halves per staged halo pixel
+    float* sw = sm;                                         // [9 taps][C0/8][3 outputs][8]
+    __half* sx = reinterpret_cast<__half*>(sw + 27 * C0);   // [kEArea][ps]
     const int img = blockIdx.z;
-    const int ty0 = blockIdx.y * kTH, tx0 = blockIdx.x * kTW;
+    const int ty0 = blockIdx.y * kETH, tx0 = blockIdx.x * kETW;
     const int tid = threadIdx.x;
     pdl_trigger();
     for (int i = tid; i < 27 * C0; i += kThreads) {
         const int t = i / (3 * C0);
         const int r = i - t * 3 * C0;
-        const int c4 = r / 12, o = (r / 4) % 3, e = r % 4;
-        sw[i] = p.w[(o * 9 + t) * C0 + 4 * c4 + e];
+        const int c8 = r / 24, o = (r / 8) % 3, e = r % 8;
+        sw[i] = p.w[(o * 9 + t) * C0 + 8 * c8 + e];
     }
     pdl_wait();
     const __half* xin = p.x + static_cast<size_t>(img) * p.Hp * p.Wp * C0;
-    // Halo staging in batches of kBatch 16-byte loads per thread, all issued
-    // before any is converted (one memory latency per batch).
-    constexpr int kBatch = 12;
     const int vec = C0 / 8;
-    for (int base = tid; base < kArea * vec; base += kBatch * kThreads) {
-        uint4 v[kBatch];
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-            const int i = base + j * kThreads;
-            v[j] = make_uint4(0, 0, 0, 0);
-            if (i < kArea * vec) {
-                const int r = i / vec;
-                const int q = i - r * vec;
-                const int yy = ty0 + r / kWW - 1;
-                const int xx = tx0 + r % kWW - 1;
-                if (yy >= 0 && yy < p.Hp && xx >= 0 && xx < p.Wp)
-                    v[j] = __ldg(reinterpret_cast<const uint4*>(xin + (static_cast<size_t>(yy) * p.Wp + xx) * C0) + q);
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-            const int i = base + j * kThreads;
-            if (i >= kArea * vec) break;
-            const int r = i / vec;
-            const int q = i - r * vec;
-            float f[8];
-            h8_to_f(v[j], f);
-            float4* d = reinterpret_cast<float4*>(sx + static_cast<size_t>(r) * ps + q * 8);
-            d[0] = make_float4(f[0], f[1], f[2], f[3]);
-            d[1] = make_float4(f[4], f[5], f[6], f[7]);
-        }
+    for (int i = tid; i < kEArea * vec; i += kThreads) {
+        const int r = i / vec;
+        const int q = i - r * vec;
+        const int yy = ty0 + r / kEWW - 1;
+        const int xx = tx0 + r % kEWW - 1;
+        const bool valid = yy >= 0 && yy < p.Hp && xx >= 0 && xx < p.Wp;
+        const __half* src = valid ? xin + (static_cast<size_t>(yy) * p.Wp + xx) * C0 + q * 8 : xin;
+        cp_async16_zfill(sx + static_cast<size_t>(r) * ps + q * 8, src, valid);
     }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
-    const int ly = tid >> 4, lx = tid & 15;
-    const int oy = ty0 + ly;
-    if (oy >= p.H) return;
-    float2 acc[2][3];
+    const int lx = tid & 31, rg = tid >> 5;  // column, group of 4 output rows
+    float2 acc[4][3];
 #pragma unroll
-    for (int q = 0; q < 2; ++q)
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int o = 0; o < 3; ++o) acc[q][o] = make_float2(0.f, 0.f);
+        for (int o = 0; o < 3; ++o) acc[r][o] = make_float2(0.f, 0.f);
 #pragma unroll 1
-    for (int t = 0; t < 9; ++t) {
-        const float* x0 = sx + static_cast<size_t>((ly + t / 3) * kWW + lx + t % 3) * ps;
-        const float* x1 = x0 + 16 * ps;
-        const float4* wt = reinterpret_cast<const float4*>(sw + t * 3 * C0);
-#pragma unroll 4
-        for (int c4 = 0; c4 < C0 / 4; ++c4) {
-            const float4 a = *reinterpret_cast<const float4*>(x0 + 4 * c4);
-            const float4 b = *reinterpret_cast<const float4*>(x1 + 4 * c4);
+    for (int c8 = 0; c8 < C0 / 8; ++c8) {
 #pragma unroll
-            for (int o = 0; o < 3; ++o) {
-                const float4 w = wt[c4 * 3 + o];
-                const float2 w01 = make_float2(w.x, w.y), w23 = make_float2(w.z, w.w);
-                acc[0][o] = ffma2(make_float2(a.x, a.y), w01, acc[0][o]);
-                acc[0][o] = ffma2(make_float2(a.z, a.w), w23, acc[0][o]);
-                acc[1][o] = ffma2(make_float2(b.x, b.y), w01, acc[1][o]);
-                acc[1][o] = ffma2(make_float2(b.z, b.w), w23, acc[1][o]);
+        for (int kx = 0; kx < 3; ++kx) {
+            float2 in[6][4];  // halo rows 4rg .. 4rg+5 at column lx+kx, channels 8c8 .. 8c8+7
+#pragma unroll
+            for (int ir = 0; ir < 6; ++ir) {
+                const uint4 v = *reinterpret_cast<const uint4*>(
+                    sx + static_cast<size_t>((4 * rg + ir) * kEWW + lx + kx) * ps + 8 * c8);
+                in[ir][0] = unpack_half2(v.x);
+                in[ir][1] = unpack_half2(v.y);
+                in[ir][2] = unpack_half2(v.z);
+                in[ir][3] = unpack_half2(v.w);
+            }
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky) {
+                const float4* wt = reinterpret_cast<const float4*>(sw + ((ky * 3 + kx) * (C0 / 8) + c8) * 24);
+                float2 w[3][4];
+#pragma unroll
+                for (int o = 0; o < 3; ++o) {
+                    const float4 a = wt[2 * o], b = wt[2 * o + 1];
+                    w[o][0] = make_float2(a.x, a.y);
+                    w[o][1] = make_float2(a.z, a.w);
+                    w[o][2] = make_float2(b.x, b.y);
+                    w[o][3] = make_float2(b.z, b.w);
+                }
+#pragma unroll
+                for (int orow = 0; orow < 4; ++orow)
+#pragma unroll
+                    for (int o = 0; o < 3; ++o)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) acc[orow][o] = ffma2(in[orow + ky][e], w[o][e], acc[orow][o]);
             }
         }
     }
     const size_t plane = static_cast<size_t>(p.H) * p.W;
     const __half* beauty = p.beauty + static_cast<size_t>(img) * p.beauty_batch_stride;
     __half* out = p.y + static_cast<size_t>(img) * 3 * plane;
+    const int ox = tx0 + lx;
+    if (ox >= p.W) return;
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        const int ox = tx0 + lx + 16 * q;
-        if (ox >= p.W) continue;
+    for (int orow = 0; orow < 4; ++orow) {
+        const int oy = ty0 + 4 * rg + orow;
+        if (oy >= p.H) break;
         const size_t o = static_cast<size_t>(oy) * p.W + ox;
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            const float r = (acc[q][c].x + acc[q][c].y) + p.b[c];
+            const float r = (acc[orow][c].x + acc[orow][c].y) + p.b[c];
             out[c * plane + o] = __float2half(finite_or_zero(__half2float(beauty[c * plane + o])) + r);
         }
     }
@@ -256,7 +257,8 @@ int launch_intro(const IntroParams& p, cudaStream_t s) {
 
 int launch_ending(const EndingParams& p, cudaStream_t s) {
     if (p.C0 % 8 != 0) return dn_fail(DN_ERR_UNSUPPORTED, "ending: base channels must be a multiple of 8");
-    const size_t smem = (static_cast<size_t>(27) * p.C0 + static_cast<size_t>(kArea) * (p.C0 + 4)) * sizeof(float);
+    const size_t smem = static_cast<size_t>(27) * p.C0 * sizeof(float) +
+                        static_cast<size_t>(kEArea) * (p.C0 + 8) * sizeof(__half);
     if (smem > 200 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "ending: too many channels");
     static bool configured = false;
     if (!configured) {
@@ -265,7 +267,7 @@ int launch_ending(const EndingParams& p, cudaStream_t s) {
         if (e != cudaSuccess) return dn_cuda_fail(e, "ending: set smem attribute");
         configured = true;
     }
-    dim3 grid((p.W + kTW - 1) / kTW, (p.H + kTH - 1) / kTH, p.N);
+    dim3 grid((p.W + kETW - 1) / kETW, (p.H + kETH - 1) / kETH, p.N);
     const cudaError_t le = launch_pdl(ending_kernel, grid, dim3(kThreads), smem, s, p);
     if (le != cudaSuccess) return dn_cuda_fail(le, "ending: launch");
     cudaError_t e = cudaGetLastError();
