@@ -46,7 +46,6 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();  // gemm_tc.cu
 namespace {
 
 constexpr int kAThreads = 256;
-constexpr int kBThreads = 128;
 
 constexpr int pow2_at_least(int v) {
     int p = 32;
@@ -379,11 +378,20 @@ __global__ void __launch_bounds__(kAThreads, 2)
 
 // ============================== phase B =====================================
 
+// 128 threads (one per tile row) at C <= 32, where four CTAs share an SM;
+// 256 at C = 64 (two CTAs per SM): two threads per row (TMEM lane) split its
+// columns, halving the serial epilogue work of each thread.
+template <int C>
+constexpr int b_threads() { return C >= 64 ? 256 : 128; }
+
 template <int C, int D, int F>
-__global__ void __launch_bounds__(kBThreads, 1)
+__global__ void __launch_bounds__(b_threads<C>(), 1)
     fused_b_kernel(const __grid_constant__ FusedBParams p, const __grid_constant__ CUtensorMap mg,
                    const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mo) {
     using G = GeoB<C, D, F>;
+    constexpr int kTh = b_threads<C>();
+    constexpr int kH = kTh / 128;  // threads per tile row
+    constexpr int CC = C / kH, DC = D / kH, FC = F / kH;  // columns per thread
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sG = smem;                  // [128][D] swizzled (span 2D)
@@ -405,11 +413,14 @@ __global__ void __launch_bounds__(kBThreads, 1)
     __shared__ uint64_t bar_w, bar_ld, bar_mma;
     __shared__ uint32_t tslot;
     __shared__ int s_fail;
+    __shared__ float2 s_stat[2][128];  // kH == 2: per-half (mean, M2) of each row
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r = (warp & 3) * 32 + lane;  // tile row == TMEM lane
+    const int hf = warp >> 2;              // column half (0 when one thread owns the row)
     const int tiles = (p.M + 127) / 128;
     const int nimg = (p.M + p.hw - 1) / p.hw;
-    for (int i = tid; i < C; i += kBThreads) {
+    for (int i = tid; i < C; i += kTh) {
         sB3[i] = p.b3[i];
         sBeta[i] = p.beta[i];
         sLw[i] = p.ln_w[i];
@@ -418,7 +429,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
         sGam[i] = p.gamma[i];
     }
     pdl_trigger();
-    for (int i = tid; i < 2 * F; i += kBThreads) sB4[i] = p.b4[i];
+    for (int i = tid; i < 2 * F; i += kTh) sB4[i] = p.b4[i];
     if (warp == 0) {
         tmem_alloc(&tslot, G::TMEM_COLS);
         tmem_relinquish();
@@ -439,13 +450,13 @@ __global__ void __launch_bounds__(kBThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tslot;
     pdl_wait();  // g, x and the SCA scale come from earlier kernels
-    for (int i = tid; i < nimg * D; i += kBThreads) sS[i] = p.s[i];
+    for (int i = tid; i < nimg * D; i += kTh) sS[i] = p.s[i];
     if (tid == 0 && blockIdx.x < tiles) {
         mbar_arrive_expect_tx(&bar_ld, G::G_BYTES + G::X_BYTES);
         tma_load_2d(sG, &mg, 0, blockIdx.x * 128, &bar_ld);
         tma_load_2d(sX, &mx, 0, blockIdx.x * 128, &bar_ld);
     }
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const bool ok = __syncthreads_and(wait_bar(&bar_w, 0, p.err, 0x40)) != 0;
     uint32_t mma_phase = 0;
     auto mma_wait = [&](uint32_t site) {
@@ -457,17 +468,17 @@ __global__ void __launch_bounds__(kBThreads, 1)
     int it = 0;
     for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
         const int m0 = t * 128;
-        const int row = m0 + tid;
+        const int row = m0 + r;
         const int img = row < p.M ? row / p.hw : 0;
         if (!wait_bar(&bar_ld, it & 1, p.err, 0x41)) s_fail = 1;
         __syncthreads();
         if (s_fail) break;
-        // SCA: g *= s in place.
+        // SCA: g *= s in place (this thread's half of the row).
         {
             const float* sc = sS + img * D;
 #pragma unroll
-            for (int q = 0; q < D / 8; ++q) {
-                uint4* ptr = reinterpret_cast<uint4*>(sG + sw_offset(tid, q, 2 * D));
+            for (int q = hf * (DC / 8); q < (hf + 1) * (DC / 8); ++q) {
+                uint4* ptr = reinterpret_cast<uint4*>(sG + sw_offset(r, q, 2 * D));
                 float f[8];
                 h8_to_f(*ptr, f);
 #pragma unroll
@@ -487,40 +498,52 @@ __global__ void __launch_bounds__(kBThreads, 1)
             mma_commit(&bar_mma);
         }
         mma_wait(0x42);
-        // y = x + beta * (acc + b3), then LayerNorm2(y) -> A of conv4.
-        float y[C];
+        // y = x + beta * (acc + b3) (this thread's columns), then LayerNorm2(y) -> A of conv4.
+        float y[CC];
+        const int cb = hf * CC;
 #pragma unroll
-        for (int c0 = 0; c0 < C; c0 += 16) {
+        for (int c0 = 0; c0 < CC; c0 += 16) {
             float v[16];
-            tmem_ld16(lane_base + c0, v);
+            tmem_ld16(lane_base + cb + c0, v);
             tmem_ld_wait();
 #pragma unroll
             for (int g2 = 0; g2 < 2; ++g2) {
                 float xv[8];
-                h8_to_f(*reinterpret_cast<const uint4*>(sX + sw_offset(tid, (c0 >> 3) + g2, 2 * C)), xv);
+                h8_to_f(*reinterpret_cast<const uint4*>(sX + sw_offset(r, ((cb + c0) >> 3) + g2, 2 * C)), xv);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const int c = c0 + 8 * g2 + i;
+                    const int cl = c0 + 8 * g2 + i, c = cb + cl;
                     // round to fp16 like the stored mid-block tensor of the reference
-                    y[c] = __half2float(__float2half(xv[i] + sBeta[c] * (v[8 * g2 + i] + sB3[c])));
+                    y[cl] = __half2float(__float2half(xv[i] + sBeta[c] * (v[8 * g2 + i] + sB3[c])));
                 }
             }
         }
         {
-            float s = 0.f;
+            float s1 = 0.f;
 #pragma unroll
-            for (int c = 0; c < C; ++c) s += y[c];
-            const float mean = s * (1.0f / C);
-            float ss = 0.f;
+            for (int c = 0; c < CC; ++c) s1 += y[c];
+            float mean = s1 * (1.0f / CC);
+            float m2 = 0.f;
 #pragma unroll
-            for (int c = 0; c < C; ++c) ss += (y[c] - mean) * (y[c] - mean);
-            const float rstd = rsqrtf(ss * (1.0f / C) + 1e-6f);
+            for (int c = 0; c < CC; ++c) m2 += (y[c] - mean) * (y[c] - mean);
+            if (kH == 2) {  // merge the two halves of the row (Chan's formula)
+                s_stat[hf][r] = make_float2(mean, m2);
+                __syncthreads();
+                const float2 o = s_stat[hf ^ 1][r];
+                const float d = mean - o.x;
+                mean = 0.5f * (mean + o.x);
+                m2 = m2 + o.y + d * d * (0.25f * C);
+            }
+            const float rstd = rsqrtf(m2 * (1.0f / C) + 1e-6f);
 #pragma unroll
-            for (int q = 0; q < C / 8; ++q) {
+            for (int q = 0; q < CC / 8; ++q) {
                 float f[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) f[i] = (y[8 * q + i] - mean) * rstd * sLw[8 * q + i] + sLb[8 * q + i];
-                *reinterpret_cast<uint4*>(sA2 + sw_offset(tid, q, 2 * C)) = f_to_h8(f);
+                for (int i = 0; i < 8; ++i) {
+                    const int c = cb + 8 * q + i;
+                    f[i] = (y[8 * q + i] - mean) * rstd * sLw[c] + sLb[c];
+                }
+                *reinterpret_cast<uint4*>(sA2 + sw_offset(r, (cb >> 3) + q, 2 * C)) = f_to_h8(f);
             }
         }
         fence_async_smem();
@@ -542,9 +565,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
             mma_commit(&bar_mma);
         }
         mma_wait(0x43);
-        // SimpleGate -> A of conv5.
+        // SimpleGate -> A of conv5 (this thread's gate channels).
+        const int fb = hf * FC;
 #pragma unroll 1
-        for (int c0 = 0; c0 < F; c0 += 16) {
+        for (int c0 = fb; c0 < fb + FC; c0 += 16) {
             float va[16], vb[16];
             tmem_ld16(lane_base + C + c0, va);
             tmem_ld16(lane_base + C + F + c0, vb);
@@ -557,7 +581,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     const int c = c0 + 8 * g2 + i;
                     f[i] = (va[8 * g2 + i] + sB4[c]) * (vb[8 * g2 + i] + sB4[F + c]);
                 }
-                *reinterpret_cast<uint4*>(sA3 + sw_offset(tid, (c0 >> 3) + g2, 2 * F)) = f_to_h8(f);
+                *reinterpret_cast<uint4*>(sA3 + sw_offset(r, (c0 >> 3) + g2, 2 * F)) = f_to_h8(f);
             }
         }
         fence_async_smem();
@@ -575,19 +599,19 @@ __global__ void __launch_bounds__(kBThreads, 1)
         mma_wait(0x44);
         // out = y + gamma * (acc + b5)
 #pragma unroll
-        for (int c0 = 0; c0 < C; c0 += 16) {
+        for (int c0 = 0; c0 < CC; c0 += 16) {
             float v[16];
-            tmem_ld16(lane_base + c0, v);
+            tmem_ld16(lane_base + cb + c0, v);
             tmem_ld_wait();
 #pragma unroll
             for (int g2 = 0; g2 < 2; ++g2) {
                 float f[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const int c = c0 + 8 * g2 + i;
-                    f[i] = y[c] + sGam[c] * (v[8 * g2 + i] + sB5[c]);
+                    const int cl = c0 + 8 * g2 + i, c = cb + cl;
+                    f[i] = y[cl] + sGam[c] * (v[8 * g2 + i] + sB5[c]);
                 }
-                *reinterpret_cast<uint4*>(sO + sw_offset(tid, (c0 >> 3) + g2, 2 * C)) = f_to_h8(f);
+                *reinterpret_cast<uint4*>(sO + sw_offset(r, ((cb + c0) >> 3) + g2, 2 * C)) = f_to_h8(f);
             }
         }
         fence_async_smem();
@@ -691,7 +715,7 @@ int run_b(const FusedBParams& p, cudaStream_t s) {
     const int tiles = (p.M + 127) / 128;
     const int per_sm = std::max(1, std::min(512 / G::TMEM_COLS, (227 * 1024) / (G::SMEM + 2048)));
     const int grid = std::min(tiles, sm_count() * per_sm);
-    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kBThreads), G::SMEM, s, p, mg, mx, mo);
+    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(b_threads<C>()), G::SMEM, s, p, mg, mx, mo);
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "fused_b: launch");
 }
 
