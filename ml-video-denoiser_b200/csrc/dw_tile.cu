@@ -219,11 +219,15 @@ int launch_dw_tile(const DwParams& p, cudaStream_t s) {
     if (rc == DN_OK) rc = encode4(&mg, p.g, p.D, p.W, p.H, p.N, kCS, kTW, kTH);
     if (rc != DN_OK) return rc;
     const int tiles = dw_tile_blocks_per_img(p.H, p.W);
-    // About two CTAs per SM in total; each walks ceil(tiles / grid_x) tiles.
+    // At most two CTAs per SM in total (one wave: a CTA over the limit would
+    // start only when another has walked all of its tiles); the tiles are
+    // then spread evenly, so every CTA walks the same ceil(tiles / grid_x).
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int per = (p.D / kCS) * p.N;
-    const int gx = std::max(1, std::min(tiles, (2 * sms + per - 1) / per));
+    const int gmax = std::max(1, std::min(tiles, 2 * sms / per));
+    const int walk = (tiles + gmax - 1) / gmax;
+    const int gx = (tiles + walk - 1) / walk;
     cudaError_t e = launch_pdl(dw_tile_kernel, dim3(gx, p.D / kCS, p.N), dim3(kThreads), kSmem, s, p, mu, mg);
     if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: launch");
     return launch_sca(p, gx, s);
