@@ -240,8 +240,8 @@ __global__ void __launch_bounds__(kDThreads, 1)
     } else if (warp == 1) {
         // ------------------------------ MMA issuer -------------------------------
         if (lane == 0) {
-            const uint32_t idesc128 = idesc_f16_f32(128, 128);
-            const uint32_t idescC = idesc_f16_f32(128, C);
+            constexpr uint32_t idesc128 = idesc_f16_f32(128, 128);
+            constexpr uint32_t idescC = idesc_f16_f32(128, C);
             uint32_t it = 0, n4 = 0;
             bool ok = true;
             auto take = [&](uint32_t site) -> uint32_t {
@@ -250,8 +250,13 @@ __global__ void __launch_bounds__(kDThreads, 1)
                 if (ok && !wait_or_abort(&full[s], ph, &s_abort, p.err, site)) ok = false;
                 return s;
             };
+            // Descriptors are built once; each MMA adds byte offsets to them.
+            const uint64_t d_ring_b = sdesc_kmajor(smem_u32(ring), 128, 1024);
+            const uint64_t d_ring_a = sdesc_kmajor_sw(smem_u32(ring), 128);
+            const uint64_t d_y = sdesc_kmajor_sw(smem_u32(sY), 128);
+            const uint64_t d_h = sdesc_kmajor_sw(smem_u32(sH), 128);
             auto bdesc = [&](uint32_t s, uint32_t off, int k) {
-                return sdesc_kmajor(smem_u32(ring + s * kUnit) + off + k * 256, 128, 1024);
+                return desc_add(d_ring_b, s * kUnit + off + k * 256);
             };
             int tl = 0;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tl) {
@@ -265,11 +270,11 @@ __global__ void __launch_bounds__(kDThreads, 1)
                     const uint32_t s = take(0x54);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t a0 = G::kGInY ? smem_u32(sY + kk * kBox) : smem_u32(ring + s * kUnit);
+                    const uint64_t a0 = G::kGInY ? desc_add(d_y, kk * kBox) : desc_add(d_ring_a, s * kUnit);
                     const uint32_t boff = G::kGInY ? 0u : static_cast<uint32_t>(kBox);
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
-                        mma_f16(tmem, sdesc_kmajor_sw(a0 + k * 32, 128), bdesc(s, boff, k), idescC, (kk | k) ? 1u : 0u);
+                        mma_f16(tmem, desc_add(a0, k * 32), bdesc(s, boff, k), idescC, (kk | k) ? 1u : 0u);
                     mma_commit(&empty[s]);
                 }
                 if (!ok) break;
@@ -291,11 +296,11 @@ __global__ void __launch_bounds__(kDThreads, 1)
 #pragma unroll
                         for (int kc = 0; kc < 2; ++kc) {
                             const int kk = 2 * m + kc;
-                            const uint32_t a0 = smem_u32(sY + kk * kBox);
+                            const uint64_t a0 = desc_add(d_y, kk * kBox);
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
-                                mma_f16(tmem + C + b * 128, sdesc_kmajor_sw(a0 + k * 32, 128), bdesc(s, kc * kBox, k),
-                                        idesc128, (kk | k) ? 1u : 0u);
+                                mma_f16(tmem + C + b * 128, desc_add(a0, k * 32), bdesc(s, kc * kBox, k), idesc128,
+                                        (kk | k) ? 1u : 0u);
                         }
                         mma_commit(&empty[s]);
                     }
@@ -325,11 +330,10 @@ __global__ void __launch_bounds__(kDThreads, 1)
                     }
                     if (!ok) return;
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sH + b * G::H_BYTES);
+                    const uint64_t a0 = desc_add(d_h, b * G::H_BYTES);
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
-                        mma_f16(tmem + G::ACC5, sdesc_kmajor_sw(a0 + k * 32, 128), bdesc(s, off, k), idescC,
-                                (j | k) ? 1u : 0u);
+                        mma_f16(tmem + G::ACC5, desc_add(a0, k * 32), bdesc(s, off, k), idescC, (j | k) ? 1u : 0u);
                     if (G::U5 == G::J || j == G::J - 1) mma_commit(&empty[s]);
                     mma_commit(&h_empty[b]);
                 };

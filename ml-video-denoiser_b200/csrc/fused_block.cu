@@ -157,6 +157,8 @@ __global__ void __launch_bounds__(kAThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    const uint64_t da1 = sdesc_kmajor_sw(smem_u32(sA), G::ROWB);
+    const uint64_t db1 = sdesc_kmajor(smem_u32(sW1), 128, (C / 8) * 128);
     pdl_wait();  // x was written by the previous kernel
     if (tid == 0 && blockIdx.x < total) {
         int img, ty0, tx0;
@@ -232,12 +234,13 @@ __global__ void __launch_bounds__(kAThreads, 2)
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t idesc = idesc_f16_f32(128, G::N1);
-            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sW1);
+            constexpr uint32_t idesc = idesc_f16_f32(128, G::N1);
+#pragma unroll
             for (int b = 0; b < G::NB; ++b)
+#pragma unroll
                 for (int k = 0; k < C / 16; ++k)
-                    mma_f16(tmem + b * G::N1, sdesc_kmajor_sw(a0 + b * 128 * G::ROWB + k * 32, G::ROWB),
-                            sdesc_kmajor(b0 + k * 256, 128, (C / 8) * 128), idesc, k > 0 ? 1u : 0u);
+                    mma_f16(tmem + b * G::N1, desc_add(da1, b * 128 * G::ROWB + k * 32), desc_add(db1, k * 256), idesc,
+                            k > 0 ? 1u : 0u);
             mma_commit(&bar_mma);
         }
         if (!wait_bar(&bar_mma, it & 1, p.err, 0x32)) s_fail = 1;
@@ -449,6 +452,9 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    const uint64_t d3a = sdesc_kmajor_sw(smem_u32(sG), 2 * D), d3b = sdesc_kmajor(smem_u32(sW3), 128, (D / 8) * 128);
+    const uint64_t d4a = sdesc_kmajor_sw(smem_u32(sA2), 2 * C), d4b = sdesc_kmajor(smem_u32(sW4), 128, (C / 8) * 128);
+    const uint64_t d5a = sdesc_kmajor_sw(smem_u32(sA3), 2 * F), d5b = sdesc_kmajor(smem_u32(sW5), 128, (F / 8) * 128);
     pdl_wait();  // g, x and the SCA scale come from earlier kernels
     for (int i = tid; i < nimg * D; i += kTh) sS[i] = p.s[i];
     if (tid == 0 && blockIdx.x < tiles) {
@@ -491,10 +497,9 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
         __syncthreads();
         if (tid == 0) {  // conv3: [128 x D] x [D -> C]
             tc_fence_after();
-            const uint32_t a0 = smem_u32(sG), b0 = smem_u32(sW3);
+#pragma unroll
             for (int k = 0; k < D / 16; ++k)
-                mma_f16(tmem, sdesc_kmajor_sw(a0 + k * 32, 2 * D), sdesc_kmajor(b0 + k * 256, 128, (D / 8) * 128),
-                        idesc_f16_f32(128, C), k > 0 ? 1u : 0u);
+                mma_f16(tmem, desc_add(d3a, k * 32), desc_add(d3b, k * 256), idesc_f16_f32(128, C), k > 0 ? 1u : 0u);
             mma_commit(&bar_mma);
         }
         mma_wait(0x42);
@@ -558,10 +563,10 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
                 tma_load_2d(sX, &mx, 0, nm, &bar_ld);
             }
             tc_fence_after();  // conv4: [128 x C] x [C -> 2F]
-            const uint32_t a0 = smem_u32(sA2), b0 = smem_u32(sW4);
+#pragma unroll
             for (int k = 0; k < C / 16; ++k)
-                mma_f16(tmem + C, sdesc_kmajor_sw(a0 + k * 32, 2 * C), sdesc_kmajor(b0 + k * 256, 128, (C / 8) * 128),
-                        idesc_f16_f32(128, 2 * F), k > 0 ? 1u : 0u);
+                mma_f16(tmem + C, desc_add(d4a, k * 32), desc_add(d4b, k * 256), idesc_f16_f32(128, 2 * F),
+                        k > 0 ? 1u : 0u);
             mma_commit(&bar_mma);
         }
         mma_wait(0x43);
@@ -590,10 +595,9 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
         __syncthreads();
         if (tid == 0) {  // conv5: [128 x F] x [F -> C]
             tc_fence_after();
-            const uint32_t a0 = smem_u32(sA3), b0 = smem_u32(sW5);
+#pragma unroll
             for (int k = 0; k < F / 16; ++k)
-                mma_f16(tmem, sdesc_kmajor_sw(a0 + k * 32, 2 * F), sdesc_kmajor(b0 + k * 256, 128, (F / 8) * 128),
-                        idesc_f16_f32(128, C), k > 0 ? 1u : 0u);
+                mma_f16(tmem, desc_add(d5a, k * 32), desc_add(d5b, k * 256), idesc_f16_f32(128, C), k > 0 ? 1u : 0u);
             mma_commit(&bar_mma);
         }
         mma_wait(0x44);

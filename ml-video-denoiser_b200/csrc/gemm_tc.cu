@@ -249,30 +249,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 13) {
         // ------------------------------ MMA issuer --------------------------------
         if (lane == 0) {
-            const uint32_t idesc = idesc_f16_f32(kRows, NT);
-            int it = 0, t = 0;
+            constexpr uint32_t idesc = idesc_f16_f32(kRows, NT);
+            // The issuing thread is on the critical path of every stage: the
+            // descriptors of stage 0 are built once, and each MMA only adds a
+            // stage offset and a K-step offset (16-byte units) to them.
+            const uint32_t sm0 = smem_u32(smem);
+            const uint64_t ad0 = a_swz ? sdesc_kmajor_sw(sm0, a_swz) : sdesc_kmajor(sm0, kALbo, 128);
+            const uint64_t bd0 = sdesc_kmajor(sm0 + kRows * kKC * 2, 128, b_sbo);
+            const uint32_t a_kstep = a_swz ? 2u : (2u * kALbo) >> 4;  // one K=16 step
+            const int nks = KC / 16;
+            int s = 0, t = 0;
+            uint32_t ph = 0;
             for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x, ++t) {
                 const int b = t & 1;
                 if (!wait_or_abort(&bar_acc_empty[b], ((t >> 1) & 1) ^ 1, &s_abort, p.err, 0x21)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + b * kAccCols;
                 bool ok = true;
-                for (int j = 0; j < nk; ++j, ++it) {
-                    const int s = it % kStages;
-                    const uint32_t ph = (it / kStages) & 1;
+                for (int j = 0; j < nk; ++j) {
                     if (!wait_or_abort(kWriteA ? &bar_full[s] : &bar_raw[s], ph, &s_abort, p.err, 0x22)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(smem + s * stage_bytes);
-                    const uint32_t b0 = a0 + kRows * kKC * 2;
-                    for (int k = 0; k < KC / 16; ++k) {
-                        const uint64_t ad = a_swz ? sdesc_kmajor_sw(a0 + k * 32, a_swz)
-                                                  : sdesc_kmajor(a0 + k * 2 * kALbo, kALbo, 128);
-                        mma_f16(acc, ad, sdesc_kmajor(b0 + k * 256, 128, b_sbo), idesc, (j > 0 || k > 0) ? 1u : 0u);
-                    }
+                    const uint64_t so = static_cast<uint64_t>(s) * (stage_bytes >> 4);
+                    const uint64_t ad = ad0 + so, bd = bd0 + so;
+#pragma unroll
+                    for (int k = 0; k < kKC / 16; ++k)
+                        if (k < nks) mma_f16(acc, ad + k * a_kstep, bd + 16 * k, idesc, (j > 0 || k > 0) ? 1u : 0u);
                     mma_commit(&bar_empty[s]);
+                    if (++s == kStages) {
+                        s = 0;
+                        ph ^= 1;
+                    }
                 }
                 if (!ok) break;
                 mma_commit(&bar_acc_full[b]);

@@ -218,6 +218,13 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw(uint32_t saddr, uint32_t row
     return d;
 }
 
+// The same descriptor with its start address moved by `bytes` (a multiple of
+// 16). An MMA issue loop builds its descriptors once and steps them with this
+// add: rebuilding them per MMA from runtime values puts ~100+ cycles of
+// integer work before every tcgen05.mma of the single issuing thread, which
+// then issues well below the tensor core's rate.
+__device__ __forceinline__ uint64_t desc_add(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
+
 // Byte offset of 16-byte chunk j of row r in a swizzled K-major tile whose
 // rows are `row_bytes` long (the TMA swizzle pattern of that span).
 __device__ __forceinline__ uint32_t sw_offset(uint32_t r, uint32_t j, uint32_t row_bytes) {
