@@ -153,10 +153,12 @@ int dn_model_stats(const dn_model* model, size_t* weight_bytes, size_t* activati
                    int* kernels_per_forward);
 
 /* Select the fused NAFBlock kernels (default 1): both passes for blocks with
- * <= 64 channels, the single-kernel second pass for 128- and 256-channel
- * blocks of a single-image forward; or the per-conv kernels everywhere (0).
- * Results agree within the parity tolerance; the switch exists for testing
- * both paths. */
+ * <= 64 channels (the first pass of 32/64-channel blocks as one tensor-core
+ * 3x3 conv of the normalised input), the single-kernel second pass for 128-
+ * and 256-channel blocks of a single-image forward; 2: the same with the
+ * first pass on the CUDA cores (LN, conv1 MMA, depthwise taps); 0: the
+ * per-conv kernels everywhere. Results agree within the parity tolerance; the
+ * switch exists for testing every path. */
 int dn_model_set_fused(dn_model* model, int enable);
 
 /* Per-launch CUDA-event timing of the engine's kernels (no reference

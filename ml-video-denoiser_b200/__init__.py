@@ -318,9 +318,12 @@ class Model:
         """Synchronise the stream and raise if a kernel flagged a device error."""
         check(lib().dn_model_sync(self._h, stream_handle(stream)))
 
-    def set_fused(self, enable: bool = True) -> None:
-        """Fused two-pass NAFBlock kernels on shallow levels (default) or per-conv kernels."""
-        check(lib().dn_model_set_fused(self._h, 1 if enable else 0))
+    def set_fused(self, enable=True) -> None:
+        """Fused NAFBlock kernels (True / 1, default), fused with the first pass of
+        the 32/64-channel blocks on the CUDA cores instead of the tensor cores (2),
+        or per-conv kernels (False / 0)."""
+        mode = int(enable) if not isinstance(enable, bool) else (1 if enable else 0)
+        check(lib().dn_model_set_fused(self._h, mode))
 
     def profile(self, enable: bool = True, detail: bool = False) -> None:
         """Bracket every kernel launch with CUDA events (see profile_report);

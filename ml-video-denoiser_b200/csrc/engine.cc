@@ -301,6 +301,35 @@ void Engine::build(const HostWeights& hw) {
             b.f4 = pack_gemm(pk, hw.to_f32(pre + ".conv4.weight"), 2 * b.ffn, C, 2 * b.ffn, &b4, 2 * b.ffn);
             b.f5 = pack_gemm(pk, hw.to_f32(pre + ".conv5.weight"), C, b.ffn, C, &b5, C);
         }
+        if (b.fused && fused_a_tc_supported(C, b.dw)) {
+            // Phase A as one 3x3 conv of the normalised input:
+            // Weff[t][o][c] = dw[o][t] * W1[o][c] * gamma1[c] (fp16), packed per
+            // (tap, 16-channel K step) as a [2dw x 16] no-swizzle K-major tile;
+            // b1'[o] = b1[o] + sum_c beta1[c] W1[o][c] (the kernel forms the
+            // depthwise bias b_dw + b1' * sum of the in-image taps' dw).
+            const int N2 = 2 * b.dw, KS = C / 16;
+            const auto w1 = hw.to_f32(pre + ".conv1.weight");
+            const auto w2 = hw.to_f32(pre + ".conv2.weight");
+            const size_t tap_bytes = static_cast<size_t>(N2) * 32;
+            std::vector<uint8_t> wb(9 * KS * tap_bytes, 0);
+            std::vector<float> b1p(N2);
+            for (int o = 0; o < N2; ++o) {
+                double sb = 0.0;
+                for (int c = 0; c < C; ++c) sb += static_cast<double>(ln1b[c]) * w1[static_cast<size_t>(o) * C + c];
+                b1p[o] = b1[o] + static_cast<float>(sb);
+                for (int t = 0; t < 9; ++t)
+                    for (int c = 0; c < C; ++c) {
+                        const float v = w2[o * 9 + t] * w1[static_cast<size_t>(o) * C + c] * ln1w[c];
+                        const __half h = __float2half(v);
+                        const int ks = c / 16, k = c % 16;
+                        uint8_t* tile = wb.data() + (static_cast<size_t>(t) * KS + ks) * tap_bytes;
+                        std::memcpy(tile + kmajor_offset_host(o, k / 8, 256) + (k % 8) * 2, &h, 2);
+                    }
+            }
+            b.fa_w = pk.add(wb.data(), wb.size());
+            b.fa_b1 = pk.add_f32(b1p);
+            b.fa_tc = true;
+        }
         return b;
     };
 
@@ -472,6 +501,7 @@ void Engine::plan(const Shape& s) {
             dw_blocks_max_ = std::max(dw_blocks_max_, dw_blocks_per_img(h, w, b.dw));
             dw_blocks_max_ = std::max(dw_blocks_max_, dw_tile_blocks_per_img(h, w));
             if (b.fused) dw_blocks_max_ = std::max(dw_blocks_max_, fused_a_grid(b.C, b.dw, static_cast<int>(nimg), h, w));
+            if (b.fa_tc) dw_blocks_max_ = std::max(dw_blocks_max_, fused_a_tc_grid(b.C, static_cast<int>(nimg), h, w));
         }
     };
     for (int l = 0; l < L; ++l) {
@@ -677,11 +707,16 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
         fa.dw_b = wptr<float>(b.dw_b);
         fa.partials = partials_;
         fa.err = err_;
-        const int grid = fused_a_grid(b.C, b.dw, nimg, h, w);
+        const bool tc = b.fa_tc && fa_tc_enabled_;
+        if (tc) {
+            fa.weff = wptr<uint8_t>(b.fa_w);
+            fa.b1p = wptr<float>(b.fa_b1);
+        }
+        const int grid = tc ? fused_a_tc_grid(b.C, nimg, h, w) : fused_a_grid(b.C, b.dw, nimg, h, w);
         launches_ += 3;
         prof_begin("fused_block_a", static_cast<double>(nimg) * hw * (b.C + b.dw) * 2,
                    2.0 * nimg * hw * (b.C * 2 * b.dw + 2 * b.dw * 9), s);
-        DN_TRY(launch_fused_a(fa, b.C, b.dw, grid, s));
+        DN_TRY(tc ? launch_fused_a_tc(fa, b.C, b.dw, grid, s) : launch_fused_a(fa, b.C, b.dw, grid, s));
         prof_end(s);
         DwParams d{};
         d.N = nimg;

@@ -39,6 +39,9 @@ struct BlockW {
     // Fused two-pass kernels (shallow levels, C <= 64): single-tile B images.
     bool fused = false;
     GemmW f1, f3, f4, f5;          // conv1 (LN folded), conv3, conv4, conv5
+    // Tensor-core phase A: Weff B tiles and b1' = b1 + W1 beta1 (fp32 [2dw]).
+    bool fa_tc = false;
+    size_t fa_w = 0, fa_b1 = 0;
     // Single-kernel second pass (C = D = F = 128 / 256): conv4 with LN2 folded
     // as 128-row tiles [64 a rows | 64 b rows] per 64-channel gate chunk.
     bool deep = false;
@@ -90,8 +93,13 @@ public:
         profiling_ = mode != 0;
         prof_detail_ = mode == 2;
     }
-    // Use the fused two-pass NAFBlock kernels where they apply (default on).
-    void set_fused(bool on) { fused_enabled_ = on; }
+    // 1: fused NAFBlock kernels where they apply (default), with phase A of the
+    // 32/64-channel blocks on the tensor cores; 2: the same with phase A on the
+    // CUDA cores; 0: per-conv kernels everywhere.
+    void set_fused(int mode) {
+        fused_enabled_ = mode != 0;
+        fa_tc_enabled_ = mode != 2;
+    }
     // Synchronises, then returns a JSON object: kind -> {launches, ms, bytes, flops}
     // accumulated since the last report (which also resets the counters).
     std::string profile_report();
@@ -189,6 +197,7 @@ private:
     bool prof_detail_ = false;
     std::string prof_tag_;  // shape suffix of the next prof_begin in detail mode
     bool fused_enabled_ = true;
+    bool fa_tc_enabled_ = true;
     std::vector<ProfRec> prof_;
     std::vector<cudaEvent_t> prof_pool_;
     size_t prof_used_ = 0;

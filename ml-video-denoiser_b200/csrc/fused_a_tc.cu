@@ -1,0 +1,447 @@
+// Phase A of a shallow NAFBlock (C = 32 / 64) on the tensor cores.
+//
+// LayerNorm1 (normalisation only), conv1 (1x1, C -> 2D) and the depthwise
+// 3x3 conv (2D channels) compose into one linear map of the normalised input,
+// so they run as a single 3x3 implicit GEMM over the normalised rows:
+//   dw(u)[p, o] = bias_p[o] + sum_t sum_c Weff[t][o][c] * n[p + t, c],
+//   Weff[t][o][c] = dw[o][t] * W1[o][c] * gamma1[c],
+//   bias_p[o]    = b_dw[o] + b1'[o] * sum_{t: p + t inside the image} dw[o][t],
+//   b1'[o]       = b1[o] + sum_c beta1[c] * W1[o][c],
+// where n = (x - mean) * rstd is zero outside the image. The reference's
+// depthwise zero padding of u therefore only masks bias taps: the kernel
+// keeps the bias of each of the 16 tap-mask classes (interior, edges,
+// corners) and every pixel looks its class up.
+//
+// A CTA owns a contiguous run of output rows of 128-pixel strips:
+//   warp 0      producer: one input row (the strip's 128 pixels and the
+//               1-pixel halo, contiguous in NHWC) per ring slot by one bulk
+//               copy; rows outside the image are zeroed instead of loaded
+//               (a tensor map with 16-byte inner boxes, which would write the
+//               MMA layout directly, moves a row many times slower);
+//   warps 1-4   LayerNorm of each row (FP32 statistics from shifted sums,
+//               FP16 result, as the reference's normalised tensor), written
+//               back in place in the no-swizzle K-major layout [C/8][130][8];
+//   warp 5      MMA issuer: per output row y, 9 taps x C/16 K steps of
+//               M = 128 (the strip's pixels), N = 2D, K = 16, into a ring of
+//               TMEM accumulators. Tap (ky, kx) reads input row y + ky - 1
+//               from pixel kx on (a 16-byte shift of the start address), so
+//               each input row is normalised once and read by three output
+//               rows;
+//   warps 6-9   epilogue: bias, SimpleGate, g stored straight from
+//               registers (64 or 128 contiguous bytes per pixel), per-pixel
+//               pool sums reduced in a fixed order (deterministic).
+//
+// Replaces the reference's layer_norm_affine_kernel, conv1 and the grouped
+// conv2 cudnnConvolutionForward calls and simple_gate_kernel
+// (src/models/nafnet.cu:146-172, src/kernels/nafnet_kernels.cu:54-106) plus
+// the pool's partial sums.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+
+#include "fused_block.h"
+#include "launch.cuh"
+#include "sm100.cuh"
+#include "status.h"
+
+namespace dnb {
+namespace {
+
+constexpr int kTcThreads = 320;
+constexpr int kMaxImg = 8;
+
+template <int C>
+struct GeoT {
+    static constexpr int D = C;                // gated channels
+    static constexpr int N = 2 * C;            // conv outputs (both gate halves)
+    static constexpr int SW = 128;             // strip width = MMA M
+    static constexpr int HP = SW + 2;          // input pixels per row (halo)
+    static constexpr int KG = C / 8;           // 16-byte channel groups
+    static constexpr int KGB = HP * 16;        // bytes per channel group of a row (LBO)
+    static constexpr int ROWB = KG * KGB;      // one input-row slot
+    static constexpr int R = C >= 64 ? 4 : 8;  // input-row slots (a power of two)
+    static constexpr int KS = C / 16;          // K = 16 steps per tap
+    static constexpr int TAPB = N * 32;        // B tile of one (tap, K step)
+    static constexpr int WB = 9 * KS * TAPB;   // all of Weff
+    static constexpr int ACC = 512 / N;        // TMEM accumulator ring (all 512 columns)
+    static constexpr int TMEM_COLS = ACC * N;
+    // floats: bias per tap-mask class [16][N], pool sums [img][warp][D]
+    static constexpr int F_FLOATS = 16 * N + kMaxImg * 4 * D;
+    // At least half of the SM's shared memory: the CTA holds all of TMEM, so a
+    // second CTA on the same SM could only wait for it.
+    static constexpr int SMEM_USED = 1024 + R * ROWB + WB + F_FLOATS * 4;
+    static constexpr int SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
+    static_assert(ROWB % 128 == 0, "row slots stay 128-byte aligned");
+    static_assert(TMEM_COLS <= 512, "TMEM ring");
+    static_assert((R & (R - 1)) == 0 && (ACC & (ACC - 1)) == 0, "ring sizes are powers of two");
+};
+
+struct Seg {
+    int img, strip, ya, yb;
+};
+
+// The segment starting at unit u of [u, u1): units enumerate (image, strip,
+// output row) with rows fastest; a segment is the run of rows of one strip.
+__device__ __forceinline__ bool seg_at(long long u, long long u1, int H, int strips, Seg& s) {
+    if (u >= u1) return false;
+    const long long per_img = static_cast<long long>(strips) * H;
+    s.img = static_cast<int>(u / per_img);
+    const long long rem = u - static_cast<long long>(s.img) * per_img;
+    s.strip = static_cast<int>(rem / H);
+    s.ya = static_cast<int>(rem - static_cast<long long>(s.strip) * H);
+    s.yb = static_cast<int>(min(static_cast<long long>(H - 1), s.ya + (u1 - u) - 1));
+    return true;
+}
+
+template <int C>
+__global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_constant__ FusedAParams p) {
+    using G = GeoT<C>;
+    constexpr int D = G::D, N = G::N;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sRow = smem;                                 // R input-row slots
+    uint8_t* sW = sRow + G::R * G::ROWB;                  // Weff B tiles
+    // Bias of a pixel by the taps whose input lies outside the image: class
+    // bits 0/1 = left/right column invalid, bits 2/3 = top/bottom row invalid
+    // (class 0 = interior).
+    float* sBias = reinterpret_cast<float*>(sW + G::WB);  // [16][N]
+    float* sPool = sBias + 16 * N;                        // [img][epilogue warp][D]
+    __shared__ uint64_t full[G::R], ready[G::R], freeb[G::R], acc_full[G::ACC], acc_empty[G::ACC];
+    __shared__ uint64_t bar_w, bar_end;
+    __shared__ uint32_t tslot;
+    __shared__ volatile int s_abort;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int strips = (p.W + G::SW - 1) / G::SW;
+    const long long T = static_cast<long long>(p.N) * strips * p.H;
+    const long long u0 = T * blockIdx.x / gridDim.x, u1 = T * (blockIdx.x + 1) / gridDim.x;
+
+    pdl_trigger();
+    for (int i = tid; i < 16 * N; i += kTcThreads) {
+        const int cls = i / N, o = i - cls * N;
+        float sum = 0.f;
+#pragma unroll
+        for (int tp = 0; tp < 9; ++tp) {
+            const int ky = tp / 3, kx = tp % 3;
+            const bool off = (kx == 0 && (cls & 1)) || (kx == 2 && (cls & 2)) || (ky == 0 && (cls & 4)) ||
+                             (ky == 2 && (cls & 8));
+            if (!off) sum += p.dw_w[tp * N + o];
+        }
+        sBias[i] = fmaf(p.b1p[o], sum, p.dw_b[o]);
+    }
+    for (int i = tid; i < kMaxImg * 4 * D; i += kTcThreads) sPool[i] = 0.f;
+    if (warp == 0) {
+        tmem_alloc(&tslot, G::TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int s = 0; s < G::R; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&ready[s], 4);
+            mbar_init(&freeb[s], 1);
+        }
+        for (int a = 0; a < G::ACC; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 4);
+        }
+        mbar_init(&bar_w, 1);
+        mbar_init(&bar_end, 1);
+        s_abort = 0;
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar_w, G::WB);
+        bulk_g2s(sW, p.weff, G::WB, &bar_w);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    pdl_wait();  // x was written by the previous kernel; g and the partials are read by it
+
+    Seg sg;
+    if (warp == 0) {
+        // ------------------------------ producer -----------------------------
+        if (lane == 0) {
+            uint32_t e = 0;
+            for (long long u = u0; !s_abort && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+                const int x0 = sg.strip * G::SW;
+                for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
+                    const uint32_t s = e % G::R, ph = (e / G::R) & 1u;
+                    if (!wait_or_abort(&freeb[s], ph ^ 1u, &s_abort, p.err, 0x70)) break;
+                    if (r < 0 || r >= p.H) {
+                        mbar_arrive(&full[s]);  // zeroed by the LayerNorm warps
+                    } else {
+                        // The strip's input pixels [x0-1, x0+129) clipped to the
+                        // image are contiguous in NHWC: one bulk copy, landing
+                        // pixel-major at their slot positions.
+                        const int pa = max(0, x0 - 1), pb = min(p.W, x0 + G::SW + 1);
+                        const uint32_t bytes = static_cast<uint32_t>(pb - pa) * C * 2;
+                        mbar_arrive_expect_tx(&full[s], bytes);
+                        bulk_g2s(sRow + s * G::ROWB + (pa - (x0 - 1)) * C * 2,
+                                 p.x + ((static_cast<size_t>(sg.img) * p.H + r) * p.W + pa) * C, bytes, &full[s]);
+                    }
+                }
+            }
+            if (s_abort) {
+                // Let the copies already issued land before the CTA's memory is released.
+                for (uint32_t k = e > G::R ? e - G::R : 0; k < e; ++k)
+                    mbar_wait(&full[k % G::R], (k / G::R) & 1u, 5000000ull);
+            }
+        }
+    } else if (warp <= 4) {
+        // ------------------------------ LayerNorm ----------------------------
+        // A pixel's C/8 16-byte chunks sit in adjacent lanes (conflict-free
+        // reads of the pixel-major row); its statistics are shifted sums
+        // (shift = its first channel) reduced over those lanes. The normalised
+        // row stays in registers until all 128 threads have read the slot, then
+        // is written back in the MMA layout [C/8][130][8 ch].
+        constexpr int CPX = C / 8, PPR = 128 / CPX, NR = (G::HP + PPR - 1) / PPR;
+        const int t = tid - 32;
+        const int cq = t % CPX, pl = t / CPX;
+        const int lead = lane & ~(CPX - 1);
+        uint32_t e = 0;
+        bool ok = true;
+        for (long long u = u0; ok && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+            const int x0 = sg.strip * G::SW;
+            for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
+                const uint32_t s = e % G::R, ph = (e / G::R) & 1u;
+                // One decision for all four LayerNorm warps: they meet at the
+                // named barrier below, so none may leave the loop alone.
+                const bool got = wait_or_abort(&full[s], ph, &s_abort, p.err, 0x71);
+                if (named_sync_or(1, 128, !got)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* row = sRow + s * G::ROWB;
+                const bool row_in = r >= 0 && r < p.H;
+                uint4 nv[NR];
+#pragma unroll
+                for (int k = 0; k < NR; ++k) {
+                    const int i = k * PPR + pl;
+                    const int xin = x0 - 1 + i;
+                    const bool valid = row_in && i < G::HP && xin >= 0 && xin < p.W;
+                    const uint4 v = valid ? *reinterpret_cast<const uint4*>(row + i * C * 2 + cq * 16)
+                                          : make_uint4(0u, 0u, 0u, 0u);
+                    const float xs = __shfl_sync(0xffffffffu, unpack_half2(v.x).x, lead);
+                    const float2 nx = make_float2(-xs, -xs), one = make_float2(1.f, 1.f);
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                    float2 a1 = make_float2(0.f, 0.f), a2 = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 d = ffma2(unpack_half2(w[j]), one, nx);
+                        a1 = ffma2(d, one, a1);
+                        a2 = ffma2(d, d, a2);
+                    }
+                    float s1 = a1.x + a1.y, s2 = a2.x + a2.y;
+#pragma unroll
+                    for (int m = 1; m < CPX; m <<= 1) {
+                        s1 += __shfl_xor_sync(0xffffffffu, s1, m);
+                        s2 += __shfl_xor_sync(0xffffffffu, s2, m);
+                    }
+                    const float dm = s1 * (1.0f / C);
+                    const float var = fmaxf(s2 * (1.0f / C) - dm * dm, 0.f);
+                    const float rstd = rsqrtf(var + 1e-6f);
+                    const float2 rs2 = make_float2(rstd, rstd);
+                    const float2 sh2 = make_float2(-(xs + dm) * rstd, -(xs + dm) * rstd);
+                    uint32_t o[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 y = ffma2(unpack_half2(w[j]), rs2, sh2);
+                        o[j] = pack_half2(y.x, y.y);
+                    }
+                    nv[k] = valid ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0u, 0u, 0u, 0u);
+                }
+                named_sync(1, 128);  // every thread has read the pixel-major row
+#pragma unroll
+                for (int k = 0; k < NR; ++k) {
+                    const int i = k * PPR + pl;
+                    if (i < G::HP) *reinterpret_cast<uint4*>(row + cq * G::KGB + i * 16) = nv[k];
+                }
+                fence_async_smem();  // the tensor core reads the row (async proxy)
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ready[s]);
+            }
+        }
+    } else if (warp == 5) {
+        // ------------------------------ MMA issuer ---------------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(128, N);
+            const uint64_t da = sdesc_kmajor(smem_u32(sRow), G::KGB, 128);
+            const uint64_t db = sdesc_kmajor(smem_u32(sW), 128, 256);
+            bool ok = wait_or_abort(&bar_w, 0, &s_abort, p.err, 0x72);
+            uint32_t eb = 0, rr = 0, waited = 0;  // entries < waited are known to be ready
+            for (long long u = u0; ok && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+                for (int y = sg.ya; y <= sg.yb; ++y, ++rr) {
+                    const uint32_t e0 = eb + static_cast<uint32_t>(y - sg.ya);
+                    const uint32_t sl[3] = {e0 & (G::R - 1), (e0 + 1) & (G::R - 1), (e0 + 2) & (G::R - 1)};
+                    // Rows y-1 and y were waited for by the previous output row
+                    // of the segment: only new entries cost a barrier wait.
+                    for (uint32_t e = max(waited, e0); ok && e < e0 + 3; ++e)
+                        if (!wait_or_abort(&ready[e & (G::R - 1)], (e / G::R) & 1u, &s_abort, p.err, 0x73)) ok = false;
+                    waited = e0 + 3;
+                    const uint32_t a = rr & (G::ACC - 1);
+                    if (ok && !wait_or_abort(&acc_empty[a], ((rr / G::ACC) & 1u) ^ 1u, &s_abort, p.err, 0x74))
+                        ok = false;
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t acc = tmem + a * N;
+#pragma unroll
+                    for (int ky = 0; ky < 3; ++ky) {
+                        const uint64_t ar = desc_add(da, sl[ky] * G::ROWB);
+#pragma unroll
+                        for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                            for (int ks = 0; ks < G::KS; ++ks)
+                                mma_f16(acc, desc_add(ar, ks * 2 * G::KGB + kx * 16),
+                                        desc_add(db, ((ky * 3 + kx) * G::KS + ks) * G::TAPB), idesc,
+                                        (ky | kx | ks) ? 1u : 0u);
+                    }
+                    mma_commit(&acc_full[a]);
+                    mma_commit(&freeb[sl[0]]);  // last use of input row y - 1
+                    if (y == sg.yb) {           // the strip segment ends: rows y and y + 1 too
+                        mma_commit(&freeb[sl[1]]);
+                        mma_commit(&freeb[sl[2]]);
+                    }
+                }
+                eb += static_cast<uint32_t>(sg.yb - sg.ya + 3);
+            }
+            mma_commit(&bar_end);  // every MMA has completed before TMEM is released
+            mbar_wait(&bar_end, 0, 5000000ull);
+        }
+    } else {
+        // ------------------------------ epilogue -----------------------------
+        const int q = warp & 3;  // TMEM lane quarter = pixels 32q .. 32q+31 of the strip
+        const int px = q * 32 + lane;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        float ps[D];
+#pragma unroll
+        for (int c = 0; c < D; ++c) ps[c] = 0.f;
+        // Pool sums of this warp's pixels -> sPool[img][q][:] (fixed order).
+        auto flush = [&](int img) {
+#pragma unroll
+            for (int c = 0; c < D; ++c) {
+                float v = ps[c];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                if (lane == 0) sPool[(img * 4 + q) * D + c] += v;
+                ps[c] = 0.f;
+            }
+        };
+        uint32_t rr = 0;
+        int cur = -1;
+        bool ok = true;
+        for (long long u = u0; ok && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+            if (cur >= 0 && sg.img != cur) flush(cur);
+            cur = sg.img;
+            const int xg = sg.strip * G::SW + px;
+            const bool col_ok = xg < p.W;
+            for (int y = sg.ya; y <= sg.yb; ++y, ++rr) {
+                const uint32_t a = rr & (G::ACC - 1);
+                ok = __all_sync(0xffffffffu,
+                                wait_or_abort(&acc_full[a], (rr / G::ACC) & 1u, &s_abort, p.err, 0x75));
+                if (!ok) break;
+                tc_fence_after();
+                // Tap mask of the bias: taps whose input pixel lies outside
+                // the image contribute no conv1 bias (the DW zero padding).
+                const int cls = (xg == 0 ? 1 : 0) | (xg == p.W - 1 ? 2 : 0) | (y == 0 ? 4 : 0) | (y == p.H - 1 ? 8 : 0);
+                const float* bias_c = sBias + cls * N;
+                __half* dst = p.g + ((static_cast<size_t>(sg.img) * p.H + y) * p.W + xg) * D;
+                // 32 gate channels per pass: both halves' accumulator columns
+                // (tcgen05.ld is warp-collective: every lane loads).
+#pragma unroll
+                for (int cc = 0; cc < D; cc += 32) {
+                    float va[32], vb[32];
+                    tmem_ld16(lane_base + a * N + cc, *reinterpret_cast<float(*)[16]>(va));
+                    tmem_ld16(lane_base + a * N + cc + 16, *reinterpret_cast<float(*)[16]>(va + 16));
+                    tmem_ld16(lane_base + a * N + D + cc, *reinterpret_cast<float(*)[16]>(vb));
+                    tmem_ld16(lane_base + a * N + D + cc + 16, *reinterpret_cast<float(*)[16]>(vb + 16));
+                    tmem_ld_wait();
+                    if (cc + 32 >= D) {  // the accumulator is drained
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[a]);
+                    }
+                    if (!col_ok) continue;
+#pragma unroll
+                    for (int c8 = 0; c8 < 32; c8 += 8) {
+                        const int c = cc + c8;
+                        float bias[16];
+#pragma unroll
+                        for (int i = 0; i < 8; i += 4) {
+                            const float4 ba = *reinterpret_cast<const float4*>(bias_c + c + i);
+                            const float4 bb = *reinterpret_cast<const float4*>(bias_c + D + c + i);
+                            bias[i] = ba.x;
+                            bias[i + 1] = ba.y;
+                            bias[i + 2] = ba.z;
+                            bias[i + 3] = ba.w;
+                            bias[8 + i] = bb.x;
+                            bias[8 + i + 1] = bb.y;
+                            bias[8 + i + 2] = bb.z;
+                            bias[8 + i + 3] = bb.w;
+                        }
+                        float gv[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) gv[i] = (va[c8 + i] + bias[i]) * (vb[c8 + i] + bias[8 + i]);
+                        const uint4 h = f_to_h8(gv);
+                        *reinterpret_cast<uint4*>(dst + c) = h;
+                        float hf[8];
+                        h8_to_f(h, hf);  // pool the stored fp16 values
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ps[c + i] += hf[i];
+                    }
+                }
+            }
+        }
+        if (cur >= 0) flush(cur);
+    }
+
+    __syncthreads();
+    for (int i = tid; i < p.N * D; i += kTcThreads) {
+        const int n = i / D, c = i - n * D;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) s += sPool[(n * 4 + w) * D + c];
+        p.partials[(static_cast<size_t>(n) * gridDim.x + blockIdx.x) * D + c] = s;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, G::TMEM_COLS);
+}
+
+template <int C>
+int run_a_tc(const FusedAParams& p, int grid, cudaStream_t s) {
+    using G = GeoT<C>;
+    auto kern = fused_a_tc_kernel<C>;
+    static bool cfg = false;
+    if (!cfg) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "fused_a_tc: smem attribute");
+        cfg = true;
+    }
+    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kTcThreads), G::SMEM, s, p);
+    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "fused_a_tc: launch");
+}
+
+}  // namespace
+
+bool fused_a_tc_supported(int C, int D) { return (C == 32 || C == 64) && D == C; }
+
+int fused_a_tc_grid(int C, int N, int H, int W) {
+    (void)C;
+    const long long units = static_cast<long long>(N) * ((W + 127) / 128) * H;
+    return static_cast<int>(std::max(1LL, std::min<long long>(units, sm_count())));
+}
+
+int launch_fused_a_tc(const FusedAParams& p, int C, int D, int grid, cudaStream_t s) {
+    if (p.N > kMaxImg) return dn_fail(DN_ERR_UNSUPPORTED, "fused_a_tc: batch > 8");
+    if (!p.weff || !p.b1p) return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: missing packed weights");
+    if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.g) & 15))
+        return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: x and g must be 16-byte aligned");
+    if (C == 32 && D == 32) return run_a_tc<32>(p, grid, s);
+    if (C == 64 && D == 64) return run_a_tc<64>(p, grid, s);
+    return dn_fail(DN_ERR_UNSUPPORTED, "fused_a_tc: channel configuration");
+}
+
+}  // namespace dnb

@@ -22,6 +22,9 @@ struct FusedAParams {
     const float* dw_b;      // [2D]
     float* partials;        // [N][grid][D] pool partial sums
     uint32_t* err;
+    // Tensor-core form (fused_a_tc.cu): LN + conv1 + depthwise as one 3x3 conv.
+    const uint8_t* weff;    // [9 taps][C/16 K steps] B tiles of Weff = dw * W1 * gamma1 (2D x 16 each)
+    const float* b1p;       // [2D] b1 + W1 beta1
 };
 
 struct FusedBParams {
@@ -38,6 +41,9 @@ struct FusedBParams {
 };
 
 bool fused_supported(int C, int D, int F);
+bool fused_a_tc_supported(int C, int D);
+int fused_a_tc_grid(int C, int N, int H, int W);
+int launch_fused_a_tc(const FusedAParams& p, int C, int D, int grid, cudaStream_t s);
 int fused_a_grid(int C, int D, int N, int H, int W);
 int launch_fused_a(const FusedAParams& p, int C, int D, int grid, cudaStream_t s);
 int launch_fused_b(const FusedBParams& p, int C, int D, int F, cudaStream_t s);

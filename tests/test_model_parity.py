@@ -82,6 +82,28 @@ def test_w32_single_image_deep_second_pass(pkg, tmp_path):
     assert float((y_fused.float() - y_ref.float()).abs().max()) <= 2e-3
 
 
+@pytest.mark.parametrize("hw,batch", [((100, 150), 2), ((37, 290), 1)], ids=["100x150_b2", "37x290"])
+def test_w32_phase_a_paths_agree(pkg, tmp_path, hw, batch):
+    """The first pass of the 32/64-channel blocks as one tensor-core 3x3 conv
+    of the normalised input (default) and on the CUDA cores (LN, conv1 MMA,
+    depthwise taps) both meet the oracle bar and agree within 2e-3. The sizes
+    leave partial 128-pixel strips (padded widths 160/80 and 304/152), short
+    strips, border pixels on every side and two images per launch."""
+    synth = synth_mod(pkg)
+    h, w = hw
+    x = np.concatenate([synth.w32_frame(h, w, seed=11 + i) for i in range(batch)])
+    x = x.astype(np.float16).astype(np.float32)
+    (err, psnr), m = _oracle_case(pkg, tmp_path, synth.CONFIG_W32, 3, x, 1)
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, ("tensor-core phase A", err, psnr)
+    xt = torch.from_numpy(x).half().cuda()
+    y_tc = m(xt).clone()
+    m.set_fused(2)
+    y_cc = m(xt)
+    m.sync()
+    diff = float((y_tc.float() - y_cc.float()).abs().max())
+    assert diff <= 2e-3, diff
+
+
 def test_w32_1080p(pkg, tmp_path):
     """NAFNet-w32 on one 1080p Poisson-Gaussian frame (the benchmark workload)."""
     synth = synth_mod(pkg)
