@@ -304,7 +304,8 @@ void Engine::build(const HostWeights& hw) {
         if (b.fused && fused_a_tc_supported(C, b.dw)) {
             // Phase A as one 3x3 conv of the normalised input:
             // Weff[t][o][c] = dw[o][t] * W1[o][c] * gamma1[c] (fp16), packed per
-            // (tap, 16-channel K step) as a [2dw x 16] no-swizzle K-major tile;
+            // (tap column kx, 16-channel K step) as three stacked [2dw x 16]
+            // no-swizzle K-major tiles, taps ky = 2, 1, 0;
             // b1'[o] = b1[o] + sum_c beta1[c] W1[o][c] (the kernel forms the
             // depthwise bias b_dw + b1' * sum of the in-image taps' dw).
             const int N2 = 2 * b.dw, KS = C / 16;
@@ -321,8 +322,9 @@ void Engine::build(const HostWeights& hw) {
                     for (int c = 0; c < C; ++c) {
                         const float v = w2[o * 9 + t] * w1[static_cast<size_t>(o) * C + c] * ln1w[c];
                         const __half h = __float2half(v);
-                        const int ks = c / 16, k = c % 16;
-                        uint8_t* tile = wb.data() + (static_cast<size_t>(t) * KS + ks) * tap_bytes;
+                        const int ks = c / 16, k = c % 16, ky = t / 3, kx = t % 3;
+                        // (kx, K step) tiles of three stacked taps [ky=2 | ky=1 | ky=0]
+                        uint8_t* tile = wb.data() + ((static_cast<size_t>(kx) * KS + ks) * 3 + (2 - ky)) * tap_bytes;
                         std::memcpy(tile + kmajor_offset_host(o, k / 8, 256) + (k % 8) * 2, &h, 2);
                     }
             }
@@ -727,6 +729,17 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
         d.sca_w = wptr<float>(b.sca_w);
         d.sca_b = wptr<float>(b.sca_b);
         d.s_out = sca_s_;
+        // Single image: the SCA kernel writes conv3's B with the scale folded
+        // in, and pass B skips its per-tile scaling of g.
+        const bool fold_sca = nimg == 1 && b3s_ != nullptr;
+        if (fold_sca) {
+            d.bsrc = wptr<uint8_t>(b.f3.bpack);
+            d.bdst = b3s_;
+            d.b_rows = b.C;
+            d.b_nt = b.f3.NT;
+            d.b_kc = b.f3.KC;
+            d.b_kchunks = b.f3.k_chunks;
+        }
         prof_begin("sca", 4.0 * nimg * grid * b.dw, 2.0 * nimg * b.dw * b.dw, s);
         DN_TRY(launch_sca(d, grid, s));
         prof_end(s);
@@ -737,8 +750,8 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
         fb.out = x;
         fb.M = static_cast<int>(nimg * hw);
         fb.hw = static_cast<int>(hw);
-        fb.s = sca_s_;
-        fb.w3 = wptr<uint8_t>(b.f3.bpack);
+        fb.s = fold_sca ? nullptr : sca_s_;
+        fb.w3 = fold_sca ? b3s_ : wptr<uint8_t>(b.f3.bpack);
         fb.w4 = wptr<uint8_t>(b.f4.bpack);
         fb.w5 = wptr<uint8_t>(b.f5.bpack);
         fb.b3 = wptr<float>(b.f3.bias);

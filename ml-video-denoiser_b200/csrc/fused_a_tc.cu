@@ -21,12 +21,15 @@
 //   warps 1-4   LayerNorm of each row (FP32 statistics from shifted sums,
 //               FP16 result, as the reference's normalised tensor), written
 //               back in place in the no-swizzle K-major layout [C/8][130][8];
-//   warp 5      MMA issuer: per output row y, 9 taps x C/16 K steps of
-//               M = 128 (the strip's pixels), N = 2D, K = 16, into a ring of
-//               TMEM accumulators. Tap (ky, kx) reads input row y + ky - 1
-//               from pixel kx on (a 16-byte shift of the start address), so
-//               each input row is normalised once and read by three output
-//               rows;
+//   warp 5      MMA issuer, into a ring of TMEM accumulators (M = 128, the
+//               strip's pixels; K = 16). At 32 channels, per input row r, 3
+//               tap columns x C/16 K steps of N = 3 x 2D: the row's
+//               contributions to output rows r-1, r, r+1 (taps ky = 2, 1, 0)
+//               in one MMA. At 64 channels (N = 128 MMAs already run at the
+//               tensor core's rate), per output row, 9 taps x C/16 K steps of
+//               N = 2D. Tap column kx reads an input row from pixel kx on (a
+//               16-byte shift of the start address), so each input row is
+//               normalised once;
 //   warps 6-9   epilogue: bias, SimpleGate, g stored straight from
 //               registers (64 or 128 contiguous bytes per pixel), per-pixel
 //               pool sums reduced in a fixed order (deterministic).
@@ -64,7 +67,7 @@ struct GeoT {
     static constexpr int ROWB = KG * KGB;      // one input-row slot
     static constexpr int R = C >= 64 ? 4 : 8;  // input-row slots (a power of two)
     static constexpr int KS = C / 16;          // K = 16 steps per tap
-    static constexpr int TAPB = N * 32;        // B tile of one (tap, K step)
+    static constexpr int TAPB = N * 32;        // B tile of one (tap, K step): 2D rows x 16
     static constexpr int WB = 9 * KS * TAPB;   // all of Weff
     static constexpr int ACC = 512 / N;        // TMEM accumulator ring (all 512 columns)
     static constexpr int TMEM_COLS = ACC * N;
@@ -94,6 +97,49 @@ __device__ __forceinline__ bool seg_at(long long u, long long u1, int H, int str
     s.ya = static_cast<int>(rem - static_cast<long long>(s.strip) * H);
     s.yb = static_cast<int>(min(static_cast<long long>(H - 1), s.ya + (u1 - u) - 1));
     return true;
+}
+
+// MMAs of one input row whose three output rows all belong to the strip
+// segment (every row but the segment's first and last), with everything but
+// the base addresses known at compile time: the issuing thread is on the
+// kernel's critical path, and runtime operand arithmetic per MMA costs several
+// times an N=64 MMA. tq[q] = TMEM address of output row r-1+q; PAT gives the
+// MMA ranges of positions, split where the slots wrap around the ring:
+// 0 = [0,3), 1 = [0,2)[2,3), 2 = [0,1)[1,3). The row's first (kx, K step)
+// writes position 2 (the first contribution to output row r+1) with
+// accumulate off.
+template <int C, int PAT>
+__device__ __forceinline__ void issue_steady_row(const uint32_t (&tq)[3], uint64_t ar, uint64_t db) {
+    using G = GeoT<C>;
+    constexpr int N = G::N;
+    static_assert(PAT != 0 || 3 * N <= 256, "three positions fit one MMA only at N <= 85");
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+        for (int ks = 0; ks < G::KS; ++ks) {
+            const bool first = kx == 0 && ks == 0;
+            const uint64_t a = desc_add(ar, ks * 2 * G::KGB + kx * 16);
+            const uint64_t b = desc_add(db, (kx * G::KS + ks) * 3 * G::TAPB);
+            if (PAT == 0) {
+                if (first) {
+                    mma_f16(tq[0], a, b, idesc_f16_f32(128, 2 * N), 1u);
+                    mma_f16(tq[2], a, desc_add(b, 2 * G::TAPB), idesc_f16_f32(128, N), 0u);
+                } else {
+                    mma_f16(tq[0], a, b, idesc_f16_f32(128, 3 * N), 1u);
+                }
+            } else if (PAT == 1) {
+                mma_f16(tq[0], a, b, idesc_f16_f32(128, 2 * N), 1u);
+                mma_f16(tq[2], a, desc_add(b, 2 * G::TAPB), idesc_f16_f32(128, N), first ? 0u : 1u);
+            } else {
+                mma_f16(tq[0], a, b, idesc_f16_f32(128, N), 1u);
+                if (first) {
+                    mma_f16(tq[1], a, desc_add(b, G::TAPB), idesc_f16_f32(128, N), 1u);
+                    mma_f16(tq[2], a, desc_add(b, 2 * G::TAPB), idesc_f16_f32(128, N), 0u);
+                } else {
+                    mma_f16(tq[1], a, desc_add(b, G::TAPB), idesc_f16_f32(128, 2 * N), 1u);
+                }
+            }
+        }
 }
 
 template <int C>
@@ -265,7 +311,98 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
             }
         }
     } else if (warp == 5) {
+      if constexpr (3 * N <= 256) {
         // ------------------------------ MMA issuer ---------------------------
+        // Input row r feeds output rows r-1, r, r+1 (taps ky = 2, 1, 0). The B
+        // tile of (kx, K step) stacks [W(ky=2) | W(ky=1) | W(ky=0)] along N, so
+        // one MMA over positions q = 0..2 adds the row into the three output
+        // rows' accumulators, which sit in consecutive TMEM slots (the output
+        // row of running index j in slot j mod ACC). An MMA is split where the
+        // slots wrap around the ring, where N would pass 256, and, for the
+        // row's first (kx, K step), before position 2: that is the first
+        // contribution to output row r+1 (accumulate off), so no slot needs
+        // zeroing. Output row r-1 is complete once row r has been issued.
+        if (lane == 0) {
+            constexpr int MAXQ = 256 / N < 3 ? 256 / N : 3;  // positions per MMA
+            const uint64_t da = sdesc_kmajor(smem_u32(sRow), G::KGB, 128);
+            const uint64_t db = sdesc_kmajor(smem_u32(sW), 128, 256);
+            bool ok = wait_or_abort(&bar_w, 0, &s_abort, p.err, 0x72);
+            uint32_t e = 0, rb = 0;  // entry counter; running index of the segment's first output row
+            for (long long u = u0; ok && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+                for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
+                    const uint32_t s_in = e & (G::R - 1);
+                    if (!wait_or_abort(&ready[s_in], (e / G::R) & 1u, &s_abort, p.err, 0x73)) {
+                        ok = false;
+                        break;
+                    }
+                    // Positions whose output row r - 1 + q lies in [ya, yb].
+                    const int qlo = max(0, sg.ya - (r - 1)), qhi = min(3, sg.yb - (r - 1) + 1);
+                    const int j0 = static_cast<int>(rb) + (r - 1 - sg.ya);  // running index at q = 0
+                    if (qhi == 3) {  // output row r + 1 starts: its slot must be drained
+                        const uint32_t j2 = static_cast<uint32_t>(j0 + 2);
+                        if (!wait_or_abort(&acc_empty[j2 & (G::ACC - 1)], ((j2 / G::ACC) & 1u) ^ 1u, &s_abort, p.err,
+                                           0x74)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    tc_fence_after();
+                    const uint64_t ar = desc_add(da, s_in * G::ROWB);
+                    if (qlo == 0 && qhi == 3) {
+                        uint32_t tq[3];
+#pragma unroll
+                        for (int q = 0; q < 3; ++q) tq[q] = tmem + (static_cast<uint32_t>(j0 + q) & (G::ACC - 1)) * N;
+                        const uint32_t p0 = static_cast<uint32_t>(j0) & (G::ACC - 1);
+                        if (p0 == G::ACC - 1) {
+                            issue_steady_row<C, 2>(tq, ar, db);
+                        } else if (3 * N > 256 || p0 == G::ACC - 2) {
+                            issue_steady_row<C, 1>(tq, ar, db);
+                        } else {
+                            issue_steady_row<C, (3 * N <= 256 ? 0 : 1)>(tq, ar, db);
+                        }
+                    } else {
+                        // Segment edges: the general split, ranges [cut[i], cut[i+1]).
+                        int cut[4], nc = 0;
+                        cut[nc++] = qlo;
+                        for (int q = qlo + 1; q < qhi; ++q)
+                            if ((static_cast<uint32_t>(j0 + q) & (G::ACC - 1)) == 0 || q - cut[nc - 1] >= MAXQ)
+                                cut[nc++] = q;
+                        cut[nc] = qhi;
+                        for (int kx = 0; kx < 3; ++kx)
+                            for (int ks = 0; ks < G::KS; ++ks) {
+                                const bool first = kx == 0 && ks == 0;
+                                const uint64_t a = desc_add(ar, ks * 2 * G::KGB + kx * 16);
+                                const uint64_t b0 = desc_add(db, (kx * G::KS + ks) * 3 * G::TAPB);
+                                auto issue = [&](int qa, int qb, uint32_t acc_on) {
+                                    const uint32_t slot = static_cast<uint32_t>(j0 + qa) & (G::ACC - 1);
+                                    mma_f16(tmem + slot * N, a, desc_add(b0, qa * G::TAPB),
+                                            idesc_f16_f32(128, (qb - qa) * N), acc_on);
+                                };
+                                for (int i = 0; i < nc; ++i) {
+                                    const int qa = cut[i], qb = cut[i + 1];
+                                    if (first && qa < 2 && qb > 2) {
+                                        issue(qa, 2, 1u);
+                                        issue(2, qb, 0u);
+                                    } else {
+                                        issue(qa, qb, (first && qa == 2) ? 0u : 1u);
+                                    }
+                                }
+                            }
+                    }
+                    if (qlo == 0) mma_commit(&acc_full[static_cast<uint32_t>(j0) & (G::ACC - 1)]);
+                    mma_commit(&freeb[s_in]);  // the row's only reader is done
+                }
+                rb += static_cast<uint32_t>(sg.yb - sg.ya + 1);
+            }
+            mma_commit(&bar_end);  // every MMA has completed before TMEM is released
+            mbar_wait(&bar_end, 0, 5000000ull);
+        }
+      } else {
+        // ------------------------------ MMA issuer ---------------------------
+        // One output row at a time (64 channels: N = 128 MMAs already run at
+        // the tensor core's rate, so the stacked form above gains nothing):
+        // 9 taps x C/16 K steps into the row's accumulator; the B tile of tap
+        // (ky, kx) sits at position 2 - ky of the stacked (kx, K step) tile.
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_f32(128, N);
             const uint64_t da = sdesc_kmajor(smem_u32(sRow), G::KGB, 128);
@@ -295,7 +432,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
 #pragma unroll
                             for (int ks = 0; ks < G::KS; ++ks)
                                 mma_f16(acc, desc_add(ar, ks * 2 * G::KGB + kx * 16),
-                                        desc_add(db, ((ky * 3 + kx) * G::KS + ks) * G::TAPB), idesc,
+                                        desc_add(db, ((kx * G::KS + ks) * 3 + (2 - ky)) * G::TAPB), idesc,
                                         (ky | kx | ks) ? 1u : 0u);
                     }
                     mma_commit(&acc_full[a]);
@@ -310,6 +447,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
             mma_commit(&bar_end);  // every MMA has completed before TMEM is released
             mbar_wait(&bar_end, 0, 5000000ull);
         }
+      }
     } else {
         // ------------------------------ epilogue -----------------------------
         const int q = warp & 3;  // TMEM lane quarter = pixels 32q .. 32q+31 of the strip

@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
         s_fail = 0;
         fence_mbar_init();
         mbar_arrive_expect_tx(&bar_w, G::W3_BYTES + G::W4_BYTES + G::W5_BYTES);
-        bulk_g2s(sW3, p.w3, G::W3_BYTES, &bar_w);
+        if (p.s) bulk_g2s(sW3, p.w3, G::W3_BYTES, &bar_w);  // else written by the SCA kernel: after the wait
         bulk_g2s(sW4, p.w4, G::W4_BYTES, &bar_w);
         bulk_g2s(sW5, p.w5, G::W5_BYTES, &bar_w);
     }
@@ -455,8 +455,12 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
     const uint64_t d3a = sdesc_kmajor_sw(smem_u32(sG), 2 * D), d3b = sdesc_kmajor(smem_u32(sW3), 128, (D / 8) * 128);
     const uint64_t d4a = sdesc_kmajor_sw(smem_u32(sA2), 2 * C), d4b = sdesc_kmajor(smem_u32(sW4), 128, (C / 8) * 128);
     const uint64_t d5a = sdesc_kmajor_sw(smem_u32(sA3), 2 * F), d5b = sdesc_kmajor(smem_u32(sW5), 128, (F / 8) * 128);
-    pdl_wait();  // g, x and the SCA scale come from earlier kernels
-    for (int i = tid; i < nimg * D; i += kTh) sS[i] = p.s[i];
+    pdl_wait();  // g, x and the SCA scale (or the SCA-scaled w3) come from earlier kernels
+    if (p.s) {
+        for (int i = tid; i < nimg * D; i += kTh) sS[i] = p.s[i];
+    } else if (tid == 0) {
+        bulk_g2s(sW3, p.w3, G::W3_BYTES, &bar_w);
+    }
     if (tid == 0 && blockIdx.x < tiles) {
         mbar_arrive_expect_tx(&bar_ld, G::G_BYTES + G::X_BYTES);
         tma_load_2d(sG, &mg, 0, blockIdx.x * 128, &bar_ld);
@@ -479,8 +483,9 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
         if (!wait_bar(&bar_ld, it & 1, p.err, 0x41)) s_fail = 1;
         __syncthreads();
         if (s_fail) break;
-        // SCA: g *= s in place (this thread's half of the row).
-        {
+        // SCA: g *= s in place (this thread's half of the row), unless the
+        // scale is folded into w3.
+        if (p.s) {
             const float* sc = sS + img * D;
 #pragma unroll
             for (int q = hf * (DC / 8); q < (hf + 1) * (DC / 8); ++q) {

@@ -23,7 +23,7 @@ struct FusedAParams {
     float* partials;        // [N][grid][D] pool partial sums
     uint32_t* err;
     // Tensor-core form (fused_a_tc.cu): LN + conv1 + depthwise as one 3x3 conv.
-    const uint8_t* weff;    // [9 taps][C/16 K steps] B tiles of Weff = dw * W1 * gamma1 (2D x 16 each)
+    const uint8_t* weff;    // [3 kx][C/16 K steps][ky = 2, 1, 0] B tiles of Weff = dw * W1 * gamma1 (2D x 16 each)
     const float* b1p;       // [2D] b1 + W1 beta1
 };
 
@@ -32,7 +32,7 @@ struct FusedBParams {
     const __half* x;        // [M, C] block input (residual)
     __half* out;            // [M, C]
     int M, hw;
-    const float* s;         // SCA scale [N][D]
+    const float* s;         // SCA scale [N][D]; nullptr: already folded into w3 by the SCA kernel
     const uint8_t* w3;      // [C x D] tile image
     const uint8_t* w4;      // [2F x C] tile image (gate halves in order)
     const uint8_t* w5;      // [C x F] tile image
