@@ -126,6 +126,23 @@ int dn_model_forward(dn_model* model, const void* x, const int64_t* shape, int n
 int dn_model_forward_host(dn_model* model, const void* x_host, const int64_t* shape, int ndim,
                           void* y_host, void* stream);
 
+/* Pipelined form of dn_model_forward_host for frame streams (no reference
+ * counterpart): enqueues the input copy, the forward and the output copy
+ * and returns without waiting. The forward runs on `stream` after the work
+ * already queued there; the copies run on two streams of the model, so the
+ * input copy of the next call and the output copy of the previous call
+ * overlap this call's forward (two staging buffer pairs on the device). The
+ * host buffers must stay untouched until the call has completed, and y_host
+ * holds the result only after dn_model_host_join(model, s) followed by a
+ * synchronisation of `s` (dn_model_sync). Pinned host buffers are needed for
+ * the copies to overlap anything. Calls for one model must come from one
+ * host thread and use one stream. */
+int dn_model_forward_host_async(dn_model* model, const void* x_host, const int64_t* shape, int ndim,
+                                void* y_host, void* stream);
+/* Makes `stream` wait for the output copies of every dn_model_forward_host_async
+ * call issued so far (asynchronous; no host wait). */
+int dn_model_host_join(dn_model* model, void* stream);
+
 /* Temporal models over a frame sequence with a frame cache (no reference
  * counterpart: the reference CLI rebuilds and re-encodes a T-frame clip for
  * every output frame, cli/main.cc:260-267). The model keeps the encoder

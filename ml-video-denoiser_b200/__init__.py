@@ -83,6 +83,8 @@ SIGNATURES = {
     "dn_model_destroy": (_I, [_P]),
     "dn_model_get_info": (_I, [_P, _c.POINTER(ModelInfo)]),
     "dn_model_forward": (_I, [_P, _P, _I64P, _I, _P, _P]),
+    "dn_model_forward_host_async": (_I, [_P, _P, _I64P, _I, _P, _P]),
+    "dn_model_host_join": (_I, [_P, _P]),
     "dn_model_forward_host": (_I, [_P, _P, _I64P, _I, _P, _P]),
     "dn_model_encode_frame": (_I, [_P, _P, _I, _I, _I, _I, _P]),
     "dn_model_decode_window": (_I, [_P, _IP, _I, _P, _I, _I, _I, _P, _P]),
@@ -294,6 +296,18 @@ class Model:
         sh = (ctypes.c_int64 * len(shape))(*shape)
         check(lib().dn_model_forward_host(self._h, ctypes.c_void_p(x_ptr), sh, len(shape),
                                           ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream_ptr)))
+
+    def forward_host_async_ptr(self, x_ptr: int, shape, y_ptr: int, stream_ptr: int = 0) -> None:
+        """Pipelined host-buffer forward (returns at once; the input copy of the
+        next call and the output copy of the previous one overlap this forward).
+        The result is in y after host_join(stream) and a synchronisation of it."""
+        sh = (ctypes.c_int64 * len(shape))(*shape)
+        check(lib().dn_model_forward_host_async(self._h, ctypes.c_void_p(x_ptr), sh, len(shape),
+                                                ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream_ptr)))
+
+    def host_join(self, stream_ptr: int = 0) -> None:
+        """Make the stream wait for the output copies of every queued async call."""
+        check(lib().dn_model_host_join(self._h, ctypes.c_void_p(stream_ptr)))
 
     def encode_frame(self, frame, slot: int, stream=None) -> None:
         """Temporal models: encoder features of one (1, C, H, W) frame into cache slot `slot`."""

@@ -3,6 +3,7 @@
 // nafnet_temporal.h:11-29 of the reference) and the CLI's per-frame loop.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <new>
@@ -19,6 +20,17 @@ struct dn_model {
     void* dx = nullptr;
     void* dy = nullptr;
     size_t dx_bytes = 0, dy_bytes = 0;
+    // Pipelined host-buffer calls: two staging pairs, one stream per copy
+    // direction, and the events that order copies and forwards.
+    struct Pipe {
+        void* dx[2] = {nullptr, nullptr};
+        void* dy[2] = {nullptr, nullptr};
+        size_t dx_bytes = 0, dy_bytes = 0;
+        cudaStream_t h2d = nullptr, d2h = nullptr;
+        cudaEvent_t call[2] = {}, in_ready[2] = {}, in_free[2] = {}, out_ready[2] = {}, out_free[2] = {};
+        unsigned count = 0;  // calls issued
+        bool init = false;
+    } pipe;
 };
 
 namespace {
@@ -87,6 +99,19 @@ int dn_model_destroy(dn_model* m) {
         cudaSetDevice(m->eng->device());
         if (m->dx) cudaFree(m->dx);
         if (m->dy) cudaFree(m->dy);
+        auto& q = m->pipe;
+        if (q.init) {
+            cudaStreamSynchronize(q.h2d);
+            cudaStreamSynchronize(q.d2h);
+            for (int k = 0; k < 2; ++k) {
+                if (q.dx[k]) cudaFree(q.dx[k]);
+                if (q.dy[k]) cudaFree(q.dy[k]);
+                for (cudaEvent_t ev : {q.call[k], q.in_ready[k], q.in_free[k], q.out_ready[k], q.out_free[k]})
+                    cudaEventDestroy(ev);
+            }
+            cudaStreamDestroy(q.h2d);
+            cudaStreamDestroy(q.d2h);
+        }
         cudaSetDevice(prev);
         delete m;
         return DN_OK;
@@ -175,6 +200,102 @@ int dn_model_forward_host(dn_model* m, const void* x_host, const int64_t* shape,
         if (rc == DN_OK) rc = m->eng->check_device(s);
         cudaSetDevice(prev);
         return rc;
+    });
+}
+
+int dn_model_forward_host_async(dn_model* m, const void* x_host, const int64_t* shape, int ndim, void* y_host,
+                                void* stream) {
+    if (!m || !x_host || !y_host) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_forward_host_async: null argument");
+    return guarded([&] {
+        int N, T, C, H, W;
+        int rc = parse_shape(*m->eng, shape, ndim, N, T, C, H, W);
+        if (rc != DN_OK) return rc;
+        const size_t xb = static_cast<size_t>(N) * T * C * H * W * 2;
+        const size_t yb = static_cast<size_t>(N) * 3 * H * W * 2;
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(m->eng->device());
+        struct Restore {
+            int d;
+            ~Restore() { cudaSetDevice(d); }
+        } restore{prev};
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        auto& q = m->pipe;
+        cudaError_t e = cudaSuccess;
+        if (!q.init) {
+            e = cudaStreamCreateWithFlags(&q.h2d, cudaStreamNonBlocking);
+            if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&q.d2h, cudaStreamNonBlocking);
+            for (int k = 0; k < 2 && e == cudaSuccess; ++k)
+                for (cudaEvent_t* ev : {&q.call[k], &q.in_ready[k], &q.in_free[k], &q.out_ready[k], &q.out_free[k]})
+                    if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+            if (e != cudaSuccess) return dn_cuda_fail(e, "dn_model_forward_host_async: set-up");
+            q.init = true;
+        }
+        if (q.dx_bytes < xb || q.dy_bytes < yb) {
+            // Larger frames: let every queued call finish before the staging grows.
+            cudaStreamSynchronize(q.h2d);
+            cudaStreamSynchronize(q.d2h);
+            cudaStreamSynchronize(s);
+            for (int k = 0; k < 2 && e == cudaSuccess; ++k) {
+                if (q.dx_bytes < xb) {
+                    if (q.dx[k]) cudaFree(q.dx[k]);
+                    q.dx[k] = nullptr;
+                    e = cudaMalloc(&q.dx[k], xb);
+                }
+                if (e == cudaSuccess && q.dy_bytes < yb) {
+                    if (q.dy[k]) cudaFree(q.dy[k]);
+                    q.dy[k] = nullptr;
+                    e = cudaMalloc(&q.dy[k], yb);
+                }
+            }
+            if (e != cudaSuccess) {
+                q.dx_bytes = q.dy_bytes = 0;
+                return dn_cuda_fail(e, "dn_model_forward_host_async: staging");
+            }
+            q.dx_bytes = std::max(q.dx_bytes, xb);
+            q.dy_bytes = std::max(q.dy_bytes, yb);
+        }
+        const int k = static_cast<int>(q.count & 1u);
+        const bool reuse = q.count >= 2;  // staging pair k was used two calls ago
+        // Input copy: after earlier work on the caller's stream and after the
+        // forward two calls back has read this staging buffer.
+        e = cudaEventRecord(q.call[k], s);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(q.h2d, q.call[k], 0);
+        if (e == cudaSuccess && reuse) e = cudaStreamWaitEvent(q.h2d, q.in_free[k], 0);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(q.dx[k], x_host, xb, cudaMemcpyHostToDevice, q.h2d);
+        if (e == cudaSuccess) e = cudaEventRecord(q.in_ready[k], q.h2d);
+        // Forward on the caller's stream, once the input has landed and the
+        // output copy two calls back has read this output buffer.
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s, q.in_ready[k], 0);
+        if (e == cudaSuccess && reuse) e = cudaStreamWaitEvent(s, q.out_free[k], 0);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "dn_model_forward_host_async: input copy");
+        rc = m->eng->forward(static_cast<const __half*>(q.dx[k]), N, T, C, H, W, static_cast<__half*>(q.dy[k]), s);
+        if (rc != DN_OK) return rc;
+        e = cudaEventRecord(q.in_free[k], s);
+        if (e == cudaSuccess) e = cudaEventRecord(q.out_ready[k], s);
+        // Output copy on its own stream: it overlaps the next call's forward.
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(q.d2h, q.out_ready[k], 0);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(y_host, q.dy[k], yb, cudaMemcpyDeviceToHost, q.d2h);
+        if (e == cudaSuccess) e = cudaEventRecord(q.out_free[k], q.d2h);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "dn_model_forward_host_async: output copy");
+        ++q.count;
+        return DN_OK;
+    });
+}
+
+int dn_model_host_join(dn_model* m, void* stream) {
+    if (!m) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_host_join: null model");
+    return guarded([&] {
+        auto& q = m->pipe;
+        if (!q.init || q.count == 0) return DN_OK;
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(m->eng->device());
+        // Output copies run in call order on one stream: the last one's event
+        // covers every queued call.
+        cudaError_t e = cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), q.out_free[(q.count - 1) & 1u], 0);
+        cudaSetDevice(prev);
+        return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "dn_model_host_join");
     });
 }
 

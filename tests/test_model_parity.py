@@ -134,6 +134,35 @@ def test_forward_host_matches_device(pkg, tmp_path):
     assert np.array_equal(yh, yd.cpu().numpy())
 
 
+def test_forward_host_async_stream_matches_device(pkg, tmp_path):
+    """Five different frames through the pipelined host-buffer call (copies of
+    neighbouring calls overlap each forward, staging pairs reused) give, after
+    the join, exactly the device-buffer forward's outputs; a larger frame
+    afterwards regrows the staging."""
+    synth = synth_mod(pkg)
+    path, _ = synth.make_model_dir(str(tmp_path), synth.CONFIG_W32, 1)
+    m = pkg.Model(path)
+    s = torch.cuda.Stream()
+    frames = [torch.from_numpy(synth.w32_frame(72, 104, seed=20 + i)).half().pin_memory() for i in range(5)]
+    outs = [torch.empty(1, 3, 72, 104, dtype=torch.float16).pin_memory() for _ in range(5)]
+    for x, y in zip(frames, outs):
+        m.forward_host_async_ptr(x.data_ptr(), (1, 3, 72, 104), y.data_ptr(), s.cuda_stream)
+    m.host_join(s.cuda_stream)
+    m.sync(s)
+    for x, y in zip(frames, outs):
+        yd = m(x.cuda())
+        m.sync()
+        assert torch.equal(y, yd.cpu())
+    big = torch.from_numpy(synth.w32_frame(96, 160, seed=30)).half().pin_memory()
+    yb = torch.empty(1, 3, 96, 160, dtype=torch.float16).pin_memory()
+    m.forward_host_async_ptr(big.data_ptr(), (1, 3, 96, 160), yb.data_ptr(), s.cuda_stream)
+    m.host_join(s.cuda_stream)
+    m.sync(s)
+    yd = m(big.cuda())
+    m.sync()
+    assert torch.equal(yb, yd.cpu())
+
+
 def test_rejects_fp32_input(pkg, tmp_path):
     synth = synth_mod(pkg)
     path, _ = synth.make_model_dir(str(tmp_path), synth.CONFIG_TINY_W16, 0)
