@@ -256,6 +256,7 @@ int launch_intro(const IntroParams& p, cudaStream_t s) {
 }
 
 int launch_ending(const EndingParams& p, cudaStream_t s) {
+    if (p.weff && ending_tc_supported(p.C0)) return launch_ending_tc(p, s);
     if (p.C0 % 8 != 0) return dn_fail(DN_ERR_UNSUPPORTED, "ending: base channels must be a multiple of 8");
     const size_t smem = static_cast<size_t>(27) * p.C0 * sizeof(float) +
                         static_cast<size_t>(kEArea) * (p.C0 + 8) * sizeof(__half);

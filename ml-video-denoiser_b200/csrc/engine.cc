@@ -224,6 +224,23 @@ void Engine::build(const HostWeights& hw) {
                 for (int t = 0; t < 9; ++t) wl[(o * 9 + t) * C0 + c] = w[(o * C0 + c) * 9 + t];
         ending_w_ = pk.add_f32(wl);
         ending_b_ = pk.add_f32(hw.to_f32("ending.bias"));
+        if (ending_tc_supported(C0)) {
+            // B tiles of the tensor-core ending: per (tap column kx, 16-channel
+            // K step) three stacked taps ky = 2, 1, 0, each [16 rows x 16] with
+            // output channels 0..2 in rows 0..2 (the rest zero).
+            const int KS = C0 / 16;
+            const size_t tap_bytes = 16 * 32;
+            std::vector<uint8_t> wb(9 * KS * tap_bytes, 0);
+            for (int o = 0; o < 3; ++o)
+                for (int t = 0; t < 9; ++t)
+                    for (int c = 0; c < C0; ++c) {
+                        const __half h = __float2half(w[(o * C0 + c) * 9 + t]);
+                        const int ks = c / 16, k = c % 16, ky = t / 3, kx = t % 3;
+                        uint8_t* tile = wb.data() + ((static_cast<size_t>(kx) * KS + ks) * 3 + (2 - ky)) * tap_bytes;
+                        std::memcpy(tile + kmajor_offset_host(o, k / 8, 256) + (k % 8) * 2, &h, 2);
+                    }
+            ending_tc_w_ = pk.add(wb.data(), wb.size());
+        }
     }
 
     auto block = [&](const std::string& pre, int C) {
@@ -992,6 +1009,8 @@ int Engine::decode_from(__half* xm, int nimg, const std::vector<__half*>& skips,
     ep.beauty = beauty;
     ep.beauty_batch_stride = beauty_stride;
     ep.y = out;
+    ep.weff = (ending_tc_w_ && fa_tc_enabled_) ? wptr<uint8_t>(ending_tc_w_) : nullptr;
+    ep.err = err_;
     ++launches_;
     prof_begin("ending", static_cast<double>(nimg) * (static_cast<double>(sh.Hp) * sh.Wp * C0 + 6.0 * H * W) * 2,
                2.0 * nimg * H * W * 3 * C0 * 9, s);

@@ -94,8 +94,8 @@ public:
         prof_detail_ = mode == 2;
     }
     // 1: fused NAFBlock kernels where they apply (default), with phase A of the
-    // 32/64-channel blocks on the tensor cores; 2: the same with phase A on the
-    // CUDA cores; 0: per-conv kernels everywhere.
+    // 32/64-channel blocks and the ending conv on the tensor cores; 2: the same
+    // with those two on the CUDA cores; 0: per-conv kernels everywhere.
     void set_fused(int mode) {
         fused_enabled_ = mode != 0;
         fa_tc_enabled_ = mode != 2;
@@ -149,6 +149,7 @@ private:
     std::vector<Level> levels_;
     std::vector<BlockW> middle_;
     size_t intro_w_ = 0, intro_b_ = 0, ending_w_ = 0, ending_b_ = 0;
+    size_t ending_tc_w_ = 0;  // tensor-core ending B tiles (0 = none)
     // temporal (C++ engine design): per level temporal_mix over
     // concat(ref, nbr_1..nbr_{T-1}) with the neighbour mean folded into B,
     // and optional offset heads (1x1, 2C -> 2).

@@ -1,5 +1,12 @@
-// Phase A of a shallow NAFBlock (C = 32 / 64) on the tensor cores.
+// Strip-walking 3x3 convolutions on the tensor cores (C = 32 / 64 input
+// channels): phase A of a shallow NAFBlock (below) and, with the same
+// producer, row ring and MMA issuer, the model's ending conv (C -> 3 outputs
+// padded to N = 16, plain zero padding and bias, the rows' LayerNorm replaced
+// by a plain relayout; the epilogue crops, adds the beauty channels and
+// writes NCHW; replaces the reference's ending cudnnConvolutionForward and
+// the residual add, src/models/nafnet.cu:375-388).
 //
+// Phase A:
 // LayerNorm1 (normalisation only), conv1 (1x1, C -> 2D) and the depthwise
 // 3x3 conv (2D channels) compose into one linear map of the normalised input,
 // so they run as a single 3x3 implicit GEMM over the normalised rows:
@@ -46,6 +53,7 @@
 #include <string>
 
 #include "fused_block.h"
+#include "kernels.h"
 #include "launch.cuh"
 #include "sm100.cuh"
 #include "status.h"
@@ -56,10 +64,13 @@ namespace {
 constexpr int kTcThreads = 320;
 constexpr int kMaxImg = 8;
 
-template <int C>
+// MODE 0: phase A of a NAFBlock (LN + conv1 + depthwise, SimpleGate, pool);
+// MODE 1: the model's ending conv (C -> 3 outputs, padded to N = 16), cropped
+// and added to the beauty channels.
+template <int C, int MODE = 0>
 struct GeoT {
-    static constexpr int D = C;                // gated channels
-    static constexpr int N = 2 * C;            // conv outputs (both gate halves)
+    static constexpr int D = C;                         // gated channels (phase A)
+    static constexpr int N = MODE == 0 ? 2 * C : 16;    // conv outputs per pixel
     static constexpr int SW = 128;             // strip width = MMA M
     static constexpr int HP = SW + 2;          // input pixels per row (halo)
     static constexpr int KG = C / 8;           // 16-byte channel groups
@@ -71,8 +82,8 @@ struct GeoT {
     static constexpr int WB = 9 * KS * TAPB;   // all of Weff
     static constexpr int ACC = 512 / N;        // TMEM accumulator ring (all 512 columns)
     static constexpr int TMEM_COLS = ACC * N;
-    // floats: bias per tap-mask class [16][N], pool sums [img][warp][D]
-    static constexpr int F_FLOATS = 16 * N + kMaxImg * 4 * D;
+    // floats: bias per tap-mask class [16][N], pool sums [img][warp][D] (phase A)
+    static constexpr int F_FLOATS = 16 * N + (MODE == 0 ? kMaxImg * 4 * D : 0);
     // At least half of the SM's shared memory: the CTA holds all of TMEM, so a
     // second CTA on the same SM could only wait for it.
     static constexpr int SMEM_USED = 1024 + R * ROWB + WB + F_FLOATS * 4;
@@ -108,9 +119,9 @@ __device__ __forceinline__ bool seg_at(long long u, long long u1, int H, int str
 // 0 = [0,3), 1 = [0,2)[2,3), 2 = [0,1)[1,3). The row's first (kx, K step)
 // writes position 2 (the first contribution to output row r+1) with
 // accumulate off.
-template <int C, int PAT>
+template <int C, int MODE, int PAT>
 __device__ __forceinline__ void issue_steady_row(const uint32_t (&tq)[3], uint64_t ar, uint64_t db) {
-    using G = GeoT<C>;
+    using G = GeoT<C, MODE>;
     constexpr int N = G::N;
     static_assert(PAT != 0 || 3 * N <= 256, "three positions fit one MMA only at N <= 85");
 #pragma unroll
@@ -142,9 +153,13 @@ __device__ __forceinline__ void issue_steady_row(const uint32_t (&tq)[3], uint64
         }
 }
 
-template <int C>
-__global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_constant__ FusedAParams p) {
-    using G = GeoT<C>;
+__device__ __forceinline__ float finite_or_zero(float v) { return (isnan(v) || isinf(v)) ? 0.f : v; }
+
+// P = FusedAParams (MODE 0) or EndingParams (MODE 1): the conv input is
+// in_h x in_w (NHWC, C channels), the outputs cover out_h x out_w.
+template <int C, int MODE, class P>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_conv_kernel(const __grid_constant__ P p) {
+    using G = GeoT<C, MODE>;
     constexpr int D = G::D, N = G::N;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -161,24 +176,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
     __shared__ volatile int s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int strips = (p.W + G::SW - 1) / G::SW;
-    const long long T = static_cast<long long>(p.N) * strips * p.H;
+    int in_h, in_w, out_h, out_w;
+    if constexpr (MODE == 0) {
+        in_h = out_h = p.H;
+        in_w = out_w = p.W;
+    } else {
+        in_h = p.Hp;
+        in_w = p.Wp;
+        out_h = p.H;
+        out_w = p.W;
+    }
+    const int strips = (out_w + G::SW - 1) / G::SW;
+    const long long T = static_cast<long long>(p.N) * strips * out_h;
     const long long u0 = T * blockIdx.x / gridDim.x, u1 = T * (blockIdx.x + 1) / gridDim.x;
 
     pdl_trigger();
     for (int i = tid; i < 16 * N; i += kTcThreads) {
         const int cls = i / N, o = i - cls * N;
-        float sum = 0.f;
+        if constexpr (MODE == 0) {
+            float sum = 0.f;
 #pragma unroll
-        for (int tp = 0; tp < 9; ++tp) {
-            const int ky = tp / 3, kx = tp % 3;
-            const bool off = (kx == 0 && (cls & 1)) || (kx == 2 && (cls & 2)) || (ky == 0 && (cls & 4)) ||
-                             (ky == 2 && (cls & 8));
-            if (!off) sum += p.dw_w[tp * N + o];
+            for (int tp = 0; tp < 9; ++tp) {
+                const int ky = tp / 3, kx = tp % 3;
+                const bool off = (kx == 0 && (cls & 1)) || (kx == 2 && (cls & 2)) || (ky == 0 && (cls & 4)) ||
+                                 (ky == 2 && (cls & 8));
+                if (!off) sum += p.dw_w[tp * N + o];
+            }
+            sBias[i] = fmaf(p.b1p[o], sum, p.dw_b[o]);
+        } else {
+            sBias[i] = o < 3 ? p.b[o] : 0.f;  // a plain conv bias: no tap mask
         }
-        sBias[i] = fmaf(p.b1p[o], sum, p.dw_b[o]);
     }
-    for (int i = tid; i < kMaxImg * 4 * D; i += kTcThreads) sPool[i] = 0.f;
+    if constexpr (MODE == 0)
+        for (int i = tid; i < kMaxImg * 4 * D; i += kTcThreads) sPool[i] = 0.f;
     if (warp == 0) {
         tmem_alloc(&tslot, G::TMEM_COLS);
         tmem_relinquish();
@@ -211,22 +241,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
         // ------------------------------ producer -----------------------------
         if (lane == 0) {
             uint32_t e = 0;
-            for (long long u = u0; !s_abort && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+            for (long long u = u0; !s_abort && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
                 const int x0 = sg.strip * G::SW;
                 for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
                     const uint32_t s = e % G::R, ph = (e / G::R) & 1u;
                     if (!wait_or_abort(&freeb[s], ph ^ 1u, &s_abort, p.err, 0x70)) break;
-                    if (r < 0 || r >= p.H) {
+                    if (r < 0 || r >= in_h) {
                         mbar_arrive(&full[s]);  // zeroed by the LayerNorm warps
                     } else {
                         // The strip's input pixels [x0-1, x0+129) clipped to the
                         // image are contiguous in NHWC: one bulk copy, landing
                         // pixel-major at their slot positions.
-                        const int pa = max(0, x0 - 1), pb = min(p.W, x0 + G::SW + 1);
+                        const int pa = max(0, x0 - 1), pb = min(in_w, x0 + G::SW + 1);
                         const uint32_t bytes = static_cast<uint32_t>(pb - pa) * C * 2;
                         mbar_arrive_expect_tx(&full[s], bytes);
                         bulk_g2s(sRow + s * G::ROWB + (pa - (x0 - 1)) * C * 2,
-                                 p.x + ((static_cast<size_t>(sg.img) * p.H + r) * p.W + pa) * C, bytes, &full[s]);
+                                 p.x + ((static_cast<size_t>(sg.img) * in_h + r) * in_w + pa) * C, bytes, &full[s]);
                     }
                 }
             }
@@ -249,7 +279,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
         const int lead = lane & ~(CPX - 1);
         uint32_t e = 0;
         bool ok = true;
-        for (long long u = u0; ok && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+        for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
             const int x0 = sg.strip * G::SW;
             for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
                 const uint32_t s = e % G::R, ph = (e / G::R) & 1u;
@@ -261,15 +291,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
                     break;
                 }
                 uint8_t* row = sRow + s * G::ROWB;
-                const bool row_in = r >= 0 && r < p.H;
+                const bool row_in = r >= 0 && r < in_h;
                 uint4 nv[NR];
 #pragma unroll
                 for (int k = 0; k < NR; ++k) {
                     const int i = k * PPR + pl;
                     const int xin = x0 - 1 + i;
-                    const bool valid = row_in && i < G::HP && xin >= 0 && xin < p.W;
+                    const bool valid = row_in && i < G::HP && xin >= 0 && xin < in_w;
                     const uint4 v = valid ? *reinterpret_cast<const uint4*>(row + i * C * 2 + cq * 16)
                                           : make_uint4(0u, 0u, 0u, 0u);
+                    if constexpr (MODE == 1) {  // the ending conv reads its input as is
+                        nv[k] = v;
+                        continue;
+                    }
                     const float xs = __shfl_sync(0xffffffffu, unpack_half2(v.x).x, lead);
                     const float2 nx = make_float2(-xs, -xs), one = make_float2(1.f, 1.f);
                     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -328,7 +362,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
             const uint64_t db = sdesc_kmajor(smem_u32(sW), 128, 256);
             bool ok = wait_or_abort(&bar_w, 0, &s_abort, p.err, 0x72);
             uint32_t e = 0, rb = 0;  // entry counter; running index of the segment's first output row
-            for (long long u = u0; ok && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+            for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
                 for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
                     const uint32_t s_in = e & (G::R - 1);
                     if (!wait_or_abort(&ready[s_in], (e / G::R) & 1u, &s_abort, p.err, 0x73)) {
@@ -354,11 +388,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
                         for (int q = 0; q < 3; ++q) tq[q] = tmem + (static_cast<uint32_t>(j0 + q) & (G::ACC - 1)) * N;
                         const uint32_t p0 = static_cast<uint32_t>(j0) & (G::ACC - 1);
                         if (p0 == G::ACC - 1) {
-                            issue_steady_row<C, 2>(tq, ar, db);
+                            issue_steady_row<C, MODE, 2>(tq, ar, db);
                         } else if (3 * N > 256 || p0 == G::ACC - 2) {
-                            issue_steady_row<C, 1>(tq, ar, db);
+                            issue_steady_row<C, MODE, 1>(tq, ar, db);
                         } else {
-                            issue_steady_row<C, (3 * N <= 256 ? 0 : 1)>(tq, ar, db);
+                            issue_steady_row<C, MODE, (3 * N <= 256 ? 0 : 1)>(tq, ar, db);
                         }
                     } else {
                         // Segment edges: the general split, ranges [cut[i], cut[i+1]).
@@ -409,7 +443,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
             const uint64_t db = sdesc_kmajor(smem_u32(sW), 128, 256);
             bool ok = wait_or_abort(&bar_w, 0, &s_abort, p.err, 0x72);
             uint32_t eb = 0, rr = 0, waited = 0;  // entries < waited are known to be ready
-            for (long long u = u0; ok && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+            for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
                 for (int y = sg.ya; y <= sg.yb; ++y, ++rr) {
                     const uint32_t e0 = eb + static_cast<uint32_t>(y - sg.ya);
                     const uint32_t sl[3] = {e0 & (G::R - 1), (e0 + 1) & (G::R - 1), (e0 + 2) & (G::R - 1)};
@@ -453,6 +487,51 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
         const int q = warp & 3;  // TMEM lane quarter = pixels 32q .. 32q+31 of the strip
         const int px = q * 32 + lane;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      if constexpr (MODE == 1) {
+        // y = finite(beauty) + conv + bias for the first 3 outputs, inside the
+        // crop, NCHW (a warp writes 32 consecutive pixels of each plane).
+        uint32_t rr = 0;
+        bool ok = true;
+        const size_t plane = static_cast<size_t>(out_h) * out_w;
+        for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+            const int xg = sg.strip * G::SW + px;
+            const bool col_ok = xg < out_w;
+            const __half* bt = p.beauty + static_cast<size_t>(sg.img) * p.beauty_batch_stride;
+            __half* yo = p.y + static_cast<size_t>(sg.img) * 3 * plane;
+            // The beauty values of a row are loaded one row ahead: their
+            // latency then overlaps the wait for the row's accumulator.
+            auto beauty_row = [&](int y, __half (&bv)[3]) {
+#pragma unroll
+                for (int c = 0; c < 3; ++c)
+                    bv[c] = col_ok ? bt[c * plane + static_cast<size_t>(y) * out_w + xg] : __float2half(0.f);
+            };
+            __half bcur[3];
+            beauty_row(sg.ya, bcur);
+            for (int y = sg.ya; y <= sg.yb; ++y, ++rr) {
+                __half bnext[3];
+                beauty_row(y < sg.yb ? y + 1 : y, bnext);
+                const uint32_t a = rr & (G::ACC - 1);
+                ok = __all_sync(0xffffffffu,
+                                wait_or_abort(&acc_full[a], (rr / G::ACC) & 1u, &s_abort, p.err, 0x75));
+                if (!ok) break;
+                tc_fence_after();
+                float v[16];
+                tmem_ld16(lane_base + a * N, v);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[a]);
+                if (col_ok) {
+                    const size_t o = static_cast<size_t>(y) * out_w + xg;
+#pragma unroll
+                    for (int c = 0; c < 3; ++c)
+                        yo[c * plane + o] = __float2half(finite_or_zero(__half2float(bcur[c])) + (v[c] + sBias[c]));
+                }
+#pragma unroll
+                for (int c = 0; c < 3; ++c) bcur[c] = bnext[c];
+            }
+        }
+      } else {
         float ps[D];
 #pragma unroll
         for (int c = 0; c < D; ++c) ps[c] = 0.f;
@@ -470,7 +549,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
         uint32_t rr = 0;
         int cur = -1;
         bool ok = true;
-        for (long long u = u0; ok && seg_at(u, u1, p.H, strips, sg); u += sg.yb - sg.ya + 1) {
+        for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
             if (cur >= 0 && sg.img != cur) flush(cur);
             cur = sg.img;
             const int xg = sg.strip * G::SW + px;
@@ -533,33 +612,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) fused_a_tc_kernel(const __grid_
             }
         }
         if (cur >= 0) flush(cur);
+      }
     }
 
     __syncthreads();
-    for (int i = tid; i < p.N * D; i += kTcThreads) {
-        const int n = i / D, c = i - n * D;
-        float s = 0.f;
+    if constexpr (MODE == 0) {
+        for (int i = tid; i < p.N * D; i += kTcThreads) {
+            const int n = i / D, c = i - n * D;
+            float s = 0.f;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) s += sPool[(n * 4 + w) * D + c];
-        p.partials[(static_cast<size_t>(n) * gridDim.x + blockIdx.x) * D + c] = s;
+            for (int w = 0; w < 4; ++w) s += sPool[(n * 4 + w) * D + c];
+            p.partials[(static_cast<size_t>(n) * gridDim.x + blockIdx.x) * D + c] = s;
+        }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, G::TMEM_COLS);
 }
 
-template <int C>
-int run_a_tc(const FusedAParams& p, int grid, cudaStream_t s) {
-    using G = GeoT<C>;
-    auto kern = fused_a_tc_kernel<C>;
+template <int C, int MODE, class P>
+int run_tc(const P& p, int grid, cudaStream_t s) {
+    using G = GeoT<C, MODE>;
+    auto kern = tc_conv_kernel<C, MODE, P>;
     static bool cfg = false;
     if (!cfg) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
-        if (e != cudaSuccess) return dn_cuda_fail(e, "fused_a_tc: smem attribute");
+        if (e != cudaSuccess) return dn_cuda_fail(e, "tc conv: smem attribute");
         cfg = true;
     }
     cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kTcThreads), G::SMEM, s, p);
-    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "fused_a_tc: launch");
+    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "tc conv: launch");
 }
 
 }  // namespace
@@ -577,9 +659,21 @@ int launch_fused_a_tc(const FusedAParams& p, int C, int D, int grid, cudaStream_
     if (!p.weff || !p.b1p) return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: missing packed weights");
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.g) & 15))
         return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: x and g must be 16-byte aligned");
-    if (C == 32 && D == 32) return run_a_tc<32>(p, grid, s);
-    if (C == 64 && D == 64) return run_a_tc<64>(p, grid, s);
+    if (C == 32 && D == 32) return run_tc<32, 0>(p, grid, s);
+    if (C == 64 && D == 64) return run_tc<64, 0>(p, grid, s);
     return dn_fail(DN_ERR_UNSUPPORTED, "fused_a_tc: channel configuration");
+}
+
+bool ending_tc_supported(int C0) { return C0 == 32 || C0 == 64; }
+
+int launch_ending_tc(const EndingParams& p, cudaStream_t s) {
+    if (!p.weff) return dn_fail(DN_ERR_INVALID_ARG, "ending_tc: missing packed weights");
+    if ((reinterpret_cast<uintptr_t>(p.x) & 15)) return dn_fail(DN_ERR_INVALID_ARG, "ending_tc: x must be 16-byte aligned");
+    const long long units = static_cast<long long>(p.N) * ((p.W + 127) / 128) * p.H;
+    const int grid = static_cast<int>(std::max(1LL, std::min<long long>(units, sm_count())));
+    if (p.C0 == 32) return run_tc<32, 1>(p, grid, s);
+    if (p.C0 == 64) return run_tc<64, 1>(p, grid, s);
+    return dn_fail(DN_ERR_UNSUPPORTED, "ending_tc: channel count");
 }
 
 }  // namespace dnb

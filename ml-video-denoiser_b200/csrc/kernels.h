@@ -125,7 +125,13 @@ struct EndingParams {
     const __half* beauty;  // NCHW input
     int beauty_batch_stride;
     __half* y;             // NCHW (N, 3, H, W)
+    // Tensor-core form (fused_a_tc.cu): B tiles [3 kx][C0/16 K steps][ky = 2, 1, 0]
+    // of 16 output rows (3 used) x 16 channels; nullptr = the CUDA-core kernel.
+    const uint8_t* weff;
+    uint32_t* err;
 };
 int launch_ending(const EndingParams& p, cudaStream_t s);
+bool ending_tc_supported(int C0);
+int launch_ending_tc(const EndingParams& p, cudaStream_t s);
 
 }  // namespace dnb
