@@ -76,18 +76,22 @@ struct GeoT {
     static constexpr int KG = C / 8;           // 16-byte channel groups
     static constexpr int KGB = HP * 16;        // bytes per channel group of a row (LBO)
     static constexpr int ROWB = KG * KGB;      // one input-row slot
-    static constexpr int R = C >= 64 ? 4 : 8;  // input-row slots (a power of two)
+    // Phase A at 32 channels runs two CTAs per SM (two MMA-issuing threads:
+    // one alone leaves the tensor pipe idle most of the time), each with half
+    // of TMEM and a 4-slot row ring.
+    static constexpr int CTAS = (MODE == 0 && C == 32) ? 2 : 1;
+    static constexpr int R = (C >= 64 || CTAS == 2) ? 4 : 8;  // input-row slots (a power of two)
     static constexpr int KS = C / 16;          // K = 16 steps per tap
     static constexpr int TAPB = N * 32;        // B tile of one (tap, K step): 2D rows x 16
     static constexpr int WB = 9 * KS * TAPB;   // all of Weff
-    static constexpr int ACC = 512 / N;        // TMEM accumulator ring (all 512 columns)
+    static constexpr int ACC = 512 / N / CTAS;  // TMEM accumulator ring (all of the CTA's share)
     static constexpr int TMEM_COLS = ACC * N;
     // floats: bias per tap-mask class [16][N], pool sums [img][warp][D] (phase A)
     static constexpr int F_FLOATS = 16 * N + (MODE == 0 ? kMaxImg * 4 * D : 0);
     // At least half of the SM's shared memory: the CTA holds all of TMEM, so a
     // second CTA on the same SM could only wait for it.
     static constexpr int SMEM_USED = 1024 + R * ROWB + WB + F_FLOATS * 4;
-    static constexpr int SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
+    static constexpr int SMEM = (CTAS == 2 || SMEM_USED > 120 * 1024) ? SMEM_USED : 120 * 1024;
     static_assert(ROWB % 128 == 0, "row slots stay 128-byte aligned");
     static_assert(TMEM_COLS <= 512, "TMEM ring");
     static_assert((R & (R - 1)) == 0 && (ACC & (ACC - 1)) == 0, "ring sizes are powers of two");
@@ -158,7 +162,7 @@ __device__ __forceinline__ float finite_or_zero(float v) { return (isnan(v) || i
 // P = FusedAParams (MODE 0) or EndingParams (MODE 1): the conv input is
 // in_h x in_w (NHWC, C channels), the outputs cover out_h x out_w.
 template <int C, int MODE, class P>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_conv_kernel(const __grid_constant__ P p) {
+__global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kernel(const __grid_constant__ P p) {
     using G = GeoT<C, MODE>;
     constexpr int D = G::D, N = G::N;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -565,24 +569,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_conv_kernel(const __grid_con
                 const int cls = (xg == 0 ? 1 : 0) | (xg == p.W - 1 ? 2 : 0) | (y == 0 ? 4 : 0) | (y == p.H - 1 ? 8 : 0);
                 const float* bias_c = sBias + cls * N;
                 __half* dst = p.g + ((static_cast<size_t>(sg.img) * p.H + y) * p.W + xg) * D;
-                // 32 gate channels per pass: both halves' accumulator columns
-                // (tcgen05.ld is warp-collective: every lane loads).
+                // EPW gate channels per pass: both halves' accumulator columns
+                // (tcgen05.ld is warp-collective: every lane loads); 16 when
+                // two CTAs share the SM's registers.
+                constexpr int EPW = G::CTAS == 2 ? 16 : 32;
 #pragma unroll
-                for (int cc = 0; cc < D; cc += 32) {
-                    float va[32], vb[32];
-                    tmem_ld16(lane_base + a * N + cc, *reinterpret_cast<float(*)[16]>(va));
-                    tmem_ld16(lane_base + a * N + cc + 16, *reinterpret_cast<float(*)[16]>(va + 16));
-                    tmem_ld16(lane_base + a * N + D + cc, *reinterpret_cast<float(*)[16]>(vb));
-                    tmem_ld16(lane_base + a * N + D + cc + 16, *reinterpret_cast<float(*)[16]>(vb + 16));
+                for (int cc = 0; cc < D; cc += EPW) {
+                    float va[EPW], vb[EPW];
+#pragma unroll
+                    for (int h = 0; h < EPW; h += 16) {
+                        tmem_ld16(lane_base + a * N + cc + h, *reinterpret_cast<float(*)[16]>(va + h));
+                        tmem_ld16(lane_base + a * N + D + cc + h, *reinterpret_cast<float(*)[16]>(vb + h));
+                    }
                     tmem_ld_wait();
-                    if (cc + 32 >= D) {  // the accumulator is drained
+                    if (cc + EPW >= D) {  // the accumulator is drained
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[a]);
                     }
                     if (!col_ok) continue;
 #pragma unroll
-                    for (int c8 = 0; c8 < 32; c8 += 8) {
+                    for (int c8 = 0; c8 < EPW; c8 += 8) {
                         const int c = cc + c8;
                         float bias[16];
 #pragma unroll
@@ -649,9 +656,9 @@ int run_tc(const P& p, int grid, cudaStream_t s) {
 bool fused_a_tc_supported(int C, int D) { return (C == 32 || C == 64) && D == C; }
 
 int fused_a_tc_grid(int C, int N, int H, int W) {
-    (void)C;
     const long long units = static_cast<long long>(N) * ((W + 127) / 128) * H;
-    return static_cast<int>(std::max(1LL, std::min<long long>(units, sm_count())));
+    const int per_sm = C == 32 ? GeoT<32, 0>::CTAS : GeoT<64, 0>::CTAS;
+    return static_cast<int>(std::max(1LL, std::min<long long>(units, static_cast<long long>(sm_count()) * per_sm)));
 }
 
 int launch_fused_a_tc(const FusedAParams& p, int C, int D, int grid, cudaStream_t s) {
