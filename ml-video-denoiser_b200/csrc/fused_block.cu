@@ -81,7 +81,9 @@ struct GeoA {
 
 template <int C, int D, int F>
 struct GeoB {
-    static constexpr int TMEM_COLS = pow2_at_least(C + 2 * F);
+    // conv3, conv4 and conv5 take turns on the same columns (each accumulator
+    // is drained before the next MMA is issued), so more CTAs share an SM.
+    static constexpr int TMEM_COLS = pow2_at_least(C > 2 * F ? C : 2 * F);
     static constexpr int G_BYTES = 128 * D * 2;
     static constexpr int X_BYTES = 128 * C * 2;
     static constexpr int A3_BYTES = 128 * F * 2;
@@ -570,7 +572,7 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
             tc_fence_after();  // conv4: [128 x C] x [C -> 2F]
 #pragma unroll
             for (int k = 0; k < C / 16; ++k)
-                mma_f16(tmem + C, desc_add(d4a, k * 32), desc_add(d4b, k * 256), idesc_f16_f32(128, 2 * F),
+                mma_f16(tmem, desc_add(d4a, k * 32), desc_add(d4b, k * 256), idesc_f16_f32(128, 2 * F),
                         k > 0 ? 1u : 0u);
             mma_commit(&bar_mma);
         }
@@ -580,8 +582,8 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
 #pragma unroll 1
         for (int c0 = fb; c0 < fb + FC; c0 += 16) {
             float va[16], vb[16];
-            tmem_ld16(lane_base + C + c0, va);
-            tmem_ld16(lane_base + C + F + c0, vb);
+            tmem_ld16(lane_base + c0, va);
+            tmem_ld16(lane_base + F + c0, vb);
             tmem_ld_wait();
 #pragma unroll
             for (int g2 = 0; g2 < 2; ++g2) {
