@@ -727,12 +727,23 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
         fa.partials = partials_;
         fa.err = err_;
         const bool tc = b.fa_tc && fa_tc_enabled_;
+        // One image through the tensor-core pass A: its last CTA also runs the
+        // SCA and folds the scale into conv3's B (no SCA launch).
+        const bool sca_in_a = tc && nimg == 1 && b3s_ != nullptr && b.f3.n_tiles == 1 && b.f3.k_chunks == 1 &&
+                              b.f3.KC == b.dw;
         if (tc) {
             fa.weff = wptr<uint8_t>(b.fa_w);
             fa.b1p = wptr<float>(b.fa_b1);
         }
+        if (sca_in_a) {
+            fa.counter = counters_;
+            fa.sca_w = wptr<float>(b.sca_w);
+            fa.sca_b = wptr<float>(b.sca_b);
+            fa.b3_src = wptr<uint8_t>(b.f3.bpack);
+            fa.b3_dst = b3s_;
+        }
         const int grid = tc ? fused_a_tc_grid(b.C, nimg, h, w) : fused_a_grid(b.C, b.dw, nimg, h, w);
-        launches_ += 3;
+        launches_ += sca_in_a ? 2 : 3;
         prof_begin("fused_block_a", static_cast<double>(nimg) * hw * (b.C + b.dw) * 2,
                    2.0 * nimg * hw * (b.C * 2 * b.dw + 2 * b.dw * 9), s);
         DN_TRY(tc ? launch_fused_a_tc(fa, b.C, b.dw, grid, s) : launch_fused_a(fa, b.C, b.dw, grid, s));
@@ -757,9 +768,11 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
             d.b_kc = b.f3.KC;
             d.b_kchunks = b.f3.k_chunks;
         }
-        prof_begin("sca", 4.0 * nimg * grid * b.dw, 2.0 * nimg * b.dw * b.dw, s);
-        DN_TRY(launch_sca(d, grid, s));
-        prof_end(s);
+        if (!sca_in_a) {
+            prof_begin("sca", 4.0 * nimg * grid * b.dw, 2.0 * nimg * b.dw * b.dw, s);
+            DN_TRY(launch_sca(d, grid, s));
+            prof_end(s);
+        }
         // Pass B: SCA scale + conv3 + beta residual + LN2 + conv4 + gate + conv5 + gamma residual.
         FusedBParams fb{};
         fb.g = buf_g_;

@@ -631,6 +631,44 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
             for (int w = 0; w < 4; ++w) s += sPool[(n * 4 + w) * D + c];
             p.partials[(static_cast<size_t>(n) * gridDim.x + blockIdx.x) * D + c] = s;
         }
+        if (p.b3_dst) {
+            // SCA in the last CTA (one image): fixed-order pool over the CTAs'
+            // rows, s = W mean + b, conv3's B columns scaled by s.
+            __shared__ int s_last;
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+            __syncthreads();
+            if (s_last) {
+                __threadfence();
+                float* s_mean = sPool;      // [D]
+                float* s_scale = sPool + D;  // [D]
+                const float inv = 1.0f / (static_cast<float>(p.H) * p.W);
+                for (int c = tid; c < D; c += kTcThreads) {
+                    float sum = 0.f;
+                    for (unsigned r = 0; r < gridDim.x; ++r) sum += __ldcg(p.partials + static_cast<size_t>(r) * D + c);
+                    s_mean[c] = sum * inv;
+                }
+                __syncthreads();
+                for (int o = tid; o < D; o += kTcThreads) {
+                    float v = p.sca_b[o];
+                    for (int c = 0; c < D; ++c) v = fmaf(p.sca_w[o * D + c], s_mean[c], v);
+                    s_scale[o] = v;
+                }
+                __syncthreads();
+                constexpr int KQ = D / 8;  // 16-byte chunks per B row
+                for (int i = tid; i < C * KQ; i += kTcThreads) {
+                    const int n = i / KQ, q = i - n * KQ;
+                    const size_t off = static_cast<size_t>(n >> 3) * (KQ * 128) + q * 128 + (n & 7) * 16;
+                    float f[8];
+                    h8_to_f(*reinterpret_cast<const uint4*>(p.b3_src + off), f);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) f[j] *= s_scale[8 * q + j];
+                    *reinterpret_cast<uint4*>(p.b3_dst + off) = f_to_h8(f);
+                }
+                if (tid == 0) *p.counter = 0u;
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -664,6 +702,8 @@ int fused_a_tc_grid(int C, int N, int H, int W) {
 int launch_fused_a_tc(const FusedAParams& p, int C, int D, int grid, cudaStream_t s) {
     if (p.N > kMaxImg) return dn_fail(DN_ERR_UNSUPPORTED, "fused_a_tc: batch > 8");
     if (!p.weff || !p.b1p) return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: missing packed weights");
+    if (p.b3_dst && (p.N != 1 || !p.counter || !p.sca_w || !p.sca_b || !p.b3_src))
+        return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: the SCA fold needs one image, a counter and the SCA weights");
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.g) & 15))
         return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: x and g must be 16-byte aligned");
     if (C == 32 && D == 32) return run_tc<32, 0>(p, grid, s);

@@ -25,6 +25,15 @@ struct FusedAParams {
     // Tensor-core form (fused_a_tc.cu): LN + conv1 + depthwise as one 3x3 conv.
     const uint8_t* weff;    // [3 kx][C/16 K steps][ky = 2, 1, 0] B tiles of Weff = dw * W1 * gamma1 (2D x 16 each)
     const float* b1p;       // [2D] b1 + W1 beta1
+    // Single image (tensor-core form): the last CTA to finish reduces the pool
+    // partials, evaluates the SCA and writes conv3's B with the scale folded
+    // in (b3_dst = b3_src, column k times s[k]; one [C x D] tile, KC = D);
+    // counter is zero on entry and reset by that CTA. b3_dst == nullptr: off.
+    unsigned* counter;
+    const float* sca_w;     // [D][D]
+    const float* sca_b;     // [D]
+    const uint8_t* b3_src;
+    uint8_t* b3_dst;
 };
 
 struct FusedBParams {
