@@ -261,6 +261,48 @@ def make_model_dir(out_dir: str, cfg: NAFConfig, seed: int, temporal: str | None
 
 
 # ---------------------------------------------------------------------------
+# Deformable-alignment front end of the temporal model with DCN alignment
+# ---------------------------------------------------------------------------
+
+ALIGN_FEAT = 64     # feature channels the DCN aligns
+ALIGN_DG = 8        # deformable groups
+# Gains on the kaiming-uniform draw of align.offset: the offset rows then give
+# offsets of about N(0, 2 px) on the synthetic windows (feature RMS ~0.33),
+# the mask rows raw masks of std ~1 (sigmoid spread over ~0.3-0.7).
+ALIGN_OFFSET_GAIN = 10.0
+ALIGN_MASK_GAIN = 5.0
+
+
+def align_param_specs(num_frames: int = 5, feat: int = ALIGN_FEAT, dg: int = ALIGN_DG,
+                      in_channels: int = 3) -> list:
+    """Keys of the alignment front end (``aligned.AlignedTemporal``):
+    feature conv 3x3 in->F, offset/mask conv 3x3 2F->3*dg*9 (2*dg*9 offsets
+    [dy, dx] per (group, tap), then dg*9 raw masks), DCNv2 3x3 F->F, fusion
+    1x1 T*F->in."""
+    kk = 9
+    return [("align.feat.weight", (feat, in_channels, 3, 3)), ("align.feat.bias", (feat,)),
+            ("align.offset.weight", (3 * dg * kk, 2 * feat, 3, 3)), ("align.offset.bias", (3 * dg * kk,)),
+            ("align.dcn.weight", (feat, feat, 3, 3)), ("align.dcn.bias", (feat,)),
+            ("align.fuse.weight", (in_channels, num_frames * feat, 1, 1)), ("align.fuse.bias", (in_channels,))]
+
+
+def make_align_dir(out_dir: str, seed: int, num_frames: int = 5, feat: int = ALIGN_FEAT, dg: int = ALIGN_DG,
+                   in_channels: int = 3) -> tuple[str, dict]:
+    """Seeded alignment weights in the reference format; returns (manifest path,
+    fp16-rounded params)."""
+    specs = align_param_specs(num_frames, feat, dg, in_channels)
+    params = init_params(specs, seed)
+    n_off = 2 * dg * 9
+    for key in ("align.offset.weight", "align.offset.bias"):
+        params[key][:n_off] *= ALIGN_OFFSET_GAIN
+        params[key][n_off:] *= ALIGN_MASK_GAIN
+    arch = {"type": "dcn_align", "in_channels": in_channels, "num_frames": num_frames,
+            "feat_channels": feat, "deform_groups": dg}
+    path = write_manifest(out_dir, params, arch, order=[n for n, _ in specs])
+    return path, round_fp16(params)
+
+
+# ---------------------------------------------------------------------------
 # Synthetic frames
 # ---------------------------------------------------------------------------
 

@@ -21,6 +21,10 @@ reference project ginzburg-dev/ml-video-denoiser:
                                 border clamp, ch0 = dx, ch1 = dy)
 * ``deform_conv2d``             src/kernels/deform_im2col.cuh:34-142 + the GEMM of
                                 src/layers/deform_conv2d.cu:134-182 (DCNv2, sigmoid mask)
+* ``aligned_temporal_forward``  the temporal model with deformable alignment: feature
+                                conv, offset/mask conv, DCN per neighbour, 1x1 fusion,
+                                NAFNet trunk (no reference model wires the DCN; this
+                                composition of the restatements is the checker for it)
 
 Architecture is discovered from the weight keys the same way the C++ engine
 does (src/models/nafnet.cu:78-92). Parameters are the fp32 values of the
@@ -384,6 +388,32 @@ def deform_conv2d(x: torch.Tensor, offsets: torch.Tensor, masks: torch.Tensor,
             res = res + bias.view(cout, 1)
         out[b] = res.view(cout, ho, wo)
     return out
+
+
+def aligned_temporal_forward(pa: dict, pt: dict, clip: torch.Tensor) -> torch.Tensor:
+    """Temporal NAFNet with deformable alignment, fp32: the wiring of the
+    engine's ``aligned.AlignedTemporal``. The reference wires its
+    DeformConv2dLayer (deform_conv2d.cu:105-184) into no model, so the wiring
+    is this project's; its pieces are the restatements above
+    (``deform_conv2d``, ``nafnet_forward``). clip: (1, T, C, H, W); the
+    centre frame is T // 2. Returns (1, 3, H, W) and the per-neighbour
+    offsets/masks tensors (for statistics)."""
+    t = clip.shape[1]
+    c = t // 2
+    feats = [conv(pa, "align.feat", clip[:, i], padding=1) for i in range(t)]
+    n_off = pa["align.offset.weight"].shape[0] * 2 // 3
+    dg = n_off // 18
+    aligned, oms = [], []
+    for i in range(t):
+        if i == c:
+            aligned.append(feats[c])
+            continue
+        om = conv(pa, "align.offset", torch.cat([feats[c], feats[i]], 1), padding=1)
+        oms.append(om)
+        aligned.append(deform_conv2d(feats[i], om[:, :n_off], om[:, n_off:], pa["align.dcn.weight"],
+                                     pa["align.dcn.bias"], pad=1, deform_groups=dg))
+    fused = conv(pa, "align.fuse", torch.cat(aligned, 1)) + clip[:, c]
+    return nafnet_forward(pt, fused), oms
 
 
 # ---------------------------------------------------------------------------

@@ -1,0 +1,92 @@
+"""Temporal NAFNet with deformable alignment (``aligned.AlignedTemporal``):
+feature conv -> offset/mask conv on concat(centre, neighbour) -> DCNv2 per
+neighbour -> 1x1 fusion + centre frame -> NAFNet trunk, against the same
+wiring composed from the oracle's restatements
+(oracle/nafnet_oracle.py:aligned_temporal_forward).
+
+Inputs follow the temporal-alignment workload: T = 5 frames of one seeded
+smooth base translated by integer shifts in [-4, 4] px, each with N(0, 20/255)
+noise; 64 feature channels, 8 deformable groups, offsets of about N(0, 2 px).
+Bar: max |out - fp32| <= 5e-3 and PSNR >= 50 dB, as for the model parity."""
+import importlib
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+from parity_util import MAX_ABS, MIN_PSNR, compare, synth_mod  # noqa: E402
+
+import nafnet_oracle as O  # noqa: E402
+
+
+def oracle_case(pkg, tmp_path, cfg, t, h, w, seed):
+    synth = synth_mod(pkg)
+    apath, pa = synth.make_align_dir(str(tmp_path / "align"), seed, num_frames=t)
+    tpath, pt = synth.make_model_dir(str(tmp_path / "trunk"), cfg, seed)
+    clip = synth.temporal_window(t, h, w, seed).astype(np.float16).astype(np.float32)
+    torch.set_num_threads(min(16, os.cpu_count() or 1))
+    ref, oms = O.aligned_temporal_forward(O.as_torch(pa), O.as_torch(pt), torch.from_numpy(clip))
+    return apath, tpath, clip, ref.numpy(), oms
+
+
+def test_oracle_wiring_statistics(pkg, tmp_path):
+    """The synthetic alignment weights give offsets of about N(0, 2 px) and
+    masks spread around 0.5 on the synthetic window (CPU, oracle only)."""
+    synth = synth_mod(pkg)
+    _, _, clip, ref, oms = oracle_case(pkg, tmp_path, synth.CONFIG_TINY_W16, 5, 48, 64, seed=2)
+    assert ref.shape == (1, 3, 48, 64) and np.isfinite(ref).all()
+    n_off = 2 * synth.ALIGN_DG * 9
+    assert len(oms) == 4 and all(om.shape == (1, 3 * synth.ALIGN_DG * 9, 48, 64) for om in oms)
+    off = torch.cat([om[:, :n_off] for om in oms]).flatten()
+    msk = torch.sigmoid(torch.cat([om[:, n_off:] for om in oms])).flatten()
+    assert 1.2 <= float(off.std()) <= 3.5, float(off.std())
+    assert 0.35 <= float(msk.mean()) <= 0.65 and float(msk.std()) >= 0.1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("h,w", [(64, 96), (50, 70)], ids=["64x96", "50x70"])
+def test_aligned_w32_matches_oracle(pkg, tmp_path, h, w):
+    synth = synth_mod(pkg)
+    aligned = importlib.import_module(pkg.__name__ + ".aligned")
+    apath, tpath, clip, ref, _ = oracle_case(pkg, tmp_path, synth.CONFIG_W32, 5, h, w, seed=2)
+    model = aligned.AlignedTemporal(apath, tpath)
+    assert (model.num_frames, model.feat_channels, model.deform_groups) == (5, 64, 8)
+    y = model(torch.from_numpy(clip).half().cuda())
+    model.sync()
+    err, psnr = compare(y.float().cpu().numpy(), ref)
+    model.close()
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+
+
+@pytest.mark.gpu
+def test_aligned_repeat_and_side_stream(pkg, tmp_path):
+    """Two calls give identical outputs, on the current stream and on a side stream."""
+    synth = synth_mod(pkg)
+    aligned = importlib.import_module(pkg.__name__ + ".aligned")
+    apath, _ = synth.make_align_dir(str(tmp_path / "align"), 3, num_frames=3)
+    tpath, _ = synth.make_model_dir(str(tmp_path / "trunk"), synth.CONFIG_TINY_W16, 3)
+    model = aligned.AlignedTemporal(apath, tpath)
+    clip = torch.from_numpy(synth.temporal_window(3, 40, 56, 3)).half().cuda()
+    a = model(clip)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    b = model(clip, stream=s)
+    s.synchronize()
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    model.close()
+
+
+@pytest.mark.gpu
+def test_aligned_rejects_bad_windows(pkg, tmp_path):
+    synth = synth_mod(pkg)
+    aligned = importlib.import_module(pkg.__name__ + ".aligned")
+    apath, _ = synth.make_align_dir(str(tmp_path / "align"), 4, num_frames=3)
+    tpath, _ = synth.make_model_dir(str(tmp_path / "trunk"), synth.CONFIG_TINY_W16, 4)
+    model = aligned.AlignedTemporal(apath, tpath)
+    with pytest.raises(ValueError):
+        model(torch.zeros(1, 5, 3, 32, 32, dtype=torch.float16, device="cuda"))
+    with pytest.raises(TypeError):
+        model(torch.zeros(1, 3, 3, 32, 32, dtype=torch.float32, device="cuda"))
+    model.close()
