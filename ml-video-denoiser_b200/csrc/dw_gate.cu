@@ -123,9 +123,9 @@ __global__ void __launch_bounds__(kThreads) dw_gate_kernel(const __grid_constant
 }
 
 // grid (D / 8, N): CTA j computes s[img][8j .. 8j+8). Every lane owns
-// float4 channel vectors v = lane + 32 i (i < V, V = ceil(D / 128)) and
-// issues all of its loads before it uses any (8 / V partial rows at a time),
-// so each phase pays about one memory latency.
+// float4 channel vectors v = lane + 32 i (i < V, V = ceil(D / 128)); each
+// phase issues all of its loads before it uses any, so it pays about one
+// memory latency.
 constexpr int kScaVec = 8;  // D <= 32 * 4 * kScaVec = 1024
 
 template <int V>
@@ -152,31 +152,31 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
     pdl_wait();
     // Fixed-order pool over all 256 threads: thread (stripe, v) sums the
     // float4 channel vector v of partial rows stripe, stripe + stripes, ...
-    // (four loads in flight); the stripe sums are then added in stripe order.
+    // in row order; the stripe sums are then added in stripe order.
     const float4* pp = reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(img) * nb * D);
     const int stripes = kThreads / nvec;
     const int v = tid % nvec, stripe = tid / nvec;
     if (stripe < stripes) {
+        // Up to kPool rows in flight per thread (one memory latency for the
+        // usual <= 12 rows per stripe), added in row order.
+        constexpr int kPool = 12;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        int b = stripe;
-        for (; b + 3 * stripes < nb; b += 4 * stripes) {
-            float4 x[4];
+        for (int b = stripe; b < nb; b += kPool * stripes) {
+            float4 x[kPool];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) x[u] = pp[static_cast<size_t>(b + u * stripes) * nvec + v];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                acc.x += x[u].x;
-                acc.y += x[u].y;
-                acc.z += x[u].z;
-                acc.w += x[u].w;
+            for (int u = 0; u < kPool; ++u) {
+                const int row = min(b + u * stripes, nb - 1);  // past the end: a row that is not added
+                x[u] = pp[static_cast<size_t>(row) * nvec + v];
             }
-        }
-        for (; b < nb; b += stripes) {
-            const float4 x = pp[static_cast<size_t>(b) * nvec + v];
-            acc.x += x.x;
-            acc.y += x.y;
-            acc.z += x.z;
-            acc.w += x.w;
+#pragma unroll
+            for (int u = 0; u < kPool; ++u) {
+                if (b + u * stripes < nb) {
+                    acc.x += x[u].x;
+                    acc.y += x[u].y;
+                    acc.z += x[u].z;
+                    acc.w += x[u].w;
+                }
+            }
         }
         reinterpret_cast<float4*>(red + stripe * D)[v] = acc;
     }
