@@ -149,6 +149,31 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
         w[i] = (o < D && v < nvec) ? reinterpret_cast<const float4*>(p.sca_w + static_cast<size_t>(o) * D)[v]
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    // The conv3 B chunks this CTA rescales (constant weights) also load
+    // before the wait: one 16-byte chunk (its 8 columns) of output rows
+    // n = tid + u * kThreads.
+    constexpr int kFold = 4;  // b_rows <= kFold * kThreads (checked at launch)
+    const bool fold = p.bdst != nullptr;
+    uint4 bv[kFold];
+    size_t boff[kFold];
+    if (fold) {
+        const int k0 = blockIdx.x * 8;
+        const int kc = k0 / p.b_kc, kq = (k0 % p.b_kc) / 8;
+        const size_t tile_b = static_cast<size_t>(p.b_nt) * p.b_kc * 2;
+        const uint32_t sbo = static_cast<uint32_t>(p.b_kc / 8) * 128u;
+#pragma unroll
+        for (int u = 0; u < kFold; ++u) {
+            const int n = tid + u * kThreads;
+            boff[u] = 0;
+            bv[u] = make_uint4(0, 0, 0, 0);
+            if (n < p.b_rows) {
+                const int nt = n / p.b_nt, nl = n - nt * p.b_nt;
+                boff[u] = (static_cast<size_t>(nt) * p.b_kchunks + kc) * tile_b + (nl >> 3) * sbo + kq * 128 +
+                          (nl & 7) * 16;
+                bv[u] = __ldg(reinterpret_cast<const uint4*>(p.bsrc + boff[u]));
+            }
+        }
+    }
     pdl_wait();
     // Fixed-order pool over all 256 threads: thread (stripe, v) sums the
     // float4 channel vector v of partial rows stripe, stripe + stripes, ...
@@ -206,25 +231,23 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
         if (lane == 0) p.s_out[static_cast<size_t>(img) * D + o] = s + p.sca_b[o];
         if (lane == 0) red[warp] = s + p.sca_b[o];  // red[] is no longer read: keep this CTA's s there
     }
-    if (p.bdst == nullptr) return;
-    // Fold s[8j .. 8j+8) into the conv3 B columns of this CTA's 8 channels:
-    // one 16-byte chunk per output row.
+    if (!fold) return;
+    // Fold s[8j .. 8j+8) into the conv3 B columns of this CTA's 8 channels
+    // (the chunks loaded before the wait).
     __syncthreads();
     const int k0 = blockIdx.x * 8;
-    const int kc = k0 / p.b_kc, kq = (k0 % p.b_kc) / 8;
-    const size_t tile_b = static_cast<size_t>(p.b_nt) * p.b_kc * 2;
-    const uint32_t sbo = static_cast<uint32_t>(p.b_kc / 8) * 128u;
     float sc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) sc[i] = (k0 + i < D) ? red[i] : 0.f;
-    for (int n = tid; n < p.b_rows; n += kThreads) {
-        const int nt = n / p.b_nt, nl = n - nt * p.b_nt;
-        const size_t off = (static_cast<size_t>(nt) * p.b_kchunks + kc) * tile_b + (nl >> 3) * sbo + kq * 128 + (nl & 7) * 16;
-        float f[8];
-        h8_to_f(*reinterpret_cast<const uint4*>(p.bsrc + off), f);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] *= sc[i];
-        *reinterpret_cast<uint4*>(p.bdst + off) = f_to_h8(f);
+    for (int u = 0; u < kFold; ++u) {
+        if (tid + u * kThreads < p.b_rows) {
+            float f[8];
+            h8_to_f(bv[u], f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] *= sc[i];
+            *reinterpret_cast<uint4*>(p.bdst + boff[u]) = f_to_h8(f);
+        }
     }
 }
 
@@ -255,6 +278,8 @@ int launch_sca_v(const DwParams& p, int nb, cudaStream_t s) {
 int launch_sca(const DwParams& p, int nb, cudaStream_t s) {
     if (p.D % 4 != 0 || p.D > 32 * 4 * kScaVec)
         return dn_fail(DN_ERR_UNSUPPORTED, "sca: channels must be a multiple of 4 and <= 1024");
+    if (p.bdst && p.b_rows > 4 * kThreads)
+        return dn_fail(DN_ERR_UNSUPPORTED, "sca: conv3 has more than 1024 output channels");
     const int nvec = p.D / 4;
     if (nvec <= 32) return launch_sca_v<1>(p, nb, s);
     if (nvec <= 64) return launch_sca_v<2>(p, nb, s);
