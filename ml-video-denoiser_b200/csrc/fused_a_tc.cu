@@ -641,30 +641,91 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
             __syncthreads();
             if (s_last) {
                 __threadfence();
-                float* s_mean = sPool;      // [D]
-                float* s_scale = sPool + D;  // [D]
+                // Every phase issues all of its loads before it uses any (a
+                // few memory latencies in all): the constant SCA weights and
+                // conv3 B chunks first, then the CTAs' pool rows.
+                constexpr int kWarps = kTcThreads / 32;
+                constexpr int kOut = (D + kWarps - 1) / kWarps;  // SCA outputs per warp
+                constexpr int kCol = D / 32;                     // weight columns per lane
+                constexpr int KQ = D / 8;                        // 16-byte chunks per B row
+                constexpr int kChunks = C * KQ;
+                constexpr int kPer = (kChunks + kTcThreads - 1) / kTcThreads;
+                float wv[kOut][kCol], bo[kOut];
+#pragma unroll
+                for (int j = 0; j < kOut; ++j) {
+                    const int o = warp + kWarps * j;
+                    bo[j] = o < D ? __ldg(p.sca_b + o) : 0.f;
+#pragma unroll
+                    for (int i = 0; i < kCol; ++i) wv[j][i] = o < D ? __ldg(p.sca_w + o * D + lane + 32 * i) : 0.f;
+                }
+                uint4 bv[kPer];
+#pragma unroll
+                for (int u = 0; u < kPer; ++u) {
+                    const int i = tid + u * kTcThreads;
+                    const int n = i / KQ, q = i - n * KQ;
+                    bv[u] = i < kChunks ? __ldg(reinterpret_cast<const uint4*>(
+                                              p.b3_src + static_cast<size_t>(n >> 3) * (KQ * 128) + q * 128 + (n & 7) * 16))
+                                        : make_uint4(0, 0, 0, 0);
+                }
+                // Fixed-order pool: thread (stripe, c) sums rows stripe,
+                // stripe + stripes, ... of channel c; stripes add in order.
+                constexpr int kStripes = kTcThreads / D;  // <= 16 (sPool holds 32 D floats)
+                constexpr int kPool = 16;
+                float* s_red = sPool;                     // [kStripes][D]
+                float* s_mean = sPool + 16 * D;           // [D]
+                float* s_scale = s_mean + D;              // [D]
+                const unsigned nb = gridDim.x;
+                {
+                    const int c = tid % D, st = tid / D;
+                    if (st < kStripes) {
+                        float sum = 0.f;
+                        for (unsigned r0 = st; r0 < nb; r0 += kPool * kStripes) {
+                            float v[kPool];
+#pragma unroll
+                            for (int u = 0; u < kPool; ++u) {
+                                const unsigned r = min(r0 + u * kStripes, nb - 1);  // past the end: not added
+                                v[u] = __ldcg(p.partials + static_cast<size_t>(r) * D + c);
+                            }
+#pragma unroll
+                            for (int u = 0; u < kPool; ++u)
+                                if (r0 + u * kStripes < nb) sum += v[u];
+                        }
+                        s_red[st * D + c] = sum;
+                    }
+                }
+                __syncthreads();
                 const float inv = 1.0f / (static_cast<float>(p.H) * p.W);
                 for (int c = tid; c < D; c += kTcThreads) {
                     float sum = 0.f;
-                    for (unsigned r = 0; r < gridDim.x; ++r) sum += __ldcg(p.partials + static_cast<size_t>(r) * D + c);
+                    for (int st = 0; st < kStripes; ++st) sum += s_red[st * D + c];
                     s_mean[c] = sum * inv;
                 }
                 __syncthreads();
-                for (int o = tid; o < D; o += kTcThreads) {
-                    float v = p.sca_b[o];
-                    for (int c = 0; c < D; ++c) v = fmaf(p.sca_w[o * D + c], s_mean[c], v);
-                    s_scale[o] = v;
+                // s = W mean + b: warp w evaluates outputs w, w + kWarps, ...
+#pragma unroll
+                for (int j = 0; j < kOut; ++j) {
+                    const int o = warp + kWarps * j;
+                    float acc = 0.f;
+#pragma unroll
+                    for (int i = 0; i < kCol; ++i) acc = fmaf(wv[j][i], s_mean[lane + 32 * i], acc);
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+                    if (lane == 0 && o < D) s_scale[o] = acc + bo[j];
                 }
                 __syncthreads();
-                constexpr int KQ = D / 8;  // 16-byte chunks per B row
-                for (int i = tid; i < C * KQ; i += kTcThreads) {
-                    const int n = i / KQ, q = i - n * KQ;
-                    const size_t off = static_cast<size_t>(n >> 3) * (KQ * 128) + q * 128 + (n & 7) * 16;
-                    float f[8];
-                    h8_to_f(*reinterpret_cast<const uint4*>(p.b3_src + off), f);
+                // conv3's B columns scaled by s.
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) f[j] *= s_scale[8 * q + j];
-                    *reinterpret_cast<uint4*>(p.b3_dst + off) = f_to_h8(f);
+                for (int u = 0; u < kPer; ++u) {
+                    const int i = tid + u * kTcThreads;
+                    if (i < kChunks) {
+                        const int n = i / KQ, q = i - n * KQ;
+                        float f[8];
+                        h8_to_f(bv[u], f);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) f[j] *= s_scale[8 * q + j];
+                        *reinterpret_cast<uint4*>(p.b3_dst + static_cast<size_t>(n >> 3) * (KQ * 128) + q * 128 +
+                                                  (n & 7) * 16) = f_to_h8(f);
+                    }
                 }
                 if (tid == 0) *p.counter = 0u;
             }
