@@ -140,8 +140,9 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
     const int img = blockIdx.y;
     const int nvec = D / 4;
     pdl_trigger();
-    // The weight row of this warp's output (constant) loads before the wait.
+    // The weight row and bias of this warp's output (constant) load before the wait.
     const int o = blockIdx.x * 8 + warp;  // 8 warps -> 8 outputs
+    const float bias_o = o < D ? p.sca_b[o] : 0.f;
     float4 w[kScaVec];
 #pragma unroll
     for (int i = 0; i < kScaVec; ++i) {
@@ -228,8 +229,8 @@ __global__ void __launch_bounds__(kThreads) sca_kernel(const __grid_constant__ D
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (lane == 0) p.s_out[static_cast<size_t>(img) * D + o] = s + p.sca_b[o];
-        if (lane == 0) red[warp] = s + p.sca_b[o];  // red[] is no longer read: keep this CTA's s there
+        if (lane == 0) p.s_out[static_cast<size_t>(img) * D + o] = s + bias_o;
+        if (lane == 0) red[warp] = s + bias_o;  // red[] is no longer read: keep this CTA's s there
     }
     if (!fold) return;
     // Fold s[8j .. 8j+8) into the conv3 B columns of this CTA's 8 channels
