@@ -44,6 +44,42 @@ def test_oracle_wiring_statistics(pkg, tmp_path):
     assert 0.35 <= float(msk.mean()) <= 0.65 and float(msk.std()) >= 0.1
 
 
+def test_oracle_wiring_matches_torchvision_composition(pkg, tmp_path):
+    """The oracle's composition equals the same wiring built from torch's
+    conv2d and torchvision's deform_conv2d (third-party DCNv2, mask = sigmoid
+    of the raw masks, offsets [dy, dx] per (group, tap)) on the synthetic
+    window (CPU). The offsets come from a conv of noisy features, so no sample
+    lands exactly on the integer border positions where the two bilinear rules
+    differ; measured agreement is ~2e-7."""
+    tv = pytest.importorskip("torchvision")
+    import torch.nn.functional as F
+
+    synth = synth_mod(pkg)
+    _, pa = synth.make_align_dir(str(tmp_path / "align"), 5, num_frames=5)
+    _, pt = synth.make_model_dir(str(tmp_path / "trunk"), synth.CONFIG_TINY_W16, 5)
+    clip = torch.from_numpy(synth.temporal_window(5, 32, 48, 5))
+    pa_t, pt_t = O.as_torch(pa), O.as_torch(pt)
+    torch.set_num_threads(min(16, os.cpu_count() or 1))
+    ref, _ = O.aligned_temporal_forward(pa_t, pt_t, clip)
+
+    conv = lambda k, x, pad: F.conv2d(x, pa_t[k + ".weight"], pa_t[k + ".bias"], padding=pad)  # noqa: E731
+    t, c = 5, 2
+    feats = [conv("align.feat", clip[:, i], 1) for i in range(t)]
+    n_off = 2 * synth.ALIGN_DG * 9
+    aligned = []
+    for i in range(t):
+        if i == c:
+            aligned.append(feats[c])
+            continue
+        om = conv("align.offset", torch.cat([feats[c], feats[i]], 1), 1)
+        aligned.append(tv.ops.deform_conv2d(feats[i], om[:, :n_off], pa_t["align.dcn.weight"], pa_t["align.dcn.bias"],
+                                            padding=(1, 1), mask=torch.sigmoid(om[:, n_off:])))
+    fused = conv("align.fuse", torch.cat(aligned, 1), 0) + clip[:, c]
+    out = O.nafnet_forward(pt_t, fused)
+    err = float((out - ref).abs().max())
+    assert err <= 1e-4, err
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("h,w", [(64, 96), (50, 70)], ids=["64x96", "50x70"])
 def test_aligned_w32_matches_oracle(pkg, tmp_path, h, w):
