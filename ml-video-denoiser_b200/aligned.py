@@ -19,12 +19,19 @@ buffers (channel slices of a batch-1 NCHW tensor are contiguous).
 Weights: manifest keys ``align.{feat,offset,dcn,fuse}.{weight,bias}`` in the
 reference format (``manifest.json`` + ``.bin``), architecture ``num_frames``
 = T; the trunk is a separate NAFNet manifest.
+
+Size limit: the fusion conv reads the T*F-channel concatenation, and a
+Conv2dLayer input holds at most 2^31 elements, so T*F*H*W <= 2^31 (T = 5,
+F = 64: frames up to about 6.7 M pixels, e.g. 1080p but not 2160x3840).
+Larger frames are rejected before any kernel is launched.
 """
 from __future__ import annotations
 
 from . import DN_ERR_INVALID_ARG, InvalidArgumentError, Model, Weights
 from .kernels import launch_add, launch_extract_frame
 from .layers import Conv2d, DeformConv2d
+
+MAX_LAYER_ELEMS = 1 << 31  # Conv2dLayer input limit (dn_conv2d_forward)
 
 
 class AlignedTemporal:
@@ -62,6 +69,9 @@ class AlignedTemporal:
                                        f"AlignedTemporal: expected (1, {self.num_frames}, {self.in_channels}, H, W)")
         t, cin, h, w = clip.shape[1:]
         f, c = self.feat_channels, t // 2
+        if t * f * h * w > MAX_LAYER_ELEMS:
+            raise InvalidArgumentError(DN_ERR_INVALID_ARG,
+                                       f"AlignedTemporal: {t}x{f}x{h}x{w} fusion input exceeds 2^31 elements")
         dev = clip.device
         s = stream if stream is not None else torch.cuda.current_stream(dev)
         # Temporaries come from the launch stream's pool, so their reuse after

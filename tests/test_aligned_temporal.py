@@ -114,6 +114,19 @@ def test_aligned_repeat_and_side_stream(pkg, tmp_path):
     model.close()
 
 
+def test_aligned_rejects_frames_beyond_the_layer_limit(pkg):
+    """A window whose fusion input (T*F*H*W) exceeds 2^31 elements is rejected
+    on the host before any kernel (2160x3840 at T = 5, F = 64). Host logic
+    only: the instance skips layer construction and the clip is a meta tensor."""
+    aligned = importlib.import_module(pkg.__name__ + ".aligned")
+    m = aligned.AlignedTemporal.__new__(aligned.AlignedTemporal)
+    m.num_frames, m.in_channels, m.feat_channels = 5, 3, 64
+    clip = torch.empty(1, 5, 3, 2160, 3840, dtype=torch.float16, device="meta")
+    with pytest.raises(ValueError, match="2\\^31"):
+        m(clip)
+    assert 5 * 64 * 1088 * 1920 <= aligned.MAX_LAYER_ELEMS  # 1080p windows stay within it
+
+
 @pytest.mark.gpu
 def test_aligned_rejects_bad_windows(pkg, tmp_path):
     synth = synth_mod(pkg)
