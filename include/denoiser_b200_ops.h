@@ -89,7 +89,10 @@ int dn_launch_global_avg_pool(const void* input, void* output, int N, int C, int
  *     any N*C <= 2048 fits; larger sizes return DN_ERR_UNSUPPORTED;
  *   - the first call on each device (with that device current) looks up the
  *     array's device address once; make that first call before any stream
- *     capture begins;
+ *     capture begins. The looked-up address is kept for the life of the
+ *     process and does not survive cudaDeviceReset: do not call this entry
+ *     point on a device after resetting it;
+ *   - a size beyond the limit is rejected on the host before any CUDA call;
  *   - the array is shared by every call on the device: calls whose work may
  *     overlap on the GPU (different streams without an event between them,
  *     or concurrent host threads) race on it and give wrong means. Order

@@ -144,7 +144,6 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant
     __shared__ uint32_t tslot;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    pdl_trigger();
     for (int i = tid; i < NT; i += kThreads) sBias[i] = p.bias[i];
     if (warp == 0) {
         tmem_alloc(&tslot, kCols);
@@ -161,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    pdl_trigger();  // only once this CTA holds its TMEM columns
     pdl_wait();
 
     const int HWo = p.Ho * p.Wo;

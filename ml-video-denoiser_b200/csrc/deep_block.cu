@@ -121,7 +121,6 @@ __global__ void __launch_bounds__(kDThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tiles = (p.M + 127) / 128;
 
-    pdl_trigger();
     for (int i = tid; i < C; i += kDThreads) {
         sB3[i] = p.b3[i];
         sBeta[i] = p.beta[i];
@@ -161,6 +160,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    pdl_trigger();  // only once this CTA holds its TMEM columns
     pdl_wait();  // g, x and the SCA-scaled conv3 image come from earlier kernels
 
     if (warp == 0 || warp >= 10) {

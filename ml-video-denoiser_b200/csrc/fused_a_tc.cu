@@ -194,7 +194,6 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
     const long long T = static_cast<long long>(p.N) * strips * out_h;
     const long long u0 = T * blockIdx.x / gridDim.x, u1 = T * (blockIdx.x + 1) / gridDim.x;
 
-    pdl_trigger();
     for (int i = tid; i < 16 * N; i += kTcThreads) {
         const int cls = i / N, o = i - cls * N;
         if constexpr (MODE == 0) {
@@ -238,6 +237,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    pdl_trigger();  // only once this CTA holds its TMEM columns
     pdl_wait();  // x was written by the previous kernel; g and the partials are read by it
 
     Seg sg;

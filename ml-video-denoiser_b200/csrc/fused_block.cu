@@ -139,7 +139,6 @@ __global__ void __launch_bounds__(kAThreads, 2)
         tx0 = (r % tiles_x) * G::TW;
     };
 
-    pdl_trigger();
     for (int i = tid; i < G::N1; i += kAThreads) sC2[i] = p.c2[i];
     for (int i = tid; i < 8 * D; i += kAThreads) sPart[i] = 0.f;
     if (warp == 0) {
@@ -159,6 +158,7 @@ __global__ void __launch_bounds__(kAThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    pdl_trigger();  // only once this CTA holds its TMEM columns
     const uint64_t da1 = sdesc_kmajor_sw(smem_u32(sA), G::ROWB);
     const uint64_t db1 = sdesc_kmajor(smem_u32(sW1), 128, (C / 8) * 128);
     pdl_wait();  // x was written by the previous kernel
@@ -433,7 +433,6 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
         sB5[i] = p.b5[i];
         sGam[i] = p.gamma[i];
     }
-    pdl_trigger();
     for (int i = tid; i < 2 * F; i += kTh) sB4[i] = p.b4[i];
     if (warp == 0) {
         tmem_alloc(&tslot, G::TMEM_COLS);
@@ -454,6 +453,7 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    pdl_trigger();  // only once this CTA holds its TMEM columns
     const uint64_t d3a = sdesc_kmajor_sw(smem_u32(sG), 2 * D), d3b = sdesc_kmajor(smem_u32(sW3), 128, (D / 8) * 128);
     const uint64_t d4a = sdesc_kmajor_sw(smem_u32(sA2), 2 * C), d4b = sdesc_kmajor(smem_u32(sW4), 128, (C / 8) * 128);
     const uint64_t d5a = sdesc_kmajor_sw(smem_u32(sA3), 2 * F), d5b = sdesc_kmajor(smem_u32(sW5), 128, (F / 8) * 128);

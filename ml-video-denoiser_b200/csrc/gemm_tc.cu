@@ -163,7 +163,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_tiles_total = m_tiles * p.n_tiles;
     const bool one_img = p.M <= p.hw;
 
-    pdl_trigger();
     // Parameter vectors -> shared memory (c2 of the LN fold lives in s_bias).
     for (int i = tid; i < p.n_tiles * NT; i += kThreads) {
         s_bias[i] = p.bias ? p.bias[i] : 0.f;
@@ -195,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
+    pdl_trigger();  // only once this CTA holds its TMEM columns
     // Everything above touched only weights; activations (A, the residual,
     // the SCA scale) were written by earlier kernels.
     pdl_wait();

@@ -9,6 +9,14 @@
 // its first global write; pdl_wait() returns once the preceding kernel has
 // completed and its writes are visible (so ordering stays transitive along
 // the stream).
+//
+// Order rule for kernels that allocate TMEM: tcgen05.alloc, the permit
+// relinquish and the barrier that publishes the TMEM address all come
+// BEFORE pdl_trigger(). A dependent grid can then only be scheduled once
+// every CTA of this grid already holds its columns. Were the trigger first,
+// a dependent CTA could take an SM's free columns while this grid's CTA on
+// that SM still waits in tcgen05.alloc (which has no timeout); the dependent
+// would then wait in griddepcontrol.wait for a grid that cannot finish.
 #pragma once
 
 #include <cuda_runtime.h>

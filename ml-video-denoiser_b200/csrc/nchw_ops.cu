@@ -575,7 +575,10 @@ std::mutex g_pool_scratch_mu;
 float* g_pool_scratch_ptr[64];  // device address of g_pool_scratch, per device ordinal
 
 // Device address of g_pool_scratch on the calling thread's current device,
-// looked up (cudaGetSymbolAddress) by the first call on that device.
+// looked up (cudaGetSymbolAddress) by the first call on that device. The
+// cached address lives as long as the device's primary context: after a
+// cudaDeviceReset the module is loaded again and the address may change, so
+// a process that resets a device must not call the no-alloc pool on it again.
 int pool_scratch(float** out, const char* name) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -793,14 +796,16 @@ int dn_launch_global_avg_pool_noalloc(const void* input, void* output, int N, in
     DN_TRY(pool_check(input, output, N, C, H, W, name));
     const PoolPlan pp = pool_plan(input, N, C, H, W);
     if (pp.planes == 0) return DN_OK;
-    float* scratch = nullptr;
-    DN_TRY(pool_scratch(&scratch, name));
+    // The size rule is checked on the host before any CUDA call, so a
+    // rejected size touches neither the device nor the runtime.
     const int64_t need = pp.planes * pp.splits;
     if (need > kNoAllocPoolFloats)
         return dn_fail_str(DN_ERR_UNSUPPORTED,
                            std::string(name) + ": N*C*splits = " + std::to_string(need) +
                                " split sums exceed the static scratch of " + std::to_string(kNoAllocPoolFloats) +
                                " floats (splits = min(128, ceil(H*W / 16384)))");
+    float* scratch = nullptr;
+    DN_TRY(pool_scratch(&scratch, name));
     return pool_launch(pp, input, output, scratch, to_stream(stream), name);
 }
 
