@@ -192,6 +192,34 @@ def cpu_baseline_fps(synth, cfg, h, w, threads: int) -> tuple[float, str]:
     return 1.0 / dt, f"1 frame {h}x{w} fp32 after a 256x256 warm-up frame ({dt:.1f} s)"
 
 
+REF_ENGINE = os.path.join(ROOT, "oracle", "_ref", "ref_engine")
+
+
+def ref_cuda_engine(path: str, x: np.ndarray, reps: int = 5) -> dict | None:
+    """The reference's own C++ FP16 engine (NAFNet::forward with cuDNN/cuBLAS,
+    built unchanged from its sources into oracle/_ref by oracle/Makefile) on
+    the same weights and frame on this GPU: mean ms per forward over `reps`
+    forwards between CUDA events, after one untimed forward. None when the
+    harness is not built."""
+    if not os.path.exists(REF_ENGINE):
+        return None
+    with tempfile.TemporaryDirectory() as tmp:
+        xin, out = os.path.join(tmp, "x.f16"), os.path.join(tmp, "y.f16")
+        np.ascontiguousarray(x.astype(np.float16)).tofile(xin)
+        n, c, h, w = x.shape
+        try:
+            r = subprocess.run([REF_ENGINE, "nafnet", path, xin, str(n), str(c), str(h), str(w), out, str(reps)],
+                               capture_output=True, text=True, timeout=600)
+        except subprocess.TimeoutExpired:
+            return {"unavailable": "reference engine timed out"}
+    if r.returncode != 0:
+        return {"unavailable": r.stderr.strip()[-300:]}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    return {"ms_per_frame": d["ms"], "frames_per_s": 1000.0 / d["ms"], "reps": d["reps"],
+            "sample": f"NAFNet::forward of the reference C++ engine (cuDNN 9 + cuBLAS, FP16), {h}x{w}, "
+                      f"same weights and frame, mean of {reps} after 1 untimed"}
+
+
 def run_reference(args, rank: int) -> None:
     if rank != 0:
         return
@@ -207,6 +235,9 @@ def run_reference(args, rank: int) -> None:
         v, sample = cpu_baseline_fps(synth, cfg, args.height, args.width, threads)
         vals.append(v)
     v = statistics.median(vals)
+    with tempfile.TemporaryDirectory() as tmp:
+        path, _ = synth.make_model_dir(tmp, cfg, seed=1)
+        ref_cuda = ref_cuda_engine(path, synth.w32_frame(args.height, args.width, seed=1))
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": args.gpus,
             "steps": len(vals), "warmup": 1, "ms_per_step": 1000.0 / v, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
@@ -215,6 +246,8 @@ def run_reference(args, rank: int) -> None:
             "cpu_baseline": {"value": v, "unit": "frames/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if ref_cuda is not None:
+        line["reference_cuda_engine"] = ref_cuda
     print(json.dumps(line), flush=True)
 
 
@@ -227,6 +260,7 @@ def main() -> None:
     ap.add_argument("--height", type=int, default=1080)
     ap.add_argument("--width", type=int, default=1920)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-engine", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -392,6 +426,10 @@ def main() -> None:
     }
     if cpu:
         line["cpu_baseline"] = cpu
+    if world == 1 and not args.no_ref_engine:
+        ref_cuda = ref_cuda_engine(path, base[0])
+        if ref_cuda is not None:
+            line["reference_cuda_engine"] = ref_cuda
     print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
