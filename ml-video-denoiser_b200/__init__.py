@@ -124,6 +124,15 @@ SIGNATURES = {
     "dn_conv2d_output_size": (_I, [_P, _I, _I, _IP, _IP]),
     "dn_conv2d_forward": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
     "dn_conv2d_sync": (_I, [_P, _P]),
+    # include/denoiser_b200_aligned.h
+    "dn_aligned_create": (_I, [_c.c_char_p, _c.c_char_p, _I, _PP]),
+    "dn_aligned_destroy": (_I, [_P]),
+    "dn_aligned_info": (_I, [_P, _IP, _IP, _IP, _IP]),
+    "dn_aligned_encode_frame": (_I, [_P, _P, _I, _I, _I, _P]),
+    "dn_aligned_align_window": (_I, [_P, _IP, _I, _P, _P]),
+    "dn_aligned_decode_window": (_I, [_P, _IP, _I, _P, _P]),
+    "dn_aligned_forward": (_I, [_P, _P, _I, _I, _P, _P]),
+    "dn_aligned_sync": (_I, [_P, _P]),
 }
 
 

@@ -45,6 +45,7 @@
 #include <vector>
 
 #include "capi_internal.h"
+#include "conv_internal.h"
 #include "denoiser_b200_layers.h"
 #include "launch.cuh"
 #include "sm100.cuh"
@@ -57,11 +58,26 @@ constexpr int kThreads = 256;
 constexpr int kKC = 64;                   // K chunk (one 128-byte swizzled row)
 constexpr int kABytes = 128 * kKC * 2;    // 16 KB
 
+// Output modes of the epilogue.
+enum : int {
+    kOutNCHW = 0,  // out[n][o][y][x]
+    kOutNHWC = 1,  // out[n][y][x][o] (a feature map that a later conv reads without a transpose)
+    kOutFuse = 2,  // no activation store: the 1x1 fusion of the output channels (below)
+};
+
 struct DcnParams {
     const __half* xt;    // input, NHWC [N][H][W][Cin]
     const __half* off;   // [N][2*dg*KK][Ho][Wo] (dy, dx per (group, tap))
     const __half* msk;   // [N][dg*KK][Ho][Wo] (pre-sigmoid)
-    __half* out;         // [N][Cout][Ho][Wo]
+    const __half* off2;  // optional second term of the offsets (same layout; summed in FP32), or null
+    const __half* msk2;  // optional second term of the raw masks, or null
+    __half* out;         // kOutNCHW: [N][Cout][Ho][Wo]; kOutNHWC: [N][Ho][Wo][Cout]
+    int out_mode;
+    // kOutFuse (batch 1): fuse_acc[j][pix] += sum_o fuse_w[j][o] * (acc[o] + bias[o]) for j < 3
+    // (FP32 planes); with fuse_out set, the sum is written there as FP16 NCHW planes instead.
+    const float* fuse_w;   // [3][NT]
+    float* fuse_acc;       // [3][Ho*Wo]
+    __half* fuse_out;      // [3][Ho*Wo] or null
     const uint8_t* bpack;  // [k_chunks][NT x 64] no-swizzle K-major tiles (this launch's output slab)
     const float* bias;     // [NT] (zero padded)
     int N, H, W, Ho, Wo, Cin, Cout;
@@ -141,6 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant
     uint8_t* sB[2] = {smem + 2 * kABytes, smem + 2 * kABytes + kBBytes};
     float* sBias = reinterpret_cast<float*>(smem + 2 * kABytes + 2 * kBBytes);
     __shared__ uint64_t bar_b[2], bar_mma[2];
+    __shared__ float sFuse[3][128];  // kOutFuse: the second column half's partial sums per tile row
     __shared__ uint32_t tslot;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -221,9 +238,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant
                     const int g = gk / p.KK, k = gk - g * p.KK;
                     const int ki = k / p.kw, kj = k - ki * p.kw;
                     const size_t ob = (static_cast<size_t>(n) * 2 * combos + 2 * gk) * HWo + pix;
-                    const float dy = __half2float(p.off[ob]);
-                    const float dx = __half2float(p.off[ob + HWo]);
-                    const float raw = __half2float(p.msk[(static_cast<size_t>(n) * combos + gk) * HWo + pix]);
+                    const size_t mb = (static_cast<size_t>(n) * combos + gk) * HWo + pix;
+                    float dy = __half2float(p.off[ob]);
+                    float dx = __half2float(p.off[ob + HWo]);
+                    float raw = __half2float(p.msk[mb]);
+                    if (p.off2) {  // offsets and masks given as two terms (uniform branch)
+                        dy += __half2float(p.off2[ob]);
+                        dx += __half2float(p.off2[ob + HWo]);
+                        raw += __half2float(p.msk2[mb]);
+                    }
                     const float mask = 1.f / (1.f + expf(-raw));
                     const float hs = static_cast<float>(ho * p.stride - p.pad + ki * p.dil) + dy;
                     const float ws = static_cast<float>(wo * p.stride - p.pad + kj * p.dil) + dx;
@@ -310,16 +333,62 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant
             const int c_lo = NT >= 32 ? half * (NT / 2) : (half == 0 ? 0 : NT);
             const int c_hi = NT >= 32 ? c_lo + NT / 2 : (half == 0 ? NT : NT);
             const int n = m / HWo, pix = m - n * HWo;
-            __half* orow = p.out + (static_cast<size_t>(n) * p.Cout + p.cout_base) * HWo + pix;
             const int cmax = p.Cout - p.cout_base;  // channels of this slab that exist
-            for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-                float v[16];
-                tmem_ld16(tmem + c0 + (static_cast<uint32_t>(q4 * 32) << 16), v);
-                tmem_ld_wait();
-                if (m < M) {
+            if (p.out_mode == kOutFuse) {
+                // 1x1 fusion of this row's output channels into three planes.
+                float f3[3] = {0.f, 0.f, 0.f};
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(tmem + c0 + (static_cast<uint32_t>(q4 * 32) << 16), v);
+                    tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        if (c0 + e < cmax) orow[static_cast<size_t>(c0 + e) * HWo] = __float2half(v[e] + sBias[c0 + e]);
+                    for (int e = 0; e < 16; ++e) {
+                        if (c0 + e < cmax) {
+                            const float a = v[e] + sBias[c0 + e];
+#pragma unroll
+                            for (int j = 0; j < 3; ++j) f3[j] = fmaf(p.fuse_w[j * NT + c0 + e], a, f3[j]);
+                        }
+                    }
+                }
+                if (half) {
+#pragma unroll
+                    for (int j = 0; j < 3; ++j) sFuse[j][r] = f3[j];
+                }
+                __syncthreads();
+                if (!half && m < M) {
+#pragma unroll
+                    for (int j = 0; j < 3; ++j) {
+                        const size_t at = static_cast<size_t>(j) * HWo + pix;
+                        const float tot = p.fuse_acc[at] + (f3[j] + sFuse[j][r]);
+                        if (p.fuse_out)
+                            p.fuse_out[at] = __float2half(tot);
+                        else
+                            p.fuse_acc[at] = tot;
+                    }
+                }
+            } else if (p.out_mode == kOutNHWC) {
+                __half* orow = p.out + static_cast<size_t>(m) * p.Cout + p.cout_base;
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(tmem + c0 + (static_cast<uint32_t>(q4 * 32) << 16), v);
+                    tmem_ld_wait();
+                    if (m < M) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            if (c0 + e < cmax) orow[c0 + e] = __float2half(v[e] + sBias[c0 + e]);
+                    }
+                }
+            } else {
+                __half* orow = p.out + (static_cast<size_t>(n) * p.Cout + p.cout_base) * HWo + pix;
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(tmem + c0 + (static_cast<uint32_t>(q4 * 32) << 16), v);
+                    tmem_ld_wait();
+                    if (m < M) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            if (c0 + e < cmax) orow[static_cast<size_t>(c0 + e) * HWo] = __float2half(v[e] + sBias[c0 + e]);
+                    }
                 }
             }
         }
@@ -426,14 +495,120 @@ struct DevGuard {
 
 }  // namespace
 
+namespace dnb {
+
+int dcn_build(const float* w, const float* bias, int cout, int cin, int kh, int kw, int pad, int stride, int dilation,
+              int deform_groups, int device, dn_dcn** out) {
+    *out = nullptr;
+    if (pad < 0 || stride <= 0 || dilation <= 0 || deform_groups <= 0 || cout <= 0 || cin <= 0 || kh <= 0 || kw <= 0)
+        return dn_fail(DN_ERR_INVALID_ARG, "dn_dcn_create: bad pad/stride/dilation/deform_groups");
+    auto L = std::make_unique<dn_dcn>();
+    L->device = device;
+    L->cout = cout;
+    L->cin = cin;
+    L->kh = kh;
+    L->kw = kw;
+    L->pad = pad;
+    L->stride = stride;
+    L->dil = dilation;
+    L->dg = deform_groups;
+    if (L->cin % deform_groups != 0)
+        return dn_fail(DN_ERR_INVALID_ARG, "dn_dcn_create: in_channels must be divisible by deform_groups");
+    L->cpg = L->cin / deform_groups;
+    if (kKC % L->cpg != 0) return dn_fail(DN_ERR_UNSUPPORTED, "dn_dcn_create: channels per deform group must divide 64");
+    if (L->cout > 256) return dn_fail(DN_ERR_UNSUPPORTED, "dn_dcn_create: out_channels > 256");
+    L->NT = std::max(16, next_pow2(L->cout));
+    const int KK = L->kh * L->kw;
+    const int K = deform_groups * KK * L->cpg;
+    L->k_chunks = (K + kKC - 1) / kKC;
+    // B tiles: K index = (g*KK + k)*cpg + c, no-swizzle K-major core matrices.
+    const size_t tile = static_cast<size_t>(L->NT) * kKC * 2;
+    std::vector<uint8_t> pk(tile * L->k_chunks, 0);
+    for (int o = 0; o < L->cout; ++o)
+        for (int g = 0; g < deform_groups; ++g)
+            for (int k = 0; k < KK; ++k)
+                for (int c = 0; c < L->cpg; ++c) {
+                    const int kidx = (g * KK + k) * L->cpg + c;
+                    const float v = w[((static_cast<size_t>(o) * L->cin + g * L->cpg + c) * KK) + k];
+                    const __half h = __float2half(v);
+                    const int j = kidx / kKC, kk = kidx % kKC;
+                    uint8_t* t = pk.data() + j * tile;
+                    const size_t offb = static_cast<size_t>(o >> 3) * 1024 + (kk / 8) * 128 + (o & 7) * 16 + (kk % 8) * 2;
+                    std::memcpy(t + offb, &h, 2);
+                }
+    std::vector<float> b(L->NT, 0.f);
+    if (bias)
+        for (int o = 0; o < L->cout; ++o) b[o] = __half2float(__float2half(bias[o]));
+    DevGuard dg(device);
+    cudaError_t e = cudaMalloc(&L->bpack, pk.size());
+    if (e == cudaSuccess) e = cudaMalloc(&L->bias, b.size() * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&L->err, 4);
+    if (e == cudaSuccess) e = cudaMemcpy(L->bpack, pk.data(), pk.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(L->bias, b.data(), b.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(L->err, 0, 4);
+    if (e != cudaSuccess) {
+        cudaFree(L->bpack);
+        cudaFree(L->bias);
+        cudaFree(L->err);
+        return dn_cuda_fail(e, "dn_dcn_create: upload");
+    }
+    *out = L.release();
+    return DN_OK;
+}
+
+int dcn_run_nhwc(dn_dcn* L, const __half* x_nhwc, const __half* off, const __half* msk, const __half* off2,
+                 const __half* msk2, int N, int H_in, int W_in, void* output, const DcnFuse* fuse, cudaStream_t s) {
+    int Ho = 0, Wo = 0;
+    dn_dcn_output_size(L, H_in, W_in, &Ho, &Wo);
+    if (Ho <= 0 || Wo <= 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_dcn_forward: output would be empty");
+    if (fuse && (N != 1 || L->cout > L->NT)) return dn_fail(DN_ERR_UNSUPPORTED, "dcn fusion epilogue: batch 1 only");
+    if ((off2 == nullptr) != (msk2 == nullptr))
+        return dn_fail(DN_ERR_INVALID_ARG, "dcn: second offset and mask terms come together");
+    DcnParams p{};
+    p.xt = x_nhwc;
+    p.off = off;
+    p.msk = msk;
+    p.off2 = off2;
+    p.msk2 = msk2;
+    p.out = static_cast<__half*>(output);
+    p.out_mode = fuse ? kOutFuse : kOutNCHW;
+    if (fuse) {
+        p.fuse_w = fuse->w;
+        p.fuse_acc = fuse->acc;
+        p.fuse_out = fuse->out16;
+    }
+    p.bpack = L->bpack;
+    p.bias = L->bias;
+    p.N = N;
+    p.H = H_in;
+    p.W = W_in;
+    p.Ho = Ho;
+    p.Wo = Wo;
+    p.Cin = L->cin;
+    p.Cout = L->cout;
+    p.kw = L->kw;
+    p.KK = L->kh * L->kw;
+    p.pad = L->pad;
+    p.stride = L->stride;
+    p.dil = L->dil;
+    p.dg = L->dg;
+    p.cpg = L->cpg;
+    p.k_chunks = L->k_chunks;
+    p.err = L->err;
+    p.cout_base = 0;
+    return run_conv_nt<true>(p, L->NT, L->device, s);
+}
+
+int dcn_nt(const dn_dcn* L) { return L->NT; }
+
+}  // namespace dnb
+
 extern "C" {
 
 int dn_dcn_create(const dn_weights* store, const char* weight_name, const char* bias_name, int pad, int stride,
                   int dilation, int deform_groups, int device, dn_dcn** out) {
     if (!store || !weight_name || !out) return dn_fail(DN_ERR_INVALID_ARG, "dn_dcn_create: null argument");
     *out = nullptr;
-    if (pad < 0 || stride <= 0 || dilation <= 0 || deform_groups <= 0)
-        return dn_fail(DN_ERR_INVALID_ARG, "dn_dcn_create: bad pad/stride/dilation/deform_groups");
     try {
         const HostWeights& hw = *store->hw;
         if (!hw.contains(weight_name)) return dn_fail_str(DN_ERR_NOT_FOUND, std::string("weight not found: ") + weight_name);
@@ -442,63 +617,15 @@ int dn_dcn_create(const dn_weights* store, const char* weight_name, const char* 
         const auto& sh = hw.entry(weight_name).shape;
         if (sh.size() != 4)
             return dn_fail_str(DN_ERR_FORMAT, "DeformConv2dLayer: weight must be 4-D, got " + std::to_string(sh.size()) + "-D");
-        auto L = std::make_unique<dn_dcn>();
-        L->device = device;
-        L->cout = static_cast<int>(sh[0]);
-        L->cin = static_cast<int>(sh[1]);
-        L->kh = static_cast<int>(sh[2]);
-        L->kw = static_cast<int>(sh[3]);
-        L->pad = pad;
-        L->stride = stride;
-        L->dil = dilation;
-        L->dg = deform_groups;
-        if (L->cin % deform_groups != 0)
-            return dn_fail(DN_ERR_INVALID_ARG, "dn_dcn_create: in_channels must be divisible by deform_groups");
-        L->cpg = L->cin / deform_groups;
-        if (kKC % L->cpg != 0)
-            return dn_fail(DN_ERR_UNSUPPORTED, "dn_dcn_create: channels per deform group must divide 64");
-        if (L->cout > 256) return dn_fail(DN_ERR_UNSUPPORTED, "dn_dcn_create: out_channels > 256");
-        L->NT = std::max(16, next_pow2(L->cout));
-        const int KK = L->kh * L->kw;
-        const int K = deform_groups * KK * L->cpg;
-        L->k_chunks = (K + kKC - 1) / kKC;
-        // B tiles: K index = (g*KK + k)*cpg + c, no-swizzle K-major core matrices.
         const auto w = hw.to_f32(weight_name);
-        const size_t tile = static_cast<size_t>(L->NT) * kKC * 2;
-        std::vector<uint8_t> pk(tile * L->k_chunks, 0);
-        for (int o = 0; o < L->cout; ++o)
-            for (int g = 0; g < deform_groups; ++g)
-                for (int k = 0; k < KK; ++k)
-                    for (int c = 0; c < L->cpg; ++c) {
-                        const int kidx = (g * KK + k) * L->cpg + c;
-                        const float v = w[((static_cast<size_t>(o) * L->cin + g * L->cpg + c) * KK) + k];
-                        const __half h = __float2half(v);
-                        const int j = kidx / kKC, kk = kidx % kKC;
-                        uint8_t* t = pk.data() + j * tile;
-                        const size_t offb = static_cast<size_t>(o >> 3) * 1024 + (kk / 8) * 128 + (o & 7) * 16 + (kk % 8) * 2;
-                        std::memcpy(t + offb, &h, 2);
-                    }
-        std::vector<float> b(L->NT, 0.f);
+        std::vector<float> bv;
         if (bias_name) {
-            const auto bv = hw.to_f32(bias_name);
-            if (static_cast<int>(bv.size()) != L->cout) return dn_fail(DN_ERR_FORMAT, "dn_dcn_create: bias size");
-            for (int o = 0; o < L->cout; ++o) b[o] = __half2float(__float2half(bv[o]));
+            bv = hw.to_f32(bias_name);
+            if (static_cast<int64_t>(bv.size()) != sh[0]) return dn_fail(DN_ERR_FORMAT, "dn_dcn_create: bias size");
         }
-        DevGuard dg(device);
-        cudaError_t e = cudaMalloc(&L->bpack, pk.size());
-        if (e == cudaSuccess) e = cudaMalloc(&L->bias, b.size() * 4);
-        if (e == cudaSuccess) e = cudaMalloc(&L->err, 4);
-        if (e == cudaSuccess) e = cudaMemcpy(L->bpack, pk.data(), pk.size(), cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemcpy(L->bias, b.data(), b.size() * 4, cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemset(L->err, 0, 4);
-        if (e != cudaSuccess) {
-            cudaFree(L->bpack);
-            cudaFree(L->bias);
-            cudaFree(L->err);
-            return dn_cuda_fail(e, "dn_dcn_create: upload");
-        }
-        *out = L.release();
-        return DN_OK;
+        return dnb::dcn_build(w.data(), bias_name ? bv.data() : nullptr, static_cast<int>(sh[0]), static_cast<int>(sh[1]),
+                              static_cast<int>(sh[2]), static_cast<int>(sh[3]), pad, stride, dilation, deform_groups,
+                              device, out);
     } catch (const std::exception& ex) {
         return dn_fail_str(DN_ERR_FORMAT, ex.what());
     }
@@ -561,31 +688,8 @@ int dn_dcn_forward(dn_dcn* L, const void* input, const void* offsets, const void
     cudaError_t e = launch_pdl(to_nhwc_kernel, dim3((HW + 31) / 32, (L->cin + 31) / 32, N), dim3(32, 8), 0, s,
                                static_cast<const __half*>(input), L->xt, L->cin, HW);
     if (e != cudaSuccess) return dn_cuda_fail(e, "dn_dcn_forward: transpose launch");
-    DcnParams p{};
-    p.xt = L->xt;
-    p.off = static_cast<const __half*>(offsets);
-    p.msk = static_cast<const __half*>(masks);
-    p.out = static_cast<__half*>(output);
-    p.bpack = L->bpack;
-    p.bias = L->bias;
-    p.N = N;
-    p.H = H_in;
-    p.W = W_in;
-    p.Ho = Ho;
-    p.Wo = Wo;
-    p.Cin = L->cin;
-    p.Cout = L->cout;
-    p.kw = L->kw;
-    p.KK = L->kh * L->kw;
-    p.pad = L->pad;
-    p.stride = L->stride;
-    p.dil = L->dil;
-    p.dg = L->dg;
-    p.cpg = L->cpg;
-    p.k_chunks = L->k_chunks;
-    p.err = L->err;
-    p.cout_base = 0;
-    return run_conv_nt<true>(p, L->NT, L->device, s);
+    return dnb::dcn_run_nhwc(L, L->xt, static_cast<const __half*>(offsets), static_cast<const __half*>(masks), nullptr,
+                             nullptr, N, H_in, W_in, output, nullptr, s);
 }
 
 int dn_dcn_sync(dn_dcn* L, void* stream) {
@@ -620,14 +724,139 @@ struct dn_conv2d {
     uint32_t* err = nullptr;
 };
 
+namespace dnb {
+
+int conv2d_build(const float* w, const float* bias, int cout, int cin_g, int kh, int kw, int pad, int stride,
+                 int dilation, int groups, int device, dn_conv2d** out) {
+    *out = nullptr;
+    if (pad < 0 || stride <= 0 || dilation <= 0 || groups <= 0 || cout <= 0 || cin_g <= 0 || kh <= 0 || kw <= 0)
+        return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_create: bad pad/stride/dilation/groups");
+    auto L = std::make_unique<dn_conv2d>();
+    L->device = device;
+    L->cout = cout;
+    L->cin_g = cin_g;
+    L->kh = kh;
+    L->kw = kw;
+    L->pad = pad;
+    L->stride = stride;
+    L->dil = dilation;
+    L->groups = groups;
+    if (L->cout % groups != 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_create: out_channels % groups != 0");
+    L->cin = L->cin_g * groups;
+    L->cb = kKC;
+    while (L->cin % L->cb != 0) L->cb >>= 1;  // largest power of two dividing Cin and 64
+    L->nblk = L->cin / L->cb;
+    const int KK = L->kh * L->kw;
+    L->k_chunks = (L->cin * KK + kKC - 1) / kKC;
+    L->NT = std::min(256, std::max(16, next_pow2(L->cout)));
+    L->slabs = (L->cout + L->NT - 1) / L->NT;
+    const size_t tile = static_cast<size_t>(L->NT) * kKC * 2;
+    const size_t slab_bytes = tile * L->k_chunks;
+    std::vector<uint8_t> pk(slab_bytes * L->slabs, 0);
+    const int cout_g = L->cout / groups;
+    for (int o = 0; o < L->cout; ++o) {
+        const int sl = o / L->NT, ol = o % L->NT, grp = o / cout_g;
+        for (int cl = 0; cl < L->cin_g; ++cl) {
+            const int ci = grp * L->cin_g + cl;
+            for (int k = 0; k < KK; ++k) {
+                const int kidx = ((ci / L->cb) * KK + k) * L->cb + (ci % L->cb);
+                const __half h = __float2half(w[(static_cast<size_t>(o) * L->cin_g + cl) * KK + k]);
+                const int j = kidx / kKC, kk = kidx % kKC;
+                const size_t offb = static_cast<size_t>(ol >> 3) * 1024 + (kk / 8) * 128 + (ol & 7) * 16 + (kk % 8) * 2;
+                std::memcpy(pk.data() + sl * slab_bytes + j * tile + offb, &h, 2);
+            }
+        }
+    }
+    std::vector<float> b(static_cast<size_t>(L->slabs) * L->NT, 0.f);
+    if (bias)
+        for (int o = 0; o < L->cout; ++o) b[o] = __half2float(__float2half(bias[o]));
+    DevGuard dg(device);
+    cudaError_t e = cudaMalloc(&L->bpack, pk.size());
+    if (e == cudaSuccess) e = cudaMalloc(&L->bias, b.size() * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&L->err, 4);
+    if (e == cudaSuccess) e = cudaMemcpy(L->bpack, pk.data(), pk.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(L->bias, b.data(), b.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(L->err, 0, 4);
+    if (e != cudaSuccess) {
+        cudaFree(L->bpack);
+        cudaFree(L->bias);
+        cudaFree(L->err);
+        return dn_cuda_fail(e, "dn_conv2d_create: upload");
+    }
+    *out = L.release();
+    return DN_OK;
+}
+
+int conv2d_run_nhwc(dn_conv2d* L, const __half* x_nhwc, int N, int H_in, int W_in, void* output, bool out_nhwc,
+                    cudaStream_t s) {
+    int Ho = 0, Wo = 0;
+    dn_conv2d_output_size(L, H_in, W_in, &Ho, &Wo);
+    if (Ho <= 0 || Wo <= 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_forward: output would be empty");
+    DcnParams p{};
+    p.xt = x_nhwc;
+    p.out = static_cast<__half*>(output);
+    p.out_mode = out_nhwc ? kOutNHWC : kOutNCHW;
+    p.N = N;
+    p.H = H_in;
+    p.W = W_in;
+    p.Ho = Ho;
+    p.Wo = Wo;
+    p.Cin = L->cin;
+    p.Cout = L->cout;
+    p.kw = L->kw;
+    p.KK = L->kh * L->kw;
+    p.pad = L->pad;
+    p.stride = L->stride;
+    p.dil = L->dil;
+    p.dg = L->nblk;
+    p.cpg = L->cb;
+    p.k_chunks = L->k_chunks;
+    p.err = L->err;
+    const size_t slab_bytes = static_cast<size_t>(L->NT) * kKC * 2 * L->k_chunks;
+    for (int sl = 0; sl < L->slabs; ++sl) {
+        p.bpack = L->bpack + sl * slab_bytes;
+        p.bias = L->bias + sl * L->NT;
+        p.cout_base = sl * L->NT;
+        DN_TRY(run_conv_nt<false>(p, L->NT, L->device, s));
+    }
+    return DN_OK;
+}
+
+int conv2d_to_nhwc(const __half* in, __half* out, int N, int C, int HW, cudaStream_t s) {
+    cudaError_t e = launch_pdl(to_nhwc_kernel, dim3((HW + 31) / 32, (C + 31) / 32, N), dim3(32, 8), 0, s, in, out, C, HW);
+    return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "NCHW -> NHWC transpose launch");
+}
+
+int conv2d_check(dn_conv2d* L) {
+    uint32_t word = 0;
+    cudaError_t e = cudaMemcpy(&word, L->err, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return dn_cuda_fail(e, "conv error word");
+    if (word) {
+        cudaMemset(L->err, 0, 4);
+        return dn_fail_str(DN_ERR_DEVICE, "conv kernel reported device error word " + std::to_string(word));
+    }
+    return DN_OK;
+}
+
+int dcn_check(dn_dcn* L) {
+    uint32_t word = 0;
+    cudaError_t e = cudaMemcpy(&word, L->err, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return dn_cuda_fail(e, "dcn error word");
+    if (word) {
+        cudaMemset(L->err, 0, 4);
+        return dn_fail_str(DN_ERR_DEVICE, "dcn kernel reported device error word " + std::to_string(word));
+    }
+    return DN_OK;
+}
+
+}  // namespace dnb
+
 extern "C" {
 
 int dn_conv2d_create(const dn_weights* store, const char* weight_name, const char* bias_name, int pad, int stride,
                      int dilation, int groups, int device, dn_conv2d** out) {
     if (!store || !weight_name || !out) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_create: null argument");
     *out = nullptr;
-    if (pad < 0 || stride <= 0 || dilation <= 0 || groups <= 0)
-        return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_create: bad pad/stride/dilation/groups");
     try {
         const HostWeights& hw = *store->hw;
         if (!hw.contains(weight_name)) return dn_fail_str(DN_ERR_NOT_FOUND, std::string("weight not found: ") + weight_name);
@@ -636,64 +865,15 @@ int dn_conv2d_create(const dn_weights* store, const char* weight_name, const cha
         const auto& sh = hw.entry(weight_name).shape;
         if (sh.size() != 4)
             return dn_fail_str(DN_ERR_FORMAT, "Conv2dLayer: weight must be 4-D, got " + std::to_string(sh.size()) + "-D");
-        auto L = std::make_unique<dn_conv2d>();
-        L->device = device;
-        L->cout = static_cast<int>(sh[0]);
-        L->cin_g = static_cast<int>(sh[1]);
-        L->kh = static_cast<int>(sh[2]);
-        L->kw = static_cast<int>(sh[3]);
-        L->pad = pad;
-        L->stride = stride;
-        L->dil = dilation;
-        L->groups = groups;
-        if (L->cout % groups != 0) return dn_fail(DN_ERR_INVALID_ARG, "dn_conv2d_create: out_channels % groups != 0");
-        L->cin = L->cin_g * groups;
-        L->cb = kKC;
-        while (L->cin % L->cb != 0) L->cb >>= 1;  // largest power of two dividing Cin and 64
-        L->nblk = L->cin / L->cb;
-        const int KK = L->kh * L->kw;
-        L->k_chunks = (L->cin * KK + kKC - 1) / kKC;
-        L->NT = std::min(256, std::max(16, next_pow2(L->cout)));
-        L->slabs = (L->cout + L->NT - 1) / L->NT;
         const auto w = hw.to_f32(weight_name);
-        const size_t tile = static_cast<size_t>(L->NT) * kKC * 2;
-        const size_t slab_bytes = tile * L->k_chunks;
-        std::vector<uint8_t> pk(slab_bytes * L->slabs, 0);
-        const int cout_g = L->cout / groups;
-        for (int o = 0; o < L->cout; ++o) {
-            const int sl = o / L->NT, ol = o % L->NT, grp = o / cout_g;
-            for (int cl = 0; cl < L->cin_g; ++cl) {
-                const int ci = grp * L->cin_g + cl;
-                for (int k = 0; k < KK; ++k) {
-                    const int kidx = ((ci / L->cb) * KK + k) * L->cb + (ci % L->cb);
-                    const __half h = __float2half(w[(static_cast<size_t>(o) * L->cin_g + cl) * KK + k]);
-                    const int j = kidx / kKC, kk = kidx % kKC;
-                    const size_t offb = static_cast<size_t>(ol >> 3) * 1024 + (kk / 8) * 128 + (ol & 7) * 16 + (kk % 8) * 2;
-                    std::memcpy(pk.data() + sl * slab_bytes + j * tile + offb, &h, 2);
-                }
-            }
-        }
-        std::vector<float> b(static_cast<size_t>(L->slabs) * L->NT, 0.f);
+        std::vector<float> bv;
         if (bias_name) {
-            const auto bv = hw.to_f32(bias_name);
-            if (static_cast<int>(bv.size()) != L->cout) return dn_fail(DN_ERR_FORMAT, "dn_conv2d_create: bias size");
-            for (int o = 0; o < L->cout; ++o) b[o] = __half2float(__float2half(bv[o]));
+            bv = hw.to_f32(bias_name);
+            if (static_cast<int64_t>(bv.size()) != sh[0]) return dn_fail(DN_ERR_FORMAT, "dn_conv2d_create: bias size");
         }
-        DevGuard dg(device);
-        cudaError_t e = cudaMalloc(&L->bpack, pk.size());
-        if (e == cudaSuccess) e = cudaMalloc(&L->bias, b.size() * 4);
-        if (e == cudaSuccess) e = cudaMalloc(&L->err, 4);
-        if (e == cudaSuccess) e = cudaMemcpy(L->bpack, pk.data(), pk.size(), cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemcpy(L->bias, b.data(), b.size() * 4, cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemset(L->err, 0, 4);
-        if (e != cudaSuccess) {
-            cudaFree(L->bpack);
-            cudaFree(L->bias);
-            cudaFree(L->err);
-            return dn_cuda_fail(e, "dn_conv2d_create: upload");
-        }
-        *out = L.release();
-        return DN_OK;
+        return dnb::conv2d_build(w.data(), bias_name ? bv.data() : nullptr, static_cast<int>(sh[0]),
+                                 static_cast<int>(sh[1]), static_cast<int>(sh[2]), static_cast<int>(sh[3]), pad, stride,
+                                 dilation, groups, device, out);
     } catch (const std::exception& ex) {
         return dn_fail_str(DN_ERR_FORMAT, ex.what());
     }
@@ -754,37 +934,8 @@ int dn_conv2d_forward(dn_conv2d* L, const void* input, int N, int C, int H_in, i
         if (e != cudaSuccess) return dn_cuda_fail(e, "dn_conv2d_forward: NHWC buffer");
         L->xt_bytes = need;
     }
-    const int HW = H_in * W_in;
-    cudaError_t e = launch_pdl(to_nhwc_kernel, dim3((HW + 31) / 32, (L->cin + 31) / 32, N), dim3(32, 8), 0, s,
-                               static_cast<const __half*>(input), L->xt, L->cin, HW);
-    if (e != cudaSuccess) return dn_cuda_fail(e, "dn_conv2d_forward: transpose launch");
-    DcnParams p{};
-    p.xt = L->xt;
-    p.out = static_cast<__half*>(output);
-    p.N = N;
-    p.H = H_in;
-    p.W = W_in;
-    p.Ho = Ho;
-    p.Wo = Wo;
-    p.Cin = L->cin;
-    p.Cout = L->cout;
-    p.kw = L->kw;
-    p.KK = L->kh * L->kw;
-    p.pad = L->pad;
-    p.stride = L->stride;
-    p.dil = L->dil;
-    p.dg = L->nblk;
-    p.cpg = L->cb;
-    p.k_chunks = L->k_chunks;
-    p.err = L->err;
-    const size_t slab_bytes = static_cast<size_t>(L->NT) * kKC * 2 * L->k_chunks;
-    for (int sl = 0; sl < L->slabs; ++sl) {
-        p.bpack = L->bpack + sl * slab_bytes;
-        p.bias = L->bias + sl * L->NT;
-        p.cout_base = sl * L->NT;
-        DN_TRY(run_conv_nt<false>(p, L->NT, L->device, s));
-    }
-    return DN_OK;
+    DN_TRY(dnb::conv2d_to_nhwc(static_cast<const __half*>(input), L->xt, N, L->cin, H_in * W_in, s));
+    return dnb::conv2d_run_nhwc(L, L->xt, N, H_in, W_in, output, false, s);
 }
 
 int dn_conv2d_sync(dn_conv2d* L, void* stream) {

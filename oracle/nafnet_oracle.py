@@ -390,14 +390,14 @@ def deform_conv2d(x: torch.Tensor, offsets: torch.Tensor, masks: torch.Tensor,
     return out
 
 
-def aligned_temporal_forward(pa: dict, pt: dict, clip: torch.Tensor) -> torch.Tensor:
-    """Temporal NAFNet with deformable alignment, fp32: the wiring of the
-    engine's ``aligned.AlignedTemporal``. The reference wires its
-    DeformConv2dLayer (deform_conv2d.cu:105-184) into no model, so the wiring
-    is this project's; its pieces are the restatements above
-    (``deform_conv2d``, ``nafnet_forward``). clip: (1, T, C, H, W); the
-    centre frame is T // 2. Returns (1, 3, H, W) and the per-neighbour
-    offsets/masks tensors (for statistics)."""
+def aligned_fusion(pa: dict, clip: torch.Tensor):
+    """The alignment stage of the temporal NAFNet with deformable alignment,
+    fp32: the trunk input fuse(concat(a_0 .. a_{T-1})) + frame_c, with
+    a_t = DCN(f_t, offset(concat(f_c, f_t))) for t != c and a_c = f_c. The
+    reference wires its DeformConv2dLayer (deform_conv2d.cu:105-184) into no
+    model, so the wiring is this project's; its pieces are the restatements
+    above. clip: (1, T, C, H, W); the centre frame is T // 2. Returns the
+    fused image and the per-neighbour offsets/masks tensors (for statistics)."""
     t = clip.shape[1]
     c = t // 2
     feats = [conv(pa, "align.feat", clip[:, i], padding=1) for i in range(t)]
@@ -413,6 +413,14 @@ def aligned_temporal_forward(pa: dict, pt: dict, clip: torch.Tensor) -> torch.Te
         aligned.append(deform_conv2d(feats[i], om[:, :n_off], om[:, n_off:], pa["align.dcn.weight"],
                                      pa["align.dcn.bias"], pad=1, deform_groups=dg))
     fused = conv(pa, "align.fuse", torch.cat(aligned, 1)) + clip[:, c]
+    return fused, oms
+
+
+def aligned_temporal_forward(pa: dict, pt: dict, clip: torch.Tensor):
+    """Temporal NAFNet with deformable alignment, fp32: ``aligned_fusion``
+    followed by the NAFNet trunk (``nafnet_forward``). Returns (1, 3, H, W)
+    and the per-neighbour offsets/masks tensors."""
+    fused, oms = aligned_fusion(pa, clip)
     return nafnet_forward(pt, fused), oms
 
 

@@ -226,8 +226,8 @@ def run_case(name: str, spec: dict):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/training",
-                    help="directory holding the reference's models.py")
+    ap.add_argument("--reference", required=True,
+                    help="directory holding the reference's models.py (its training/ folder)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
     sys.path.insert(0, args.reference)

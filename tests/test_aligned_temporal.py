@@ -81,7 +81,7 @@ def test_oracle_wiring_matches_torchvision_composition(pkg, tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("h,w", [(64, 96), (50, 70)], ids=["64x96", "50x70"])
+@pytest.mark.parametrize("h,w", [(64, 96), (50, 70), (256, 448)], ids=["64x96", "50x70", "256x448"])
 def test_aligned_w32_matches_oracle(pkg, tmp_path, h, w):
     synth = synth_mod(pkg)
     aligned = importlib.import_module(pkg.__name__ + ".aligned")
@@ -114,19 +114,6 @@ def test_aligned_repeat_and_side_stream(pkg, tmp_path):
     model.close()
 
 
-def test_aligned_rejects_frames_beyond_the_layer_limit(pkg):
-    """A window whose fusion input (T*F*H*W) exceeds 2^31 elements is rejected
-    on the host before any kernel (2160x3840 at T = 5, F = 64). Host logic
-    only: the instance skips layer construction and the clip is a meta tensor."""
-    aligned = importlib.import_module(pkg.__name__ + ".aligned")
-    m = aligned.AlignedTemporal.__new__(aligned.AlignedTemporal)
-    m.num_frames, m.in_channels, m.feat_channels = 5, 3, 64
-    clip = torch.empty(1, 5, 3, 2160, 3840, dtype=torch.float16, device="meta")
-    with pytest.raises(ValueError, match="2\\^31"):
-        m(clip)
-    assert 5 * 64 * 1088 * 1920 <= aligned.MAX_LAYER_ELEMS  # 1080p windows stay within it
-
-
 @pytest.mark.gpu
 def test_aligned_rejects_bad_windows(pkg, tmp_path):
     synth = synth_mod(pkg)
@@ -138,4 +125,74 @@ def test_aligned_rejects_bad_windows(pkg, tmp_path):
         model(torch.zeros(1, 5, 3, 32, 32, dtype=torch.float16, device="cuda"))
     with pytest.raises(TypeError):
         model(torch.zeros(1, 3, 3, 32, 32, dtype=torch.float32, device="cuda"))
+    model.close()
+
+
+@pytest.mark.gpu
+def test_alignment_stage_1080p_matches_oracle(pkg, tmp_path):
+    """The alignment stage (trunk input) of a 5-frame 1080p window, 64
+    features, 8 deformable groups, against the oracle's composition. The
+    engine aligns the whole frame; the oracle runs on row bands with a
+    32-row margin (the features, the offset conv and every deformable sample
+    of the compared rows lie inside the band: offsets are about N(0, 2 px)),
+    at the top and bottom borders and in the middle."""
+    synth = synth_mod(pkg)
+    aligned = importlib.import_module(pkg.__name__ + ".aligned")
+    h, w, t = 1080, 1920, 5
+    apath, pa = synth.make_align_dir(str(tmp_path / "align"), 2, num_frames=t)
+    tpath, _ = synth.make_model_dir(str(tmp_path / "trunk"), synth.CONFIG_TINY_W16, 2)
+    clip = synth.temporal_window(t, h, w, seed=2).astype(np.float16).astype(np.float32)
+    model = aligned.AlignedTemporal(apath, tpath)
+    xc = torch.from_numpy(clip).half().cuda()
+    for i in range(t):
+        model.encode_frame(xc[:, i], i)
+    fused = model.align_window(list(range(t)), h, w)
+    model.sync()
+    got = fused.float().cpu().numpy()
+    model.close()
+    torch.set_num_threads(min(16, os.cpu_count() or 1))
+    pa_t = O.as_torch(pa)
+    for lo, hi, c0, c1 in ((0, 96, 0, 64), (500, 628, 532, 596), (984, 1080, 1016, 1080)):
+        ref, _ = O.aligned_fusion(pa_t, torch.from_numpy(clip[:, :, :, lo:hi]))
+        ref = ref.numpy()[:, :, c0 - lo:c1 - lo]
+        err, psnr = compare(got[:, :, c0:c1], ref)
+        assert err <= MAX_ABS and psnr >= MIN_PSNR, ((lo, hi), err, psnr)
+
+
+@pytest.mark.gpu
+def test_frame_cache_matches_window_forward(pkg, tmp_path):
+    """A sequence through the frame cache (each frame encoded once, slot
+    f % T, edge replication by repeated slots) equals one forward per
+    assembled window, bit for bit."""
+    synth = synth_mod(pkg)
+    aligned = importlib.import_module(pkg.__name__ + ".aligned")
+    sharding = importlib.import_module(pkg.__name__ + ".sharding")
+    t, n, h, w = 5, 7, 40, 56
+    apath, _ = synth.make_align_dir(str(tmp_path / "align"), 6, num_frames=t)
+    tpath, _ = synth.make_model_dir(str(tmp_path / "trunk"), synth.CONFIG_TINY_W16, 6)
+    model = aligned.AlignedTemporal(apath, tpath)
+    seq = torch.from_numpy(synth.temporal_window(n, h, w, 6)[0]).half().cuda()
+    cached = sharding.denoise_segment(model, lambda i: seq[i], n, 1, 0, num_frames=t)
+    direct = sharding.denoise_segment(model, lambda i: seq[i], n, 1, 0, num_frames=t, cache=False)
+    model.sync()
+    assert [i for i, _ in cached] == list(range(n))
+    for (_, a), (_, b) in zip(cached, direct):
+        assert torch.equal(a, b)
+    model.close()
+
+
+@pytest.mark.gpu
+def test_aligned_rejects_frames_beyond_the_layer_limit(pkg, tmp_path):
+    """A frame whose offset-conv output (3*dg*9 channels) would exceed 2^31
+    elements is rejected on the host before any copy or kernel (4320x7680;
+    2160x3840 is within the limit). The frame buffer has the full size."""
+    synth = synth_mod(pkg)
+    aligned = importlib.import_module(pkg.__name__ + ".aligned")
+    apath, _ = synth.make_align_dir(str(tmp_path / "align"), 4, num_frames=3)
+    tpath, _ = synth.make_model_dir(str(tmp_path / "trunk"), synth.CONFIG_TINY_W16, 4)
+    model = aligned.AlignedTemporal(apath, tpath)
+    big = torch.zeros(1, 3, 4320, 7680, dtype=torch.float16, device="cuda")
+    with pytest.raises(pkg.DenoiserError, match="2\\^31"):
+        model.encode_frame(big, 0)
+    assert 216 * 2160 * 3840 < 2 ** 31
     model.close()
