@@ -15,6 +15,7 @@ the same workload.
 from __future__ import annotations
 
 import argparse
+import importlib
 import json
 import os
 import statistics
@@ -220,6 +221,86 @@ def ref_cuda_engine(path: str, x: np.ndarray, reps: int = 5) -> dict | None:
                       f"same weights and frame, mean of {reps} after 1 untimed"}
 
 
+def temporal_workloads(args, pkg, synth, rank: int, world: int, dist) -> dict:
+    """The temporal model with deformable alignment (5-frame windows, 64
+    features, 8 deformable groups, NAFNet-w32 trunk, random init seed 2):
+      config4: a 16-frame 1080p sequence (one seeded smooth base translated by
+        integer shifts in [-4, 4] px, N(0, 20/255) noise per frame) through
+        the frame cache on each GPU;
+      config5: a 240-frame 2160x3840 clip (a seeded smooth base panned 1 px
+        per frame, Poisson-Gaussian noise gain 0.01 / read 0.02) sharded into
+        contiguous segments over the ranks, each rank encoding 2 halo frames
+        at each inner segment edge (sharding.denoise_segment); frames resident
+        in HBM (file I/O excluded); fps = 240 / the slowest rank's time.
+    Times are CUDA events on the launching stream, max over ranks."""
+    import torch
+
+    aligned = importlib.import_module(pkg.__name__ + ".aligned")
+    sharding = importlib.import_module(pkg.__name__ + ".sharding")
+    T = 5
+    out = {}
+    tmp = tempfile.mkdtemp(prefix=f"aligned_r{rank}_")
+    apath, _ = synth.make_align_dir(os.path.join(tmp, "align"), 2, num_frames=T)
+    tpath, _ = synth.make_model_dir(os.path.join(tmp, "trunk"), synth.CONFIG_W32, seed=2)
+    model = aligned.AlignedTemporal(apath, tpath, device=torch.cuda.current_device())
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # ---- config 4: 1080p sequence through the frame cache ----
+    n4 = 16
+    seq = torch.from_numpy(synth.temporal_window(n4, 1080, 1920, seed=2)[0]).half().cuda()
+    sharding.denoise_segment(model, lambda i: seq[i], T, 1, 0, num_frames=T)  # warm-up (plans the buffers)
+    model.sync()
+    ms4 = timed(lambda: sharding.denoise_segment(model, lambda i: seq[i], n4, 1, 0, num_frames=T))
+    model.sync()
+    out["config4_1080p"] = {"frames": n4, "frames_per_s": world * n4 / (ms4 / 1000.0), "ms_per_frame": ms4 / n4,
+                            "n_gpus": world, "scaling": "weak",
+                            "workload": "temporal model with deformable alignment, 5-frame windows of 1x3x1080x1920, "
+                                        "frame cache (each frame encoded once)"}
+    del seq
+    if args.no_clip:
+        model.close()
+        return out
+
+    # ---- config 5: 240-frame 4K clip sharded over the ranks ----
+    n5, h5, w5 = 240, 2160, 3840
+    base = synth.pan_clip_base(h5, w5, n5, seed=5, device="cuda")
+    need = sharding.needed_frames(n5, world, rank, T)
+    held = {f: synth.pan_clip_frame(base, f, w5, seed=5)[0] for f in need}
+    del base
+    sharding.denoise_segment(model, lambda i: held[need[i]], T, 1, 0, num_frames=T)  # warm-up at 4K
+    model.sync()
+    res = []
+    ms5 = timed(lambda: res.extend(sharding.denoise_segment(model, lambda i: held[i], n5, world, rank, num_frames=T)))
+    model.sync()
+    seg = sharding.segment(n5, world, rank)
+    assert [i for i, _ in res] == list(range(*seg))
+    out["config5_4k_clip"] = {"frames": n5, "frame": f"{h5}x{w5}", "frames_per_s": n5 / (ms5 / 1000.0),
+                              "ms": ms5, "n_gpus": world, "scaling": "strong", "halo_frames": T // 2,
+                              "frames_loaded_rank0": len(need) if rank == 0 else None,
+                              "workload": "240-frame 2160x3840 clip panned 1 px/frame, Poisson-Gaussian noise, "
+                                          "temporal model with deformable alignment (T=5), contiguous segments "
+                                          "with 2 halo frames, frames resident in HBM"}
+    del held, res
+    model.close()
+    return out
+
+
 def run_reference(args, rank: int) -> None:
     if rank != 0:
         return
@@ -261,6 +342,8 @@ def main() -> None:
     ap.add_argument("--width", type=int, default=1920)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-engine", action="store_true")
+    ap.add_argument("--no-temporal", action="store_true", help="skip the temporal-alignment workloads")
+    ap.add_argument("--no-clip", action="store_true", help="skip the 240-frame 4K clip")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -290,7 +373,12 @@ def main() -> None:
     path, _ = synth.make_model_dir(tmp, cfg, seed=1)
     model = pkg.Model(path, device=local_rank)
 
-    # Input ring: this rank's frame segment (distinct frames, > L2 in total).
+    # The clip: steps frames per rank, split into contiguous segments
+    # (sharding.segment); rank r denoises frames [s, e). Frame i is taken from
+    # a ring of distinct frames resident in HBM (> L2 in total).
+    sharding = importlib.import_module(pkg.__name__ + ".sharding")
+    n_clip = args.steps * world
+    seg0, seg1 = sharding.segment(n_clip, world, rank)
     base = [synth.w32_frame(h, w, seed=1 + 100 * rank + i) for i in range(2)]
     ring = []
     for i in range(RING):
@@ -317,7 +405,7 @@ def main() -> None:
     time.sleep(0.3)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for i in range(args.steps):
+    for i in range(seg0, seg1):
         model(ring[i % RING], out=outs[i % 2])
     ev1.record(stream)
     torch.cuda.synchronize()
@@ -329,7 +417,7 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    value = world * args.steps / (ms / 1000.0)
+    value = n_clip / (ms / 1000.0)
 
     # ---------------- end to end: host buffers through the C-ABI ----------------
     # A stream of frames through the pipelined host-buffer call: the input copy
@@ -385,6 +473,7 @@ def main() -> None:
     frame_bytes, frame_flops = frame_algorithmic(cfg, h, w)
     t_floor = max(frame_bytes / (peaks["hbm_gbs"] * 1e9), frame_flops / (peaks["bf16_tflops_sustained"] * 1e12))
     step_ms = ms / args.steps
+    extra = {} if args.no_temporal else temporal_workloads(args, pkg, synth, rank, world, dist)
 
     if rank != 0:
         if dist:
@@ -411,7 +500,8 @@ def main() -> None:
         "config": {"workload": WORKLOAD, "global_batch": world, "frame": f"{h}x{w}",
                    "l2": f"ring of {RING} distinct input frames ({RING * 3 * h * w * 2 / 1e6:.0f} MB) > 126 MB L2; "
                          "each forward also streams ~1.2 GB of activations",
-                   "parallelism": f"frame sharding over {world} GPU(s), one engine per GPU, no collectives"},
+                   "parallelism": f"frame sharding over {world} GPU(s), one engine per GPU, no collectives",
+                   "clip": f"{n_clip} frames, contiguous segments of {args.steps} per rank (sharding.segment)"},
         "roofline": {"bound": "tensor" if tensor_bound else "hbm", "kernel": dom_kind, "achieved": ach,
                      "peak": peak, "unit": unit, "frac": ach / peak, "traffic": traffic,
                      "alg_bytes_per_launch": by_l, "alg_flops_per_launch": fl_l,
@@ -424,6 +514,7 @@ def main() -> None:
         "gpu_launches": kpf * args.steps,
         "clocks": clk,
     }
+    line.update(extra)
     if cpu:
         line["cpu_baseline"] = cpu
     if world == 1 and not args.no_ref_engine:

@@ -345,12 +345,12 @@ def smooth_noise(h: int, w: int, seed: int, channels: int = 3, octaves: int = 4)
         fx = xs - x0
         fy = fy * fy * (3 - 2 * fy)
         fx = fx * fx * (3 - 2 * fx)
-        g00 = grid[:, y0][:, :, x0]
-        g01 = grid[:, y0][:, :, x0 + 1]
-        g10 = grid[:, y0 + 1][:, :, x0]
-        g11 = grid[:, y0 + 1][:, :, x0 + 1]
-        top = g00 * (1 - fx) + g01 * fx
-        bot = g10 * (1 - fx) + g11 * fx
+        # Separable: interpolate every grid row along x first (gh rows), then
+        # pick the two rows of each output row (the same products and sums
+        # as the four-corner form, in the same order).
+        gx = grid[:, :, x0] * (1 - fx) + grid[:, :, x0 + 1] * fx
+        top = gx[:, y0]
+        bot = gx[:, y0 + 1]
         amp = 0.5 ** o
         out += amp * (top * (1 - fy[:, None]) + bot * fy[:, None])
         amp_total += amp
@@ -388,3 +388,49 @@ def temporal_window(t: int, h: int, w: int, seed: int, sigma: float = 20.0 / 255
         f = base[:, m + dy: m + dy + h, m + dx: m + dx + w]
         frames.append(f + rng.normal(0.0, sigma, f.shape).astype(np.float32))
     return np.stack(frames)[None].astype(np.float32)
+
+
+def pan_clip_base(h: int, w: int, n_frames: int, seed: int, device="cuda"):
+    """Smooth base image for a clip panned 1 px per frame, (3, h, w + n_frames)
+    float32 on `device`: ``smooth_noise`` with the same seeded grids,
+    evaluated with torch on the device (4K bases in milliseconds)."""
+    import torch
+
+    w = w + n_frames
+    rng = np.random.default_rng(seed)
+    out = torch.zeros((3, h, w), dtype=torch.float32, device=device)
+    amp_total = 0.0
+    for o in range(4):
+        cells = 4 * (2 ** o)
+        gh, gw = cells + 2, int(cells * w / max(h, 1)) + 2
+        grid = torch.from_numpy(rng.random((3, gh, gw)).astype(np.float32)).to(device)
+        ys = torch.linspace(0, cells, h, dtype=torch.float32, device=device)
+        xs = torch.linspace(0, gw - 2, w, dtype=torch.float32, device=device)
+        y0, x0 = ys.floor().long(), xs.floor().long()
+        fy, fx = ys - y0, xs - x0
+        fy = fy * fy * (3 - 2 * fy)
+        fx = fx * fx * (3 - 2 * fx)
+        gx = grid[:, :, x0] * (1 - fx) + grid[:, :, x0 + 1] * fx
+        amp = 0.5 ** o
+        out += amp * (gx[:, y0] * (1 - fy[:, None]) + gx[:, y0 + 1] * fy[:, None])
+        amp_total += amp
+    out /= amp_total
+    lo = out.amin(dim=(1, 2), keepdim=True)
+    hi = out.amax(dim=(1, 2), keepdim=True)
+    return (out - lo) / (hi - lo).clamp_min(1e-6)
+
+
+def pan_clip_frame(base, i: int, w: int, seed: int, gain: float = 0.01, read_sigma: float = 0.02):
+    """Frame i of the panned clip as a (1, 3, h, w) FP16 torch tensor on the
+    device of `base` (a float32 torch tensor from ``pan_clip_base``): the
+    window base[:, :, i:i+w] with Poisson-Gaussian noise (the formula of
+    ``training/noise_generators.py:176-187``), drawn from a generator seeded
+    with (seed, i) on that device."""
+    import torch
+
+    g = torch.Generator(device=base.device)
+    g.manual_seed(int(seed) * 1000003 + int(i))
+    clean = base[:, :, i:i + w].clamp_min(0.0)
+    shot = torch.poisson(clean / gain, generator=g) * gain
+    noisy = shot + torch.randn(clean.shape, generator=g, device=base.device) * read_sigma
+    return noisy.half().unsqueeze(0).contiguous()

@@ -112,6 +112,15 @@ def test_w32_1080p(pkg, tmp_path):
     assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
 
 
+def test_w32_4k(pkg, tmp_path):
+    """NAFNet-w32 on one 2160x3840 frame: the trunk size of the 4K clip
+    workload (2160 is a multiple of 16, so no padding)."""
+    synth = synth_mod(pkg)
+    x = synth.w32_frame(2160, 3840, seed=7).astype(np.float16).astype(np.float32)
+    (err, psnr), _ = _oracle_case(pkg, tmp_path, synth.CONFIG_W32, 2, x)
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+
+
 def test_repeat_forward_is_deterministic(pkg, tmp_path):
     synth = synth_mod(pkg)
     path, _ = synth.make_model_dir(str(tmp_path), synth.CONFIG_TINY_W16, 0)
