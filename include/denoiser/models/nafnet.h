@@ -34,7 +34,8 @@ public:
         if (x.dtype() != DType::kFloat16) throw std::runtime_error("NAFNet::forward: expected FP16 input");
         const auto& s = x.shape();
         if (static_cast<int>(s.size()) != ndim) throw std::invalid_argument("forward: unexpected input rank");
-        Tensor y = Tensor::empty({s[0], 3, s[ndim - 2], s[ndim - 1]}, DType::kFloat16);
+        // Stream-ordered output: no device-wide synchronisation per frame.
+        Tensor y = Tensor::empty({s[0], 3, s[ndim - 2], s[ndim - 1]}, DType::kFloat16, stream);
         check(dn_model_forward(m_, x.data(), s.data(), ndim, y.data(), stream));
         return y;
     }

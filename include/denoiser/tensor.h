@@ -52,26 +52,39 @@ public:
     Tensor() = default;
 
     // Uninitialised device tensor; every dimension must be > 0.
-    static Tensor empty(std::vector<int64_t> shape, DType dtype, cudaStream_t /*stream*/ = nullptr) {
+    //
+    // Unlike the reference (cudaMalloc per tensor, cudaFree in the destructor,
+    // src/tensor.cu:13-23, 66-71, which synchronises the whole device on
+    // every free), memory comes from the device's stream-ordered pool:
+    // cudaMallocAsync on `stream`, and the destructor returns it with
+    // cudaFreeAsync on that same stream, ordered after the work queued there.
+    // With the default stream (nullptr = the legacy stream, which orders
+    // against every blocking stream) the lifetime rules are the reference's;
+    // a tensor allocated on a stream must not be freed while another,
+    // non-blocking stream still uses it.
+    static Tensor empty(std::vector<int64_t> shape, DType dtype, cudaStream_t stream = nullptr) {
         int64_t n = 1;
         for (int64_t d : shape) {
             if (d <= 0) throw std::invalid_argument("Tensor::empty: all dimensions must be > 0");
             n *= d;
         }
         void* p = nullptr;
-        CUDA_CHECK(cudaMalloc(&p, static_cast<size_t>(n) * dtype_size(dtype)));
-        return Tensor(p, std::move(shape), dtype, true);
+        CUDA_CHECK(cudaMallocAsync(&p, static_cast<size_t>(n) * dtype_size(dtype), stream));
+        Tensor t(p, std::move(shape), dtype, true);
+        t.stream_ = stream;
+        return t;
     }
 
     // Device copy of host data; synchronous when stream == nullptr.
     static Tensor from_host(const void* data, std::vector<int64_t> shape, DType dtype, cudaStream_t stream = nullptr) {
         if (!data) throw std::invalid_argument("Tensor::from_host: data must not be null");
-        Tensor t = empty(std::move(shape), dtype);
+        Tensor t = empty(std::move(shape), dtype, stream);
         t.copy(t.d_ptr_, data, cudaMemcpyHostToDevice, stream);
         return t;
     }
 
-    Tensor(Tensor&& o) noexcept : d_ptr_(o.d_ptr_), shape_(std::move(o.shape_)), dtype_(o.dtype_), owns_memory_(o.owns_memory_) {
+    Tensor(Tensor&& o) noexcept
+        : d_ptr_(o.d_ptr_), shape_(std::move(o.shape_)), dtype_(o.dtype_), owns_memory_(o.owns_memory_), stream_(o.stream_) {
         o.d_ptr_ = nullptr;
         o.owns_memory_ = false;
     }
@@ -82,6 +95,7 @@ public:
             shape_ = std::move(o.shape_);
             dtype_ = o.dtype_;
             owns_memory_ = o.owns_memory_;
+            stream_ = o.stream_;
             o.d_ptr_ = nullptr;
             o.owns_memory_ = false;
         }
@@ -93,7 +107,7 @@ public:
 
     Tensor clone(cudaStream_t stream = nullptr) const {
         if (!is_valid()) return Tensor{};
-        Tensor t = empty(shape_, dtype_);
+        Tensor t = empty(shape_, dtype_, stream);
         copy(t.d_ptr_, d_ptr_, cudaMemcpyDeviceToDevice, stream);
         return t;
     }
@@ -162,12 +176,13 @@ private:
     std::vector<int64_t> shape_;
     DType dtype_ = DType::kFloat32;
     bool owns_memory_ = true;
+    cudaStream_t stream_ = nullptr;  // the stream the memory was allocated on (and is freed on)
 
     Tensor(void* p, std::vector<int64_t> shape, DType dtype, bool owns) noexcept
         : d_ptr_(p), shape_(std::move(shape)), dtype_(dtype), owns_memory_(owns) {}
 
     void release() noexcept {
-        if (owns_memory_ && d_ptr_) cudaFree(d_ptr_);  // a destructor must not throw
+        if (owns_memory_ && d_ptr_) cudaFreeAsync(d_ptr_, stream_);  // a destructor must not throw
         d_ptr_ = nullptr;
     }
     void copy(void* dst, const void* src, cudaMemcpyKind kind, cudaStream_t stream) const {

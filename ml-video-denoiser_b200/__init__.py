@@ -124,6 +124,10 @@ SIGNATURES = {
     "dn_conv2d_output_size": (_I, [_P, _I, _I, _IP, _IP]),
     "dn_conv2d_forward": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
     "dn_conv2d_sync": (_I, [_P, _P]),
+    # include/denoiser_b200_io.h
+    "dn_image_probe": (_I, [_c.c_char_p, _IP, _IP, _IP]),
+    "dn_image_read": (_I, [_c.c_char_p, _P, _I, _I, _I]),
+    "dn_image_write": (_I, [_c.c_char_p, _P, _I, _I, _I]),
     # include/denoiser_b200_aligned.h
     "dn_aligned_create": (_I, [_c.c_char_p, _c.c_char_p, _I, _PP]),
     "dn_aligned_destroy": (_I, [_P]),

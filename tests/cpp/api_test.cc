@@ -138,6 +138,26 @@ static int gpu_checks(char** a) {
     std::vector<char> ob(out.nbytes());
     out.to_host(ob.data());
     EXPECT(rb.size() == ob.size() && std::memcmp(rb.data(), ob.data(), ob.size()) == 0);
+
+    // Device memory stays flat over 100 forwards on a stream (the reference's
+    // disabled VRAMStableUnder100Iters, tests/test_unet_forward.cc:133-241):
+    // outputs come from the stream-ordered pool and go back to it.
+    cudaStream_t st = nullptr;
+    CUDA_CHECK(cudaStreamCreate(&st));
+    for (int i = 0; i < 3; ++i) (void)net.forward(x, st);
+    CUDA_CHECK(cudaStreamSynchronize(st));
+    size_t free0 = 0, total = 0, free1 = 0;
+    CUDA_CHECK(cudaMemGetInfo(&free0, &total));
+    for (int i = 0; i < 100; ++i) {
+        Tensor yi = net.forward(x, st);
+        EXPECT(yi.height() == H);
+    }
+    CUDA_CHECK(cudaStreamSynchronize(st));
+    CUDA_CHECK(cudaMemGetInfo(&free1, &total));
+    const double drift_mb = (static_cast<double>(free0) - static_cast<double>(free1)) / (1024.0 * 1024.0);
+    std::printf("vram drift over 100 forwards: %.3f MB\n", drift_mb);
+    EXPECT(drift_mb <= 1.0);
+    CUDA_CHECK(cudaStreamDestroy(st));
     std::printf("gpu ok\n");
     return 0;
 }
