@@ -54,14 +54,15 @@ public:
     // Uninitialised device tensor; every dimension must be > 0.
     //
     // Unlike the reference (cudaMalloc per tensor, cudaFree in the destructor,
-    // src/tensor.cu:13-23, 66-71, which synchronises the whole device on
-    // every free), memory comes from the device's stream-ordered pool:
-    // cudaMallocAsync on `stream`, and the destructor returns it with
-    // cudaFreeAsync on that same stream, ordered after the work queued there.
-    // With the default stream (nullptr = the legacy stream, which orders
-    // against every blocking stream) the lifetime rules are the reference's;
-    // a tensor allocated on a stream must not be freed while another,
-    // non-blocking stream still uses it.
+    // src/tensor.cu:13-23, 66-71, which blocks the host and synchronises the
+    // whole device on every free), memory comes from the device's
+    // stream-ordered pool: cudaMallocAsync on `stream`, and the destructor
+    // returns it with cudaFreeAsync on the legacy default stream. That free
+    // is ordered after the work already queued on every blocking stream
+    // (streams from cudaStreamCreate, the reference CLI's kind) and needs no
+    // stream to outlive the tensor, so the reference's lifetime rules hold;
+    // work on a stream created with cudaStreamNonBlocking that still reads a
+    // tensor must be synchronised before the tensor is destroyed.
     static Tensor empty(std::vector<int64_t> shape, DType dtype, cudaStream_t stream = nullptr) {
         int64_t n = 1;
         for (int64_t d : shape) {
@@ -70,9 +71,7 @@ public:
         }
         void* p = nullptr;
         CUDA_CHECK(cudaMallocAsync(&p, static_cast<size_t>(n) * dtype_size(dtype), stream));
-        Tensor t(p, std::move(shape), dtype, true);
-        t.stream_ = stream;
-        return t;
+        return Tensor(p, std::move(shape), dtype, true);
     }
 
     // Device copy of host data; synchronous when stream == nullptr.
@@ -84,7 +83,7 @@ public:
     }
 
     Tensor(Tensor&& o) noexcept
-        : d_ptr_(o.d_ptr_), shape_(std::move(o.shape_)), dtype_(o.dtype_), owns_memory_(o.owns_memory_), stream_(o.stream_) {
+        : d_ptr_(o.d_ptr_), shape_(std::move(o.shape_)), dtype_(o.dtype_), owns_memory_(o.owns_memory_) {
         o.d_ptr_ = nullptr;
         o.owns_memory_ = false;
     }
@@ -95,7 +94,6 @@ public:
             shape_ = std::move(o.shape_);
             dtype_ = o.dtype_;
             owns_memory_ = o.owns_memory_;
-            stream_ = o.stream_;
             o.d_ptr_ = nullptr;
             o.owns_memory_ = false;
         }
@@ -176,13 +174,12 @@ private:
     std::vector<int64_t> shape_;
     DType dtype_ = DType::kFloat32;
     bool owns_memory_ = true;
-    cudaStream_t stream_ = nullptr;  // the stream the memory was allocated on (and is freed on)
 
     Tensor(void* p, std::vector<int64_t> shape, DType dtype, bool owns) noexcept
         : d_ptr_(p), shape_(std::move(shape)), dtype_(dtype), owns_memory_(owns) {}
 
     void release() noexcept {
-        if (owns_memory_ && d_ptr_) cudaFreeAsync(d_ptr_, stream_);  // a destructor must not throw
+        if (owns_memory_ && d_ptr_) cudaFreeAsync(d_ptr_, nullptr);  // a destructor must not throw
         d_ptr_ = nullptr;
     }
     void copy(void* dst, const void* src, cudaMemcpyKind kind, cudaStream_t stream) const {

@@ -128,6 +128,12 @@ SIGNATURES = {
     "dn_image_probe": (_I, [_c.c_char_p, _IP, _IP, _IP]),
     "dn_image_read": (_I, [_c.c_char_p, _P, _I, _I, _I]),
     "dn_image_write": (_I, [_c.c_char_p, _P, _I, _I, _I]),
+    # include/denoiser_b200_infer.h
+    "dn_tile_extract": (_I, [_P, _P, _I64, _I, _I, _I, _I, _I, _I, _P]),
+    "dn_tile_accumulate": (_I, [_P, _c.POINTER(_c.c_float), _c.POINTER(_c.c_float), _I, _I, _I, _I, _I, _I, _I, _I,
+                                _P]),
+    "dn_tile_normalize": (_I, [_c.POINTER(_c.c_float), _c.POINTER(_c.c_float), _P, _I, _I, _I, _P]),
+    "dn_average_pair": (_I, [_P, _P, _P, _I64, _P]),
     # include/denoiser_b200_aligned.h
     "dn_aligned_create": (_I, [_c.c_char_p, _c.c_char_p, _I, _PP]),
     "dn_aligned_destroy": (_I, [_P]),

@@ -21,6 +21,10 @@ Cases:
   assembled here from the reference's own NAFNet modules (its temporal_mix /
   offset heads are plain 1x1 convs) and a pixel-unit warp that follows
   ``warp_bilinear_kernel`` (nafnet_kernels.cu:221-262);
+* frame-level inference of training/infer.py run by its own functions:
+  ``_tile_inference`` (tiled spatial, ramp blending) and
+  ``denoise_temporal_sequence`` with temporal flip averaging (untiled and
+  tiled);
 * DCNv2 (deform_im2col.cuh + deform_conv2d.cu) through the third-party
   ``torchvision.ops.deform_conv2d`` (torchvision 0.26.0) with
   mask = sigmoid(raw mask) and the same [dy, dx] offset layout.
@@ -78,7 +82,25 @@ CASES = {
     "dcn_c16_dg4_20x24": dict(kind="dcn", cin=16, cout=16, dg=4, hw=(20, 24), seed=8),
 }
 
-TEMPORAL_KIND = {"spatial": None, "temporal_py": "py", "temporal_legacy": "legacy"}
+# Frame-level inference (training/infer.py) through the reference's own
+# functions: tiled spatial inference, and temporal sequences with flip
+# averaging (untiled and tiled).
+CASES.update({
+    "tile_spatial_w16_70x90_t32": dict(cfg=dict(base_channels=16, enc_blocks=(1, 1), middle_blocks=1,
+                                                dec_blocks=(1, 1), dw_expand=1, ffn_expand=2),
+                                       kind="tile_spatial", wseed=6, shape=(1, 3, 70, 90), xseed=16, tile=32),
+    "flip_temporal_py_w8_t3_seq5": dict(cfg=dict(base_channels=8, enc_blocks=(1, 1), middle_blocks=1,
+                                                 dec_blocks=(1, 1), dw_expand=1, ffn_expand=1),
+                                        kind="flip_temporal", frames=3, warp=False, wseed=7,
+                                        shape=(5, 3, 24, 40), xseed=17, tile=0),
+    "flip_temporal_py_w8_t3_seq4_t16": dict(cfg=dict(base_channels=8, enc_blocks=(1, 1), middle_blocks=1,
+                                                     dec_blocks=(1, 1), dw_expand=1, ffn_expand=1),
+                                            kind="flip_temporal", frames=3, warp=True, wseed=8,
+                                            shape=(4, 3, 24, 40), xseed=18, tile=16),
+})
+
+TEMPORAL_KIND = {"spatial": None, "temporal_py": "py", "temporal_legacy": "legacy", "tile_spatial": None,
+                 "flip_temporal": "py"}
 
 
 def make_input(spec: dict) -> np.ndarray:
@@ -205,6 +227,25 @@ def run_case(name: str, spec: dict):
     params = synth.round_fp16(synth.init_params(specs, spec["wseed"]))
     rcfg = NAFNetConfig(**{k: (tuple(v) if isinstance(v, (list, tuple)) else v) for k, v in spec["cfg"].items()})
     x = make_input(spec)
+    if spec["kind"] in ("tile_spatial", "flip_temporal"):
+        import infer as ref_infer  # the reference's training/infer.py
+
+        dev = torch.device("cpu")
+        with torch.no_grad():
+            if spec["kind"] == "tile_spatial":
+                m = NAFNet(rcfg)
+                load_into(m, params)
+                y = ref_infer._tile_inference(m.eval(), torch.from_numpy(x), spec["tile"], False, dev)
+            else:
+                m = NAFNetTemporal(rcfg, num_frames=frames, use_warp=warp)
+                load_into(m, params)
+                seq = [f.transpose(1, 2, 0).copy() for f in x]  # (H, W, C) frames
+                outs = ref_infer.denoise_temporal_sequence(m.eval(), seq, dev, use_amp=False,
+                                                          temporal_flip=True, tile_size=spec["tile"])
+                y = torch.from_numpy(np.stack([o.transpose(2, 0, 1) for o in outs]))
+        meta = dict(kind=spec["kind"], cfg=spec["cfg"], wseed=spec["wseed"], frames=frames, warp=warp,
+                    tile=spec["tile"])
+        return dict(x=x, expected=y.numpy().astype(np.float32), meta=json.dumps(meta))
     with torch.no_grad():
         if tk is None:
             m = NAFNet(rcfg)
