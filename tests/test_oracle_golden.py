@@ -12,7 +12,8 @@ sys.path.insert(0, os.path.join(os.path.dirname(HERE), "oracle"))
 import nafnet_oracle as O  # noqa: E402
 
 GOLDEN = os.path.join(HERE, "golden")
-CASES = sorted(f[:-4] for f in os.listdir(GOLDEN) if f.endswith(".npz"))
+# model and layer cases (the frame-level tiling / flip cases are in test_infer.py)
+CASES = sorted(f[:-4] for f in os.listdir(GOLDEN) if f.endswith(".npz") and not f.startswith(("tile_", "flip_")))
 
 
 def load_case(name):
