@@ -150,3 +150,76 @@ def test_frame_cache_matches_clip_forward(pkg, S, tmp_path, kind, T):
         assert float((got[i].float() - ref[i].float()).abs().max()) <= 2e-3, i
     with pytest.raises(pkg.InvalidArgumentError):
         m.encode_frame(seq[0].unsqueeze(0), T)
+
+
+# ---------------------------------------------------------------------------
+# Clip coordinator: a worker that dies or fails mid-segment (host only)
+# ---------------------------------------------------------------------------
+
+def _coord_main(rank, world, n, T, port, out_dir, fail_rank, fail_after, mode):
+    import torch.distributed as dist
+
+    from __graft_entry__ import load_package
+
+    S = importlib.import_module(load_package().__name__ + ".sharding")
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=__import__("datetime").timedelta(seconds=60))
+    frames = [np.full((2, 3), float(i), np.float64) + np.arange(6).reshape(2, 3) * 0.01 for i in range(n)]
+    coord = S.ClipCoordinator(store, rank, world, n, heartbeat_s=0.05, dead_after_s=0.6, poll_s=0.02)
+    count = [0]
+
+    def process_range(s, e, on_frame):
+        for i in range(s, e):
+            if rank == fail_rank and count[0] == fail_after:
+                if mode == "exit":
+                    os._exit(3)  # the process vanishes: no flag, the heartbeat stops
+                raise RuntimeError("simulated worker failure")
+            y = _fake_denoise(frames, S.window(i, T, n))
+            np.save(os.path.join(out_dir, f"f{i:03d}_r{rank}.npy"), y)
+            count[0] += 1
+            on_frame(i)
+
+    try:
+        coord.run(process_range)
+    except RuntimeError:
+        pass  # reported to rank 0 through the store
+    if rank == 0:
+        with open(os.path.join(out_dir, "requeued.txt"), "w") as fh:
+            fh.write(repr(coord.requeued()))
+        # keep the store up until the others have seen `finished`
+        import time
+        time.sleep(0.5)
+
+
+@pytest.mark.parametrize("mode", ["exit", "raise"])
+def test_coordinator_requeues_a_failed_segment(pkg, tmp_path, mode):
+    """Three CPU ranks share a 12-frame, T = 3 clip; rank 1 fails after one
+    frame of its segment [4, 8), by vanishing or by raising. Rank 0 declares
+    it dead and re-queues frames 5-7 to a live rank; every frame comes out
+    exactly as in a single-rank run."""
+    import multiprocessing as mp
+    import socket
+
+    S = importlib.import_module(pkg.__name__ + ".sharding")
+    n, T, world = 12, 3, 3
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_coord_main, args=(r, world, n, T, port, str(tmp_path), 1, 1, mode))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(not p.is_alive() for p in procs)
+    assert procs[0].exitcode == 0 and procs[2].exitcode == 0
+    requeued = __import__("ast").literal_eval((tmp_path / "requeued.txt").read_text())
+    assert len(requeued) == 1 and requeued[0][:2] == (5, 8) and requeued[0][2] in (0, 2)
+    frames = [np.full((2, 3), float(i), np.float64) + np.arange(6).reshape(2, 3) * 0.01 for i in range(n)]
+    for i in range(n):
+        outs = sorted(tmp_path.glob(f"f{i:03d}_r*.npy"))
+        assert outs, f"frame {i} missing"
+        want = _fake_denoise(frames, S.window(i, T, n))
+        for o in outs:
+            assert np.array_equal(np.load(o), want)
+    assert not list(tmp_path.glob("f00[5-7]_r1.npy"))  # rank 1 never finished them
