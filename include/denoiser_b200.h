@@ -173,7 +173,9 @@ int dn_model_stats(const dn_model* model, size_t* weight_bytes, size_t* activati
  * <= 64 channels (the first pass of 32/64-channel blocks as one tensor-core
  * 3x3 conv of the normalised input), the single-kernel second pass for 128-
  * and 256-channel blocks of a single-image forward, the ending conv of a
- * 32/64-channel model on the tensor cores; 2: the same with the first pass
+ * 32/64-channel model on the tensor cores; 3: the same with the first pass
+ * of single images as conv1 on the tensor cores and the depthwise conv on the
+ * CUDA cores (a slower alternative kept for comparison); 2: the first pass
  * (LN, conv1 MMA, depthwise taps) and the ending on the CUDA cores; 0: the
  * per-conv kernels everywhere. Results agree within the parity tolerance; the
  * switch exists for testing every path. */

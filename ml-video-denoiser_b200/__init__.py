@@ -354,7 +354,9 @@ class Model:
     def set_fused(self, enable=True) -> None:
         """Fused NAFBlock kernels (True / 1, default), fused with the first pass of
         the 32/64-channel blocks on the CUDA cores instead of the tensor cores (2),
-        or per-conv kernels (False / 0)."""
+        fused with the first pass of single images as conv1 on the tensor cores
+        and the depthwise conv on the CUDA cores (3), or per-conv kernels
+        (False / 0)."""
         mode = int(enable) if not isinstance(enable, bool) else (1 if enable else 0)
         check(lib().dn_model_set_fused(self._h, mode))
 

@@ -726,11 +726,12 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
         fa.dw_b = wptr<float>(b.dw_b);
         fa.partials = partials_;
         fa.err = err_;
+        const bool split = fa_split_enabled_ && b.fa_tc && fused_a_split_supported(b.C, b.dw, nimg);
         const bool tc = b.fa_tc && fa_tc_enabled_;
-        // One image through the tensor-core pass A: its last CTA also runs the
-        // SCA and folds the scale into conv3's B (no SCA launch).
-        const bool sca_in_a = tc && nimg == 1 && b3s_ != nullptr && b.f3.n_tiles == 1 && b.f3.k_chunks == 1 &&
-                              b.f3.KC == b.dw;
+        // One image through the tensor-core pass A (either form): its last CTA
+        // also runs the SCA and folds the scale into conv3's B (no SCA launch).
+        const bool sca_in_a = (tc || split) && nimg == 1 && b3s_ != nullptr && b.f3.n_tiles == 1 &&
+                              b.f3.k_chunks == 1 && b.f3.KC == b.dw;
         if (tc) {
             fa.weff = wptr<uint8_t>(b.fa_w);
             fa.b1p = wptr<float>(b.fa_b1);
@@ -742,11 +743,13 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
             fa.b3_src = wptr<uint8_t>(b.f3.bpack);
             fa.b3_dst = b3s_;
         }
-        const int grid = tc ? fused_a_tc_grid(b.C, nimg, h, w) : fused_a_grid(b.C, b.dw, nimg, h, w);
+        const int grid = split ? fused_a_split_grid(b.C, h, w)
+                               : (tc ? fused_a_tc_grid(b.C, nimg, h, w) : fused_a_grid(b.C, b.dw, nimg, h, w));
         launches_ += sca_in_a ? 2 : 3;
         prof_begin("fused_block_a", static_cast<double>(nimg) * hw * (b.C + b.dw) * 2,
                    2.0 * nimg * hw * (b.C * 2 * b.dw + 2 * b.dw * 9), s);
-        DN_TRY(tc ? launch_fused_a_tc(fa, b.C, b.dw, grid, s) : launch_fused_a(fa, b.C, b.dw, grid, s));
+        DN_TRY(split ? launch_fused_a_split(fa, b.C, b.dw, grid, s)
+                     : (tc ? launch_fused_a_tc(fa, b.C, b.dw, grid, s) : launch_fused_a(fa, b.C, b.dw, grid, s)));
         prof_end(s);
         DwParams d{};
         d.N = nimg;

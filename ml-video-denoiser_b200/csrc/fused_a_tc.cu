@@ -53,6 +53,7 @@
 #include <string>
 
 #include "fused_block.h"
+#include "sca_fold.cuh"
 #include "kernels.h"
 #include "launch.cuh"
 #include "sm100.cuh"
@@ -631,105 +632,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
             for (int w = 0; w < 4; ++w) s += sPool[(n * 4 + w) * D + c];
             p.partials[(static_cast<size_t>(n) * gridDim.x + blockIdx.x) * D + c] = s;
         }
-        if (p.b3_dst) {
-            // SCA in the last CTA (one image): fixed-order pool over the CTAs'
-            // rows, s = W mean + b, conv3's B columns scaled by s.
-            __shared__ int s_last;
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
-            __syncthreads();
-            if (s_last) {
-                __threadfence();
-                // Every phase issues all of its loads before it uses any (a
-                // few memory latencies in all): the constant SCA weights and
-                // conv3 B chunks first, then the CTAs' pool rows.
-                constexpr int kWarps = kTcThreads / 32;
-                constexpr int kOut = (D + kWarps - 1) / kWarps;  // SCA outputs per warp
-                constexpr int kCol = D / 32;                     // weight columns per lane
-                constexpr int KQ = D / 8;                        // 16-byte chunks per B row
-                constexpr int kChunks = C * KQ;
-                constexpr int kPer = (kChunks + kTcThreads - 1) / kTcThreads;
-                float wv[kOut][kCol], bo[kOut];
-#pragma unroll
-                for (int j = 0; j < kOut; ++j) {
-                    const int o = warp + kWarps * j;
-                    bo[j] = o < D ? __ldg(p.sca_b + o) : 0.f;
-#pragma unroll
-                    for (int i = 0; i < kCol; ++i) wv[j][i] = o < D ? __ldg(p.sca_w + o * D + lane + 32 * i) : 0.f;
-                }
-                uint4 bv[kPer];
-#pragma unroll
-                for (int u = 0; u < kPer; ++u) {
-                    const int i = tid + u * kTcThreads;
-                    const int n = i / KQ, q = i - n * KQ;
-                    bv[u] = i < kChunks ? __ldg(reinterpret_cast<const uint4*>(
-                                              p.b3_src + static_cast<size_t>(n >> 3) * (KQ * 128) + q * 128 + (n & 7) * 16))
-                                        : make_uint4(0, 0, 0, 0);
-                }
-                // Fixed-order pool: thread (stripe, c) sums rows stripe,
-                // stripe + stripes, ... of channel c; stripes add in order.
-                constexpr int kStripes = kTcThreads / D;  // <= 16 (sPool holds 32 D floats)
-                constexpr int kPool = 16;
-                float* s_red = sPool;                     // [kStripes][D]
-                float* s_mean = sPool + 16 * D;           // [D]
-                float* s_scale = s_mean + D;              // [D]
-                const unsigned nb = gridDim.x;
-                {
-                    const int c = tid % D, st = tid / D;
-                    if (st < kStripes) {
-                        float sum = 0.f;
-                        for (unsigned r0 = st; r0 < nb; r0 += kPool * kStripes) {
-                            float v[kPool];
-#pragma unroll
-                            for (int u = 0; u < kPool; ++u) {
-                                const unsigned r = min(r0 + u * kStripes, nb - 1);  // past the end: not added
-                                v[u] = __ldcg(p.partials + static_cast<size_t>(r) * D + c);
-                            }
-#pragma unroll
-                            for (int u = 0; u < kPool; ++u)
-                                if (r0 + u * kStripes < nb) sum += v[u];
-                        }
-                        s_red[st * D + c] = sum;
-                    }
-                }
-                __syncthreads();
-                const float inv = 1.0f / (static_cast<float>(p.H) * p.W);
-                for (int c = tid; c < D; c += kTcThreads) {
-                    float sum = 0.f;
-                    for (int st = 0; st < kStripes; ++st) sum += s_red[st * D + c];
-                    s_mean[c] = sum * inv;
-                }
-                __syncthreads();
-                // s = W mean + b: warp w evaluates outputs w, w + kWarps, ...
-#pragma unroll
-                for (int j = 0; j < kOut; ++j) {
-                    const int o = warp + kWarps * j;
-                    float acc = 0.f;
-#pragma unroll
-                    for (int i = 0; i < kCol; ++i) acc = fmaf(wv[j][i], s_mean[lane + 32 * i], acc);
-#pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-                    if (lane == 0 && o < D) s_scale[o] = acc + bo[j];
-                }
-                __syncthreads();
-                // conv3's B columns scaled by s.
-#pragma unroll
-                for (int u = 0; u < kPer; ++u) {
-                    const int i = tid + u * kTcThreads;
-                    if (i < kChunks) {
-                        const int n = i / KQ, q = i - n * KQ;
-                        float f[8];
-                        h8_to_f(bv[u], f);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) f[j] *= s_scale[8 * q + j];
-                        *reinterpret_cast<uint4*>(p.b3_dst + static_cast<size_t>(n >> 3) * (KQ * 128) + q * 128 +
-                                                  (n & 7) * 16) = f_to_h8(f);
-                    }
-                }
-                if (tid == 0) *p.counter = 0u;
-            }
-        }
+        if (p.b3_dst) sca_fold_last_cta<C, D, kTcThreads>(p, sPool, tid, warp, lane);
     }
     tc_fence_before();
     __syncthreads();

@@ -53,6 +53,12 @@ bool fused_supported(int C, int D, int F);
 bool fused_a_tc_supported(int C, int D);
 int fused_a_tc_grid(int C, int N, int H, int W);
 int launch_fused_a_tc(const FusedAParams& p, int C, int D, int grid, cudaStream_t s);
+// Phase A with conv1 on the tensor cores and the depthwise conv on the CUDA
+// cores (fused_a_split.cu): single image, C = D = 32 / 64; uses w1, c2,
+// dw_w, dw_b, partials and the SCA fold fields.
+bool fused_a_split_supported(int C, int D, int N);
+int fused_a_split_grid(int C, int H, int W);
+int launch_fused_a_split(const FusedAParams& p, int C, int D, int grid, cudaStream_t s);
 int fused_a_grid(int C, int D, int N, int H, int W);
 int launch_fused_a(const FusedAParams& p, int C, int D, int grid, cudaStream_t s);
 int launch_fused_b(const FusedBParams& p, int C, int D, int F, cudaStream_t s);

@@ -104,6 +104,33 @@ def test_w32_phase_a_paths_agree(pkg, tmp_path, hw, batch):
     assert diff <= 2e-3, diff
 
 
+@pytest.mark.parametrize("hw", [(100, 150), (37, 290), (1080, 1920)], ids=["100x150", "37x290", "1080p"])
+def test_w32_split_phase_a_agrees(pkg, tmp_path, hw):
+    """The first pass of single-image 32/64-channel blocks as conv1 on the
+    tensor cores and the depthwise conv on the CUDA cores (mode 3) meets the
+    oracle bar and agrees with the default tensor-core 3x3 form within 2e-3:
+    partial 126-column strips, border pixels on every side, the SCA fold in
+    its last CTA."""
+    synth = synth_mod(pkg)
+    h, w = hw
+    x = synth.w32_frame(h, w, seed=21).astype(np.float16).astype(np.float32)
+    synth_path, params = synth.make_model_dir(str(tmp_path), synth.CONFIG_W32, 3)
+    m = pkg.Model(synth_path)
+    xt = torch.from_numpy(x).half().cuda()
+    y_def = m(xt).clone()
+    m.set_fused(3)
+    y_split = m(xt)
+    m.sync()
+    diff = float((y_def.float() - y_split.float()).abs().max())
+    assert diff <= 2e-3, diff
+    if h * w <= 20000:
+        torch.set_num_threads(min(16, os.cpu_count() or 1))
+        ref = O.nafnet_forward(O.as_torch(params), torch.from_numpy(x)).numpy()
+        err, psnr = compare(y_split.float().cpu().numpy(), ref)
+        assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+    m.close()
+
+
 def test_w32_1080p(pkg, tmp_path):
     """NAFNet-w32 on one 1080p Poisson-Gaussian frame (the benchmark workload)."""
     synth = synth_mod(pkg)
