@@ -193,6 +193,38 @@ def cpu_baseline_fps(synth, cfg, h, w, threads: int) -> tuple[float, str]:
     return 1.0 / dt, f"1 frame {h}x{w} fp32 after a 256x256 warm-up frame ({dt:.1f} s)"
 
 
+# The conv layer shapes of NAFNet-w32 at 1080p (FP16 NHWC) and the engine
+# kernel that runs each inside the forward (several are fused with their
+# neighbours, so the kernel's own algorithmic bytes and FLOPs are reported).
+MICRO_SHAPES = [
+    ("1x1 conv 32->64 @1088x1920 (M=2088960, N=64, K=32) and depthwise 3x3 on 64 ch @1088x1920",
+     "fused_block_a@C32_1088x1920", "LN1 + conv1 1x1 32->64 + depthwise 3x3 (64 ch) + SimpleGate + pool, one kernel"),
+    ("3x3 conv 3->32 @1088x1920", "intro@C32_1088x1920", "reflect pad + nan_to_num + 3x3 conv 3->32"),
+    ("1x1 conv 256->512 @136x240 (M=32640, N=512, K=256)", "gemm_ln@M32640_N512_K256",
+     "LN1 folded + conv1 1x1 256->512 (tcgen05 GEMM)"),
+    ("LayerNorm2d + SimpleGate + SCA on 64 ch @544x960", "fused_block_a@C64_544x960",
+     "LN1 + conv1 1x1 64->128 + depthwise + SimpleGate + pool + SCA (last CTA), one kernel"),
+]
+
+
+def conv_microbench(rep_shape: dict, peaks: dict) -> list:
+    """Per config-3 shape: the engine kernel's time per launch inside the
+    1080p forward (CUDA events around each launch), its algorithmic bytes and
+    FLOPs, and the fraction of the measured HBM and tensor peaks."""
+    out = []
+    for shape, key, what in MICRO_SHAPES:
+        v = rep_shape.get(key)
+        if not v or not v["launches"]:
+            continue
+        us = 1000.0 * v["ms"] / v["launches"]
+        by, fl = v["bytes"] / v["launches"], v["flops"] / v["launches"]
+        gbs, tfs = by / (us * 1e-6) / 1e9, fl / (us * 1e-6) / 1e12
+        out.append({"shape": shape, "kernel": key, "runs": what, "us_per_launch": us, "alg_bytes": by,
+                    "alg_flops": fl, "gb_per_s": gbs, "tflop_per_s": tfs, "hbm_frac": gbs / peaks["hbm_gbs"],
+                    "tensor_frac": tfs / peaks["bf16_tflops"]})
+    return out
+
+
 REF_ENGINE = os.path.join(ROOT, "oracle", "_ref", "ref_engine")
 
 
@@ -344,6 +376,8 @@ def main() -> None:
     ap.add_argument("--no-ref-engine", action="store_true")
     ap.add_argument("--no-temporal", action="store_true", help="skip the temporal-alignment workloads")
     ap.add_argument("--no-clip", action="store_true", help="skip the 240-frame 4K clip")
+    ap.add_argument("--forward-only", action="store_true",
+                    help="diagnostics: the warm-up and timed forwards only (a short workload for ncu captures)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -418,6 +452,15 @@ def main() -> None:
         ms = float(t.item())
         dist.barrier()
     value = n_clip / (ms / 1000.0)
+    if args.forward_only:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+                              "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                              "mode": "forward-only (diagnostics, not a bench line)",
+                              "kernels_per_forward": kpf, "clocks": clk}), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
 
     # ---------------- end to end: host buffers through the C-ABI ----------------
     # A stream of frames through the pipelined host-buffer call: the input copy
@@ -450,12 +493,17 @@ def main() -> None:
     e2e = world * e2e_steps / (ems / 1000.0)
 
     # ---------------- per-kernel roofline (profiled pass, outside timing) ----------------
-    model.profile(True)
+    model.profile(True, detail=True)
     nprof = 3
     for i in range(nprof):
         model(ring[i % RING], out=outs[i % 2])
-    rep = model.profile_report()
+    rep_shape = model.profile_report()
     model.profile(False)
+    rep = {}
+    for k, v in rep_shape.items():  # per kernel kind ("kind@shape" -> "kind")
+        a = rep.setdefault(k.split("@")[0], {"launches": 0, "ms": 0.0, "bytes": 0.0, "flops": 0.0})
+        for f in a:
+            a[f] += v[f]
     peaks = measured_peaks()
     dom_kind, dom = max(rep.items(), key=lambda kv: kv[1]["ms"])
     per_launch_ms = dom["ms"] / dom["launches"]
@@ -509,6 +557,7 @@ def main() -> None:
         "frame_roofline": {"alg_bytes": frame_bytes, "alg_flops": frame_flops, "t_floor_ms": t_floor * 1000.0,
                            "frac": t_floor * 1000.0 / step_ms, "peak_source": peaks["source"]},
         "kernel_breakdown_ms_per_frame": {k: v["ms"] / nprof for k, v in sorted(rep.items(), key=lambda kv: -kv[1]["ms"])},
+        "conv_microbench": conv_microbench(rep_shape, peaks),
         "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": 3 * h * w * 2,
                 "d2h_bytes_per_step": 3 * h * w * 2, "steps": e2e_steps},
         "gpu_launches": kpf * args.steps,

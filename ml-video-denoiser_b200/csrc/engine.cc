@@ -665,8 +665,8 @@ int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cuda
     p.err = err_;
     ++launches_;
     if (profiling_) {
-        const char* kind = epi == kEpiShuffleAdd ? "gemm_up_shuffle"
-                           : amode == kAS2x2     ? "gemm_down_s2"
+        const char* kind = (epi == kEpiShuffleAdd || epi == kEpiShuffleRows) ? "gemm_up_shuffle"
+                           : (amode == kAS2x2 || amode == kAPairs) ? "gemm_down_s2"
                            : epi == kEpiGate     ? "gemm_ln_gate"
                            : pro == kProLayerNorm ? "gemm_ln"
                            : pro == kProScale    ? "gemm_sca_residual"
@@ -674,8 +674,9 @@ int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cuda
                                                  : "gemm_store";
         const double rows = p.M, n_w = static_cast<double>(g.n_tiles) * g.NT;
         double bytes = rows * g.K * 2 + n_w * g.K * 2;
-        const double n_out = epi == kEpiShuffleAdd ? 4.0 * p.out_c : p.n_out;
-        bytes += rows * n_out * 2 * (epi == kEpiResidual || epi == kEpiShuffleAdd ? 2 : 1);
+        const bool shuffle = epi == kEpiShuffleAdd || epi == kEpiShuffleRows;
+        const double n_out = shuffle ? 4.0 * p.out_c : p.n_out;
+        bytes += rows * n_out * 2 * (epi == kEpiResidual || shuffle ? 2 : 1);
         const std::string block_tag = prof_tag_;
         if (prof_detail_)
             prof_tag_ = "M" + std::to_string(p.M) + "_N" + std::to_string(g.n_tiles * g.NT) + "_K" + std::to_string(g.K);
@@ -966,10 +967,12 @@ int Engine::encode_into(const __half* src, int nimg, int in_stride, int slot0, c
     ip.w = wptr<float>(intro_w_);
     ip.b = wptr<float>(intro_b_);
     ip.y = slot_ptr(enc_x_[0], 0);
+    ip.err = err_;
     ++launches_;
+    if (prof_detail_) prof_tag_ = "C" + std::to_string(C0) + "_" + std::to_string(sh.Hp) + "x" + std::to_string(sh.Wp);
     prof_begin("intro", static_cast<double>(nimg) * (static_cast<double>(in_c) * H * W + static_cast<double>(sh.Hp) * sh.Wp * C0) * 2,
                2.0 * nimg * sh.Hp * sh.Wp * C0 * in_c * 9, s);
-    DN_TRY(launch_intro(ip, s));
+    DN_TRY(fa_tc_enabled_ && intro_tc_supported(in_c, C0) ? launch_intro_tc(ip, s) : launch_intro(ip, s));
     prof_end(s);
     for (int l = 0; l < L; ++l) {
         const int h = sh.Hp >> l, w = sh.Wp >> l;
@@ -981,7 +984,12 @@ int Engine::encode_into(const __half* src, int nimg, int in_stride, int slot0, c
         p.a[0] = xl;
         p.out = (l + 1 < L) ? slot_ptr(enc_x_[l + 1], l + 1) : slot_ptr(mid_x_, L);
         p.out_c = 2 * levels_[l].C;
-        DN_TRY(gemm(levels_[l].down, kProNone, kEpiStore, kAS2x2, p, s));
+        // Stride-2 A tiles by TMA (input rows viewed as pixel pairs) when a K
+        // chunk fits a pair of pixels; the cp.async gather otherwise.
+        const GemmW& gd = levels_[l].down;
+        const bool pairs = gemm_tma_enabled_ && gd.KC <= 2 * levels_[l].C && (2 * levels_[l].C) % gd.KC == 0 &&
+                           gd.a_swz == 2 * gd.KC;
+        DN_TRY(gemm(gd, kProNone, kEpiStore, pairs ? kAPairs : kAS2x2, p, s));
     }
     return DN_OK;
 }
@@ -1008,7 +1016,12 @@ int Engine::decode_from(__half* xm, int nimg, const std::vector<__half*>& skips,
         p.out = dec_x_[lev];
         p.out_c = levels_[lev].C;
         p.skip = skips[lev];
-        DN_TRY(gemm(levels_[lev].up, kProNone, kEpiShuffleAdd, kARows, p, s));
+        // PixelShuffle through a staged tile (two contiguous fine-row runs by
+        // TMA) when one N tile holds all four sub-pixels of 32/64 channels.
+        const GemmW& gu = levels_[lev].up;
+        const bool rows = gemm_tma_enabled_ && gu.n_tiles == 1 && gu.NT == 4 * p.out_c &&
+                          (p.out_c == 32 || p.out_c == 64);
+        DN_TRY(gemm(gu, kProNone, rows ? kEpiShuffleRows : kEpiShuffleAdd, kARows, p, s));
         DN_TRY(run_stage(levels_[lev].dec, dec_x_[lev], nimg, 2 * h, 2 * w, s));
         cur = dec_x_[lev];
     }

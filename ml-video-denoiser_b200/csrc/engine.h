@@ -100,6 +100,7 @@ public:
         fused_enabled_ = mode != 0;
         fa_tc_enabled_ = mode != 2;
         fa_split_enabled_ = mode == 3;
+        gemm_tma_enabled_ = mode == 1 || mode == 3;
     }
     // Synchronises, then returns a JSON object: kind -> {launches, ms, bytes, flops}
     // accumulated since the last report (which also resets the counters).
@@ -200,6 +201,7 @@ private:
     std::string prof_tag_;  // shape suffix of the next prof_begin in detail mode
     bool fused_enabled_ = true;
     bool fa_tc_enabled_ = true;
+    bool gemm_tma_enabled_ = true;   // stride-2 down by TMA pair loads, staged pixel-shuffle up (modes 1, 3)
     bool fa_split_enabled_ = false;  // phase A of single images: conv1 MMA + CUDA-core depthwise (mode 3)
     std::vector<ProfRec> prof_;
     std::vector<cudaEvent_t> prof_pool_;

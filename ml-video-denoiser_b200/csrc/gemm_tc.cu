@@ -111,7 +111,12 @@ struct Staging {
 template <int PRO, int EPI, int NT>
 struct SmemPlan {
     static constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
-    static constexpr int kStgBytes = (EPI == kEpiShuffleAdd) ? 0 : Staging<kOutCols>::kBytes;
+    // The row-tiled shuffle stages both fine rows of its tile: 2 x 256 pixels x NT/4 channels.
+    // At NT = 128 two such tiles alternate, so that the next tile's skip
+    // loads while the current one is finished.
+    static constexpr int kStgBytes = (EPI == kEpiShuffleAdd) ? 0
+                                     : (EPI == kEpiShuffleRows) ? (NT <= 128 ? 2 : 1) * 256 * NT
+                                                                : Staging<kOutCols>::kBytes;
     static int param_floats(const GemmParams& p) {
         return p.n_tiles * NT * (PRO == kProLayerNorm ? 2 : 1) + (EPI == kEpiResidual ? p.n_out : 0) +
                (PRO == kProScale ? p.K : 0);
@@ -135,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // launch reserves 1 KB of slack).
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     __shared__ uint64_t bar_raw[kStages], bar_full[kStages], bar_empty[kStages];
-    __shared__ uint64_t bar_acc_full[2], bar_acc_empty[2], bar_st_full[2], bar_st_empty[2], bar_res;
+    __shared__ uint64_t bar_acc_full[2], bar_acc_empty[2], bar_st_full[2], bar_st_empty[2], bar_res, bar_skip[2];
     __shared__ float2 s_stats[2][kRows];  // LN (mean, rstd) per tile row, double-buffered
     __shared__ uint32_t tslot;
     __shared__ volatile int s_abort;
@@ -159,9 +164,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    const int m_tiles = (p.M + kRows - 1) / kRows;
+    // Row-aligned tiles (2x2 stride-2 by TMA, staged shuffle): a tile is up to
+    // 128 pixels of one output row, so that its A rows / output rows map to
+    // contiguous pixel runs; otherwise 128 consecutive rows of M.
+    constexpr bool kRowT = (AMODE == kAPairs) || (EPI == kEpiShuffleRows);
+    const int xch = kRowT ? (p.Wo + kRows - 1) / kRows : 1;
+    const int m_tiles = kRowT ? (p.M / p.Wo) * xch : (p.M + kRows - 1) / kRows;
     const int n_tiles_total = m_tiles * p.n_tiles;
     const bool one_img = p.M <= p.hw;
+    // m0: first row of the tile in M; rid / x0: output row and first column
+    // (row-aligned tiles); nval: rows of the tile that exist.
+    auto tgeo = [&](int tile, int& m0, int& rid, int& x0, int& nval) {
+        const int tm = tile / p.n_tiles;
+        if (kRowT) {
+            rid = tm / xch;
+            x0 = (tm - rid * xch) * kRows;
+            m0 = rid * p.Wo + x0;
+            nval = min(kRows, p.Wo - x0);
+        } else {
+            rid = 0;
+            x0 = 0;
+            m0 = tm * kRows;
+            nval = min(kRows, p.M - m0);
+        }
+    };
 
     // Parameter vectors -> shared memory (c2 of the LN fold lives in s_bias).
     for (int i = tid; i < p.n_tiles * NT; i += kThreads) {
@@ -187,6 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bar_st_empty[b], 8);
         }
         mbar_init(&bar_res, 1);
+        mbar_init(&bar_skip[0], 1);
+        mbar_init(&bar_skip[1], 1);
         s_abort = 0;
         fence_mbar_init();
     }
@@ -213,7 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0;
             for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x) {
                 const int n_tile = tile % p.n_tiles;
-                const int m0 = (tile / p.n_tiles) * kRows;
+                int m0, rid, x0, nval;
+                tgeo(tile, m0, rid, x0, nval);
                 for (int j = 0; j < nk; ++j, ++it) {
                     const int s = it % kStages;
                     const uint32_t ph = (it / kStages) & 1;
@@ -227,7 +256,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         continue;
                     }
                     mbar_arrive_expect_tx(&bar_raw[s], AMODE == kAS2x2 ? 0u : a_bytes);
-                    if (AMODE != kAS2x2) {
+                    if (AMODE == kAPairs) {
+                        // Input row 2*rid + ky as pixel pairs: k = (2 ky + kx) C + c.
+                        const int k0 = j * KC;
+                        const int ky = k0 / (2 * p.seg_c);
+                        tma_load_3d(sa, &maps.a[0], k0 - ky * 2 * p.seg_c, x0, 2 * rid + ky, &bar_raw[s]);
+                    } else if (AMODE != kAS2x2) {
                         const int k0 = j * KC;
                         if (a_swz) {
                             // One KC-wide swizzled box (KC <= segment width).
@@ -294,7 +328,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0, t = 0;
             int s2_prev = -1;  // 2x2 gather: stage whose copies are still in flight
             for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x, ++t) {
-                const int row = (tile / p.n_tiles) * kRows + r;
+                int m0, rid, tx0, nval;
+                tgeo(tile, m0, rid, tx0, nval);
+                const int row = m0 + r;
                 const bool row_ok = row < p.M;
                 const int img = row_ok ? row / p.hw : 0;
                 const int pix = row - img * p.hw;
@@ -414,20 +450,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 hi = ch == 0 ? cols : 0;
             }
         };
-        const bool tma_epi = (EPI != kEpiShuffleAdd) && (p.out_c % kOutCols == 0);
+        const bool tma_epi = (EPI == kEpiShuffleRows) || ((EPI != kEpiShuffleAdd) && (p.out_c % kOutCols == 0));
+        int pf_slot = -1;        // staged shuffle: slot of a skip prefetch not yet waited for (leader)
+        uint32_t pf_par = 0;
         int t = 0;
         for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t) {
             const int b = t & 1;
             bool got = wait_or_abort(&bar_acc_full[b], (t >> 1) & 1, &s_abort, p.err, 0x24);
             if (kLN && got) got = wait_or_abort(&bar_st_full[b], (t >> 1) & 1, &s_abort, p.err, 0x26);
-            if (tma_epi && leader) bulk_wait_read0();  // previous tile's store has read the staging
+            // previous tile's store has read the staging (the double-buffered
+            // shuffle waits for its other buffer instead, before its prefetch)
+            if (tma_epi && leader && !(EPI == kEpiShuffleRows && NT <= 128)) bulk_wait_read0();
             // Uniform exit decision; also the "staging is free again" barrier.
             if (epi_sync_or(!got || s_abort)) break;
             tc_fence_after();
             const int n_tile = tile % p.n_tiles;
-            const int m0 = (tile / p.n_tiles) * kRows;
+            int m0, rid, x0, nval;
+            tgeo(tile, m0, rid, x0, nval);
             const int row = m0 + r;
-            const bool row_ok = row < p.M;
+            const bool row_ok = r < nval;
             const int img = row_ok ? row / p.hw : 0;
             const int pix = row - img * p.hw;
             const uint32_t lane_base = tmem + b * kAccCols + (static_cast<uint32_t>(wq * 32) << 16);
@@ -447,6 +488,74 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_2d(stg + bx * Stg::kBoxBytes, &maps.res, col0 + bx * Stg::EB, m0, &bar_res);
                 }
                 wait_or_abort(&bar_res, t & 1, &s_abort, p.err, 0x27);
+            }
+            if (EPI == kEpiShuffleRows) {
+                // PixelShuffle(2) + skip through the staging tile: column n =
+                // ij * cout + ch of coarse pixel (rid, x0 + r) lands at fine
+                // pixel (2 rid + ij/2, 2 (x0 + r) + ij%2). The tile's outputs are
+                // two contiguous runs of 256 fine pixels (rows 2 rid, 2 rid + 1):
+                // the skip of both arrives by TMA into the staging tile, each
+                // thread adds its values in place, and TMA stores the two rows
+                // (columns past the image are clipped by the tensor map). With
+                // two staging tiles (NT = 128), tile t uses tile t % 2, and the
+                // skip of the next tile is requested as soon as the stores of
+                // tile t - 1 have read its buffer.
+                constexpr int kCout = NT / 4;
+                constexpr int kRowBytes = kCout * 2;
+                constexpr int kFineRow = 256 * kRowBytes;
+                constexpr bool kDbl = NT <= 128;
+                uint8_t* sb = stg + (kDbl ? (t & 1) * 2 * kFineRow : 0);
+                auto skip_load = [&](int tl, uint8_t* dst, uint64_t* bar) {
+                    int tm0, trid, tx0, tnv;
+                    tgeo(tl, tm0, trid, tx0, tnv);
+                    mbar_arrive_expect_tx(bar, 2 * kFineRow);
+                    tma_load_3d(dst, &maps.res, 0, 2 * tx0, 2 * trid, bar);
+                    tma_load_3d(dst + kFineRow, &maps.res, 0, 2 * tx0, 2 * trid + 1, bar);
+                };
+                if (leader && (!kDbl || t == 0)) skip_load(tile, sb, &bar_skip[kDbl ? (t & 1) : 0]);
+                const int sk_slot = kDbl ? (t & 1) : 0;
+                const uint32_t sk_par = kDbl ? ((t >> 1) & 1) : (t & 1);
+                wait_or_abort(&bar_skip[sk_slot], sk_par, &s_abort, p.err, 0x28);
+                pf_slot = -1;
+                int c_lo, c_hi;
+                span(NT, c_lo, c_hi);
+#pragma unroll 1
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+                    float va[16];
+                    tmem_ld16(lane_base + c0, va);
+                    tmem_ld_wait();
+                    if (!row_ok) continue;
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        const int n = c0 + 8 * g;
+                        const int ij = n / kCout, ch = n - ij * kCout;
+                        uint8_t* sp = sb + (ij >> 1) * kFineRow + sw_offset(2 * r + (ij & 1), ch >> 3, kRowBytes);
+                        float f[8], rr[8];
+                        h8_to_f(*reinterpret_cast<const uint4*>(sp), rr);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) f[i] = va[8 * g + i] + s_bias[n + i] + rr[i];
+                        *reinterpret_cast<uint4*>(sp) = f_to_h8(f);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+                fence_async_smem();
+                epi_sync();
+                if (leader) {
+                    tma_store_3d(&maps.out, 0, 2 * x0, 2 * rid, sb);
+                    tma_store_3d(&maps.out, 0, 2 * x0, 2 * rid + 1, sb + kFineRow);
+                    bulk_commit();
+                    const int next = tile + static_cast<int>(gridDim.x);
+                    if (kDbl && next < n_tiles_total) {
+                        // The other buffer was last read by tile t - 1's stores.
+                        bulk_wait_read1();
+                        skip_load(next, stg + ((t + 1) & 1) * 2 * kFineRow, &bar_skip[(t + 1) & 1]);
+                        pf_slot = (t + 1) & 1;
+                        pf_par = static_cast<uint32_t>(((t + 1) >> 1) & 1);
+                    }
+                }
+                continue;
             }
             if (EPI == kEpiShuffleAdd) {
                 // PixelShuffle(2) scatter + skip: column n = ij * cout + ch of input
@@ -653,12 +762,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_async_smem();
             epi_sync();
             if (leader) {
-                for (int bx = 0; bx < Stg::kBoxes; ++bx)
-                    tma_store_2d(&maps.out, col0 + bx * Stg::EB, m0, stg + bx * Stg::kBoxBytes);
+                for (int bx = 0; bx < Stg::kBoxes; ++bx) {
+                    if (kRowT)
+                        tma_store_3d(&maps.out, col0 + bx * Stg::EB, x0, rid, stg + bx * Stg::kBoxBytes);
+                    else
+                        tma_store_2d(&maps.out, col0 + bx * Stg::EB, m0, stg + bx * Stg::kBoxBytes);
+                }
                 bulk_commit();
             }
         }
         if (leader) bulk_wait0();
+        // After an abort, a skip prefetch may still be landing in shared memory.
+        if (EPI == kEpiShuffleRows && leader && pf_slot >= 0) mbar_wait(&bar_skip[pf_slot], pf_par, 5000000ull);
     }
 
     __syncthreads();
@@ -700,6 +815,28 @@ int make_map(CUtensorMap* m, const void* base, long long rows, int cols, long lo
     return DN_OK;
 }
 
+// 3-D map over rows of `width` pixels of `ch` fp16 channels ([rows][width][ch],
+// contiguous) with a box of box_ch x box_w x 1 (pixels past `width` and rows
+// past `rows` read as zero and are not written).
+int make_map3(CUtensorMap* m, const void* base, long long rows, int width, int ch, int box_ch, int box_w,
+              CUtensorMapSwizzle swz) {
+    auto fn = encode_fn();
+    if (!fn) return dn_fail(DN_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ch * 2) % 16)
+        return dn_fail(DN_ERR_INVALID_ARG, "gemm: operand must be 16-byte aligned");
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(ch), static_cast<cuuint64_t>(width),
+                                static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ch) * 2, static_cast<cuuint64_t>(width) * ch * 2};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_ch), static_cast<cuuint32_t>(box_w), 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return dn_fail_str(DN_ERR_CUDA, "gemm: cuTensorMapEncodeTiled (3-D) failed (" + std::to_string(r) + ")");
+    return DN_OK;
+}
+
 CUtensorMapSwizzle swizzle_for(int row_bytes) {
     return row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
            : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
@@ -733,7 +870,17 @@ int launch_one(const GemmParams& p, cudaStream_t s) {
     if (PRO == kProLayerNorm && !p.ln_c1) return dn_fail(DN_ERR_INVALID_ARG, "gemm: LN fold needs c1");
     GemmMaps maps;
     std::memset(&maps, 0, sizeof(maps));
-    if (AMODE != kAS2x2) {
+    constexpr bool kRowT = (AMODE == kAPairs) || (EPI == kEpiShuffleRows);
+    if (kRowT && (p.Wo <= 0 || p.M % p.Wo != 0)) return dn_fail(DN_ERR_INVALID_ARG, "gemm: rows must be whole output rows");
+    if (AMODE == kAPairs) {
+        // Input [N * 2Ho rows][Wo pixel pairs][2 seg_c]: chunk j of K is row
+        // 2y + ky, pair channels k0 .. k0 + KC.
+        if (p.nseg != 1 || p.a_swz != p.KC * 2 || (2 * p.seg_c) % p.KC != 0 || p.K != 4 * p.seg_c)
+            return dn_fail(DN_ERR_UNSUPPORTED, "gemm: pair loads need one source, a swizzled A and KC | 2C");
+        const int rc = make_map3(&maps.a[0], p.a[0], static_cast<long long>(p.M / p.Wo) * 2, p.Wo, 2 * p.seg_c, p.KC,
+                                 kRows, swizzle_for(p.a_swz));
+        if (rc != DN_OK) return rc;
+    } else if (AMODE != kAS2x2) {
         if (p.nseg > 1 && p.M != p.hw) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: concat sources need one image");
         if (p.nseg == 1 && p.M != p.hw && p.a_img_stride != static_cast<long long>(p.hw) * p.seg_c)
             return dn_fail(DN_ERR_UNSUPPORTED, "gemm: batched A rows must be contiguous");
@@ -746,15 +893,25 @@ int launch_one(const GemmParams& p, cudaStream_t s) {
             if (rc != DN_OK) return rc;
         }
     }
-    if (EPI != kEpiShuffleAdd && p.out_c % kOutCols == 0) {
-        int rc = make_map(&maps.out, p.out, p.M, p.out_c, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
+    if (EPI == kEpiShuffleRows) {
+        // Fine output and skip: [N * 2Ho rows][2 Wo][out_c], boxes of one
+        // 256-pixel fine-row run of the tile.
+        if (p.out_c * 4 != NT || (p.out_c != 32 && p.out_c != 64) || p.n_tiles != 1)
+            return dn_fail(DN_ERR_UNSUPPORTED, "gemm: the staged shuffle needs NT = 4 * out_c, out_c 32 or 64");
+        const long long frows = static_cast<long long>(p.M / p.Wo) * 2;
+        int rc = make_map3(&maps.out, p.out, frows, 2 * p.Wo, p.out_c, p.out_c, 256, swizzle_for(p.out_c * 2));
+        if (rc == DN_OK) rc = make_map3(&maps.res, p.skip, frows, 2 * p.Wo, p.out_c, p.out_c, 256, swizzle_for(p.out_c * 2));
+        if (rc != DN_OK) return rc;
+    } else if (EPI != kEpiShuffleAdd && p.out_c % kOutCols == 0) {
+        int rc = kRowT ? make_map3(&maps.out, p.out, p.M / p.Wo, p.Wo, p.out_c, Stg::EB, kRows, swizzle_for(Stg::kRowBytes))
+                       : make_map(&maps.out, p.out, p.M, p.out_c, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
         if (rc != DN_OK) return rc;
         if (EPI == kEpiResidual) {
             rc = make_map(&maps.res, p.res, p.M, p.out_c, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
             if (rc != DN_OK) return rc;
         }
     }
-    const int m_tiles = (p.M + kRows - 1) / kRows;
+    const int m_tiles = kRowT ? (p.M / p.Wo) * ((p.Wo + kRows - 1) / kRows) : (p.M + kRows - 1) / kRows;
     const long long tiles = static_cast<long long>(m_tiles) * p.n_tiles;
     // TMEM: 2 accumulators of NT columns each; at most 512 columns per SM.
     const int by_tmem = 512 / (2 * (NT < 32 ? 32 : NT));
@@ -819,6 +976,13 @@ int launch_gemm(const GemmParams& p, int pro, int epi, int amode, int nt, cudaSt
         return launch_nt<kProNone, kEpiShuffleAdd, kARows>(p, nt, s);
     if (amode == kAS2x2 && pro == kProNone && epi == kEpiStore)
         return launch_nt<kProNone, kEpiStore, kAS2x2>(p, nt, s);
+    if (amode == kAPairs && pro == kProNone && epi == kEpiStore)
+        return launch_nt<kProNone, kEpiStore, kAPairs>(p, nt, s);
+    if (amode == kARows && pro == kProNone && epi == kEpiShuffleRows) {
+        if (nt == 128) return launch_one<kProNone, kEpiShuffleRows, kARows, 128>(p, s);
+        if (nt == 256) return launch_one<kProNone, kEpiShuffleRows, kARows, 256>(p, s);
+        return dn_fail(DN_ERR_UNSUPPORTED, "gemm: the staged shuffle needs a 128- or 256-wide tile");
+    }
     return dn_fail(DN_ERR_UNSUPPORTED, "gemm: unsupported prologue/epilogue combination");
 }
 

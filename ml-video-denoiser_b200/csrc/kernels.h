@@ -26,11 +26,15 @@ enum GemmEpi : int {
     kEpiGate = 1,        // SimpleGate: out[c] = (acc+b)[c] * (acc+b)[c + half] (in-tile pairs)
     kEpiResidual = 2,    // out = res + res_scale[n] * (acc + bias)
     kEpiShuffleAdd = 3,  // PixelShuffle(2) scatter + skip add
+    kEpiShuffleRows = 4, // PixelShuffle(2) + skip add through a staged tile: row-aligned tiles, NT = 4 * out_c,
+                         // out_c in {32, 64}; the skip arrives and the two fine rows leave by TMA
 };
 
 enum GemmAMode : int {
     kARows = 0,   // row m = pixel m of each segment (1x1 conv; K = nseg * seg_c)
     kAS2x2 = 1,   // 2x2 stride-2 gather: K = 4 * seg_c, tap = k / seg_c
+    kAPairs = 2,  // 2x2 stride-2 by TMA: row-aligned tiles, A chunk = input row 2y+ky viewed as pixel pairs
+                  // [Wo][2 seg_c] (k = (2 ky + kx) seg_c + c), needs KC <= 2 seg_c and a swizzled A
 };
 
 constexpr int kMaxSeg = 8;
@@ -112,8 +116,12 @@ struct IntroParams {
     const float* w;        // [C0][Cin][3][3]
     const float* b;        // [C0]
     __half* y;
+    uint32_t* err;         // error word of the tensor-core form
 };
 int launch_intro(const IntroParams& p, cudaStream_t s);
+// The same conv on the tensor cores (intro_tc.cu): an im2col MMA per strip row.
+bool intro_tc_supported(int Cin, int C0);
+int launch_intro_tc(const IntroParams& p, cudaStream_t s);
 
 // ending: NHWC (N, Hp, Wp, C0) -> 3x3 conv C0 -> 3 + bias, crop to (H, W),
 // + beauty (nan_to_num of the first 3 channels of the NCHW input) -> NCHW fp16.

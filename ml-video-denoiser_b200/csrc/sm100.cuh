@@ -338,6 +338,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int c0, 
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, int c0, int c1, int c2, int c3,
                                             uint64_t* bar) {
     asm volatile(
@@ -354,6 +362,13 @@ __device__ __forceinline__ void tma_store_2d(const void* map, int c0, int c1, co
                  : "memory");
 }
 
+__device__ __forceinline__ void tma_store_3d(const void* map, int c0, int c1, int c2, const void* src) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_store_4d(const void* map, int c0, int c1, int c2, int c3, const void* src) {
     asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
                      reinterpret_cast<uint64_t>(map)),
@@ -364,6 +379,9 @@ __device__ __forceinline__ void tma_store_4d(const void* map, int c0, int c1, in
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
