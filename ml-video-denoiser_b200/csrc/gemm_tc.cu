@@ -58,6 +58,9 @@ constexpr int kRows = 128;
 constexpr int kStages = 3;
 constexpr int kKC = 64;                 // shared-memory footprint is sized for KC = 64
 constexpr int kThreads = 480;
+// The LayerNorm-folded kernels add warps 15-18: a second group of row
+// statistics warps, so that each group handles every other ring stage.
+constexpr int kThreadsLN = 608;
 constexpr uint32_t kALbo = kRows * 16;  // 2 KB between K-adjacent core-matrix columns
 
 struct GemmMaps {
@@ -127,7 +130,7 @@ struct SmemPlan {
 };
 
 template <int PRO, int EPI, int AMODE, int NT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 1)
     gemm_ws_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ GemmMaps maps) {
     constexpr bool kLN = (PRO == kProLayerNorm);
     constexpr bool kWriteA = (PRO == kProScale) || (AMODE == kAS2x2);  // MMA waits for the transform
@@ -142,6 +145,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ uint64_t bar_raw[kStages], bar_full[kStages], bar_empty[kStages];
     __shared__ uint64_t bar_acc_full[2], bar_acc_empty[2], bar_st_full[2], bar_st_empty[2], bar_res, bar_skip[2];
     __shared__ float2 s_stats[2][kRows];  // LN (mean, rstd) per tile row, double-buffered
+    __shared__ float2 s_part[2][kRows];   // LN: second statistics group's (sum, sum of squares) per tile row
+    __shared__ uint64_t bar_part[2], bar_pfree[2];
     __shared__ uint32_t tslot;
     __shared__ volatile int s_abort;
 
@@ -190,12 +195,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     // Parameter vectors -> shared memory (c2 of the LN fold lives in s_bias).
-    for (int i = tid; i < p.n_tiles * NT; i += kThreads) {
+    constexpr int kNThr = kLN ? kThreadsLN : kThreads;
+    for (int i = tid; i < p.n_tiles * NT; i += kNThr) {
         s_bias[i] = p.bias ? p.bias[i] : 0.f;
         if (kLN) s_c1[i] = p.ln_c1[i];
     }
     if (EPI == kEpiResidual)
-        for (int i = tid; i < p.n_out; i += kThreads) s_rsc[i] = p.res_scale[i];
+        for (int i = tid; i < p.n_out; i += kNThr) s_rsc[i] = p.res_scale[i];
     if (warp == 0) {
         tmem_alloc(&tslot, kCols);
         tmem_relinquish();
@@ -215,6 +221,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bar_res, 1);
         mbar_init(&bar_skip[0], 1);
         mbar_init(&bar_skip[1], 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bar_part[b], 4);
+            mbar_init(&bar_pfree[b], 4);
+        }
         s_abort = 0;
         fence_mbar_init();
     }
@@ -227,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the SCA scale) were written by earlier kernels.
     pdl_wait();
     if (PRO == kProScale && one_img) {
-        for (int i = tid; i < p.K; i += kThreads) s_sca[i] = p.pro_scale[i];
+        for (int i = tid; i < p.K; i += kNThr) s_sca[i] = p.pro_scale[i];
         __syncthreads();
     }
 
@@ -321,10 +331,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mma_commit(&bar_acc_full[b]);
             }
         }
-    } else if (warp < 4) {
+    } else if (warp < 4 || warp >= 15) {
         // ------------------------------ transform ---------------------------------
+        // LN: statistics group g (warps 0-3, or 15-18) takes the ring stages
+        // it with it % 2 == g; group 1 hands its partial sums of each tile to
+        // group 0 through s_part.
+        const int g = warp >= 15 ? 1 : 0;
         if (kLN || kWriteA) {
-            const int r = tid;  // tile row
+            const int r = g ? tid - 15 * 32 : tid;  // tile row
             int it = 0, t = 0;
             int s2_prev = -1;  // 2x2 gather: stage whose copies are still in flight
             for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x, ++t) {
@@ -334,9 +348,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool row_ok = row < p.M;
                 const int img = row_ok ? row / p.hw : 0;
                 const int pix = row - img * p.hw;
-                float x0 = 0.f, s1 = 0.f, s2 = 0.f;
+                float s1 = 0.f, s2 = 0.f;
                 bool ok = true;
                 for (int j = 0; j < nk; ++j, ++it) {
+                    if (kLN && (it & 1) != g) continue;  // the other group's stage
                     const int s = it % kStages;
                     const uint32_t ph = (it / kStages) & 1;
                     if (!wait_or_abort(&bar_raw[s], ph, &s_abort, p.err, 0x23)) {
@@ -345,15 +360,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* sa = smem + s * stage_bytes;
                     if (kLN) {
-                        // Shifted sums of the row (shift = its first element):
-                        // every load first, then two independent packed chains.
+                        // Row sums and sums of squares. The stage is released as
+                        // soon as its values are in registers (the arrive orders
+                        // the reads before the producer's next write).
                         const int nq = min(KC, p.K - j * KC) >> 3;
                         uint4 v[8];
 #pragma unroll
                         for (int q = 0; q < 8; ++q)
                             if (q < nq) v[q] = *reinterpret_cast<const uint4*>(sa + a_off(r, q));
-                        if (j == 0) x0 = unpack_half2(v[0].x).x;
-                        const float2 nx = make_float2(-x0, -x0), one = make_float2(1.f, 1.f);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bar_empty[s]);
+                        const float2 one = make_float2(1.f, 1.f);
                         float2 a1[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
                         float2 a2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -362,16 +379,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
 #pragma unroll
                                 for (int i = 0; i < 4; ++i) {
-                                    const float2 d = ffma2(unpack_half2(w[i]), one, nx);
-                                    a1[i & 1] = ffma2(d, one, a1[i & 1]);
-                                    a2[i & 1] = ffma2(d, d, a2[i & 1]);
+                                    const float2 x = unpack_half2(w[i]);
+                                    a1[i & 1] = ffma2(x, one, a1[i & 1]);
+                                    a2[i & 1] = ffma2(x, x, a2[i & 1]);
                                 }
                             }
                         }
                         s1 += (a1[0].x + a1[0].y) + (a1[1].x + a1[1].y);
                         s2 += (a2[0].x + a2[0].y) + (a2[1].x + a2[1].y);
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&bar_empty[s]);
                     } else if (AMODE == kAS2x2) {
                         // Gather this stage's patch rows with cp.async (zero fill
                         // outside), then release the previous stage once its copies
@@ -414,11 +429,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 if (kLN) {
                     const int sb = t & 1;
+                    const uint32_t pp = (t >> 1) & 1;
+                    if (g == 1) {
+                        // Hand the partial sums over (the slot of tile t - 2 must
+                        // have been read first).
+                        if (!wait_or_abort(&bar_pfree[sb], pp ^ 1, &s_abort, p.err, 0x2a)) break;
+                        s_part[sb][r] = make_float2(s1, s2);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bar_part[sb]);
+                        continue;
+                    }
+                    if (!wait_or_abort(&bar_part[sb], pp, &s_abort, p.err, 0x2b)) break;
+                    const float2 o = s_part[sb][r];
+                    s1 += o.x;
+                    s2 += o.y;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bar_pfree[sb]);
                     if (!wait_or_abort(&bar_st_empty[sb], ((t >> 1) & 1) ^ 1, &s_abort, p.err, 0x25)) break;
                     const float inv = 1.0f / static_cast<float>(p.K);
                     const float dm = s1 * inv;
                     const float var = fmaxf(s2 * inv - dm * dm, 0.f);
-                    s_stats[sb][r] = make_float2(x0 + dm, rsqrtf(var + 1e-6f));
+                    s_stats[sb][r] = make_float2(dm, rsqrtf(var + 1e-6f));
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&bar_st_full[sb]);
                 }
@@ -918,7 +949,8 @@ int launch_one(const GemmParams& p, cudaStream_t s) {
     const int by_smem = (227 * 1024) / (smem + 2048);
     const int per_sm = std::max(1, std::min(by_tmem, by_smem));
     const long long grid = std::min<long long>(tiles, static_cast<long long>(num_sms()) * per_sm);
-    cudaError_t e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem, s, p, maps);
+    cudaError_t e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)),
+                               dim3(PRO == kProLayerNorm ? kThreadsLN : kThreads), smem, s, p, maps);
     if (e != cudaSuccess) return dn_cuda_fail(e, "gemm: launch");
     return DN_OK;
 }
