@@ -802,7 +802,9 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
                 bulk_commit();
             }
         }
-        if (leader) bulk_wait0();
+        // The last store has read the staging tile (its writes complete with
+        // the grid, before any dependent grid passes its wait).
+        if (leader) bulk_wait_read0();
         // After an abort, a skip prefetch may still be landing in shared memory.
         if (EPI == kEpiShuffleRows && leader && pf_slot >= 0) mbar_wait(&bar_skip[pf_slot], pf_par, 5000000ull);
     }
