@@ -100,6 +100,11 @@ __global__ void __launch_bounds__(kDThreads, 1)
     deep_b_kernel(const __grid_constant__ DeepBParams p, const __grid_constant__ CUtensorMap mg,
                   const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mo) {
     using G = GeoD<C>;
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&mg);
+        prefetch_tmap(&mx);
+        prefetch_tmap(&mo);
+    }
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sY = smem;                   // C/64 boxes [128 x 64], 128-byte swizzle: (g,) y, out

@@ -55,6 +55,10 @@ constexpr int kThreads = 256;
 __global__ void __launch_bounds__(kThreads, 2)
     dw_tile_kernel(const __grid_constant__ DwParams p, const __grid_constant__ CUtensorMap mu,
                    const __grid_constant__ CUtensorMap mg) {
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&mu);
+        prefetch_tmap(&mg);
+    }
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
     uint8_t* sOut = smem + 4 * kBufB;                              // [TH*TW][CS] fp16

@@ -114,6 +114,10 @@ __global__ void __launch_bounds__(kAThreads, 2)
     fused_a_kernel(const __grid_constant__ FusedAParams p, const __grid_constant__ CUtensorMap mx,
                    const __grid_constant__ CUtensorMap mg) {
     using G = GeoA<C, D>;
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&mx);
+        prefetch_tmap(&mg);
+    }
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sA = smem;
@@ -394,6 +398,11 @@ __global__ void __launch_bounds__(b_threads<C>(), 1)
     fused_b_kernel(const __grid_constant__ FusedBParams p, const __grid_constant__ CUtensorMap mg,
                    const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mo) {
     using G = GeoB<C, D, F>;
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&mg);
+        prefetch_tmap(&mx);
+        prefetch_tmap(&mo);
+    }
     constexpr int kTh = b_threads<C>();
     constexpr int kH = kTh / 128;  // threads per tile row
     constexpr int CC = C / kH, DC = D / kH, FC = F / kH;  // columns per thread

@@ -194,6 +194,14 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
         }
     };
 
+    // The tensor maps this instantiation uses (the ones the launcher encoded).
+    if (tid == 0) {
+        if (AMODE != kAS2x2)
+            for (int sgi = 0; sgi < (AMODE == kAPairs ? 1 : p.nseg); ++sgi) prefetch_tmap(&maps.a[sgi]);
+        const bool out_map = (EPI == kEpiShuffleRows) || ((EPI != kEpiShuffleAdd) && (p.out_c % kOutCols == 0));
+        if (out_map) prefetch_tmap(&maps.out);
+        if (out_map && (EPI == kEpiResidual || EPI == kEpiShuffleRows)) prefetch_tmap(&maps.res);
+    }
     // Parameter vectors -> shared memory (c2 of the LN fold lives in s_bias).
     constexpr int kNThr = kLN ? kThreadsLN : kThreads;
     for (int i = tid; i < p.n_tiles * NT; i += kNThr) {

@@ -59,6 +59,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Bring a kernel-parameter tensor map into the TMA descriptor cache, so that
+// the first copy after the grid-dependency wait does not fetch it.
+__device__ __forceinline__ void prefetch_tmap(const void* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 // Bounded wait on an mbarrier phase. Gives up after `limit_ns` of wall time
 // (checked every 64 polls) and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
