@@ -147,8 +147,11 @@ __device__ __forceinline__ typename Vec<VEC>::T pack_vec(const float (&f)[VEC]) 
 // the sample points are integer, so each item copies one vector of the NHWC
 // input (zero outside the image = zero padding); `dg` then counts blocks of
 // `cpg` input channels and B is block-diagonal for grouped convolutions.
+// Two CTAs per SM (at most ~100 KB of shared memory and 256 TMEM columns
+// each): the A-tile builders of one CTA wait on global loads while the other
+// CTA's run.
 template <int NT, int VEC, bool DEFORM>
-__global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant__ DcnParams p) {
+__global__ void __launch_bounds__(kThreads, 2) conv_kernel(const __grid_constant__ DcnParams p) {
     constexpr int kBBytes = NT * kKC * 2;
     constexpr uint32_t kCols = NT < 32 ? 32 : NT;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -204,8 +207,115 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant
                 mbar_arrive_expect_tx(&bar_b[s], kBBytes);
                 bulk_g2s(sB[s], p.bpack + static_cast<size_t>(j) * kBBytes, kBBytes, &bar_b[s]);
             }
-            // Modulated samples of chunk j: item = (pixel r, combo lc).
-            for (int item = tid; item < 128 * cpc; item += kThreads) {
+            // A tile of chunk j. The common shapes take batched paths that put
+            // all of a thread's loads in flight before any is used (one memory
+            // latency per chunk instead of one or two per item):
+            bool built = false;
+            if constexpr (!DEFORM && VEC == 8) {
+                // Regular conv, 8-channel vectors: 128 pixels x 8 vectors; thread
+                // tid takes vector kv = tid % 8 of pixels tid / 8 + 32 u, so a
+                // warp reads 4 pixels x 128 contiguous bytes.
+                const int kv = tid & 7;
+                const int kk = kv * 8, lc = kk / p.cpg, v0 = kk - lc * p.cpg;
+                const int gk = j * cpc + lc;
+                uint4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int r = (tid >> 3) + 32 * u;
+                    const int m = tile * 128 + r;
+                    v[u] = make_uint4(0u, 0u, 0u, 0u);
+                    if (m < M && gk < combos) {
+                        const int n = m / HWo;
+                        const int pix = m - n * HWo;
+                        const int ho = pix / p.Wo, wo = pix - ho * p.Wo;
+                        const int g = gk / p.KK, k = gk - g * p.KK;
+                        const int ki = k / p.kw, kj = k - ki * p.kw;
+                        const int yy = ho * p.stride - p.pad + ki * p.dil;
+                        const int xx = wo * p.stride - p.pad + kj * p.dil;
+                        if (yy >= 0 && yy < p.H && xx >= 0 && xx < p.W)
+                            v[u] = *reinterpret_cast<const uint4*>(
+                                p.xt + ((static_cast<size_t>(n) * p.H + yy) * p.W + xx) * p.Cin + g * p.cpg + v0);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    *reinterpret_cast<uint4*>(sA[s] + sw_offset((tid >> 3) + 32 * u, kv, 128)) = v[u];
+                built = true;
+            }
+            if constexpr (DEFORM && VEC == 8) {
+                if (p.cpg == 8) {
+                    // Deformable, 8 channels per group: 8 (group, tap) combos per
+                    // chunk; thread tid samples pixel tid % 128 for combos
+                    // tid / 128 + 2 u: offsets and masks of all four first, then
+                    // all 16 corner vectors, then the blends.
+                    const int r = tid & 127;
+                    const int m = tile * 128 + r;
+                    const int n = m / HWo;
+                    const int pix = m - n * HWo;
+                    const int ho = pix / p.Wo, wo = pix - ho * p.Wo;
+                    float dy[4], dx[4], raw[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int gk = j * cpc + (tid >> 7) + 2 * u;
+                        dy[u] = dx[u] = raw[u] = 0.f;
+                        if (m < M && gk < combos) {
+                            const size_t ob = (static_cast<size_t>(n) * 2 * combos + 2 * gk) * HWo + pix;
+                            const size_t mb = (static_cast<size_t>(n) * combos + gk) * HWo + pix;
+                            dy[u] = __half2float(p.off[ob]);
+                            dx[u] = __half2float(p.off[ob + HWo]);
+                            raw[u] = __half2float(p.msk[mb]);
+                            if (p.off2) {  // offsets and masks given as two terms (uniform branch)
+                                dy[u] += __half2float(p.off2[ob]);
+                                dx[u] += __half2float(p.off2[ob + HWo]);
+                                raw[u] += __half2float(p.msk2[mb]);
+                            }
+                        }
+                    }
+                    uint4 cv[4][4];
+                    float cw[4][4];
+                    const __half* base = p.xt + static_cast<size_t>(n) * p.H * p.W * p.Cin;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int gk = j * cpc + (tid >> 7) + 2 * u;
+                        const int g = gk / p.KK, k = gk - g * p.KK;
+                        const int ki = k / p.kw, kj = k - ki * p.kw;
+                        const float hs = static_cast<float>(ho * p.stride - p.pad + ki * p.dil) + dy[u];
+                        const float ws = static_cast<float>(wo * p.stride - p.pad + kj * p.dil) + dx[u];
+                        const bool in = m < M && gk < combos &&
+                                        !(hs < -1.f || hs > static_cast<float>(p.H) || ws < -1.f || ws > static_cast<float>(p.W));
+                        const int h0 = in ? static_cast<int>(floorf(hs)) : 0, w0 = in ? static_cast<int>(floorf(ws)) : 0;
+                        const float dh = hs - static_cast<float>(h0), dw = ws - static_cast<float>(w0);
+                        const float wq[4] = {(1.f - dh) * (1.f - dw), (1.f - dh) * dw, dh * (1.f - dw), dh * dw};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const int yy = h0 + (q >> 1), xx = w0 + (q & 1);
+                            cv[u][q] = make_uint4(0u, 0u, 0u, 0u);
+                            cw[u][q] = 0.f;
+                            if (in && yy >= 0 && yy < p.H && xx >= 0 && xx < p.W) {
+                                cv[u][q] = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(yy) * p.W + xx) * p.Cin + g * 8);
+                                cw[u][q] = wq[q];
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float mask = 1.f / (1.f + expf(-raw[u]));
+                        float vv[4][8], acc[8];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) h8_to_f(cv[u][q], vv[q]);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const float val = vv[0][e] * cw[u][0] + vv[1][e] * cw[u][1] + vv[2][e] * cw[u][2] +
+                                              vv[3][e] * cw[u][3];
+                            acc[e] = val * mask;
+                        }
+                        *reinterpret_cast<uint4*>(sA[s] + sw_offset(r, (tid >> 7) + 2 * u, 128)) = f_to_h8(acc);
+                    }
+                    built = true;
+                }
+            }
+            // Other shapes: item = (pixel r, combo lc), one at a time.
+            for (int item = built ? 128 * cpc : tid; item < 128 * cpc; item += kThreads) {
                 const int r = item & 127;
                 const int lc = item >> 7;
                 const int gk = j * cpc + lc;
@@ -456,7 +566,7 @@ int run_conv(const DcnParams& p, int device, cudaStream_t s) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     const int tiles = (p.N * p.Ho * p.Wo + 127) / 128;
-    const int grid = std::max(1, std::min(tiles, sms));
+    const int grid = std::max(1, std::min(tiles, 2 * sms));  // two CTAs per SM
     cudaError_t e = launch_pdl(conv_kernel<NT, VEC, DEFORM>, dim3(grid), dim3(kThreads), smem, s, p);
     return e == cudaSuccess ? DN_OK : dn_cuda_fail(e, "conv: launch");
 }
