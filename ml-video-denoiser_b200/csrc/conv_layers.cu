@@ -161,10 +161,20 @@ __global__ void __launch_bounds__(kThreads, 2) conv_kernel(const __grid_constant
     float* sBias = reinterpret_cast<float*>(smem + 2 * kABytes + 2 * kBBytes);
     __shared__ uint64_t bar_b[2], bar_mma[2];
     __shared__ float sFuse[3][128];  // kOutFuse: the second column half's partial sums per tile row
+    // Per (group/block, tap) combo: the channel offset g * cpg and the tap's
+    // row / column offsets (ki * dil, kj * dil), for the batched A builders.
+    constexpr int kMaxCombos = 512;
+    __shared__ int2 sCombo[kMaxCombos];
     __shared__ uint32_t tslot;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     for (int i = tid; i < NT; i += kThreads) sBias[i] = p.bias[i];
+    const int n_combos = p.dg * p.KK;
+    for (int gk = tid; gk < n_combos && gk < kMaxCombos; gk += kThreads) {
+        const int g = gk / p.KK, k = gk - g * p.KK;
+        const int ki = k / p.kw, kj = k - ki * p.kw;
+        sCombo[gk] = make_int2(g * p.cpg, (ki * p.dil) | ((kj * p.dil) << 16));
+    }
     if (warp == 0) {
         tmem_alloc(&tslot, kCols);
         tmem_relinquish();
@@ -191,7 +201,29 @@ __global__ void __launch_bounds__(kThreads, 2) conv_kernel(const __grid_constant
     const uint32_t idesc = idesc_f16_f32(128, NT);
     int it = 0;  // chunk counter across tiles (stage = it & 1, use = it >> 1)
     bool ok = true;
+    // The batched builders index with 32-bit element offsets and the combo
+    // table: they run when every tensor they index has < 2^31 elements.
+    const bool fast = n_combos <= kMaxCombos &&
+                      static_cast<long long>(p.N) * p.H * p.W * p.Cin < (1LL << 31) &&
+                      (!DEFORM || static_cast<long long>(p.N) * 2 * n_combos * HWo < (1LL << 31));
     for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        // Pixel coordinates of this thread's rows of the tile (batched builders):
+        // regular: rows tid / 8 + 32 u; deformable: row tid % 128.
+        int py[4], px[4], pn[4];
+        bool pok[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int r = DEFORM ? (tid & 127) : (tid >> 3) + 32 * u;
+            const int m = tile * 128 + r;
+            pok[u] = m < M;
+            const int n = pok[u] ? m / HWo : 0;
+            const int pix = pok[u] ? m - n * HWo : 0;
+            const int ho = pix / p.Wo, wo = pix - ho * p.Wo;
+            py[u] = ho * p.stride - p.pad;
+            px[u] = wo * p.stride - p.pad;
+            pn[u] = DEFORM ? pix : n * p.H;  // deformable: keep the plane index; n below
+        }
+        const int dn = DEFORM && pok[0] ? (tile * 128 + (tid & 127)) / HWo : 0;  // image of the deformable row
         for (int j = 0; j < p.k_chunks; ++j, ++it) {
             const int s = it & 1;
             const uint32_t use = static_cast<uint32_t>(it >> 1);
@@ -212,55 +244,45 @@ __global__ void __launch_bounds__(kThreads, 2) conv_kernel(const __grid_constant
             // latency per chunk instead of one or two per item):
             bool built = false;
             if constexpr (!DEFORM && VEC == 8) {
-                // Regular conv, 8-channel vectors: 128 pixels x 8 vectors; thread
-                // tid takes vector kv = tid % 8 of pixels tid / 8 + 32 u, so a
-                // warp reads 4 pixels x 128 contiguous bytes.
-                const int kv = tid & 7;
-                const int kk = kv * 8, lc = kk / p.cpg, v0 = kk - lc * p.cpg;
-                const int gk = j * cpc + lc;
-                uint4 v[4];
+                if (fast) {
+                    // Regular conv, 8-channel vectors: 128 pixels x 8 vectors; thread
+                    // tid takes vector kv = tid % 8 of pixels tid / 8 + 32 u, so a
+                    // warp reads 4 pixels x 128 contiguous bytes.
+                    const int kv = tid & 7;
+                    const int kk = kv * 8, lc = kk / p.cpg, v0 = kk - lc * p.cpg;
+                    const int gk = j * cpc + lc;
+                    const int2 cb = gk < combos ? sCombo[gk] : make_int2(0, 0);
+                    const int oy = cb.y & 0xFFFF, ox = cb.y >> 16;
+                    uint4 v[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int r = (tid >> 3) + 32 * u;
-                    const int m = tile * 128 + r;
-                    v[u] = make_uint4(0u, 0u, 0u, 0u);
-                    if (m < M && gk < combos) {
-                        const int n = m / HWo;
-                        const int pix = m - n * HWo;
-                        const int ho = pix / p.Wo, wo = pix - ho * p.Wo;
-                        const int g = gk / p.KK, k = gk - g * p.KK;
-                        const int ki = k / p.kw, kj = k - ki * p.kw;
-                        const int yy = ho * p.stride - p.pad + ki * p.dil;
-                        const int xx = wo * p.stride - p.pad + kj * p.dil;
-                        if (yy >= 0 && yy < p.H && xx >= 0 && xx < p.W)
-                            v[u] = *reinterpret_cast<const uint4*>(
-                                p.xt + ((static_cast<size_t>(n) * p.H + yy) * p.W + xx) * p.Cin + g * p.cpg + v0);
+                    for (int u = 0; u < 4; ++u) {
+                        const int yy = py[u] + oy, xx = px[u] + ox;
+                        v[u] = make_uint4(0u, 0u, 0u, 0u);
+                        if (pok[u] && gk < combos && yy >= 0 && yy < p.H && xx >= 0 && xx < p.W)
+                            v[u] = *reinterpret_cast<const uint4*>(p.xt + (((pn[u] + yy) * p.W + xx) * p.Cin + cb.x + v0));
                     }
-                }
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    *reinterpret_cast<uint4*>(sA[s] + sw_offset((tid >> 3) + 32 * u, kv, 128)) = v[u];
-                built = true;
+                    for (int u = 0; u < 4; ++u)
+                        *reinterpret_cast<uint4*>(sA[s] + sw_offset((tid >> 3) + 32 * u, kv, 128)) = v[u];
+                    built = true;
+                }
             }
             if constexpr (DEFORM && VEC == 8) {
-                if (p.cpg == 8) {
+                if (p.cpg == 8 && fast) {
                     // Deformable, 8 channels per group: 8 (group, tap) combos per
                     // chunk; thread tid samples pixel tid % 128 for combos
                     // tid / 128 + 2 u: offsets and masks of all four first, then
-                    // all 16 corner vectors, then the blends.
+                    // all 16 corner vectors, then the blends (packed fp32).
                     const int r = tid & 127;
-                    const int m = tile * 128 + r;
-                    const int n = m / HWo;
-                    const int pix = m - n * HWo;
-                    const int ho = pix / p.Wo, wo = pix - ho * p.Wo;
+                    const int pix = pn[0];
                     float dy[4], dx[4], raw[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int gk = j * cpc + (tid >> 7) + 2 * u;
                         dy[u] = dx[u] = raw[u] = 0.f;
-                        if (m < M && gk < combos) {
-                            const size_t ob = (static_cast<size_t>(n) * 2 * combos + 2 * gk) * HWo + pix;
-                            const size_t mb = (static_cast<size_t>(n) * combos + gk) * HWo + pix;
+                        if (pok[0] && gk < combos) {
+                            const int ob = (dn * 2 * combos + 2 * gk) * HWo + pix;
+                            const int mb = (dn * combos + gk) * HWo + pix;
                             dy[u] = __half2float(p.off[ob]);
                             dx[u] = __half2float(p.off[ob + HWo]);
                             raw[u] = __half2float(p.msk[mb]);
@@ -273,15 +295,14 @@ __global__ void __launch_bounds__(kThreads, 2) conv_kernel(const __grid_constant
                     }
                     uint4 cv[4][4];
                     float cw[4][4];
-                    const __half* base = p.xt + static_cast<size_t>(n) * p.H * p.W * p.Cin;
+                    const __half* base = p.xt + static_cast<size_t>(dn) * p.H * p.W * p.Cin;
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int gk = j * cpc + (tid >> 7) + 2 * u;
-                        const int g = gk / p.KK, k = gk - g * p.KK;
-                        const int ki = k / p.kw, kj = k - ki * p.kw;
-                        const float hs = static_cast<float>(ho * p.stride - p.pad + ki * p.dil) + dy[u];
-                        const float ws = static_cast<float>(wo * p.stride - p.pad + kj * p.dil) + dx[u];
-                        const bool in = m < M && gk < combos &&
+                        const int2 cb = gk < combos ? sCombo[gk] : make_int2(0, 0);
+                        const float hs = static_cast<float>(py[0] + (cb.y & 0xFFFF)) + dy[u];
+                        const float ws = static_cast<float>(px[0] + (cb.y >> 16)) + dx[u];
+                        const bool in = pok[0] && gk < combos &&
                                         !(hs < -1.f || hs > static_cast<float>(p.H) || ws < -1.f || ws > static_cast<float>(p.W));
                         const int h0 = in ? static_cast<int>(floorf(hs)) : 0, w0 = in ? static_cast<int>(floorf(ws)) : 0;
                         const float dh = hs - static_cast<float>(h0), dw = ws - static_cast<float>(w0);
@@ -292,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_kernel(const __grid_constant
                             cv[u][q] = make_uint4(0u, 0u, 0u, 0u);
                             cw[u][q] = 0.f;
                             if (in && yy >= 0 && yy < p.H && xx >= 0 && xx < p.W) {
-                                cv[u][q] = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(yy) * p.W + xx) * p.Cin + g * 8);
+                                cv[u][q] = *reinterpret_cast<const uint4*>(base + ((yy * p.W + xx) * p.Cin + cb.x));
                                 cw[u][q] = wq[q];
                             }
                         }
@@ -300,16 +321,25 @@ __global__ void __launch_bounds__(kThreads, 2) conv_kernel(const __grid_constant
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const float mask = 1.f / (1.f + expf(-raw[u]));
-                        float vv[4][8], acc[8];
+                        const uint32_t c0[4] = {cv[u][0].x, cv[u][0].y, cv[u][0].z, cv[u][0].w};
+                        const uint32_t c1[4] = {cv[u][1].x, cv[u][1].y, cv[u][1].z, cv[u][1].w};
+                        const uint32_t c2[4] = {cv[u][2].x, cv[u][2].y, cv[u][2].z, cv[u][2].w};
+                        const uint32_t c3[4] = {cv[u][3].x, cv[u][3].y, cv[u][3].z, cv[u][3].w};
+                        const float2 w0 = make_float2(cw[u][0], cw[u][0]), w1 = make_float2(cw[u][1], cw[u][1]);
+                        const float2 w2 = make_float2(cw[u][2], cw[u][2]), w3 = make_float2(cw[u][3], cw[u][3]);
+                        const float2 mk = make_float2(mask, mask), z = make_float2(0.f, 0.f);
+                        uint32_t o[4];
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) h8_to_f(cv[u][q], vv[q]);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const float val = vv[0][e] * cw[u][0] + vv[1][e] * cw[u][1] + vv[2][e] * cw[u][2] +
-                                              vv[3][e] * cw[u][3];
-                            acc[e] = val * mask;
+                        for (int i = 0; i < 4; ++i) {
+                            float2 t = ffma2(unpack_half2(c0[i]), w0, z);
+                            t = ffma2(unpack_half2(c1[i]), w1, t);
+                            t = ffma2(unpack_half2(c2[i]), w2, t);
+                            t = ffma2(unpack_half2(c3[i]), w3, t);
+                            t = ffma2(t, mk, z);
+                            o[i] = pack_half2(t.x, t.y);
                         }
-                        *reinterpret_cast<uint4*>(sA[s] + sw_offset(r, (tid >> 7) + 2 * u, 128)) = f_to_h8(acc);
+                        *reinterpret_cast<uint4*>(sA[s] + sw_offset(r, (tid >> 7) + 2 * u, 128)) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
                     }
                     built = true;
                 }
