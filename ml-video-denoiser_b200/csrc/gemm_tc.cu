@@ -649,46 +649,77 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
                 continue;
             }
             if (!tma_epi) {
-                // Direct per-row stores (outputs narrower than a staging box).
+                // Direct per-row stores from registers (outputs narrower than a
+                // staging box): per 64 columns the
+                // residual vectors are loaded before any is used; the LN fold
+                // and the gate run in packed fp32 as in the staged path.
                 int c_lo, c_hi;
                 span(kOutCols, c_lo, c_hi);
+                const float2 one2 = make_float2(1.f, 1.f);
+                const float2 rs2 = make_float2(rstd, rstd);
+                const float2 nm2 = make_float2(-rstd * mean, -rstd * mean);
+                auto fold = [&](const float* acc, int n, float2 (&y)[4]) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 bb = make_float2(s_bias[n + 2 * i], s_bias[n + 2 * i + 1]);
+                        if (kLN)
+                            y[i] = ffma2(rs2, make_float2(acc[2 * i], acc[2 * i + 1]),
+                                         ffma2(nm2, make_float2(s_c1[n + 2 * i], s_c1[n + 2 * i + 1]), bb));
+                        else
+                            y[i] = ffma2(make_float2(acc[2 * i], acc[2 * i + 1]), one2, bb);
+                    }
+                };
+                const size_t rowoff = static_cast<size_t>(row) * p.out_c;
 #pragma unroll 1
-                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-                    float va[16], vb[16];
-                    tmem_ld16(lane_base + c0, va);
-                    if (EPI == kEpiGate) tmem_ld16(lane_base + NT / 2 + c0, vb);
-                    tmem_ld_wait();
-                    const int n0 = n_tile * NT + c0;
-                    const int o0 = col0 + c0;
-                    if (!row_ok || o0 >= p.n_out) continue;
+                for (int cb = c_lo; cb < c_hi; cb += 64) {
+                    uint4 rv[8];
+                    if (EPI == kEpiResidual) {
 #pragma unroll
-                    for (int g = 0; g < 2; ++g) {
-                        const int n = n0 + 8 * g;
-                        const int o = o0 + 8 * g;
-                        if (o >= p.n_out) break;
-                        float f[8];
+                        for (int g = 0; g < 8; ++g) {
+                            const int o = col0 + cb + 8 * g;
+                            rv[g] = (row_ok && cb + 8 * g < c_hi && o < p.n_out)
+                                        ? *reinterpret_cast<const uint4*>(p.res + rowoff + o)
+                                        : make_uint4(0u, 0u, 0u, 0u);
+                        }
+                    }
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            float v = va[8 * g + i];
-                            if (kLN) v = rstd * (v - mean * s_c1[n + i]) + s_bias[n + i];
-                            else v += s_bias[n + i];
+                    for (int h = 0; h < 4; ++h) {
+                        const int c0 = cb + 16 * h;
+                        if (c0 >= c_hi) break;  // uniform across the warp
+                        float va[16], vb[16];
+                        tmem_ld16(lane_base + c0, va);
+                        if (EPI == kEpiGate) tmem_ld16(lane_base + NT / 2 + c0, vb);
+                        tmem_ld_wait();
+                        if (!row_ok) continue;
+#pragma unroll
+                        for (int g = 0; g < 2; ++g) {
+                            const int n = n_tile * NT + c0 + 8 * g;
+                            const int o = col0 + c0 + 8 * g;
+                            if (o >= p.n_out) break;
+                            float2 y[4];
+                            fold(va + 8 * g, n, y);
                             if (EPI == kEpiGate) {
-                                const int nb2 = n + NT / 2;
-                                float w2 = vb[8 * g + i];
-                                if (kLN) w2 = rstd * (w2 - mean * s_c1[nb2 + i]) + s_bias[nb2 + i];
-                                else w2 += s_bias[nb2 + i];
-                                v *= w2;
-                            }
-                            f[i] = (EPI == kEpiStore && p.relu) ? fmaxf(v, 0.f) : v;
-                        }
-                        const size_t off = static_cast<size_t>(row) * p.out_c + o;
-                        if (EPI == kEpiResidual) {
-                            float rr[8];
-                            h8_to_f(*reinterpret_cast<const uint4*>(p.res + off), rr);
+                                float2 y2[4];
+                                fold(vb + 8 * g, n + NT / 2, y2);
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) f[i] = rr[i] + s_rsc[o + i] * f[i];
+                                for (int i = 0; i < 4; ++i) y[i] = ffma2(y[i], y2[i], make_float2(0.f, 0.f));
+                            }
+                            if (EPI == kEpiStore && p.relu) {
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) y[i] = make_float2(fmaxf(y[i].x, 0.f), fmaxf(y[i].y, 0.f));
+                            }
+                            if (EPI == kEpiResidual) {
+                                const uint4 rr = rv[2 * h + g];
+                                const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+                                for (int i = 0; i < 4; ++i)
+                                    y[i] = ffma2(make_float2(s_rsc[o + 2 * i], s_rsc[o + 2 * i + 1]), y[i],
+                                                 unpack_half2(rw[i]));
+                            }
+                            *reinterpret_cast<uint4*>(p.out + rowoff + o) =
+                                make_uint4(pack_half2(y[0].x, y[0].y), pack_half2(y[1].x, y[1].y),
+                                           pack_half2(y[2].x, y[2].y), pack_half2(y[3].x, y[3].y));
                         }
-                        *reinterpret_cast<uint4*>(p.out + off) = f_to_h8(f);
                     }
                 }
                 tc_fence_before();
