@@ -297,46 +297,62 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
                 }
                 uint8_t* row = sRow + s * G::ROWB;
                 const bool row_in = r >= 0 && r < in_h;
+                // Phases over the NR pixel passes, so that their latency chains
+                // overlap: every load, then the partial sums, the lane
+                // reductions interleaved across passes, the rsqrts, and the
+                // normalisation.
                 uint4 nv[NR];
+                bool valid[NR];
 #pragma unroll
                 for (int k = 0; k < NR; ++k) {
                     const int i = k * PPR + pl;
                     const int xin = x0 - 1 + i;
-                    const bool valid = row_in && i < G::HP && xin >= 0 && xin < in_w;
-                    const uint4 v = valid ? *reinterpret_cast<const uint4*>(row + i * C * 2 + cq * 16)
-                                          : make_uint4(0u, 0u, 0u, 0u);
-                    if constexpr (MODE == 1) {  // the ending conv reads its input as is
-                        nv[k] = v;
-                        continue;
-                    }
-                    const float xs = __shfl_sync(0xffffffffu, unpack_half2(v.x).x, lead);
-                    const float2 nx = make_float2(-xs, -xs), one = make_float2(1.f, 1.f);
-                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                    float2 a1 = make_float2(0.f, 0.f), a2 = make_float2(0.f, 0.f);
+                    valid[k] = row_in && i < G::HP && xin >= 0 && xin < in_w;
+                    nv[k] = valid[k] ? *reinterpret_cast<const uint4*>(row + i * C * 2 + cq * 16)
+                                     : make_uint4(0u, 0u, 0u, 0u);
+                }
+                if constexpr (MODE == 0) {
+                    float xs[NR], s1[NR], s2[NR];
+                    const float2 one = make_float2(1.f, 1.f);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float2 d = ffma2(unpack_half2(w[j]), one, nx);
-                        a1 = ffma2(d, one, a1);
-                        a2 = ffma2(d, d, a2);
+                    for (int k = 0; k < NR; ++k) {
+                        xs[k] = __shfl_sync(0xffffffffu, unpack_half2(nv[k].x).x, lead);
+                        const float2 nx = make_float2(-xs[k], -xs[k]);
+                        const uint32_t w[4] = {nv[k].x, nv[k].y, nv[k].z, nv[k].w};
+                        float2 a1 = make_float2(0.f, 0.f), a2 = make_float2(0.f, 0.f);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float2 d = ffma2(unpack_half2(w[j]), one, nx);
+                            a1 = ffma2(d, one, a1);
+                            a2 = ffma2(d, d, a2);
+                        }
+                        s1[k] = a1.x + a1.y;
+                        s2[k] = a2.x + a2.y;
                     }
-                    float s1 = a1.x + a1.y, s2 = a2.x + a2.y;
 #pragma unroll
                     for (int m = 1; m < CPX; m <<= 1) {
-                        s1 += __shfl_xor_sync(0xffffffffu, s1, m);
-                        s2 += __shfl_xor_sync(0xffffffffu, s2, m);
-                    }
-                    const float dm = s1 * (1.0f / C);
-                    const float var = fmaxf(s2 * (1.0f / C) - dm * dm, 0.f);
-                    const float rstd = rsqrtf(var + 1e-6f);
-                    const float2 rs2 = make_float2(rstd, rstd);
-                    const float2 sh2 = make_float2(-(xs + dm) * rstd, -(xs + dm) * rstd);
-                    uint32_t o[4];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float2 y = ffma2(unpack_half2(w[j]), rs2, sh2);
-                        o[j] = pack_half2(y.x, y.y);
+                        for (int k = 0; k < NR; ++k) {
+                            s1[k] += __shfl_xor_sync(0xffffffffu, s1[k], m);
+                            s2[k] += __shfl_xor_sync(0xffffffffu, s2[k], m);
+                        }
                     }
-                    nv[k] = valid ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                    for (int k = 0; k < NR; ++k) {
+                        const float dm = s1[k] * (1.0f / C);
+                        const float var = fmaxf(s2[k] * (1.0f / C) - dm * dm, 0.f);
+                        const float rstd = rsqrtf(var + 1e-6f);
+                        const float2 rs2 = make_float2(rstd, rstd);
+                        const float2 sh2 = make_float2(-(xs[k] + dm) * rstd, -(xs[k] + dm) * rstd);
+                        const uint32_t w[4] = {nv[k].x, nv[k].y, nv[k].z, nv[k].w};
+                        uint32_t o[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float2 y = ffma2(unpack_half2(w[j]), rs2, sh2);
+                            o[j] = pack_half2(y.x, y.y);
+                        }
+                        nv[k] = valid[k] ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0u, 0u, 0u, 0u);
+                    }
                 }
                 named_sync(1, 128);  // every thread has read the pixel-major row
 #pragma unroll
