@@ -274,14 +274,13 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
     } else if (warp <= 4) {
         // ------------------------------ LayerNorm ----------------------------
         // A pixel's C/8 16-byte chunks sit in adjacent lanes (conflict-free
-        // reads of the pixel-major row); its statistics are shifted sums
-        // (shift = its first channel) reduced over those lanes. The normalised
+        // reads of the pixel-major row); its statistics (sum and sum of
+        // squares) are reduced over those lanes. The normalised
         // row stays in registers until all 128 threads have read the slot, then
         // is written back in the MMA layout [C/8][130][8 ch].
         constexpr int CPX = C / 8, PPR = 128 / CPX, NR = (G::HP + PPR - 1) / PPR;
         const int t = tid - 32;
         const int cq = t % CPX, pl = t / CPX;
-        const int lead = lane & ~(CPX - 1);
         uint32_t e = 0;
         bool ok = true;
         for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
@@ -312,17 +311,17 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
                                      : make_uint4(0u, 0u, 0u, 0u);
                 }
                 if constexpr (MODE == 0) {
-                    float xs[NR], s1[NR], s2[NR];
+                    // Sums and sums of squares of the pixel's channels (fp32 over C
+                    // values: E[x^2] - mean^2 loses nothing at these sizes).
+                    float s1[NR], s2[NR];
                     const float2 one = make_float2(1.f, 1.f);
 #pragma unroll
                     for (int k = 0; k < NR; ++k) {
-                        xs[k] = __shfl_sync(0xffffffffu, unpack_half2(nv[k].x).x, lead);
-                        const float2 nx = make_float2(-xs[k], -xs[k]);
                         const uint32_t w[4] = {nv[k].x, nv[k].y, nv[k].z, nv[k].w};
                         float2 a1 = make_float2(0.f, 0.f), a2 = make_float2(0.f, 0.f);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            const float2 d = ffma2(unpack_half2(w[j]), one, nx);
+                            const float2 d = unpack_half2(w[j]);
                             a1 = ffma2(d, one, a1);
                             a2 = ffma2(d, d, a2);
                         }
@@ -343,7 +342,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
                         const float var = fmaxf(s2[k] * (1.0f / C) - dm * dm, 0.f);
                         const float rstd = rsqrtf(var + 1e-6f);
                         const float2 rs2 = make_float2(rstd, rstd);
-                        const float2 sh2 = make_float2(-(xs[k] + dm) * rstd, -(xs[k] + dm) * rstd);
+                        const float2 sh2 = make_float2(-dm * rstd, -dm * rstd);
                         const uint32_t w[4] = {nv[k].x, nv[k].y, nv[k].z, nv[k].w};
                         uint32_t o[4];
 #pragma unroll
