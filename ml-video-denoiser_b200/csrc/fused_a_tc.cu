@@ -77,10 +77,10 @@ struct GeoT {
     static constexpr int KG = C / 8;           // 16-byte channel groups
     static constexpr int KGB = HP * 16;        // bytes per channel group of a row (LBO)
     static constexpr int ROWB = KG * KGB;      // one input-row slot
-    // Phase A at 32 channels runs two CTAs per SM (two MMA-issuing threads:
-    // one alone leaves the tensor pipe idle most of the time), each with half
-    // of TMEM and a 4-slot row ring.
-    static constexpr int CTAS = (MODE == 0 && C == 32) ? 2 : 1;
+    // At 32 channels (phase A and the ending) two CTAs run per SM (two
+    // row pipelines, so that one's latencies overlap the other's), each with
+    // half of TMEM and a 4-slot row ring.
+    static constexpr int CTAS = C == 32 ? 2 : 1;
     static constexpr int R = (C >= 64 || CTAS == 2) ? 4 : 8;  // input-row slots (a power of two)
     static constexpr int KS = C / 16;          // K = 16 steps per tap
     static constexpr int TAPB = N * 32;        // B tile of one (tap, K step): 2D rows x 16
@@ -696,7 +696,8 @@ int launch_ending_tc(const EndingParams& p, cudaStream_t s) {
     if (!p.weff) return dn_fail(DN_ERR_INVALID_ARG, "ending_tc: missing packed weights");
     if ((reinterpret_cast<uintptr_t>(p.x) & 15)) return dn_fail(DN_ERR_INVALID_ARG, "ending_tc: x must be 16-byte aligned");
     const long long units = static_cast<long long>(p.N) * ((p.W + 127) / 128) * p.H;
-    const int grid = static_cast<int>(std::max(1LL, std::min<long long>(units, sm_count())));
+    const int per_sm = p.C0 == 32 ? GeoT<32, 1>::CTAS : GeoT<64, 1>::CTAS;
+    const int grid = static_cast<int>(std::max(1LL, std::min<long long>(units, static_cast<long long>(sm_count()) * per_sm)));
     if (p.C0 == 32) return run_tc<32, 1>(p, grid, s);
     if (p.C0 == 64) return run_tc<64, 1>(p, grid, s);
     return dn_fail(DN_ERR_UNSUPPORTED, "ending_tc: channel count");
