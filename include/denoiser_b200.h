@@ -175,10 +175,12 @@ int dn_model_stats(const dn_model* model, size_t* weight_bytes, size_t* activati
  * and 256-channel blocks of a single-image forward, the ending conv of a
  * 32/64-channel model on the tensor cores; 3: the same with the first pass
  * of single images as conv1 on the tensor cores and the depthwise conv on the
- * CUDA cores (a slower alternative kept for comparison); 2: the first pass
- * (LN, conv1 MMA, depthwise taps) and the ending on the CUDA cores; 0: the
- * per-conv kernels everywhere. Results agree within the parity tolerance; the
- * switch exists for testing every path. */
+ * CUDA cores (a slower alternative kept for comparison); 4: the same as 1
+ * with the 1x1-conv GEMMs of 128/256-wide tiles on CTA pairs (cta_group::2
+ * MMAs, each CTA loading half of every B tile; also slower, kept for
+ * comparison); 2: the first pass (LN, conv1 MMA, depthwise taps) and the
+ * ending on the CUDA cores; 0: the per-conv kernels everywhere. Results agree
+ * within the parity tolerance; the switch exists for testing every path. */
 int dn_model_set_fused(dn_model* model, int enable);
 
 /* Per-launch CUDA-event timing of the engine's kernels (no reference

@@ -355,7 +355,8 @@ class Model:
         """Fused NAFBlock kernels (True / 1, default), fused with the first pass of
         the 32/64-channel blocks on the CUDA cores instead of the tensor cores (2),
         fused with the first pass of single images as conv1 on the tensor cores
-        and the depthwise conv on the CUDA cores (3), or per-conv kernels
+        and the depthwise conv on the CUDA cores (3), fused with the 1x1-conv
+        GEMMs on CTA pairs (cta_group::2 MMAs, 4), or per-conv kernels
         (False / 0)."""
         mode = int(enable) if not isinstance(enable, bool) else (1 if enable else 0)
         check(lib().dn_model_set_fused(self._h, mode))

@@ -314,7 +314,7 @@ int dn_model_stats(const dn_model* m, size_t* weight_bytes, size_t* activation_b
 
 int dn_model_set_fused(dn_model* m, int enable) {
     if (!m) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_set_fused: null model");
-    if (enable < 0 || enable > 3) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_set_fused: mode must be 0, 1, 2 or 3");
+    if (enable < 0 || enable > 4) return dn_fail(DN_ERR_INVALID_ARG, "dn_model_set_fused: mode must be 0 to 4");
     m->eng->set_fused(enable);
     return DN_OK;
 }

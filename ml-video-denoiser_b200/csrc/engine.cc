@@ -663,6 +663,11 @@ int Engine::gemm(const GemmW& g, int pro, int epi, int amode, GemmParams p, cuda
     p.ln_c1 = g.has_c1 ? wptr<float>(g.c1) : nullptr;
     p.n_out = g.n_out;
     p.err = err_;
+    // 1x1 convs with 128/256-wide tiles run on CTA pairs (cta_group::2):
+    // each SM then loads half of every B tile.
+    if (amode == kARows && gemm_pair_enabled_ && (g.NT == 128 || g.NT == 256) && p.nseg == 1 &&
+        p.M >= 2 * 128 && (epi == kEpiStore || epi == kEpiGate || epi == kEpiResidual))
+        amode = kARowsPair;
     ++launches_;
     if (profiling_) {
         const char* kind = (epi == kEpiShuffleAdd || epi == kEpiShuffleRows) ? "gemm_up_shuffle"

@@ -101,6 +101,8 @@ public:
         fa_tc_enabled_ = mode != 2;
         fa_split_enabled_ = mode == 3;
         gemm_tma_enabled_ = mode == 1 || mode == 3;
+        gemm_pair_enabled_ = mode == 4;
+        if (mode == 4) gemm_tma_enabled_ = true;
     }
     // Synchronises, then returns a JSON object: kind -> {launches, ms, bytes, flops}
     // accumulated since the last report (which also resets the counters).
@@ -202,6 +204,7 @@ private:
     bool fused_enabled_ = true;
     bool fa_tc_enabled_ = true;
     bool gemm_tma_enabled_ = true;   // stride-2 down by TMA pair loads, staged pixel-shuffle up (modes 1, 3)
+    bool gemm_pair_enabled_ = false;  // 1x1 conv GEMMs on CTA pairs, cta_group::2 (mode 4)
     bool fa_split_enabled_ = false;  // phase A of single images: conv1 MMA + CUDA-core depthwise (mode 3)
     std::vector<ProfRec> prof_;
     std::vector<cudaEvent_t> prof_pool_;

@@ -111,8 +111,11 @@ struct Staging {
 // Dynamic shared memory of one instantiation: the stage ring, the epilogue
 // staging tile (none for the PixelShuffle scatter, which stores directly)
 // and the parameter vectors it uses.
-template <int PRO, int EPI, int NT>
+template <int PRO, int EPI, int NT, int AMODE = kARows>
 struct SmemPlan {
+    // CTA pairs: 4 stages of A (128 rows) + half of the B tile.
+    static constexpr int kSt = AMODE == kARowsPair ? 4 : kStages;
+    static constexpr int kStage = kRows * kKC * 2 + (AMODE == kARowsPair ? NT / 2 : NT) * kKC * 2;
     static constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
     // The row-tiled shuffle stages both fine rows of its tile: 2 x 256 pixels x NT/4 channels.
     // At NT = 128 two such tiles alternate, so that the next tile's skip
@@ -124,9 +127,7 @@ struct SmemPlan {
         return p.n_tiles * NT * (PRO == kProLayerNorm ? 2 : 1) + (EPI == kEpiResidual ? p.n_out : 0) +
                (PRO == kProScale ? p.K : 0);
     }
-    static int bytes(const GemmParams& p) {
-        return 1024 + kStages * (kRows * kKC * 2 + NT * kKC * 2) + kStgBytes + param_floats(p) * 4;
-    }
+    static int bytes(const GemmParams& p) { return 1024 + kSt * kStage + kStgBytes + param_floats(p) * 4; }
 };
 
 template <int PRO, int EPI, int AMODE, int NT>
@@ -134,6 +135,14 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
     gemm_ws_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ GemmMaps maps) {
     constexpr bool kLN = (PRO == kProLayerNorm);
     constexpr bool kWriteA = (PRO == kProScale) || (AMODE == kAS2x2);  // MMA waits for the transform
+    // CTA pairs (kARowsPair): a tile is 256 rows; CTA `rank` of the pair owns
+    // rows [128 rank, 128 rank + 128) and loads its A rows and B rows
+    // [NT/2 rank, NT/2 rank + NT/2) into the same shared-memory offsets as its
+    // peer; the even CTA issues the M = 256 MMAs for both, the odd CTA's MMA
+    // thread forwards its stages' arrival to it.
+    constexpr bool kPair = (AMODE == kARowsPair);
+    using Plan = SmemPlan<PRO, EPI, NT, AMODE>;
+    constexpr int kSt = Plan::kSt;
     constexpr uint32_t kAccCols = NT < 32 ? 32 : NT;
     constexpr uint32_t kCols = 2 * kAccCols;  // two accumulators
     constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
@@ -142,7 +151,7 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
     // Swizzled TMA staging needs 1024-byte alignment: align by hand (the
     // launch reserves 1 KB of slack).
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    __shared__ uint64_t bar_raw[kStages], bar_full[kStages], bar_empty[kStages];
+    __shared__ uint64_t bar_raw[kSt], bar_full[kSt], bar_empty[kSt], bar_peer[kSt], bar_done;
     __shared__ uint64_t bar_acc_full[2], bar_acc_empty[2], bar_st_full[2], bar_st_empty[2], bar_res, bar_skip[2];
     __shared__ float2 s_stats[2][kRows];  // LN (mean, rstd) per tile row, double-buffered
     __shared__ float2 s_part[2][kRows];   // LN: second statistics group's (sum, sum of squares) per tile row
@@ -155,14 +164,14 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
     const uint32_t a_bytes = kRows * KC * 2;
     const uint32_t b_bytes = NT * KC * 2;
     const uint32_t b_sbo = static_cast<uint32_t>(KC / 8) * 128u;
-    const uint32_t stage_bytes = kRows * kKC * 2 + NT * kKC * 2;
+    const uint32_t stage_bytes = Plan::kStage;
     const uint32_t a_swz = static_cast<uint32_t>(p.a_swz);
     // Byte offset of 16-byte chunk q (8 channels) of tile row r in an A stage.
     auto a_off = [a_swz](int r, int q) -> uint32_t {
         return a_swz ? sw_offset(r, q, a_swz) : static_cast<uint32_t>(q) * kALbo + r * 16;
     };
-    uint8_t* stg = smem + kStages * stage_bytes;  // 1024-aligned: stage_bytes is a multiple of 1024
-    float* s_bias = reinterpret_cast<float*>(stg + SmemPlan<PRO, EPI, NT>::kStgBytes);
+    uint8_t* stg = smem + kSt * stage_bytes;  // 1024-aligned: stage_bytes is a multiple of 1024
+    float* s_bias = reinterpret_cast<float*>(stg + Plan::kStgBytes);
     float* s_c1 = s_bias + p.n_tiles * NT;                                   // LN fold only
     float* s_rsc = s_c1 + (kLN ? p.n_tiles * NT : 0);                        // residual only
     float* s_sca = s_rsc + (EPI == kEpiResidual ? p.n_out : 0);             // SCA scale of image 0
@@ -174,7 +183,11 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
     // contiguous pixel runs; otherwise 128 consecutive rows of M.
     constexpr bool kRowT = (AMODE == kAPairs) || (EPI == kEpiShuffleRows);
     const int xch = kRowT ? (p.Wo + kRows - 1) / kRows : 1;
-    const int m_tiles = kRowT ? (p.M / p.Wo) * xch : (p.M + kRows - 1) / kRows;
+    constexpr int kTileRows = kPair ? 2 * kRows : kRows;
+    const int m_tiles = kRowT ? (p.M / p.Wo) * xch : (p.M + kTileRows - 1) / kTileRows;
+    const uint32_t rank = kPair ? cluster_rank() : 0u;
+    const int tile0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int tstep = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
     const int n_tiles_total = m_tiles * p.n_tiles;
     const bool one_img = p.M <= p.hw;
     // m0: first row of the tile in M; rid / x0: output row and first column
@@ -189,8 +202,8 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
         } else {
             rid = 0;
             x0 = 0;
-            m0 = tm * kRows;
-            nval = min(kRows, p.M - m0);
+            m0 = tm * kTileRows + static_cast<int>(rank) * kRows;
+            nval = min(kRows, p.M - m0);  // <= 0 for the odd CTA past the last row
         }
     };
 
@@ -211,18 +224,25 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
     if (EPI == kEpiResidual)
         for (int i = tid; i < p.n_out; i += kNThr) s_rsc[i] = p.res_scale[i];
     if (warp == 0) {
-        tmem_alloc(&tslot, kCols);
-        tmem_relinquish();
+        if (kPair) {
+            tmem_alloc_pair(&tslot, kCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(&tslot, kCols);
+            tmem_relinquish();
+        }
     }
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kSt; ++s) {
             mbar_init(&bar_raw[s], 2);  // the A and the B producer
             mbar_init(&bar_full[s], 4);
             mbar_init(&bar_empty[s], kLN ? 5 : 1);  // LN: MMA commit + 4 statistics warps
+            mbar_init(&bar_peer[s], 1);             // pairs: the odd CTA's stage has landed
         }
+        mbar_init(&bar_done, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bar_acc_full[b], 1);
-            mbar_init(&bar_acc_empty[b], 8);
+            mbar_init(&bar_acc_empty[b], kPair ? 16 : 8);  // pairs: both CTAs' epilogue warps
             mbar_init(&bar_st_full[b], 4);
             mbar_init(&bar_st_empty[b], 8);
         }
@@ -237,7 +257,10 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
         fence_mbar_init();
     }
     tc_fence_before();
-    __syncthreads();
+    if (kPair)
+        cluster_sync_all();  // both CTAs' barriers exist before either arrives on the other's
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
     pdl_trigger();  // only once this CTA holds its TMEM columns
@@ -257,19 +280,22 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
         const bool is_b = (warp == 14);
         if (lane == 0) {
             int it = 0;
-            for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x) {
+            for (int tile = tile0; tile < n_tiles_total && !s_abort; tile += tstep) {
                 const int n_tile = tile % p.n_tiles;
                 int m0, rid, x0, nval;
                 tgeo(tile, m0, rid, x0, nval);
                 for (int j = 0; j < nk; ++j, ++it) {
-                    const int s = it % kStages;
-                    const uint32_t ph = (it / kStages) & 1;
+                    const int s = it % kSt;
+                    const uint32_t ph = (it / kSt) & 1;
                     if (!wait_or_abort(&bar_empty[s], ph ^ 1, &s_abort, p.err, 0x20)) break;
                     uint8_t* sa = smem + s * stage_bytes;
                     uint8_t* sb = sa + kRows * kKC * 2;
                     if (is_b) {
-                        mbar_arrive_expect_tx(&bar_raw[s], b_bytes);
-                        bulk_g2s(sb, p.bpack + (static_cast<size_t>(n_tile) * nk + j) * b_bytes, b_bytes,
+                        // Pairs: this CTA's half of the B tile (its first NT/2 rows are
+                        // the first half of the tile image).
+                        const uint32_t bb = kPair ? b_bytes / 2 : b_bytes;
+                        mbar_arrive_expect_tx(&bar_raw[s], bb);
+                        bulk_g2s(sb, p.bpack + (static_cast<size_t>(n_tile) * nk + j) * b_bytes + rank * bb, bb,
                                  &bar_raw[s]);
                         continue;
                     }
@@ -297,11 +323,37 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
                     }
                 }
             }
+            // Pairs: the even CTA's MMA commits arrive on this CTA's stage
+            // barriers; before the CTA may exit, every issued stage must have
+            // been released (so no arrive lands after it).
+            if (kPair && !is_b && !s_abort)
+                for (int k = max(0, it - kSt); k < it; ++k)
+                    if (!wait_or_abort(&bar_empty[k % kSt], (k / kSt) & 1, &s_abort, p.err, 0x2c)) break;
         }
     } else if (warp == 13) {
         // ------------------------------ MMA issuer --------------------------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(kRows, NT);
+        if (lane == 0 && kPair && rank == 1) {
+            // The odd CTA of a pair: forward each stage's arrival in this CTA's
+            // shared memory to the even CTA, whose thread issues the MMAs.
+            int s = 0;
+            uint32_t ph = 0;
+            for (int tile = tile0; tile < n_tiles_total && !s_abort; tile += tstep) {
+                bool ok = true;
+                for (int j = 0; j < nk; ++j) {
+                    if (!wait_or_abort(kWriteA ? &bar_full[s] : &bar_raw[s], ph, &s_abort, p.err, 0x2d)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_remote(peer_addr(&bar_peer[s], 0));
+                    if (++s == kSt) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+                if (!ok) break;
+            }
+        } else if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(kPair ? 2 * kRows : kRows, NT);
             // The issuing thread is on the critical path of every stage: the
             // descriptors of stage 0 are built once, and each MMA only adds a
             // stage offset and a K-step offset (16-byte units) to them.
@@ -312,14 +364,15 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
             const int nks = KC / 16;
             int s = 0, t = 0;
             uint32_t ph = 0;
-            for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x, ++t) {
+            for (int tile = tile0; tile < n_tiles_total && !s_abort; tile += tstep, ++t) {
                 const int b = t & 1;
                 if (!wait_or_abort(&bar_acc_empty[b], ((t >> 1) & 1) ^ 1, &s_abort, p.err, 0x21)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + b * kAccCols;
                 bool ok = true;
                 for (int j = 0; j < nk; ++j) {
-                    if (!wait_or_abort(kWriteA ? &bar_full[s] : &bar_raw[s], ph, &s_abort, p.err, 0x22)) {
+                    if (!wait_or_abort(kWriteA ? &bar_full[s] : &bar_raw[s], ph, &s_abort, p.err, 0x22) ||
+                        (kPair && !wait_or_abort(&bar_peer[s], ph, &s_abort, p.err, 0x2e))) {
                         ok = false;
                         break;
                     }
@@ -327,16 +380,28 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
                     const uint64_t so = static_cast<uint64_t>(s) * (stage_bytes >> 4);
                     const uint64_t ad = ad0 + so, bd = bd0 + so;
 #pragma unroll
-                    for (int k = 0; k < kKC / 16; ++k)
-                        if (k < nks) mma_f16(acc, ad + k * a_kstep, bd + 16 * k, idesc, (j > 0 || k > 0) ? 1u : 0u);
-                    mma_commit(&bar_empty[s]);
-                    if (++s == kStages) {
+                    for (int k = 0; k < kKC / 16; ++k) {
+                        if (k < nks) {
+                            if (kPair)
+                                mma_f16_pair(acc, ad + k * a_kstep, bd + 16 * k, idesc, (j > 0 || k > 0) ? 1u : 0u);
+                            else
+                                mma_f16(acc, ad + k * a_kstep, bd + 16 * k, idesc, (j > 0 || k > 0) ? 1u : 0u);
+                        }
+                    }
+                    if (kPair)
+                        mma_commit_pair(&bar_empty[s]);  // both CTAs' stage s
+                    else
+                        mma_commit(&bar_empty[s]);
+                    if (++s == kSt) {
                         s = 0;
                         ph ^= 1;
                     }
                 }
                 if (!ok) break;
-                mma_commit(&bar_acc_full[b]);
+                if (kPair)
+                    mma_commit_pair(&bar_acc_full[b]);
+                else
+                    mma_commit(&bar_acc_full[b]);
             }
         }
     } else if (warp < 4 || warp >= 15) {
@@ -349,7 +414,7 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
             const int r = g ? tid - 15 * 32 : tid;  // tile row
             int it = 0, t = 0;
             int s2_prev = -1;  // 2x2 gather: stage whose copies are still in flight
-            for (int tile = blockIdx.x; tile < n_tiles_total && !s_abort; tile += gridDim.x, ++t) {
+            for (int tile = tile0; tile < n_tiles_total && !s_abort; tile += tstep, ++t) {
                 int m0, rid, tx0, nval;
                 tgeo(tile, m0, rid, tx0, nval);
                 const int row = m0 + r;
@@ -360,8 +425,8 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
                 bool ok = true;
                 for (int j = 0; j < nk; ++j, ++it) {
                     if (kLN && (it & 1) != g) continue;  // the other group's stage
-                    const int s = it % kStages;
-                    const uint32_t ph = (it / kStages) & 1;
+                    const int s = it % kSt;
+                    const uint32_t ph = (it / kSt) & 1;
                     if (!wait_or_abort(&bar_raw[s], ph, &s_abort, p.err, 0x23)) {
                         ok = false;
                         break;
@@ -478,6 +543,14 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
         const int r = wq * 32 + lane;            // tile row == TMEM lane
         const int ch = (warp - 4) >> 2;          // column group
         const bool leader = (tid == 128);
+        // The accumulator is drained: pairs count both CTAs' epilogue warps on
+        // the even CTA's barrier.
+        auto release_acc = [&](int b) {
+            if (kPair && rank == 1)
+                mbar_arrive_remote(peer_addr(&bar_acc_empty[b], 0));
+            else
+                mbar_arrive(&bar_acc_empty[b]);
+        };
         // [lo, hi) of a span of `cols` columns for this warp's group (spans
         // narrower than 32 stay with group 0)
         auto span = [ch](int cols, int& lo, int& hi) {
@@ -493,7 +566,7 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
         int pf_slot = -1;        // staged shuffle: slot of a skip prefetch not yet waited for (leader)
         uint32_t pf_par = 0;
         int t = 0;
-        for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t) {
+        for (int tile = tile0; tile < n_tiles_total; tile += tstep, ++t) {
             const int b = t & 1;
             bool got = wait_or_abort(&bar_acc_full[b], (t >> 1) & 1, &s_abort, p.err, 0x24);
             if (kLN && got) got = wait_or_abort(&bar_st_full[b], (t >> 1) & 1, &s_abort, p.err, 0x26);
@@ -578,7 +651,7 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+                if (lane == 0) release_acc(b);
                 fence_async_smem();
                 epi_sync();
                 if (leader) {
@@ -645,7 +718,7 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+                if (lane == 0) release_acc(b);
                 continue;
             }
             if (!tma_epi) {
@@ -724,7 +797,7 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+                if (lane == 0) release_acc(b);
                 continue;
             }
             // Swizzled staging tile -> TMA tensor store. Per 8 columns:
@@ -828,10 +901,10 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
             // TMEM of this accumulator is no longer needed.
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+            if (lane == 0) release_acc(b);
             fence_async_smem();
             epi_sync();
-            if (leader) {
+            if (leader && nval > 0) {  // (the odd CTA of a pair can lie wholly past the last row)
                 for (int bx = 0; bx < Stg::kBoxes; ++bx) {
                     if (kRowT)
                         tma_store_3d(&maps.out, col0 + bx * Stg::EB, x0, rid, stg + bx * Stg::kBoxBytes);
@@ -851,14 +924,26 @@ __global__ void __launch_bounds__(PRO == kProLayerNorm ? kThreadsLN : kThreads, 
     __syncthreads();
     if (s_abort && tid == 0) {
         // Let in-flight copies and MMAs land before the CTA's memory is released.
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kSt; ++s) {
             mbar_wait(&bar_raw[s], 0, 5000000ull);
             mbar_wait(&bar_empty[s], 0, 5000000ull);
         }
     }
+    if (kPair && tid == 0) {
+        // Neither CTA of a pair leaves (or frees its TMEM) before the other
+        // is done with the MMAs that read its shared memory and with its
+        // arrives on the other's barriers.
+        mbar_arrive_remote(peer_addr(&bar_done, rank ^ 1u));
+        if (!mbar_wait(&bar_done, 0)) report_error(p.err, 0x2f, kErrMbarTimeout);
+    }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, kCols);
+    if (warp == 0) {
+        if (kPair)
+            tmem_dealloc_pair(tmem, kCols);
+        else
+            tmem_dealloc(tmem, kCols);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -931,7 +1016,7 @@ int launch_one(const GemmParams& p, cudaStream_t s) {
     auto kern = gemm_ws_kernel<PRO, EPI, AMODE, NT>;
     constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
     using Stg = Staging<kOutCols>;
-    const int smem = SmemPlan<PRO, EPI, NT>::bytes(p);
+    const int smem = SmemPlan<PRO, EPI, NT, AMODE>::bytes(p);
     if (smem > 225 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: tile does not fit in shared memory");
     static int configured = 0;  // largest dynamic footprint granted so far
     if (smem > configured) {
@@ -983,15 +1068,24 @@ int launch_one(const GemmParams& p, cudaStream_t s) {
             if (rc != DN_OK) return rc;
         }
     }
-    const int m_tiles = kRowT ? (p.M / p.Wo) * ((p.Wo + kRows - 1) / kRows) : (p.M + kRows - 1) / kRows;
+    constexpr bool kPair = (AMODE == kARowsPair);
+    constexpr int kTileRows = kPair ? 2 * kRows : kRows;
+    const int m_tiles = kRowT ? (p.M / p.Wo) * ((p.Wo + kRows - 1) / kRows) : (p.M + kTileRows - 1) / kTileRows;
     const long long tiles = static_cast<long long>(m_tiles) * p.n_tiles;
     // TMEM: 2 accumulators of NT columns each; at most 512 columns per SM.
     const int by_tmem = 512 / (2 * (NT < 32 ? 32 : NT));
     const int by_smem = (227 * 1024) / (smem + 2048);
     const int per_sm = std::max(1, std::min(by_tmem, by_smem));
-    const long long grid = std::min<long long>(tiles, static_cast<long long>(num_sms()) * per_sm);
-    cudaError_t e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)),
-                               dim3(PRO == kProLayerNorm ? kThreadsLN : kThreads), smem, s, p, maps);
+    const dim3 block(PRO == kProLayerNorm ? kThreadsLN : kThreads);
+    cudaError_t e;
+    if (kPair) {
+        // One cluster of two CTAs per pair tile, at most one pair per two SMs.
+        const long long pairs = std::min<long long>(tiles, static_cast<long long>(num_sms() / 2) * per_sm);
+        e = launch_pdl_pair(kern, dim3(static_cast<unsigned>(2 * pairs)), block, smem, s, p, maps);
+    } else {
+        const long long grid = std::min<long long>(tiles, static_cast<long long>(num_sms()) * per_sm);
+        e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), block, smem, s, p, maps);
+    }
     if (e != cudaSuccess) return dn_cuda_fail(e, "gemm: launch");
     return DN_OK;
 }
@@ -1035,6 +1129,27 @@ int launch_gemm(const GemmParams& p, int pro, int epi, int amode, int nt, cudaSt
     if (pro == kProLayerNorm && p.nseg != 1) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: LN needs one source");
     if (p.nseg < 1 || p.nseg > kMaxSeg) return dn_fail(DN_ERR_INVALID_ARG, "gemm: bad segment count");
     // Instantiated combinations (the ones the planner emits).
+    if (amode == kARowsPair) {  // CTA pairs: 128/256-wide tiles of the 1x1 convs
+        if (p.nseg == 1 && (nt == 128 || nt == 256)) {
+            const bool w = nt == 256;
+            if (pro == kProLayerNorm && epi == kEpiStore)
+                return w ? launch_one<kProLayerNorm, kEpiStore, kARowsPair, 256>(p, s)
+                         : launch_one<kProLayerNorm, kEpiStore, kARowsPair, 128>(p, s);
+            if (pro == kProLayerNorm && epi == kEpiGate)
+                return w ? launch_one<kProLayerNorm, kEpiGate, kARowsPair, 256>(p, s)
+                         : launch_one<kProLayerNorm, kEpiGate, kARowsPair, 128>(p, s);
+            if (pro == kProScale && epi == kEpiResidual)
+                return w ? launch_one<kProScale, kEpiResidual, kARowsPair, 256>(p, s)
+                         : launch_one<kProScale, kEpiResidual, kARowsPair, 128>(p, s);
+            if (pro == kProNone && epi == kEpiResidual)
+                return w ? launch_one<kProNone, kEpiResidual, kARowsPair, 256>(p, s)
+                         : launch_one<kProNone, kEpiResidual, kARowsPair, 128>(p, s);
+            if (pro == kProNone && epi == kEpiStore)
+                return w ? launch_one<kProNone, kEpiStore, kARowsPair, 256>(p, s)
+                         : launch_one<kProNone, kEpiStore, kARowsPair, 128>(p, s);
+        }
+        amode = kARows;
+    }
     if (amode == kARows && pro == kProLayerNorm && epi == kEpiStore)
         return launch_nt<kProLayerNorm, kEpiStore, kARows>(p, nt, s);
     if (amode == kARows && pro == kProLayerNorm && epi == kEpiGate)

@@ -33,6 +33,8 @@ enum GemmEpi : int {
 enum GemmAMode : int {
     kARows = 0,   // row m = pixel m of each segment (1x1 conv; K = nseg * seg_c)
     kAS2x2 = 1,   // 2x2 stride-2 gather: K = 4 * seg_c, tap = k / seg_c
+    kARowsPair = 3,  // kARows on CTA pairs (clusters of 2): 256-row tiles, one cta_group::2 MMA per K step,
+                     // each CTA loading its 128 A rows and half of the B tile
     kAPairs = 2,  // 2x2 stride-2 by TMA: row-aligned tiles, A chunk = input row 2y+ky viewed as pixel pairs
                   // [Wo][2 seg_c] (k = (2 ky + kx) seg_c + c), needs KC <= 2 seg_c and a swizzled A
 };

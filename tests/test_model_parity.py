@@ -131,6 +131,35 @@ def test_w32_split_phase_a_agrees(pkg, tmp_path, hw):
     m.close()
 
 
+@pytest.mark.parametrize("hw,batch", [((200, 328), 1), ((100, 150), 2), ((1080, 1920), 1)],
+                         ids=["200x328", "100x150_b2", "1080p"])
+def test_w32_pair_gemms_agree(pkg, tmp_path, hw, batch):
+    """The 1x1-conv GEMMs on CTA pairs (mode 4: cta_group::2 MMAs over 256-row
+    tiles, each CTA loading half of every B tile) meet the oracle bar and agree
+    with the default single-CTA GEMMs within 2e-3. The sizes give partial last
+    pair tiles, and at 1080p (M = 32640 at 256 channels) a last pair whose odd
+    CTA lies wholly past the last row; batch 2 runs the SCA-scaled conv3."""
+    synth = synth_mod(pkg)
+    h, w = hw
+    x = np.concatenate([synth.w32_frame(h, w, seed=31 + i) for i in range(batch)])
+    x = x.astype(np.float16).astype(np.float32)
+    path, params = synth.make_model_dir(str(tmp_path), synth.CONFIG_W32, 4)
+    m = pkg.Model(path)
+    xt = torch.from_numpy(x).half().cuda()
+    y_def = m(xt).clone()
+    m.set_fused(4)
+    y_pair = m(xt)
+    m.sync()
+    diff = float((y_def.float() - y_pair.float()).abs().max())
+    assert diff <= 2e-3, diff
+    if h * w <= 70000:
+        torch.set_num_threads(min(16, os.cpu_count() or 1))
+        ref = O.nafnet_forward(O.as_torch(params), torch.from_numpy(x)).numpy()
+        err, psnr = compare(y_pair.float().cpu().numpy(), ref)
+        assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+    m.close()
+
+
 def test_w32_1080p(pkg, tmp_path):
     """NAFNet-w32 on one 1080p Poisson-Gaussian frame (the benchmark workload)."""
     synth = synth_mod(pkg)
