@@ -27,7 +27,7 @@ struct dn_model {
         void* dy[2] = {nullptr, nullptr};
         size_t dx_bytes = 0, dy_bytes = 0;
         cudaStream_t h2d = nullptr, d2h = nullptr;
-        cudaEvent_t call[2] = {}, in_ready[2] = {}, in_free[2] = {}, out_ready[2] = {}, out_free[2] = {};
+        cudaEvent_t in_ready[2] = {}, in_free[2] = {}, out_ready[2] = {}, out_free[2] = {};
         unsigned count = 0;  // calls issued
         bool init = false;
     } pipe;
@@ -106,7 +106,7 @@ int dn_model_destroy(dn_model* m) {
             for (int k = 0; k < 2; ++k) {
                 if (q.dx[k]) cudaFree(q.dx[k]);
                 if (q.dy[k]) cudaFree(q.dy[k]);
-                for (cudaEvent_t ev : {q.call[k], q.in_ready[k], q.in_free[k], q.out_ready[k], q.out_free[k]})
+                for (cudaEvent_t ev : {q.in_ready[k], q.in_free[k], q.out_ready[k], q.out_free[k]})
                     cudaEventDestroy(ev);
             }
             cudaStreamDestroy(q.h2d);
@@ -226,7 +226,7 @@ int dn_model_forward_host_async(dn_model* m, const void* x_host, const int64_t* 
             e = cudaStreamCreateWithFlags(&q.h2d, cudaStreamNonBlocking);
             if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&q.d2h, cudaStreamNonBlocking);
             for (int k = 0; k < 2 && e == cudaSuccess; ++k)
-                for (cudaEvent_t* ev : {&q.call[k], &q.in_ready[k], &q.in_free[k], &q.out_ready[k], &q.out_free[k]})
+                for (cudaEvent_t* ev : {&q.in_ready[k], &q.in_free[k], &q.out_ready[k], &q.out_free[k]})
                     if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
             if (e != cudaSuccess) return dn_cuda_fail(e, "dn_model_forward_host_async: set-up");
             q.init = true;
@@ -257,11 +257,11 @@ int dn_model_forward_host_async(dn_model* m, const void* x_host, const int64_t* 
         }
         const int k = static_cast<int>(q.count & 1u);
         const bool reuse = q.count >= 2;  // staging pair k was used two calls ago
-        // Input copy: after earlier work on the caller's stream and after the
-        // forward two calls back has read this staging buffer.
-        e = cudaEventRecord(q.call[k], s);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(q.h2d, q.call[k], 0);
-        if (e == cudaSuccess && reuse) e = cudaStreamWaitEvent(q.h2d, q.in_free[k], 0);
+        // Input copy: once the forward two calls back has read this staging
+        // buffer. It does not wait for the work already queued on the
+        // caller's stream (the previous call's forward): that is what lets
+        // it overlap that forward. The host data is ready at the call.
+        if (reuse) e = cudaStreamWaitEvent(q.h2d, q.in_free[k], 0);
         if (e == cudaSuccess) e = cudaMemcpyAsync(q.dx[k], x_host, xb, cudaMemcpyHostToDevice, q.h2d);
         if (e == cudaSuccess) e = cudaEventRecord(q.in_ready[k], q.h2d);
         // Forward on the caller's stream, once the input has landed and the
