@@ -6,13 +6,16 @@
 //   * two TMA loads bring the (TH+2) x (TW+2) halo of both gate halves of the
 //     slice (u channels [c, c+32) and [D+c, D+c+32)) into shared memory,
 //     zero-filled outside the image (the conv's zero padding);
-//   * a thread owns one gate half x 8 channels (taps in registers) at one
-//     column and produces two vertically adjacent outputs from a 4-row
-//     sliding window; the halves of a gate pair are adjacent lanes;
-//   * the gated tile leaves by one TMA store; the tile's per-channel sums
-//     (of the stored fp16 values) add, in the CTA's fixed tile order, to the
-//     CTA's running sums, written once to partials[img][blockIdx.x][channel]
-//     (one pool row per CTA keeps the SCA kernel's re-reduction short).
+//   * a thread owns one gate half x 8 channels (fp16 taps in registers) at
+//     one column and produces four vertically adjacent outputs from a 6-row
+//     window, multiplying fp16 inputs by fp16 taps into fp32 sums with
+//     mixed-precision FMAs (the fp32 result of the widened operands, without
+//     converting them); the halves of a gate pair are lanes l and l^8;
+//   * the gated tile leaves by one TMA store; each thread adds the stored
+//     fp16 values of its column to running sums, in the CTA's fixed tile
+//     order; after the walk they reduce over columns and warps in a fixed
+//     order into partials[img][blockIdx.x][channel] (one pool row per CTA
+//     keeps the SCA kernel's re-reduction short).
 // Each input element crosses the memory system once (plus the 1-pixel halo),
 // instead of once per tap.
 //
@@ -40,13 +43,14 @@ namespace {
 
 constexpr int kCS = 32;            // gated channels per CTA
 constexpr int kTH = 8, kTW = 32;   // output tile
+constexpr int kR = 4;              // output rows per thread per window
 constexpr int kHH = kTH + 2, kWW = kTW + 2;
 constexpr int kP = kHH * kWW;      // halo pixels
 constexpr int kRowB = kCS * 2;     // 64 bytes per halo pixel and half
 constexpr int kBufB = ((kP * kRowB + 127) / 128) * 128;
 constexpr int kOutB = kTH * kTW * kCS * 2;
-constexpr int kSmem = 128 + 4 * kBufB + kOutB + kTW * kCS * 4;  // 2 halo buffers x 2 gate halves
 constexpr int kThreads = 256;
+constexpr int kSmem = 128 + 4 * kBufB + kOutB + (kThreads / 32) * kCS * 4;  // 2 halo buffers x 2 gate halves
 
 // Lane layout inside a warp (32 lanes = 4 columns): bits 0-1 channel group,
 // bit 2 column low bit, bit 3 gate half, bit 4 column high bit. Eight
@@ -62,7 +66,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
     uint8_t* sOut = smem + 4 * kBufB;                              // [TH*TW][CS] fp16
-    float* sRed = reinterpret_cast<float*>(sOut + kOutB);          // [TW columns][CS]
+    float* sRed = reinterpret_cast<float*>(sOut + kOutB);          // [warps][CS]
     __shared__ uint64_t bar[2];
 
     const int tid = threadIdx.x;
@@ -83,15 +87,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int half = (lane >> 3) & 1;
     const int px = (tid >> 5) * 4 + ((lane >> 4) << 1) + ((lane >> 2) & 1);  // 0..31
     const int cin = half * D + cs0 + cg * 8;
-    float2 w[9][4];
-    float2 bias[4];
+    uint32_t w[9][4];  // taps of channels (cin + 2i, cin + 2i + 1) as fp16 pairs
+    float bias[8];
 #pragma unroll
-    for (int t = 0; t < 9; ++t)
+    for (int t = 0; t < 9; ++t) {
+        const uint4 v = *reinterpret_cast<const uint4*>(p.w16 + t * 2 * D + cin);
+        w[t][0] = v.x;
+        w[t][1] = v.y;
+        w[t][2] = v.z;
+        w[t][3] = v.w;
+    }
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            w[t][i] = make_float2(p.w[t * 2 * D + cin + 2 * i], p.w[t * 2 * D + cin + 2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) bias[i] = make_float2(p.b[cin + 2 * i], p.b[cin + 2 * i + 1]);
+    for (int i = 0; i < 8; ++i) bias[i] = p.b[cin + i];
     __syncthreads();  // barriers initialised before anyone waits on them
     pdl_wait();
     // Halo of tile t (both gate halves) into buffer b.
@@ -107,7 +114,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (static_cast<int>(blockIdx.x + gridDim.x) < ntiles) load(blockIdx.x + gridDim.x, 1);
     }
 
-    float cta_sum = 0.f;  // threads tid < kCS: running pool sum of channel cs0 + tid
+    // Running pool sums over the CTA's tiles (in its fixed tile order) of
+    // channels cs0 + cg * 8 + half * 4 + i at this thread's column.
+    float ps[4] = {0, 0, 0, 0};
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int b = it & 1;
@@ -120,40 +129,42 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         const uint8_t* src = smem + b * 2 * kBufB + half * kBufB + cg * 16;
         const bool col_in = tx0 + px < p.W;
-        float ps[4] = {0, 0, 0, 0};
 #pragma unroll 1
-        for (int py = 0; py < kTH; py += 2) {
-            float2 a0[4], a1[4];
+        for (int py = 0; py < kTH; py += kR) {
+            // kR output rows from a window of kR + 2 input rows: each loaded
+            // pixel feeds every output row whose 3x3 window holds it, with
+            // fp16 x fp16 products accumulated in fp32 (no unpacking).
+            float acc[kR][8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a0[i] = a1[i] = bias[i];
+            for (int r = 0; r < kR; ++r)
 #pragma unroll
-            for (int rr = 0; rr < 4; ++rr) {
+                for (int i = 0; i < 8; ++i) acc[r][i] = bias[i];
+#pragma unroll
+            for (int rr = 0; rr < kR + 2; ++rr) {
 #pragma unroll
                 for (int kx = 0; kx < 3; ++kx) {
                     const uint4 v = *reinterpret_cast<const uint4*>(src + ((py + rr) * kWW + px + kx) * kRowB);
                     const uint32_t q[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 u = unpack_half2(q[i]);
-                        if (rr <= 2) a0[i] = ffma2(u, w[rr * 3 + kx][i], a0[i]);
-                        if (rr >= 1) a1[i] = ffma2(u, w[(rr - 1) * 3 + kx][i], a1[i]);
+                    for (int r = 0; r < kR; ++r) {
+                        const int ky = rr - r;
+                        if (ky < 0 || ky > 2) continue;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            fma_mix2(acc[r][2 * i], acc[r][2 * i + 1], q[i], w[ky * 3 + kx][i]);
                     }
                 }
             }
 #pragma unroll
-            for (int r2 = 0; r2 < 2; ++r2) {
+            for (int r2 = 0; r2 < kR; ++r2) {
                 // this lane keeps channels [4*half, 4*half+4) of its group
                 float o[4];
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const float2 lo = r2 ? a1[j] : a0[j];
-                    const float2 hi = r2 ? a1[2 + j] : a0[2 + j];
-                    const float2 mine = half ? hi : lo;
-                    const float2 give = half ? lo : hi;
-                    const float gx = __shfl_xor_sync(0xffffffffu, give.x, 8);
-                    const float gy = __shfl_xor_sync(0xffffffffu, give.y, 8);
-                    o[2 * j] = mine.x * gx;
-                    o[2 * j + 1] = mine.y * gy;
+                for (int j = 0; j < 4; ++j) {
+                    const float lo = acc[r2][j], hi = acc[r2][4 + j];
+                    const float mine = half ? hi : lo;
+                    const float give = half ? lo : hi;
+                    o[j] = mine * __shfl_xor_sync(0xffffffffu, give, 8);
                 }
                 const int oy = py + r2;
                 const uint32_t h01 = pack_half2(o[0], o[1]), h23 = pack_half2(o[2], o[3]);
@@ -167,22 +178,32 @@ __global__ void __launch_bounds__(kThreads, 2)
                 }
             }
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sRed[px * kCS + cg * 8 + half * 4 + i] = ps[i];
         fence_async_smem();
-        __syncthreads();  // every thread is done with halo buffer b, sOut and sRed are complete
+        __syncthreads();  // every thread is done with halo buffer b and sOut is complete
         if (tid == 0) {
             tma_store_4d(&mg, cs0, tx0, ty0, img, sOut);
             bulk_commit();
             if (t + 2 * static_cast<int>(gridDim.x) < ntiles) load(t + 2 * gridDim.x, b);
         }
-        if (tid < kCS) {
-            float sum = 0.f;
-            for (int c = 0; c < kTW; ++c) sum += sRed[c * kCS + tid];
-            cta_sum += sum;
-        }
     }
-    if (tid < kCS) p.partials[(static_cast<size_t>(img) * gridDim.x + blockIdx.x) * D + cs0 + tid] = cta_sum;
+    // Pool partials of the walk: the 4 columns of a warp (lane bits 2 and 4),
+    // then the 8 warps in order.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        ps[i] += __shfl_xor_sync(0xffffffffu, ps[i], 4);
+        ps[i] += __shfl_xor_sync(0xffffffffu, ps[i], 16);
+    }
+    if ((lane & 0x14) == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sRed[(tid >> 5) * kCS + cg * 8 + half * 4 + i] = ps[i];
+    }
+    __syncthreads();
+    if (tid < kCS) {
+        float sum = 0.f;
+#pragma unroll
+        for (int w8 = 0; w8 < kThreads / 32; ++w8) sum += sRed[w8 * kCS + tid];
+        p.partials[(static_cast<size_t>(img) * gridDim.x + blockIdx.x) * D + cs0 + tid] = sum;
+    }
     if (tid == 0) bulk_wait0();
 }
 

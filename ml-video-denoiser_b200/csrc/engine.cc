@@ -288,6 +288,9 @@ void Engine::build(const HostWeights& hw) {
             for (int c = 0; c < 2 * b.dw; ++c)
                 for (int t = 0; t < 9; ++t) wt[t * 2 * b.dw + c] = w2[c * 9 + t];
             b.dw_w = pk.add_f32(wt);
+            std::vector<__half> wt16(wt.size());
+            for (size_t i = 0; i < wt.size(); ++i) wt16[i] = __float2half_rn(wt[i]);
+            b.dw_w16 = pk.add(wt16.data(), wt16.size() * sizeof(__half));
             b.dw_b = pk.add_f32(hw.to_f32(pre + ".conv2.bias"));
         }
         b.sca_w = pk.add_f32(hw.to_f32(pre + ".sca.1.weight"));
@@ -820,6 +823,7 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
     d.u = buf_u_;
     d.g = buf_g_;
     d.w = wptr<float>(b.dw_w);
+    d.w16 = wptr<__half>(b.dw_w16);
     d.b = wptr<float>(b.dw_b);
     d.N = nimg;
     d.H = h;

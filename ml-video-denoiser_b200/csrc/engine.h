@@ -35,6 +35,7 @@ struct BlockW {
     size_t ln1w = 0, ln1b = 0, ln2w = 0, ln2b = 0, beta = 0, gamma = 0;  // fp32 [C]
     GemmW conv1, conv3, conv4, conv5;
     size_t dw_w = 0, dw_b = 0;     // fp32 [9][2dw], [2dw]
+    size_t dw_w16 = 0;             // fp16 [9][2dw]: the same taps, for the mixed-precision depthwise
     size_t sca_w = 0, sca_b = 0;   // fp32 [dw][dw], [dw]
     // Fused two-pass kernels (shallow levels, C <= 64): single-tile B images.
     bool fused = false;

@@ -79,6 +79,7 @@ struct DwParams {
     const __half* u;       // [N, H, W, 2D]
     __half* g;             // [N, H, W, D]
     const float* w;        // [9][2D] taps (ky*3+kx) x channel
+    const __half* w16;     // [9][2D] the same taps in fp16 (the weights' own precision)
     const float* b;        // [2D]
     int N, H, W, D;
     float* partials;       // [N][blocks][D]

@@ -403,6 +403,20 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return d;
 }
 
+// Mixed-precision FMA on the two halves of packed fp16 pairs (sm_100):
+// c0 += lo(u) * lo(w), c1 += hi(u) * hi(w) in fp32. A product of two fp16
+// values is exact in fp32, so this equals fmaf on the widened operands
+// without the two conversions.
+__device__ __forceinline__ void fma_mix2(float& c0, float& c1, uint32_t u, uint32_t w) {
+    asm("{\n\t.reg .f16 ul, uh, wl, wh;\n\t"
+        "mov.b32 {ul, uh}, %2;\n\t"
+        "mov.b32 {wl, wh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, ul, wl, %0;\n\t"
+        "fma.rn.f32.f16 %1, uh, wh, %1;\n\t}"
+        : "+f"(c0), "+f"(c1)
+        : "r"(u), "r"(w));
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
