@@ -1011,13 +1011,71 @@ int num_sms() {
     return n;
 }
 
+// Kernels launched by the last launch_gemm call of this thread.
+thread_local int t_gemm_launches = 0;
+
+// Dynamic shared memory a kernel may request: the device's opt-in limit per
+// block minus the kernel's static shared memory.
+template <class K>
+int query_dyn_smem_limit(K kern) {
+    int dev = 0, optin = 0;
+    cudaFuncAttributes fa{};
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fa, kern) != cudaSuccess)
+        return -1;
+    return optin - static_cast<int>(fa.sharedSizeBytes);
+}
+
+// col0: output columns before this launch's first (column groups of a wide
+// GEMM, below); p.out / p.res / p.res_scale already point at column col0.
 template <int PRO, int EPI, int AMODE, int NT>
-int launch_one(const GemmParams& p, cudaStream_t s) {
+int launch_one(const GemmParams& p, cudaStream_t s, int col0 = 0) {
     auto kern = gemm_ws_kernel<PRO, EPI, AMODE, NT>;
     constexpr int kOutCols = (EPI == kEpiGate) ? NT / 2 : NT;
     using Stg = Staging<kOutCols>;
-    const int smem = SmemPlan<PRO, EPI, NT, AMODE>::bytes(p);
-    if (smem > 225 * 1024) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: tile does not fit in shared memory");
+    using Plan = SmemPlan<PRO, EPI, NT, AMODE>;
+    const int smem = Plan::bytes(p);
+    static int limit = -1;  // per instantiation: its static shared memory differs
+    if (limit < 0) limit = query_dyn_smem_limit(kern);
+    if (limit < 0) return dn_fail(DN_ERR_CUDA, "gemm: kernel attributes");
+    if (smem > limit) {
+        // A wide N: the per-column parameter vectors (bias, LN fold, residual
+        // scale) no longer fit beside the ring and the staging tile. Run
+        // column groups of N tiles as separate launches, each with its slice
+        // of B, of the vectors and of the output columns.
+        constexpr bool kSplit = (AMODE == kARows || AMODE == kARowsPair) &&
+                                (EPI == kEpiStore || EPI == kEpiGate || EPI == kEpiResidual);
+        GemmParams q = p;
+        int per = p.n_tiles;
+        while (per > 1 && Plan::bytes(q) > limit) {
+            per = (per + 1) / 2;
+            q.n_tiles = per;
+            q.n_out = std::min(p.n_out, per * kOutCols);
+        }
+        if (!kSplit || col0 != 0 || Plan::bytes(q) > limit)
+            return dn_fail(DN_ERR_UNSUPPORTED, "gemm: tile does not fit in shared memory");
+        int launched = 0;
+        for (int t0 = 0; t0 < p.n_tiles; t0 += per) {
+            const int c0 = t0 * kOutCols;
+            if (c0 >= p.n_out) break;
+            q = p;
+            q.n_tiles = std::min(per, p.n_tiles - t0);
+            q.bpack = p.bpack + static_cast<size_t>(t0) * p.k_chunks * gemm_btile_bytes(NT, p.KC);
+            if (p.bias) q.bias = p.bias + static_cast<size_t>(t0) * NT;
+            if (p.ln_c1) q.ln_c1 = p.ln_c1 + static_cast<size_t>(t0) * NT;
+            q.out = p.out + c0;
+            if (p.res) q.res = p.res + c0;
+            if (p.res_scale) q.res_scale = p.res_scale + c0;
+            q.n_out = std::min(p.n_out - c0, q.n_tiles * kOutCols);
+            const int rc = launch_one<PRO, EPI, AMODE, NT>(q, s, c0);
+            if (rc != DN_OK) return rc;
+            ++launched;
+        }
+        t_gemm_launches = launched;
+        return DN_OK;
+    }
+    t_gemm_launches = 1;
     static int configured = 0;  // largest dynamic footprint granted so far
     if (smem > configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1061,10 +1119,10 @@ int launch_one(const GemmParams& p, cudaStream_t s) {
         if (rc != DN_OK) return rc;
     } else if (EPI != kEpiShuffleAdd && p.out_c % kOutCols == 0) {
         int rc = kRowT ? make_map3(&maps.out, p.out, p.M / p.Wo, p.Wo, p.out_c, Stg::EB, kRows, swizzle_for(Stg::kRowBytes))
-                       : make_map(&maps.out, p.out, p.M, p.out_c, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
+                       : make_map(&maps.out, p.out, p.M, p.out_c - col0, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
         if (rc != DN_OK) return rc;
         if (EPI == kEpiResidual) {
-            rc = make_map(&maps.res, p.res, p.M, p.out_c, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
+            rc = make_map(&maps.res, p.res, p.M, p.out_c - col0, p.out_c, Stg::EB, swizzle_for(Stg::kRowBytes));
             if (rc != DN_OK) return rc;
         }
     }
@@ -1120,7 +1178,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+int gemm_last_launches() { return t_gemm_launches; }
+
 int launch_gemm(const GemmParams& p, int pro, int epi, int amode, int nt, cudaStream_t s) {
+    t_gemm_launches = 0;
     if (p.KC != 16 && p.KC != 32 && p.KC != 64) return dn_fail(DN_ERR_UNSUPPORTED, "gemm: KC must be 16/32/64");
     if (p.a_swz != 0 && p.a_swz != 32 && p.a_swz != 64 && p.a_swz != 128)
         return dn_fail(DN_ERR_UNSUPPORTED, "gemm: bad A swizzle span");

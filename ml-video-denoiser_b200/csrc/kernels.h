@@ -66,7 +66,11 @@ struct GemmParams {
 };
 
 // NT in {16, 32, 64, 128, 256}
+// A GEMM whose per-column parameter vectors do not fit in shared memory beside
+// its ring (very wide N) runs as column groups of N tiles, one launch each.
 int launch_gemm(const GemmParams& p, int pro, int epi, int amode, int nt, cudaStream_t s);
+// Kernels launched by this thread's last launch_gemm call.
+int gemm_last_launches();
 
 // Bytes of one packed B tile.
 inline size_t gemm_btile_bytes(int nt, int kc) { return static_cast<size_t>(nt) * kc * 2; }
@@ -95,6 +99,11 @@ struct DwParams {
     const uint8_t* bsrc;
     uint8_t* bdst;
     int b_rows, b_nt, b_kc, b_kchunks;
+    // Optional (launch_dw_tile): [N][2] words, zero before the first launch
+    // (arrival count, generation). With it the depthwise kernel evaluates
+    // the SCA itself after a grid-wide arrival barrier per image, instead of
+    // a separate SCA launch.
+    unsigned* grid_bar;
 };
 
 int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s);
@@ -104,7 +113,10 @@ int dw_blocks_per_img(int H, int W, int D);
 // TMA-tiled variant (8x32 output tiles x 32-channel slices), then SCA.
 bool dw_tile_supported(int D);
 int dw_tile_blocks_per_img(int H, int W);
-int launch_dw_tile(const DwParams& p, cudaStream_t s);
+// The SCA runs inside the depthwise kernel when p.grid_bar is set and the
+// grid fits on the GPU at once, else as a second kernel; *launches (if
+// given) receives the number of kernels launched.
+int launch_dw_tile(const DwParams& p, cudaStream_t s, int* launches = nullptr);
 
 // ---------------------------------------------------------------------------
 // Dense 3x3 convs at the network boundary (CUDA cores)

@@ -65,6 +65,20 @@ def test_w32_batch2_ragged(pkg, tmp_path, fused):
     assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "perconv"])
+@pytest.mark.parametrize("hw,batch", [((200, 328), 1), ((100, 150), 2)], ids=["200x328", "100x150x2"])
+def test_w32_literal_expansion(pkg, tmp_path, fused, hw, batch):
+    """NAFNet-w32 with dw_expand=2 / ffn_expand=2 in the repo's convention
+    (64.68 M params: every depthwise and FFN runs at twice the channels of the
+    paper-convention model), single image and a ragged batch of 2."""
+    synth = synth_mod(pkg)
+    h, w = hw
+    x = np.concatenate([synth.w32_frame(h, w, seed=41 + i) for i in range(batch)])
+    x = x.astype(np.float16).astype(np.float32)
+    (err, psnr), _ = _oracle_case(pkg, tmp_path, synth.CONFIG_W32_LITERAL, 3, x, fused)
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+
+
 def test_w32_single_image_deep_second_pass(pkg, tmp_path):
     """Single image, so the 128- and 256-channel blocks run their second pass
     as one kernel (conv3 -> LN2/conv4/gate -> conv5); 200x328 leaves partial

@@ -95,6 +95,17 @@ def test_w32_ragged_vs_reference_engine(pkg, tmp_path):
 
 
 @need_ref
+def test_w32_literal_expansion_1080p_vs_reference_engine(pkg, tmp_path):
+    """NAFNet-w32 with dw_expand=2 / ffn_expand=2 (the repo-literal reading of
+    "expansion 2", 64.68 M params) on one 1080p frame."""
+    synth = synth_mod(pkg)
+    x = synth.w32_frame(1080, 1920, seed=3).astype(np.float16).astype(np.float32)
+    err, psnr = _spatial_case(pkg, tmp_path, synth.CONFIG_W32_LITERAL, 3, x)
+    print(f"vs reference engine: max abs {err:.3e}, PSNR {psnr:.2f} dB")
+    assert err <= MAX_ABS and psnr >= MIN_PSNR, (err, psnr)
+
+
+@need_ref
 def test_w32_1080p_vs_reference_engine(pkg, tmp_path):
     """NAFNet-w32 on one 1080p Poisson-Gaussian frame, seed-1 weights (the
     benchmark workload)."""
