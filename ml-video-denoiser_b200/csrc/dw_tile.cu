@@ -15,17 +15,7 @@
 //     fp16 values of its column to running sums, in the CTA's fixed tile
 //     order; after the walk they reduce over columns and warps in a fixed
 //     order into partials[img][blockIdx.x][channel] (one pool row per CTA
-//     keeps the SCA re-reduction short).
-// Then the SCA of the image (when the grid fits on the GPU at once, so that
-// every CTA is resident): each CTA stores its partial row and arrives on a
-// per-image arrival barrier in global memory (count + generation, the last
-// arriver resets the count and bumps the generation); the first D/8 CTAs of
-// the image also wait on it (bounded) and each evaluates 8 outputs of
-//   s = W_sca mean_{HW}(g) + b_sca
-// re-reducing all partial rows in a fixed order, and, for a single image,
-// writes conv3's B operand with those 8 columns scaled by s. Their weight
-// rows and B chunks load before the wait. Without the barrier words the
-// launcher runs the same SCA as a separate kernel.
+//     keeps the SCA kernel's re-reduction short).
 // Each input element crosses the memory system once (plus the 1-pixel halo),
 // instead of once per tap.
 //
@@ -62,187 +52,10 @@ constexpr int kOutB = kTH * kTW * kCS * 2;
 constexpr int kThreads = 256;
 constexpr int kSmem = 128 + 4 * kBufB + kOutB + (kThreads / 32) * kCS * 4;  // 2 halo buffers x 2 gate halves
 
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// The SCA of image `img` after the walk (see the file comment). V = float4
-// channel vectors per lane of a weight row (D <= 128 V). Bit-identical to
-// the stand-alone SCA kernel: the same fixed-order pool and matvec.
-template <int V>
-__device__ __forceinline__ void sca_tail(const DwParams& p, uint8_t* smem, int img, int tid) {
-    const int D = p.D;
-    const unsigned per_img = gridDim.x * gridDim.y;
-    const unsigned lin = blockIdx.x + gridDim.x * blockIdx.y;
-    const int ngroups = D / 8;
-    const bool evaluates = static_cast<int>(lin) < ngroups;
-    unsigned* bcnt = p.grid_bar + 2 * img;
-    unsigned* bgen = bcnt + 1;
-    __shared__ unsigned s_gen;
-    __shared__ int s_ok;
-    __threadfence();
-    __syncthreads();  // this CTA's partial row is stored and fenced
-    if (tid == 0) {
-        // The generation is read before arriving (acquire keeps the order), so
-        // it cannot yet be the one this launch's last arriver writes.
-        s_gen = ld_acquire_gpu(bgen);
-        if (atomicAdd(bcnt, 1u) == per_img - 1) {
-            atomicExch(bcnt, 0u);
-            __threadfence();
-            atomicAdd(bgen, 1u);
-        }
-    }
-    if (!evaluates) return;
-    const int warp = tid >> 5, lane = tid & 31;
-    const int nvec = D / 4;
-    float* mean = reinterpret_cast<float*>(smem);   // [D <= 1024]
-    float* red = mean + 1024;                       // [stripes][D] = 4 * kThreads floats
-    float* scl = red + 4 * kThreads;                // [8]
-    // Constant weights of a group (warp w: row 8j + w of W_sca and its bias;
-    // thread: the 16-byte B chunks of conv3 rows tid + u * kThreads at
-    // columns 8j .. 8j + 8).
-    constexpr int kFold = 4;  // b_rows <= kFold * kThreads (checked at launch)
-    const bool fold = p.bdst != nullptr;
-    float4 w[V];
-    float bias_o = 0.f;
-    uint4 bv[kFold];
-    size_t boff[kFold];
-    auto load_group = [&](int j) {
-        const int o = j * 8 + warp;
-        bias_o = p.sca_b[o];
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-            const int v = lane + 32 * i;
-            w[i] = v < nvec ? reinterpret_cast<const float4*>(p.sca_w + static_cast<size_t>(o) * D)[v]
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        if (fold) {
-            const int k0 = j * 8;
-            const int kc = k0 / p.b_kc, kq = (k0 % p.b_kc) / 8;
-            const size_t tile_b = static_cast<size_t>(p.b_nt) * p.b_kc * 2;
-            const uint32_t sbo = static_cast<uint32_t>(p.b_kc / 8) * 128u;
-#pragma unroll
-            for (int u = 0; u < kFold; ++u) {
-                const int n = tid + u * kThreads;
-                boff[u] = 0;
-                bv[u] = make_uint4(0, 0, 0, 0);
-                if (n < p.b_rows) {
-                    const int nt = n / p.b_nt, nl = n - nt * p.b_nt;
-                    boff[u] = (static_cast<size_t>(nt) * p.b_kchunks + kc) * tile_b + (nl >> 3) * sbo + kq * 128 +
-                              (nl & 7) * 16;
-                    bv[u] = __ldg(reinterpret_cast<const uint4*>(p.bsrc + boff[u]));
-                }
-            }
-        }
-    };
-    load_group(static_cast<int>(lin));
-    if (tid == 0) {
-        bool ok = ld_acquire_gpu(bgen) != s_gen;
-        if (!ok) {
-            const uint64_t t0 = globaltimer_ns();
-            for (uint32_t i = 1;; ++i) {
-                if (ld_acquire_gpu(bgen) != s_gen) {
-                    ok = true;
-                    break;
-                }
-                if ((i & 63u) == 0u && globaltimer_ns() - t0 > 2000000000ull) break;
-            }
-        }
-        if (!ok) report_error(p.err, 0x51, kErrMbarTimeout);
-        s_ok = ok;
-    }
-    __syncthreads();
-    if (!s_ok) return;
-    __threadfence();
-    // Fixed-order pool over all threads: thread (stripe, v) sums the float4
-    // channel vector v of partial rows stripe, stripe + stripes, ... in row
-    // order; the stripe sums are then added in stripe order.
-    const int nb = gridDim.x;
-    const float4* pp = reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(img) * nb * D);
-    const int stripes = kThreads / nvec;
-    {
-        const int v = tid % nvec, stripe = tid / nvec;
-        if (stripe < stripes) {
-            constexpr int kPool = 12;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int b = stripe; b < nb; b += kPool * stripes) {
-                float4 x[kPool];
-#pragma unroll
-                for (int u = 0; u < kPool; ++u) {
-                    const int row = min(b + u * stripes, nb - 1);  // past the end: a row that is not added
-                    x[u] = __ldcg(pp + static_cast<size_t>(row) * nvec + v);
-                }
-#pragma unroll
-                for (int u = 0; u < kPool; ++u) {
-                    if (b + u * stripes < nb) {
-                        acc.x += x[u].x;
-                        acc.y += x[u].y;
-                        acc.z += x[u].z;
-                        acc.w += x[u].w;
-                    }
-                }
-            }
-            reinterpret_cast<float4*>(red + stripe * D)[v] = acc;
-        }
-    }
-    __syncthreads();
-    const float inv = 1.0f / static_cast<float>(p.H * p.W);
-    for (int c = tid; c < D; c += kThreads) {
-        float s = 0.f;
-        for (int st = 0; st < stripes; ++st) s += red[st * D + c];
-        mean[c] = s * inv;
-    }
-    __syncthreads();
-    for (int j = static_cast<int>(lin);;) {
-        const int o = j * 8 + warp;
-        float s = 0.f;
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-            const int v = lane + 32 * i;
-            if (v < nvec) {
-                const float4 m = reinterpret_cast<const float4*>(mean)[v];
-                s = fmaf(w[i].x, m.x, s);
-                s = fmaf(w[i].y, m.y, s);
-                s = fmaf(w[i].z, m.z, s);
-                s = fmaf(w[i].w, m.w, s);
-            }
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (lane == 0) {
-            p.s_out[static_cast<size_t>(img) * D + o] = s + bias_o;
-            scl[warp] = s + bias_o;
-        }
-        if (fold) {
-            __syncthreads();
-            float sc[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sc[i] = scl[i];
-#pragma unroll
-            for (int u = 0; u < kFold; ++u) {
-                if (tid + u * kThreads < p.b_rows) {
-                    float f[8];
-                    h8_to_f(bv[u], f);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) f[i] *= sc[i];
-                    *reinterpret_cast<uint4*>(p.bdst + boff[u]) = f_to_h8(f);
-                }
-            }
-        }
-        j += static_cast<int>(per_img);
-        if (j >= ngroups) break;
-        __syncthreads();  // scl is read by every thread before the next group writes it
-        load_group(j);
-    }
-}
-
 // Lane layout inside a warp (32 lanes = 4 columns): bits 0-1 channel group,
 // bit 2 column low bit, bit 3 gate half, bit 4 column high bit. Eight
 // consecutive lanes then read 128 contiguous bytes of one half (no bank
 // conflicts) and the two halves of a gate pair are lanes l and l^8.
-template <int V>
 __global__ void __launch_bounds__(kThreads, 2)
     dw_tile_kernel(const __grid_constant__ DwParams p, const __grid_constant__ CUtensorMap mu,
                    const __grid_constant__ CUtensorMap mg) {
@@ -391,7 +204,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int w8 = 0; w8 < kThreads / 32; ++w8) sum += sRed[w8 * kCS + tid];
         p.partials[(static_cast<size_t>(img) * gridDim.x + blockIdx.x) * D + cs0 + tid] = sum;
     }
-    if (p.grid_bar) sca_tail<V>(p, smem, img, tid);
     if (tid == 0) bulk_wait0();
 }
 
@@ -419,16 +231,12 @@ bool dw_tile_supported(int D) { return D % kCS == 0; }
 
 int dw_tile_blocks_per_img(int H, int W) { return ((H + kTH - 1) / kTH) * ((W + kTW - 1) / kTW); }
 
-namespace {
-
-template <int V>
-int launch_dw_tile_v(const DwParams& p, cudaStream_t s, int* launches) {
+int launch_dw_tile(const DwParams& p, cudaStream_t s) {
+    if (!dw_tile_supported(p.D)) return dn_fail(DN_ERR_UNSUPPORTED, "dw_tile: channels must be a multiple of 32");
     static bool configured = false;
-    static int occ = 0;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(dw_tile_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dw_tile_kernel<V>, kThreads, kSmem);
-        if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: kernel attributes");
+        cudaError_t e = cudaFuncSetAttribute(dw_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: smem attribute");
         configured = true;
     }
     CUtensorMap mu, mg;
@@ -445,29 +253,9 @@ int launch_dw_tile_v(const DwParams& p, cudaStream_t s, int* launches) {
     const int gmax = std::max(1, std::min(tiles, 2 * sms / per));
     const int walk = (tiles + gmax - 1) / gmax;
     const int gx = (tiles + walk - 1) / walk;
-    // The in-kernel SCA waits for every CTA of its image, so it needs the
-    // whole grid resident at once; otherwise the SCA runs as its own kernel.
-    DwParams q = p;
-    const long long grid = static_cast<long long>(gx) * per;
-    if (grid > static_cast<long long>(std::min(occ, 2)) * sms) q.grid_bar = nullptr;
-    cudaError_t e = launch_pdl(dw_tile_kernel<V>, dim3(gx, p.D / kCS, p.N), dim3(kThreads), kSmem, s, q, mu, mg);
+    cudaError_t e = launch_pdl(dw_tile_kernel, dim3(gx, p.D / kCS, p.N), dim3(kThreads), kSmem, s, p, mu, mg);
     if (e != cudaSuccess) return dn_cuda_fail(e, "dw_tile: launch");
-    if (launches) *launches = q.grid_bar ? 1 : 2;
-    return q.grid_bar ? DN_OK : launch_sca(q, gx, s);
-}
-
-}  // namespace
-
-int launch_dw_tile(const DwParams& p, cudaStream_t s, int* launches) {
-    if (!dw_tile_supported(p.D)) return dn_fail(DN_ERR_UNSUPPORTED, "dw_tile: channels must be a multiple of 32");
-    if (p.D > 1024) return dn_fail(DN_ERR_UNSUPPORTED, "dw_tile: more than 1024 channels");
-    if (p.bdst && p.b_rows > 4 * kThreads)
-        return dn_fail(DN_ERR_UNSUPPORTED, "dw_tile: conv3 has more than 1024 output channels");
-    const int nvec = p.D / 4;
-    if (nvec <= 32) return launch_dw_tile_v<1>(p, s, launches);
-    if (nvec <= 64) return launch_dw_tile_v<2>(p, s, launches);
-    if (nvec <= 128) return launch_dw_tile_v<4>(p, s, launches);
-    return launch_dw_tile_v<8>(p, s, launches);
+    return launch_sca(p, gx, s);
 }
 
 }  // namespace dnb

@@ -562,8 +562,7 @@ void Engine::plan(const Shape& s) {
         }
     }
     req.push_back({n_enc * dw_blocks_max_ * dmax * 4, reinterpret_cast<void**>(&partials_)});
-    // [n_enc] phase-A tickets, then [n_enc][2] depthwise SCA barrier words.
-    req.push_back({n_enc * 3 * 4, reinterpret_cast<void**>(&counters_)});
+    req.push_back({n_enc * 4, reinterpret_cast<void**>(&counters_)});
     req.push_back({n_enc * dmax * 4, reinterpret_cast<void**>(&sca_s_)});
     {
         size_t b3 = 0;
@@ -592,8 +591,7 @@ void Engine::plan(const Shape& s) {
         *r.second = aarena_ + off;
         off += align256(r.first);
     }
-    dw_bar_ = counters_ + n_enc;
-    e = cudaMemset(counters_, 0, n_enc * 3 * 4);
+    e = cudaMemset(counters_, 0, n_enc * 4);
     if (e == cudaSuccess) e = cudaMemset(err_, 0, 256);
     if (e != cudaSuccess) throw std::runtime_error(std::string("arena init: ") + cudaGetErrorString(e));
 }
@@ -849,15 +847,12 @@ int Engine::run_block(const BlockW& b, __half* x, int nimg, int h, int w, cudaSt
         d.b_kc = b.conv3.KC;
         d.b_kchunks = b.conv3.k_chunks;
     }
+    launches_ += 2;  // depthwise + SCA
     if (fused_enabled_ && dw_tile_supported(b.dw)) {
-        d.grid_bar = dw_bar_;
-        int nl = 0;
         prof_begin("dw_tile_sca", static_cast<double>(nimg) * hw * 3 * b.dw * 2,
                    static_cast<double>(nimg) * hw * 2 * b.dw * 9 * 2 + 2.0 * b.dw * b.dw, s);
-        DN_TRY(launch_dw_tile(d, s, &nl));
-        launches_ += nl;
+        DN_TRY(launch_dw_tile(d, s));
     } else {
-        launches_ += 2;  // depthwise + SCA
         prof_begin("dw_gate_sca", static_cast<double>(nimg) * hw * 3 * b.dw * 2,
                    static_cast<double>(nimg) * hw * 2 * b.dw * 9 * 2 + 2.0 * b.dw * b.dw, s);
         DN_TRY(launch_dw_gate_sca(d, dw_blocks_per_img(h, w, b.dw), s));

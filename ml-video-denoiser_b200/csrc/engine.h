@@ -185,7 +185,6 @@ private:
     __half* oh_h_ = nullptr;              // offset head: hidden layer [HW][C]
     float* partials_ = nullptr;
     unsigned* counters_ = nullptr;
-    unsigned* dw_bar_ = nullptr;  // [n_enc][2] depthwise SCA barrier words (inside counters_)
     float* sca_s_ = nullptr;
     uint8_t* b3s_ = nullptr;              // conv3 B with the SCA scale folded in (single image)
     uint32_t* err_ = nullptr;

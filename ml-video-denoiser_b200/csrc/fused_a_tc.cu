@@ -25,9 +25,13 @@
 //               copy; rows outside the image are zeroed instead of loaded
 //               (a tensor map with 16-byte inner boxes, which would write the
 //               MMA layout directly, moves a row many times slower);
-//   warps 1-4   LayerNorm of each row (FP32 statistics from shifted sums,
-//               FP16 result, as the reference's normalised tensor), written
-//               back in place in the no-swizzle K-major layout [C/8][130][8];
+//   warps 1-4   LayerNorm of each row (FP32 statistics, FP16 result, as the
+//               reference's normalised tensor) into the no-swizzle K-major
+//               layout [C/8][130][8]. At 64 channels the four warps share a
+//               row and write it back in place; at 32 channels the producer
+//               lands rows in a second (pixel-major) ring and each warp
+//               normalises whole rows on its own (a lane per pixel, no
+//               shuffles), so four rows are in flight at once;
 //   warp 5      MMA issuer, into a ring of TMEM accumulators (M = 128, the
 //               strip's pixels; K = 16). At 32 channels, per input row r, 3
 //               tap columns x C/16 K steps of N = 3 x 2D: the row's
@@ -89,9 +93,14 @@ struct GeoT {
     static constexpr int TMEM_COLS = ACC * N;
     // floats: bias per tap-mask class [16][N], pool sums [img][warp][D] (phase A)
     static constexpr int F_FLOATS = 16 * N + (MODE == 0 ? kMaxImg * 4 * D : 0);
+    // At 32 channels each LayerNorm warp owns whole rows (WR): the producer
+    // lands rows in a separate pixel-major ring, the warp writes the MMA
+    // layout into the row ring, so four rows are normalised at once.
+    static constexpr bool WR = C == 32;
+    static constexpr int RAWB = WR ? R * ROWB : 0;
     // At least half of the SM's shared memory: the CTA holds all of TMEM, so a
     // second CTA on the same SM could only wait for it.
-    static constexpr int SMEM_USED = 1024 + R * ROWB + WB + F_FLOATS * 4;
+    static constexpr int SMEM_USED = 1024 + R * ROWB + WB + F_FLOATS * 4 + RAWB;
     static constexpr int SMEM = (CTAS == 2 || SMEM_USED > 120 * 1024) ? SMEM_USED : 120 * 1024;
     static_assert(ROWB % 128 == 0, "row slots stay 128-byte aligned");
     static_assert(TMEM_COLS <= 512, "TMEM ring");
@@ -175,7 +184,8 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
     // (class 0 = interior).
     float* sBias = reinterpret_cast<float*>(sW + G::WB);  // [16][N]
     float* sPool = sBias + 16 * N;                        // [img][epilogue warp][D]
-    __shared__ uint64_t full[G::R], ready[G::R], freeb[G::R], acc_full[G::ACC], acc_empty[G::ACC];
+    uint8_t* sRaw = reinterpret_cast<uint8_t*>(sPool + (MODE == 0 ? kMaxImg * 4 * D : 0));  // WR: R pixel-major rows
+    __shared__ uint64_t full[G::R], ready[G::R], freeb[G::R], rawfree[G::R], acc_full[G::ACC], acc_empty[G::ACC];
     __shared__ uint64_t bar_w, bar_end;
     __shared__ uint32_t tslot;
     __shared__ volatile int s_abort;
@@ -220,8 +230,9 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
     if (tid == 0) {
         for (int s = 0; s < G::R; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&ready[s], 4);
+            mbar_init(&ready[s], G::WR ? 1 : 4);
             mbar_init(&freeb[s], 1);
+            mbar_init(&rawfree[s], 1);
         }
         for (int a = 0; a < G::ACC; ++a) {
             mbar_init(&acc_full[a], 1);
@@ -250,7 +261,10 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
                 const int x0 = sg.strip * G::SW;
                 for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
                     const uint32_t s = e % G::R, ph = (e / G::R) & 1u;
-                    if (!wait_or_abort(&freeb[s], ph ^ 1u, &s_abort, p.err, 0x70)) break;
+                    // WR: the raw slot is free once its LayerNorm warp has read it;
+                    // otherwise the row slot is reused in place, free once its MMAs
+                    // have completed.
+                    if (!wait_or_abort(G::WR ? &rawfree[s] : &freeb[s], ph ^ 1u, &s_abort, p.err, 0x70)) break;
                     if (r < 0 || r >= in_h) {
                         mbar_arrive(&full[s]);  // zeroed by the LayerNorm warps
                     } else {
@@ -260,7 +274,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
                         const int pa = max(0, x0 - 1), pb = min(in_w, x0 + G::SW + 1);
                         const uint32_t bytes = static_cast<uint32_t>(pb - pa) * C * 2;
                         mbar_arrive_expect_tx(&full[s], bytes);
-                        bulk_g2s(sRow + s * G::ROWB + (pa - (x0 - 1)) * C * 2,
+                        bulk_g2s((G::WR ? sRaw : sRow) + s * G::ROWB + (pa - (x0 - 1)) * C * 2,
                                  p.x + ((static_cast<size_t>(sg.img) * in_h + r) * in_w + pa) * C, bytes, &full[s]);
                     }
                 }
@@ -272,6 +286,88 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
             }
         }
     } else if (warp <= 4) {
+      if constexpr (G::WR) {
+        // ------------------------- LayerNorm, a row per warp -----------------
+        // Warp w takes the ring entries e = w (mod 4) (slot e mod R). A lane
+        // owns pixels lane + 32k of the row: its statistics need no shuffles.
+        // It reads the pixel's four 16-byte chunks in a lane-rotated order
+        // (conflict-free pixel-major reads) and writes each normalised chunk
+        // to its place in the MMA layout [C/8][130][8 ch] of the row slot,
+        // once the MMAs of that slot's previous row have completed.
+        static_assert(G::R == 4 && C == 32, "one slot per LayerNorm warp");
+        const int w = warp - 1;
+        const int rot = (lane >> 1) & 3;
+        uint32_t e = 0;
+        bool ok = true;
+        for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+            const int x0 = sg.strip * G::SW;
+            for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
+                if (static_cast<int>(e & 3u) != w) continue;
+                const uint32_t s = e % G::R, ph = (e / G::R) & 1u;
+                ok = __all_sync(0xffffffffu, wait_or_abort(&full[s], ph, &s_abort, p.err, 0x71));
+                if (ok) ok = __all_sync(0xffffffffu, wait_or_abort(&freeb[s], ph ^ 1u, &s_abort, p.err, 0x76));
+                if (!ok) break;
+                const uint8_t* raw = sRaw + s * G::ROWB;
+                uint8_t* row = sRow + s * G::ROWB;
+                const bool row_in = r >= 0 && r < in_h;
+                constexpr int NP = (G::HP + 31) / 32;  // pixel passes
+#pragma unroll 1
+                for (int k = 0; k < NP; ++k) {
+                    const int i = k * 32 + lane;
+                    const int xin = x0 - 1 + i;
+                    const bool valid = row_in && i < G::HP && xin >= 0 && xin < in_w;
+                    uint4 cur[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        cur[q] = valid ? *reinterpret_cast<const uint4*>(raw + i * 64 + ((q + rot) & 3) * 16)
+                                       : make_uint4(0u, 0u, 0u, 0u);
+                    if constexpr (MODE == 0) {
+                        // Sums and sums of squares of the pixel's 32 channels (fp32;
+                        // zero rows and pixels outside the image stay zero).
+                        const float2 one = make_float2(1.f, 1.f);
+                        float2 a1 = make_float2(0.f, 0.f), a2 = make_float2(0.f, 0.f);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint32_t wv[4] = {cur[q].x, cur[q].y, cur[q].z, cur[q].w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float2 d = unpack_half2(wv[j]);
+                                a1 = ffma2(d, one, a1);
+                                a2 = ffma2(d, d, a2);
+                            }
+                        }
+                        const float dm = (a1.x + a1.y) * (1.0f / C);
+                        const float var = fmaxf((a2.x + a2.y) * (1.0f / C) - dm * dm, 0.f);
+                        const float rstd = rsqrtf(var + 1e-6f);
+                        const float2 rs2 = make_float2(rstd, rstd);
+                        const float2 sh2 = make_float2(-dm * rstd, -dm * rstd);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint32_t wv[4] = {cur[q].x, cur[q].y, cur[q].z, cur[q].w};
+                            uint32_t o[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float2 y = ffma2(unpack_half2(wv[j]), rs2, sh2);
+                                o[j] = pack_half2(y.x, y.y);
+                            }
+                            cur[q] = valid ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0u, 0u, 0u, 0u);
+                        }
+                    }
+                    if (i < G::HP) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            *reinterpret_cast<uint4*>(row + ((q + rot) & 3) * G::KGB + i * 16) = cur[q];
+                    }
+                }
+                fence_async_smem();  // the tensor core reads the row (async proxy)
+                __syncwarp();        // every lane has read the raw row and written its chunks
+                if (lane == 0) {
+                    mbar_arrive(&rawfree[s]);
+                    mbar_arrive(&ready[s]);
+                }
+            }
+        }
+      } else {
         // ------------------------------ LayerNorm ----------------------------
         // A pixel's C/8 16-byte chunks sit in adjacent lanes (conflict-free
         // reads of the pixel-major row); its statistics (sum and sum of
@@ -364,6 +460,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
                 if (lane == 0) mbar_arrive(&ready[s]);
             }
         }
+      }
     } else if (warp == 5) {
       if constexpr (3 * N <= 256) {
         // ------------------------------ MMA issuer ---------------------------

@@ -99,11 +99,6 @@ struct DwParams {
     const uint8_t* bsrc;
     uint8_t* bdst;
     int b_rows, b_nt, b_kc, b_kchunks;
-    // Optional (launch_dw_tile): [N][2] words, zero before the first launch
-    // (arrival count, generation). With it the depthwise kernel evaluates
-    // the SCA itself after a grid-wide arrival barrier per image, instead of
-    // a separate SCA launch.
-    unsigned* grid_bar;
 };
 
 int launch_dw_gate_sca(const DwParams& p, int blocks_per_img, cudaStream_t s);
@@ -113,10 +108,7 @@ int dw_blocks_per_img(int H, int W, int D);
 // TMA-tiled variant (8x32 output tiles x 32-channel slices), then SCA.
 bool dw_tile_supported(int D);
 int dw_tile_blocks_per_img(int H, int W);
-// The SCA runs inside the depthwise kernel when p.grid_bar is set and the
-// grid fits on the GPU at once, else as a second kernel; *launches (if
-// given) receives the number of kernels launched.
-int launch_dw_tile(const DwParams& p, cudaStream_t s, int* launches = nullptr);
+int launch_dw_tile(const DwParams& p, cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // Dense 3x3 convs at the network boundary (CUDA cores)
