@@ -113,14 +113,15 @@ struct Seg {
 
 // The segment starting at unit u of [u, u1): units enumerate (image, strip,
 // output row) with rows fastest; a segment is the run of rows of one strip.
-__device__ __forceinline__ bool seg_at(long long u, long long u1, int H, int strips, Seg& s) {
+// Units are 32-bit: the launchers reject inputs with 2^31 units or more.
+__device__ __forceinline__ bool seg_at(int u, int u1, int H, int strips, Seg& s) {
     if (u >= u1) return false;
-    const long long per_img = static_cast<long long>(strips) * H;
-    s.img = static_cast<int>(u / per_img);
-    const long long rem = u - static_cast<long long>(s.img) * per_img;
-    s.strip = static_cast<int>(rem / H);
-    s.ya = static_cast<int>(rem - static_cast<long long>(s.strip) * H);
-    s.yb = static_cast<int>(min(static_cast<long long>(H - 1), s.ya + (u1 - u) - 1));
+    const int per_img = strips * H;
+    s.img = u / per_img;
+    const int rem = u - s.img * per_img;
+    s.strip = rem / H;
+    s.ya = rem - s.strip * H;
+    s.yb = min(H - 1, s.ya + (u1 - u) - 1);
     return true;
 }
 
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
     }
     const int strips = (out_w + G::SW - 1) / G::SW;
     const long long T = static_cast<long long>(p.N) * strips * out_h;
-    const long long u0 = T * blockIdx.x / gridDim.x, u1 = T * (blockIdx.x + 1) / gridDim.x;
+    const int u0 = static_cast<int>(T * blockIdx.x / gridDim.x), u1 = static_cast<int>(T * (blockIdx.x + 1) / gridDim.x);
 
     for (int i = tid; i < 16 * N; i += kTcThreads) {
         const int cls = i / N, o = i - cls * N;
@@ -257,7 +258,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
         // ------------------------------ producer -----------------------------
         if (lane == 0) {
             uint32_t e = 0;
-            for (long long u = u0; !s_abort && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+            for (int u = u0; !s_abort && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
                 const int x0 = sg.strip * G::SW;
                 for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
                     const uint32_t s = e % G::R, ph = (e / G::R) & 1u;
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
         const int rot = (lane >> 1) & 3;
         uint32_t e = 0;
         bool ok = true;
-        for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+        for (int u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
             const int x0 = sg.strip * G::SW;
             for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
                 if (static_cast<int>(e & 3u) != w) continue;
@@ -379,7 +380,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
         const int cq = t % CPX, pl = t / CPX;
         uint32_t e = 0;
         bool ok = true;
-        for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+        for (int u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
             const int x0 = sg.strip * G::SW;
             for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
                 const uint32_t s = e % G::R, ph = (e / G::R) & 1u;
@@ -479,7 +480,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
             const uint64_t db = sdesc_kmajor(smem_u32(sW), 128, 256);
             bool ok = wait_or_abort(&bar_w, 0, &s_abort, p.err, 0x72);
             uint32_t e = 0, rb = 0;  // entry counter; running index of the segment's first output row
-            for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+            for (int u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
                 for (int r = sg.ya - 1; r <= sg.yb + 1; ++r, ++e) {
                     const uint32_t s_in = e & (G::R - 1);
                     if (!wait_or_abort(&ready[s_in], (e / G::R) & 1u, &s_abort, p.err, 0x73)) {
@@ -560,7 +561,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
             const uint64_t db = sdesc_kmajor(smem_u32(sW), 128, 256);
             bool ok = wait_or_abort(&bar_w, 0, &s_abort, p.err, 0x72);
             uint32_t eb = 0, rr = 0, waited = 0;  // entries < waited are known to be ready
-            for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+            for (int u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
                 for (int y = sg.ya; y <= sg.yb; ++y, ++rr) {
                     const uint32_t e0 = eb + static_cast<uint32_t>(y - sg.ya);
                     const uint32_t sl[3] = {e0 & (G::R - 1), (e0 + 1) & (G::R - 1), (e0 + 2) & (G::R - 1)};
@@ -610,7 +611,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
         uint32_t rr = 0;
         bool ok = true;
         const size_t plane = static_cast<size_t>(out_h) * out_w;
-        for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+        for (int u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
             const int xg = sg.strip * G::SW + px;
             const bool col_ok = xg < out_w;
             const __half* bt = p.beauty + static_cast<size_t>(sg.img) * p.beauty_batch_stride;
@@ -666,7 +667,7 @@ __global__ void __launch_bounds__(kTcThreads, GeoT<C, MODE>::CTAS) tc_conv_kerne
         uint32_t rr = 0;
         int cur = -1;
         bool ok = true;
-        for (long long u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
+        for (int u = u0; ok && seg_at(u, u1, out_h, strips, sg); u += sg.yb - sg.ya + 1) {
             if (cur >= 0 && sg.img != cur) flush(cur);
             cur = sg.img;
             const int xg = sg.strip * G::SW + px;
@@ -782,6 +783,8 @@ int launch_fused_a_tc(const FusedAParams& p, int C, int D, int grid, cudaStream_
         return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: the SCA fold needs one image, a counter and the SCA weights");
     if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (reinterpret_cast<uintptr_t>(p.g) & 15))
         return dn_fail(DN_ERR_INVALID_ARG, "fused_a_tc: x and g must be 16-byte aligned");
+    if (static_cast<long long>(p.N) * ((p.W + 127) / 128) * p.H >= (1LL << 31))
+        return dn_fail(DN_ERR_UNSUPPORTED, "fused_a_tc: too many strip rows");
     if (C == 32 && D == 32) return run_tc<32, 0>(p, grid, s);
     if (C == 64 && D == 64) return run_tc<64, 0>(p, grid, s);
     return dn_fail(DN_ERR_UNSUPPORTED, "fused_a_tc: channel configuration");
@@ -793,6 +796,7 @@ int launch_ending_tc(const EndingParams& p, cudaStream_t s) {
     if (!p.weff) return dn_fail(DN_ERR_INVALID_ARG, "ending_tc: missing packed weights");
     if ((reinterpret_cast<uintptr_t>(p.x) & 15)) return dn_fail(DN_ERR_INVALID_ARG, "ending_tc: x must be 16-byte aligned");
     const long long units = static_cast<long long>(p.N) * ((p.W + 127) / 128) * p.H;
+    if (units >= (1LL << 31)) return dn_fail(DN_ERR_UNSUPPORTED, "ending_tc: too many strip rows");
     const int per_sm = p.C0 == 32 ? GeoT<32, 1>::CTAS : GeoT<64, 1>::CTAS;
     const int grid = static_cast<int>(std::max(1LL, std::min<long long>(units, static_cast<long long>(sm_count()) * per_sm)));
     if (p.C0 == 32) return run_tc<32, 1>(p, grid, s);
